@@ -1,0 +1,299 @@
+/*
+ * gs3d.h — C ABI of libgs3d.so, a B200-native (sm_100a) engine for the 3D Gaussian
+ * Splatting render / gradient / optimizer / densification hot path of
+ * ThreeDGaussianSplatting.jl.
+ *
+ * Every entry point is `extern "C"`, takes plain device pointers, sizes and POD structs,
+ * returns an int status (GS3D_OK == 0, negative on error; details through
+ * gs3d_last_error_string()) and is asynchronous on the cudaStream_t it is given, unless
+ * stated otherwise.
+ *
+ * Array layouts are the reference's (Julia column-major, first index fastest); "k x n"
+ * means k contiguous fp32 per Gaussian. Index values stored in arrays are 1-based
+ * (0 = invalid), exactly as the reference stores them, so buffers can be shared with
+ * CUDA.jl CuArrays unchanged.
+ *
+ * Reference citations are `path:line` inside LaurensDiels/ThreeDGaussianSplatting.jl.
+ */
+#ifndef GS3D_H
+#define GS3D_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(_WIN32)
+#define GS3D_API __declspec(dllexport)
+#else
+#define GS3D_API __attribute__((visibility("default")))
+#endif
+
+typedef struct CUstream_st* gs3d_stream_t; /* ABI-compatible with cudaStream_t */
+
+/* ---- status codes ------------------------------------------------------------------- */
+#define GS3D_OK 0
+#define GS3D_ERR_INVALID_ARGUMENT (-1)
+#define GS3D_ERR_CUDA (-2)
+#define GS3D_ERR_CAPACITY (-3)   /* duplicated-key count exceeds the caller's capacity   */
+#define GS3D_ERR_WORKSPACE (-4)  /* workspace smaller than the *_workspace_size answer   */
+#define GS3D_ERR_UNSUPPORTED (-5)
+
+/* Device-side status bits written into render_buffers.device_counts[2]. */
+#define GS3D_STATUS_DUP_OVERFLOW 1u
+
+/* render flags */
+#define GS3D_RENDER_NO_HOST_SYNC 1u /* never block: D is checked on the device only      */
+
+/* backward flags */
+#define GS3D_BACKWARD_FIX_SH16 1u /* use coefficient 16 in the degree-3 direction Jacobian
+                                     (the reference reads coefficient 15: sh.jl:249)     */
+
+/* ---- POD parameter structs ---------------------------------------------------------- */
+
+/* PinholeCamera (cameras.jl:50-106). P is the 3x4 projection matrix K [R_w2c | t_w2c]
+ * stored column-major (P[i + 3*j] = row i, column j), position is the optical centre. */
+typedef struct gs3d_camera {
+    int32_t width, height;
+    float fx, fy, skew, cx, cy;
+    float near_z, far_z;
+    float P[12];
+    float position[3];
+} gs3d_camera;
+
+/* RenderOptions (forward_structs.jl:579-719). Clip values are in continuous pixel
+ * coordinates. clipping_mode: 0 = CovarianceBoundaryClamp, 1 = BoundaryFilter. */
+typedef struct gs3d_render_options {
+    float background[3];
+    float antialiasing_min_factor;
+    float min_alpha, max_alpha, min_transmittance;
+    float dilation_x, dilation_y;
+    float clip_x_min, clip_x_max, clip_y_min, clip_y_max;
+    int32_t sh_degree;
+    int32_t clipping_mode;
+    int32_t use_antialiasing;
+} gs3d_render_options;
+
+/* Tiling (forward_structs.jl:340-424). */
+typedef struct gs3d_tiling {
+    int32_t tile_width, tile_height;
+    int32_t nb_tiles_x, nb_tiles_y;
+} gs3d_tiling;
+
+/* TrainableGaussiansVector (gaussians.jl:30-52): SoA of AoS-k arrays. */
+typedef struct gs3d_gaussians {
+    int32_t n;
+    int32_t sh_degree;              /* storage degree: sh_coeffs holds (d+1)^2 x 3 x n */
+    float* means_opacity_features;  /* 4 x n : x, y, z, logit(opacity)                 */
+    float* scaling_features;        /* 3 x n : log-scales                              */
+    float* rotation_features;       /* 4 x n : unnormalised quaternion (r, x, y, z)    */
+    float* sh_coeffs;               /* (d+1)^2 x 3 x n                                 */
+} gs3d_gaussians;
+
+/* RenderBuffers (forward_structs.jl:1541-1600) + Filtered2DGaussiansVector
+ * (forward_structs.jl:762-786). All arrays are caller-owned. */
+typedef struct gs3d_render_buffers {
+    int64_t capacity_n;            /* >= n                                              */
+    int64_t capacity_dup;          /* capacity of the four duplicated-key arrays        */
+    uint8_t* keep_gaussians;       /* n   (Bool)                                        */
+    int32_t* keep_gaussians_cs;    /* n   inclusive cumsum (may be NULL)                */
+    int32_t* fgidx_to_gidx;        /* n   1-based                                       */
+    float* depths;                 /* n                                                 */
+    float* means2d_opacities_inverse_covariances_colors; /* 9 x n                       */
+    int32_t* intersected_tile_ranges;                   /* 2 x 2 x n: xmin ymin xmax ymax */
+    int32_t* nb_overlapped_tiles;      /* n                                             */
+    int32_t* nb_overlapped_tiles_cs;   /* n   inclusive cumsum                          */
+    int64_t* df2dgs_codes;         /* capacity_dup  tile << 32 | depth bits             */
+    int32_t* dfgidx_to_fgidx;      /* capacity_dup                                      */
+    int64_t* sdf2dgs_codes;        /* capacity_dup  sorted                              */
+    int32_t* sdfgidx_to_fgidx;     /* capacity_dup  sorted                              */
+    int32_t* tiles_end_sdfgidx;    /* nb_tiles                                          */
+    int32_t* device_counts;        /* >= 4 int32: [0] F, [1] D, [2] status bits         */
+    void* workspace;               /* scan / sort scratch                               */
+    size_t workspace_bytes;
+} gs3d_render_buffers;
+
+/* RenderOutputs (forward_structs.jl:1-65). Any pointer may be NULL except that backward
+ * needs transmittance and last_contributing. rgb is 3 x h x w, the others h x w. */
+typedef struct gs3d_render_outputs {
+    float* rgb;
+    float* transmittance;
+    float* depth;
+    int32_t* last_contributing_sdfgids;
+} gs3d_render_outputs;
+
+/* FilteredGaussiansGradientsVector (backward_structs.jl:1-29), indexed by fgidx. */
+typedef struct gs3d_fgradients {
+    int32_t sh_degree;               /* storage degree of sh_coeffs_grads               */
+    float* mean2d_grads;             /* 2 x n */
+    float* opacity_grads;            /* n     */
+    float* licov2d_grads;            /* 3 x n */
+    float* color_grads;              /* 3 x n */
+    float* mean3d_grads;             /* 3 x n */
+    float* opacity_feature_grads;    /* n     */
+    float* scaling_features_grads;   /* 3 x n */
+    float* rotation_features_grads;  /* 4 x n */
+    float* sh_coeffs_grads;          /* (d+1)^2 x 3 x n */
+} gs3d_fgradients;
+
+/* GaussianAdamMomentsLearningRatesVector (optimizer.jl:9-29): moments interleaved
+ * [m1, m2] per scalar. */
+typedef struct gs3d_adam_moments {
+    int32_t sh_degree;
+    float* means_moments;              /* 2 x 3 x n */
+    float* opacity_features_moments;   /* 2 x n     */
+    float* scaling_features_moments;   /* 2 x 3 x n */
+    float* rotation_features_moments;  /* 2 x 4 x n */
+    float* sh_coeffs_moments;          /* 2 x (d+1)^2 x 3 x n */
+} gs3d_adam_moments;
+
+/* Adam hyper-parameters (optimizer.jl:831-833, training_structs.jl:43-85). */
+typedef struct gs3d_adam_params {
+    float lr_means, lr_opacity_features, lr_scaling_features, lr_rotation_features;
+    float lr_sh_dc, lr_sh_rest;
+    float beta1, beta2, epsilon;
+    int32_t update_count;  /* before this step; the step uses t = update_count + 1 */
+    int32_t sh_degree;     /* render-options degree of the step (Val(sh) in update!) */
+} gs3d_adam_params;
+
+/* AdaptiveDensityControlBuffers (training_structs.jl:259-290). */
+typedef struct gs3d_adc_buffers {
+    float* accumulated_mean2d_grad_norms_ndc; /* n */
+    int32_t* rendering_contribution_counts;   /* n */
+    float* max_scale_features;                /* n */
+    uint8_t* should_prune;                    /* n */
+    uint8_t* should_densify;                  /* n */
+    uint8_t* should_clone;                    /* n */
+    uint8_t* new_gaussian_counts;             /* n */
+    int32_t* new_gaussian_counts_cs;          /* n */
+    int32_t* ngidx_to_gidx;                   /* n' (capacity 2 n)                    */
+    void* workspace;
+    size_t workspace_bytes;
+} gs3d_adc_buffers;
+
+/* Thresholds of one densify/prune decision (training.jl:325-364). */
+typedef struct gs3d_adc_params {
+    float densification_mean2d_grad_norm_threshold_ndc;
+    float densification_size_threshold;   /* already scaled by the scene radius */
+    float pruning_min_opacity;
+    float pruning_3d_max_scale;           /* already scaled by the scene radius */
+    int32_t use_max_scale_pruning;        /* iteration > opacity_reset_interval */
+} gs3d_adc_params;
+
+/* ---- drop-in replacement of deps/cub_sort_pairs (cub_sort_pairs_wrapper.cu:31-62) --- */
+
+/* Same signature as the reference's `determine_sort_pairs_temp_storage`
+ * (cub_sort_pairs_wrapper.cu:49-62, bound by forward_core.jl:629-638). */
+GS3D_API size_t determine_sort_pairs_temp_storage(
+    const int64_t* keys_in, int64_t* keys_out,
+    const int32_t* values_in, int32_t* values_out,
+    int nb_items, int highest_key_bit);
+
+/* Same signature as the reference's `sort_pairs` (cub_sort_pairs_wrapper.cu:31-43, bound
+ * by forward_core.jl:646-659): stable LSD radix sort of int64 keys with int32 values over
+ * bits [0, highest_key_bit). Runs on the legacy default stream, as the reference does. */
+GS3D_API void sort_pairs(
+    void* temp_storage, size_t temp_storage_bytes,
+    const int64_t* keys_in, int64_t* keys_out,
+    const int32_t* values_in, int32_t* values_out,
+    int nb_items, int highest_key_bit);
+
+/* Stream-ordered variant of sort_pairs that reports errors. */
+GS3D_API int gs3d_sort_pairs_async(
+    void* temp_storage, size_t temp_storage_bytes,
+    const int64_t* keys_in, int64_t* keys_out,
+    const int32_t* values_in, int32_t* values_out,
+    int nb_items, int highest_key_bit, gs3d_stream_t stream);
+
+/* ---- render forward: render! GPU (forward_core.jl:196-314) -------------------------- */
+
+/* Bytes of render_buffers.workspace needed for these capacities. */
+GS3D_API int gs3d_render_forward_workspace_size(
+    int64_t capacity_n, int64_t capacity_dup, int32_t nb_tiles, size_t* bytes);
+
+/* Filter (F1), compact (F2), project (F3), count + scan duplicates (F4), write keys (F5),
+ * sort (F6), tile ranges (F7), alpha-blend (F8) or fill the void image (F9).
+ * F and D are written to render_buffers.device_counts[0..1]; when host_counts is not NULL
+ * they are also copied there (pinned memory; valid after the stream reaches this point).
+ * Without GS3D_RENDER_NO_HOST_SYNC the call waits once for D and returns
+ * GS3D_ERR_CAPACITY (host_counts filled, outputs undefined) when D > capacity_dup. */
+GS3D_API int gs3d_render_forward(
+    const gs3d_render_outputs* outputs, const gs3d_gaussians* gaussians,
+    const gs3d_camera* camera, const gs3d_tiling* tiling,
+    const gs3d_render_options* options, gs3d_render_buffers* buffers,
+    int32_t* host_counts, uint32_t flags, gs3d_stream_t stream);
+
+/* ---- backward: backward! (backward_core.jl:37-72) ----------------------------------- */
+
+/* Zeroes the 2D gradients (B1), runs the reverse blend with warp-reduced atomics (B2) and
+ * the projection backward (B3, B4). rgb_image_grad is 3 x h x w. */
+GS3D_API int gs3d_backward(
+    const gs3d_fgradients* fgradients, const float* rgb_image_grad,
+    const gs3d_render_outputs* outputs, const gs3d_gaussians* gaussians,
+    const gs3d_camera* camera, const gs3d_tiling* tiling,
+    const gs3d_render_options* options, const gs3d_render_buffers* buffers,
+    uint32_t flags, gs3d_stream_t stream);
+
+/* ---- optimizer: update! (optimizer.jl:964-1009) ------------------------------------- */
+
+/* One sparse Adam step over the F filtered Gaussians (F read from device_counts[0]);
+ * fgidx_to_gidx entries <= 0 are skipped (optimizer.jl:1099-1103). All 59 parameters of a
+ * Gaussian are updated in one fused kernel. */
+GS3D_API int gs3d_adam_step(
+    const gs3d_gaussians* gaussians, const gs3d_adam_moments* moments,
+    const gs3d_fgradients* fgradients, const int32_t* fgidx_to_gidx,
+    const int32_t* device_counts, const gs3d_adam_params* params, gs3d_stream_t stream);
+
+/* ---- loss: training.jl:196-217 (L1 + weight * DSSIM, with gradient) ----------------- */
+
+GS3D_API int gs3d_loss_workspace_size(int32_t width, int32_t height, size_t* bytes);
+
+/* rendered and target are 3 x h x w. Writes the scalar loss to loss_device[0] (and
+ * [1] = L1, [2] = DSSIM) and the gradient image. */
+GS3D_API int gs3d_loss_l1_dssim(
+    const float* rendered, const float* target, int32_t width, int32_t height,
+    float dssim_weight, float* loss_device, float* rgb_image_grad,
+    void* workspace, size_t workspace_bytes, gs3d_stream_t stream);
+
+/* ---- adaptive density control: training.jl:313-580, gaussians.jl:1526-1694 ---------- */
+
+/* update_adc_stats_kernel! (training.jl:472-497). */
+GS3D_API int gs3d_adc_stats(
+    const gs3d_adc_buffers* adc, const gs3d_fgradients* fgradients,
+    const int32_t* fgidx_to_gidx, const int32_t* device_counts,
+    int32_t width, int32_t height, gs3d_stream_t stream);
+
+GS3D_API int gs3d_adc_workspace_size(int32_t n, size_t* bytes);
+
+/* Masks, counts and their scan (training.jl:325-389) and ngidx_to_gidx
+ * (training.jl:557-580). Blocks once and returns n' through new_n. */
+GS3D_API int gs3d_densify_prune_plan(
+    const gs3d_adc_buffers* adc, const gs3d_gaussians* gaussians,
+    const gs3d_adc_params* params, int32_t* new_n, gs3d_stream_t stream);
+
+/* Fill the n' Gaussians and moments (gaussians.jl:1589-1694, optimizer.jl:1342-1378) into
+ * caller-allocated outputs and retarget fgidx_to_gidx (training.jl:514-541). Split means
+ * use a counter-based normal sampler keyed by (seed, old gidx). */
+GS3D_API int gs3d_densify_apply(
+    const gs3d_adc_buffers* adc, const gs3d_gaussians* old_gaussians,
+    const gs3d_adam_moments* old_moments, const gs3d_gaussians* new_gaussians,
+    const gs3d_adam_moments* new_moments, int32_t* fgidx_to_gidx,
+    const int32_t* device_counts, float log_splitting_scale_factor, uint64_t seed,
+    gs3d_stream_t stream);
+
+/* reset_opacities! (gaussians.jl:1093-1101) + zero_opacity_features_adam_moments!
+ * (optimizer.jl:754-756). */
+GS3D_API int gs3d_opacity_reset(
+    const gs3d_gaussians* gaussians, const gs3d_adam_moments* moments,
+    float max_opacity, gs3d_stream_t stream);
+
+/* ---- misc ---------------------------------------------------------------------------- */
+GS3D_API const char* gs3d_last_error_string(void);
+GS3D_API int gs3d_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GS3D_H */

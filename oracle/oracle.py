@@ -1,0 +1,245 @@
+"""ctypes front end of the CPU oracle — TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference legs may import
+this module, and only as the checker or the timed CPU baseline, never as a product path.
+The C++ it loads restates ThreeDGaussianSplatting.jl (see the .cpp headers for file:line).
+
+Parity pinning: the oracle is checked against every golden vector of the reference's own
+tests (tests/test_oracle_golden.py, fixtures in tests/golden/); the SSIM term of the loss is
+the exception (FastCUDASSIM is not vendored: parity unpinned).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import sys
+from pathlib import Path
+
+import numpy as np
+
+_REPO = Path(__file__).resolve().parent.parent
+_PKG = _REPO / "threedgaussiansplatting.jl_b200"
+if str(_PKG) not in sys.path:
+    sys.path.insert(0, str(_PKG))
+
+from gs3d import _abi  # noqa: E402  (ctypes mirrors of include/gs3d.h)
+
+from . import build as _build  # noqa: E402
+
+_LIB = None
+
+
+def lib():
+    global _LIB
+    if _LIB is None:
+        path = _build.build_oracle()
+        _LIB = C.CDLL(str(path))
+        vp = C.c_void_p
+        P = C.POINTER
+        _LIB.oracle_render.restype = C.c_int
+        _LIB.oracle_render.argtypes = [P(_abi.GaussiansC), P(_abi.Camera), P(_abi.TilingC),
+                                       P(_abi.RenderOptionsC)] + [vp] * 8 + [C.c_int64] + [vp] * 10
+        _LIB.oracle_backward.restype = C.c_int
+        _LIB.oracle_backward.argtypes = [P(_abi.GaussiansC), P(_abi.Camera), P(_abi.TilingC),
+                                         P(_abi.RenderOptionsC), C.c_int32] + [vp] * 7 + \
+            [C.c_uint32] + [vp] * 9 + [C.c_int32]
+        _LIB.oracle_sort_pairs.restype = C.c_int
+        _LIB.oracle_sort_pairs.argtypes = [vp, vp, vp, vp, C.c_int64, C.c_int]
+        _LIB.oracle_cpu_render.restype = C.c_int32
+        _LIB.oracle_cpu_render.argtypes = [P(_abi.GaussiansC), P(_abi.Camera),
+                                           P(_abi.RenderOptionsC), vp, vp, vp, C.c_int32]
+        _LIB.oracle_adam.restype = C.c_int
+        _LIB.oracle_adam.argtypes = [P(_abi.GaussiansC), P(_abi.AdamMomentsC), P(_abi.FGradientsC),
+                                     vp, C.c_int32, P(_abi.AdamParamsC), C.c_float, C.c_float]
+        _LIB.oracle_loss.restype = C.c_int
+        _LIB.oracle_loss.argtypes = [vp, vp, C.c_int32, C.c_int32, C.c_float, vp, vp]
+        _LIB.oracle_adc_stats.restype = C.c_int
+        _LIB.oracle_adc_stats.argtypes = [vp, vp, vp, vp, C.c_int32, C.c_int32, C.c_int32]
+        _LIB.oracle_adc_plan.restype = C.c_int32
+        _LIB.oracle_adc_plan.argtypes = [P(_abi.GaussiansC), vp, vp, P(_abi.AdcParamsC)] + [vp] * 7
+        _LIB.oracle_adc_apply.restype = C.c_int
+        _LIB.oracle_adc_apply.argtypes = [P(_abi.GaussiansC), P(_abi.AdamMomentsC),
+                                          P(_abi.GaussiansC), P(_abi.AdamMomentsC)] + [vp] * 5 + \
+            [C.c_int32, C.c_float, C.c_uint64]
+        _LIB.oracle_opacity_reset.restype = C.c_int
+        _LIB.oracle_opacity_reset.argtypes = [P(_abi.GaussiansC), P(_abi.AdamMomentsC), C.c_float]
+        _LIB.oracle_expf.restype = C.c_float
+        _LIB.oracle_expf.argtypes = [C.c_float]
+        _LIB.oracle_logf.restype = C.c_float
+        _LIB.oracle_logf.argtypes = [C.c_float]
+        _LIB.oracle_split_normals.restype = None
+        _LIB.oracle_split_normals.argtypes = [C.c_uint64, C.c_uint64, vp]
+        _LIB.oracle_compact.restype = C.c_int32
+        _LIB.oracle_compact.argtypes = [vp, C.c_int64, vp, vp]
+        _LIB.oracle_dup_keys.restype = C.c_int64
+        _LIB.oracle_dup_keys.argtypes = [C.c_int32, vp, vp, vp, C.c_int32, vp, vp]
+        _LIB.oracle_tiles_end.restype = None
+        _LIB.oracle_tiles_end.argtypes = [vp, C.c_int64, C.c_int32, vp]
+    return _LIB
+
+
+def compact(keep: np.ndarray):
+    keep = np.ascontiguousarray(keep, np.uint8)
+    cs = np.zeros(keep.size, np.int32)
+    f2g = np.zeros(keep.size, np.int32)
+    F = lib().oracle_compact(_p(keep), keep.size, _p(cs), _p(f2g))
+    return cs, f2g[:F]
+
+
+def dup_keys(ntiles: np.ndarray, ranges: np.ndarray, depths: np.ndarray, tiles_x: int):
+    ntiles = np.ascontiguousarray(ntiles, np.int32)
+    ranges = np.ascontiguousarray(ranges, np.int32).reshape(-1, 4)
+    depths = np.ascontiguousarray(depths, np.float32)
+    D = int(ntiles.sum())
+    codes = np.zeros(max(D, 1), np.int64)
+    dfg = np.zeros(max(D, 1), np.int32)
+    lib().oracle_dup_keys(ntiles.size, _p(ntiles), _p(ranges), _p(depths), tiles_x, _p(codes), _p(dfg))
+    return codes[:D], dfg[:D]
+
+
+def tiles_end(scodes: np.ndarray, nb_tiles: int):
+    scodes = np.ascontiguousarray(scodes, np.int64)
+    out = np.zeros(nb_tiles, np.int32)
+    lib().oracle_tiles_end(_p(scodes), scodes.size, nb_tiles, _p(out))
+    return out
+
+
+def _p(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+class NpGaussians:
+    """Gaussians as C-contiguous float32 numpy arrays in the reference layouts."""
+
+    def __init__(self, means_opacity_features, scaling_features, rotation_features, sh_coeffs):
+        f = lambda a: np.ascontiguousarray(np.asarray(a, dtype=np.float32))
+        self.mo, self.sf, self.rf, self.sh = map(f, (means_opacity_features, scaling_features,
+                                                     rotation_features, sh_coeffs))
+
+    @classmethod
+    def from_vector(cls, gv) -> "NpGaussians":
+        return cls(*(t.detach().cpu().numpy() for t in gv.tensors()))
+
+    @property
+    def n(self):
+        return self.mo.shape[0]
+
+    @property
+    def sh_degree(self):
+        return int(round(np.sqrt(self.sh.shape[2]))) - 1
+
+    def to_c(self):
+        g = _abi.GaussiansC()
+        g.n, g.sh_degree = self.n, self.sh_degree
+        g.means_opacity_features = _p(self.mo)
+        g.scaling_features = _p(self.sf)
+        g.rotation_features = _p(self.rf)
+        g.sh_coeffs = _p(self.sh)
+        return g
+
+    def copy(self):
+        return NpGaussians(self.mo.copy(), self.sf.copy(), self.rf.copy(), self.sh.copy())
+
+
+def render(g: NpGaussians, camera, tiling, options, dup_capacity: int | None = None) -> dict:
+    """GPU-path render restatement; returns every intermediate in reference layouts."""
+    n, W, H = g.n, camera.width, camera.height
+    cap = max(n, 1)
+    out = dict(
+        keep=np.zeros(cap, np.uint8), keep_cs=np.zeros(cap, np.int32),
+        fgidx_to_gidx=np.zeros(cap, np.int32), depths=np.zeros(cap, np.float32),
+        f2d=np.zeros((cap, 9), np.float32), ranges=np.zeros((cap, 4), np.int32),
+        ntiles=np.zeros(cap, np.int32), ntiles_cs=np.zeros(cap, np.int32),
+        tiles_end=np.zeros(tiling.nb_tiles, np.int32), rgb=np.zeros((W, H, 3), np.float32),
+        trans=np.zeros((W, H), np.float32), depth=np.zeros((W, H), np.float32),
+        last=np.zeros((W, H), np.int32))
+    counts = np.zeros(2, np.int64)
+    dc = dup_capacity or max(4 * n, 1024)
+    gc, cc, tc, oc = g.to_c(), camera.to_c(), tiling.to_c(), options.to_c()
+    while True:
+        dup = dict(codes=np.zeros(dc, np.int64), dfg=np.zeros(dc, np.int32),
+                   scodes=np.zeros(dc, np.int64), sfg=np.zeros(dc, np.int32))
+        st = lib().oracle_render(C.byref(gc), C.byref(cc), C.byref(tc), C.byref(oc),
+                                 _p(out["keep"]), _p(out["keep_cs"]), _p(out["fgidx_to_gidx"]),
+                                 _p(out["depths"]), _p(out["f2d"]), _p(out["ranges"]),
+                                 _p(out["ntiles"]), _p(out["ntiles_cs"]), dc, _p(dup["codes"]),
+                                 _p(dup["dfg"]), _p(dup["scodes"]), _p(dup["sfg"]),
+                                 _p(out["tiles_end"]), _p(out["rgb"]), _p(out["trans"]),
+                                 _p(out["depth"]), _p(out["last"]), _p(counts))
+        if st == _abi.GS3D_ERR_CAPACITY:
+            dc = int(counts[1]) + 16
+            continue
+        assert st == 0
+        break
+    F, D = int(counts[0]), int(counts[1])
+    out.update(dup)
+    out["F"], out["D"] = F, D
+    for k in ("keep", "keep_cs"):
+        out[k] = out[k][:n]
+    for k in ("fgidx_to_gidx", "depths", "f2d", "ranges", "ntiles", "ntiles_cs"):
+        out[k] = out[k][:F]
+    for k in ("codes", "dfg", "scodes", "sfg"):
+        out[k] = out[k][:D]
+    return out
+
+
+def backward(g: NpGaussians, camera, tiling, options, fwd: dict, rgb_grad: np.ndarray,
+             flags: int = 0, sh_grad_degree: int | None = None) -> dict:
+    F = fwd["F"]
+    d = g.sh_degree if sh_grad_degree is None else sh_grad_degree
+    S = (d + 1) ** 2
+    cap = max(F, 1)
+    o = dict(mean2d=np.zeros((cap, 2), np.float32), opacity=np.zeros(cap, np.float32),
+             licov=np.zeros((cap, 3), np.float32), color=np.zeros((cap, 3), np.float32),
+             mean3d=np.zeros((cap, 3), np.float32), opacity_feature=np.zeros(cap, np.float32),
+             scaling=np.zeros((cap, 3), np.float32), rotation=np.zeros((cap, 4), np.float32),
+             sh=np.zeros((cap, 3, S), np.float32))
+    rg = np.ascontiguousarray(rgb_grad, dtype=np.float32)
+    sfg = fwd["sfg"] if fwd["D"] > 0 else np.zeros(1, np.int32)
+    gc, cc, tc, oc = g.to_c(), camera.to_c(), tiling.to_c(), options.to_c()
+    st = lib().oracle_backward(C.byref(gc), C.byref(cc), C.byref(tc), C.byref(oc), F,
+                               _p(np.ascontiguousarray(fwd["fgidx_to_gidx"])), _p(np.ascontiguousarray(fwd["f2d"])),
+                               _p(np.ascontiguousarray(sfg)), _p(fwd["tiles_end"]), _p(fwd["trans"]),
+                               _p(fwd["last"]), _p(rg), flags, _p(o["mean2d"]), _p(o["opacity"]),
+                               _p(o["licov"]), _p(o["color"]), _p(o["mean3d"]),
+                               _p(o["opacity_feature"]), _p(o["scaling"]), _p(o["rotation"]),
+                               _p(o["sh"]), d)
+    assert st == 0
+    return {k: v[:F] for k, v in o.items()}
+
+
+def sort_pairs(keys: np.ndarray, vals: np.ndarray, highest_key_bit: int):
+    keys = np.ascontiguousarray(keys, np.int64)
+    vals = np.ascontiguousarray(vals, np.int32)
+    ko, vo = np.empty_like(keys), np.empty_like(vals)
+    lib().oracle_sort_pairs(_p(keys), _p(ko), _p(vals), _p(vo), keys.size, highest_key_bit)
+    return ko, vo
+
+
+def cpu_render(g: NpGaussians, camera, options, nthreads: int = 1):
+    W, H = camera.width, camera.height
+    rgb = np.zeros((W, H, 3), np.float32)
+    trans = np.zeros((W, H), np.float32)
+    depth = np.zeros((W, H), np.float32)
+    gc, cc, oc = g.to_c(), camera.to_c(), options.to_c()
+    F = lib().oracle_cpu_render(C.byref(gc), C.byref(cc), C.byref(oc), _p(rgb), _p(trans),
+                                _p(depth), nthreads)
+    return dict(rgb=rgb, trans=trans, depth=depth, F=F)
+
+
+def loss(rendered: np.ndarray, target: np.ndarray, weight: float = 0.2):
+    """(loss, l1, dssim), gradient (w, h, 3)."""
+    K = np.ascontiguousarray(rendered, np.float32)
+    I = np.ascontiguousarray(target, np.float32)
+    W, H = K.shape[0], K.shape[1]
+    out = np.zeros(3, np.float64)
+    grad = np.zeros_like(K)
+    lib().oracle_loss(_p(K), _p(I), W, H, weight, _p(out), _p(grad))
+    return out, grad
+
+
+def expf(x: float) -> float:
+    return lib().oracle_expf(x)
+
+
+def logf(x: float) -> float:
+    return lib().oracle_logf(x)

@@ -1,0 +1,164 @@
+"""Render forward on the GPU (through libgs3d.so) against the CPU oracle.
+
+Bar: keep mask, scans, compaction, depths, tile rectangles, duplicate keys, the sorted
+key/value arrays and tile ends are bit-exact; images within 1e-4 max abs (they are expected
+to be bit-exact too: both sides follow the same operation order and the same exp/log).
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+import gs3d
+from gs3d import RenderBuffers, RenderOptions, RenderOutputs, Tiling
+from gs3d.scene import CONFIGS, SceneSpec, create_test_scene, look_at_camera, synthetic_gaussians
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def gpu_render(gv, cam, til, opt, device, capacity_dup=None, host_sync=True):
+    g = gv.to(device)
+    out = RenderOutputs.create(cam.width, cam.height, device, include_depth=True)
+    buf = RenderBuffers.create(g.n, til.nb_tiles, device, capacity_dup=capacity_dup)
+    gs3d.render(out, g, cam, til, opt, buf, host_sync=host_sync)
+    torch.cuda.synchronize()
+    F, D = gs3d.counts(buf)
+    cpu = lambda t: t.cpu().numpy()
+    r = dict(F=F, D=D, keep=cpu(buf.keep_gaussians[: g.n]), keep_cs=cpu(buf.keep_gaussians_cs[: g.n]),
+             fgidx_to_gidx=cpu(buf.fgidx_to_gidx[:F]), depths=cpu(buf.depths[:F]),
+             f2d=cpu(buf.f2d[:F]), ranges=cpu(buf.intersected_tile_ranges[:F]),
+             ntiles=cpu(buf.nb_overlapped_tiles[:F]), ntiles_cs=cpu(buf.nb_overlapped_tiles_cs[:F]),
+             codes=cpu(buf.df2dgs_codes[:D]), dfg=cpu(buf.dfgidx_to_fgidx[:D]),
+             scodes=cpu(buf.sdf2dgs_codes[:D]), sfg=cpu(buf.sdfgidx_to_fgidx[:D]),
+             tiles_end=cpu(buf.tiles_end_sdfgidx[: til.nb_tiles]), rgb=cpu(out.rgb),
+             trans=cpu(out.transmittance), depth=cpu(out.depth),
+             last=cpu(out.last_contributing_sdfgids), status=int(buf.device_counts[2].item()))
+    return r, buf
+
+
+def compare(gpu, ref, exact_images=True):
+    assert gpu["F"] == ref["F"] and gpu["D"] == ref["D"]
+    for k in ("keep", "keep_cs", "fgidx_to_gidx", "ranges", "ntiles", "ntiles_cs", "codes", "dfg",
+              "scodes", "sfg", "last"):
+        assert np.array_equal(gpu[k], ref[k]), k
+    if ref["D"] > 0:
+        assert np.array_equal(gpu["tiles_end"], ref["tiles_end"])
+    assert np.array_equal(gpu["depths"].view(np.uint32), ref["depths"].view(np.uint32))
+    nonempty = ref["ntiles"] > 0
+    assert np.array_equal(gpu["f2d"][nonempty].view(np.uint32), ref["f2d"][nonempty].view(np.uint32))
+    for k in ("rgb", "trans", "depth"):
+        both_inf = np.isinf(gpu[k]) & np.isinf(ref[k])
+        diff = np.where(both_inf, 0.0, np.abs(gpu[k].astype(np.float64) - ref[k]))
+        assert diff.max() <= 1e-4, (k, diff.max())
+        if exact_images:
+            assert np.array_equal(gpu[k], ref[k]), (k, np.count_nonzero(gpu[k] != ref[k]))
+
+
+@pytest.mark.parametrize("deg", [0, 1, 2, 3])
+def test_test_scene(cuda, deg):
+    gv, cams = create_test_scene(deg)
+    cam = cams[0]
+    opt = RenderOptions.for_camera(cam, deg)
+    til = Tiling.for_camera(cam, 16, 16)
+    gpu, _ = gpu_render(gv, cam, til, opt, cuda)
+    ref = O.render(O.NpGaussians.from_vector(gv), cam, til, opt)
+    compare(gpu, ref)
+
+
+CASES = [
+    # name, spec, seed, (w, h, fov, pos), tile, options kwargs, render degree
+    ("cfg0", SceneSpec(16_384, "uniform:1", -4.0, 0.5), 0, (256, 256, 60.0, (0, 0, 3)), None, {}, 3),
+    ("cfg0_filter", SceneSpec(16_384, "uniform:1", -4.0, 0.5), 0, (256, 256, 60.0, (0, 0, 3)), None,
+     dict(clipping_mode=gs3d.FILTER), 3),
+    ("cfg0_aa_bg", SceneSpec(16_384, "uniform:1", -4.0, 0.5), 5, (256, 256, 60.0, (0.3, 0.2, 2.5)),
+     None, dict(use_antialiasing=True, background=(0.2, 0.5, 0.9)), 3),
+    ("deg1_of3", SceneSpec(20_000, "uniform:1.5", -4.5, 0.5), 6, (320, 200, 70.0, (0, 1, 3)), None, {}, 1),
+    ("ragged_720p", SceneSpec(60_000, "uniform:3", -4.0, 0.6), 7, (1280, 720, 50.0, (0, 1.5, 6)),
+     (16, 16), {}, 3),
+    ("big_tiles_1080", SceneSpec(40_000, "normal:1.5", -4.0, 0.5), 8, (1920, 1080, 50.0, (1, 2, 5)),
+     (16, 32), {}, 2),
+    ("odd_size", SceneSpec(5_000, "uniform:1", -3.5, 0.5), 9, (333, 171, 80.0, (0, 0, 2.2)), (32, 8), {}, 0),
+]
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
+def test_random_scenes(cuda, case):
+    _, spec, seed, (w, h, fov, pos), tile, kw, deg = case
+    gv = synthetic_gaussians(spec, seed)
+    cam = look_at_camera(w, h, fov, pos)
+    opt = RenderOptions.for_camera(cam, deg, **kw)
+    til = Tiling.for_camera(cam, *(tile or (None, None)))
+    gpu, _ = gpu_render(gv, cam, til, opt, cuda)
+    ref = O.render(O.NpGaussians.from_vector(gv), cam, til, opt)
+    assert ref["F"] > 0 and ref["D"] > 0
+    compare(gpu, ref)
+
+
+def test_empty_and_void(cuda):
+    cam = look_at_camera(64, 48, 60.0, (0, 0, 3))
+    til = Tiling.for_camera(cam)
+    opt = RenderOptions.for_camera(cam, 0, background=(0.1, 0.2, 0.3))
+    # n = 0
+    empty = synthetic_gaussians(SceneSpec(0, "uniform:1", -4, 0.5, sh_degree=0), 0)
+    gpu, _ = gpu_render(empty, cam, til, opt, cuda)
+    assert gpu["F"] == 0 and np.all(gpu["trans"] == 1) and np.all(np.isinf(gpu["depth"]))
+    assert np.allclose(gpu["rgb"], [0.1, 0.2, 0.3]) and np.all(gpu["last"] == 0)
+    # everything behind the camera: F = 0
+    gv = synthetic_gaussians(SceneSpec(100, "uniform:0.5", -4, 0.5, sh_degree=0), 1)
+    gv.means_opacity_features[:, 2] += 10.0  # z in [9.5, 10.5], camera at z=3 looking at -z
+    gpu, _ = gpu_render(gv, cam, til, opt, cuda)
+    ref = O.render(O.NpGaussians.from_vector(gv), cam, til, opt)
+    assert gpu["F"] == ref["F"] == 0
+    compare(gpu, ref)
+    # in front but far off-screen: F > 0, D = 0
+    gv = synthetic_gaussians(SceneSpec(100, "uniform:0.5", -6, 0.1, sh_degree=0), 2)
+    gv.means_opacity_features[:, 0] += 50.0
+    gpu, _ = gpu_render(gv, cam, til, opt, cuda)
+    ref = O.render(O.NpGaussians.from_vector(gv), cam, til, opt)
+    assert ref["F"] > 0 and ref["D"] == 0
+    compare(gpu, ref)
+
+
+def test_dup_capacity_growth_and_overflow_flag(cuda):
+    gv = synthetic_gaussians(SceneSpec(16_384, "uniform:1", -4.0, 0.5), 0)
+    cam = look_at_camera(256, 256, 60.0, (0, 0, 3))
+    opt = RenderOptions.for_camera(cam, 3)
+    til = Tiling.for_camera(cam)
+    ref = O.render(O.NpGaussians.from_vector(gv), cam, til, opt)
+    gpu, buf = gpu_render(gv, cam, til, opt, cuda, capacity_dup=1000)  # grows and retries
+    assert buf.capacity_dup >= ref["D"]
+    compare(gpu, ref)
+    gpu, _ = gpu_render(gv, cam, til, opt, cuda, capacity_dup=1000, host_sync=False)
+    assert gpu["status"] & 1  # GS3D_STATUS_DUP_OVERFLOW, outputs undefined but in bounds
+
+
+def _sort_gpu(keys, vals, bits, device):
+    lib = gs3d.lib()
+    n = keys.size
+    k_in = torch.from_numpy(keys).to(device)
+    v_in = torch.from_numpy(vals).to(device)
+    k_out = torch.empty_like(k_in)
+    v_out = torch.empty_like(v_in)
+    nbytes = lib.determine_sort_pairs_temp_storage(None, None, None, None, n, bits)
+    tmp = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=device)
+    torch.cuda.synchronize()
+    lib.sort_pairs(C.c_void_p(tmp.data_ptr()), nbytes, C.c_void_p(k_in.data_ptr()),
+                   C.c_void_p(k_out.data_ptr()), C.c_void_p(v_in.data_ptr()),
+                   C.c_void_p(v_out.data_ptr()), n, bits)
+    torch.cuda.synchronize()
+    assert np.array_equal(k_in.cpu().numpy(), keys)  # input untouched
+    return k_out.cpu().numpy(), v_out.cpu().numpy()
+
+
+@pytest.mark.parametrize("n,bits", [(1, 35), (7, 35), (4096, 41), (4097, 44), (100_003, 46),
+                                    (250_000, 64), (10_000, 8), (10_000, 1)])
+def test_sort_pairs_dropin(cuda, n, bits):
+    rng = np.random.default_rng(n + bits)
+    keys = rng.integers(0, 1 << 62, n, dtype=np.int64)
+    keys[: n // 3] = keys[0]  # many exact duplicates: stability matters
+    vals = rng.permutation(n).astype(np.int32)
+    ko, vo = _sort_gpu(keys, vals, bits, cuda)
+    rk, rv = O.sort_pairs(keys, vals, bits)
+    assert np.array_equal(ko, rk) and np.array_equal(vo, rv)

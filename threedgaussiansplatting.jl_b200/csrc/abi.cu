@@ -1,0 +1,83 @@
+// abi.cu — error plumbing, version, and the drop-in replacement of the reference's only
+// native component, deps/cub_sort_pairs/cub_sort_pairs_wrapper.cu (sort_pairs and
+// determine_sort_pairs_temp_storage, same signatures, bound by forward_core.jl:629-659).
+#include <cstdarg>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace gs3d {
+
+namespace {
+thread_local char g_error[512] = "no error";
+}
+
+void set_error(const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_error, sizeof(g_error), fmt, ap);
+    va_end(ap);
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    set_error("CUDA error in %s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+    return GS3D_ERR_CUDA;
+}
+
+int invalid(const char* fmt, ...) {
+    char buf[400];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    set_error("invalid argument: %s", buf);
+    return GS3D_ERR_INVALID_ARGUMENT;
+}
+
+int device_sm_count() {
+    int dev = 0, sms = kSMs;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms;
+}
+
+}  // namespace gs3d
+
+using namespace gs3d;
+
+extern "C" {
+
+GS3D_API const char* gs3d_last_error_string(void) { return g_error; }
+
+GS3D_API int gs3d_version(void) { return 1; }
+
+GS3D_API size_t determine_sort_pairs_temp_storage(const int64_t* keys_in, int64_t* keys_out,
+                                                  const int32_t* values_in, int32_t* values_out,
+                                                  int nb_items, int highest_key_bit) {
+    (void)keys_in; (void)keys_out; (void)values_in; (void)values_out; (void)highest_key_bit;
+    return radix_sort_workspace_bytes(nb_items > 0 ? nb_items : 1);
+}
+
+GS3D_API int gs3d_sort_pairs_async(void* temp_storage, size_t temp_storage_bytes,
+                                   const int64_t* keys_in, int64_t* keys_out,
+                                   const int32_t* values_in, int32_t* values_out, int nb_items,
+                                   int highest_key_bit, gs3d_stream_t stream) {
+    if (nb_items < 0) return invalid("nb_items = %d", nb_items);
+    if (nb_items == 0) return GS3D_OK;
+    if (!temp_storage || !keys_in || !keys_out || !values_in || !values_out)
+        return invalid("NULL pointer");
+    return radix_sort_pairs(temp_storage, temp_storage_bytes, keys_in, keys_out, values_in,
+                            values_out, nb_items, nullptr, nb_items, highest_key_bit,
+                            reinterpret_cast<cudaStream_t>(stream));
+}
+
+// The reference's wrapper drops CUB's status and passes no stream (legacy default stream);
+// this one keeps that signature. Errors are available through gs3d_last_error_string().
+GS3D_API void sort_pairs(void* temp_storage, size_t temp_storage_bytes, const int64_t* keys_in,
+                         int64_t* keys_out, const int32_t* values_in, int32_t* values_out,
+                         int nb_items, int highest_key_bit) {
+    (void)gs3d_sort_pairs_async(temp_storage, temp_storage_bytes, keys_in, keys_out, values_in,
+                                values_out, nb_items, highest_key_bit, nullptr);
+}
+
+}  // extern "C"

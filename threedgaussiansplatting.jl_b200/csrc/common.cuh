@@ -1,0 +1,186 @@
+// common.cuh — shared device/host helpers of libgs3d.so (sm_100a).
+//
+// Numerics contract: every translation unit is compiled with -fmad=false, so a*b+c is two
+// IEEE roundings unless written fmaf(); division and sqrt are IEEE round-to-nearest
+// (nvcc's default -prec-div/-prec-sqrt). exp and log are this file's gs_expf / gs_logf,
+// implemented from published methods so that results are reproducible off the GPU:
+//   * gs_expf: Cody & Waite reduction x = k ln2 + r (|r| <= ln2/2) and the degree-7 Taylor
+//     polynomial of e^r (Horner, fused multiply-adds), scaled by 2^k in two exact steps.
+//   * gs_logf: x = 2^e m, m in [sqrt(1/2), sqrt(2)); log m = 2 atanh((m-1)/(m+1)) by the
+//     odd Taylor series of atanh through the 9th power.
+// Both are within about 2 ulp of the true value.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <cstdio>
+#include <climits>
+#include <cstring>
+#include <algorithm>
+
+#include "../../include/gs3d.h"
+
+#define GS_HD __host__ __device__ __forceinline__
+
+namespace gs3d {
+
+// ---- error plumbing (defined in abi.cu) ------------------------------------------------
+void set_error(const char* fmt, ...);
+int cuda_fail(cudaError_t e, const char* what);
+int invalid(const char* fmt, ...);
+
+#define GS3D_CUDA(expr, what)                                           \
+    do {                                                                \
+        cudaError_t e_ = (expr);                                        \
+        if (e_ != cudaSuccess) return ::gs3d::cuda_fail(e_, what);      \
+    } while (0)
+#define GS3D_LAUNCHED(what)                                             \
+    do {                                                                \
+        cudaError_t e_ = cudaGetLastError();                            \
+        if (e_ != cudaSuccess) return ::gs3d::cuda_fail(e_, what);      \
+    } while (0)
+#define GS3D_RETURN_IF(status)                                          \
+    do {                                                                \
+        int s_ = (status);                                              \
+        if (s_ != GS3D_OK) return s_;                                   \
+    } while (0)
+
+// ---- bit casts ----------------------------------------------------------------------------
+GS_HD float u2f(uint32_t u) {
+#ifdef __CUDA_ARCH__
+    return __uint_as_float(u);
+#else
+    float f; memcpy(&f, &u, 4); return f;
+#endif
+}
+GS_HD uint32_t f2u(float f) {
+#ifdef __CUDA_ARCH__
+    return __float_as_uint(f);
+#else
+    uint32_t u; memcpy(&u, &f, 4); return u;
+#endif
+}
+
+// ---- exp / log (see header comment) --------------------------------------------------------
+GS_HD float gs_expf(float x) {
+    if (x != x) return x;
+    if (x > 88.72283935546875f) return u2f(0x7f800000u);
+    if (x < -104.0f) return 0.0f;
+    const float k = rintf(x * 1.44269502162933349609375f);
+    float r = fmaf(-k, 0.693147182464599609375f, x);
+    r = fmaf(-k, -1.904654323148236e-09f, r);
+    float p = 1.98412698e-04f;
+    p = fmaf(p, r, 1.38888892e-03f);
+    p = fmaf(p, r, 8.33333377e-03f);
+    p = fmaf(p, r, 4.16666679e-02f);
+    p = fmaf(p, r, 1.66666672e-01f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    const int ki = (int)k;
+    const int k1 = ki / 2;
+    const int k2 = ki - k1;
+    return (p * u2f((uint32_t)(k1 + 127) << 23)) * u2f((uint32_t)(k2 + 127) << 23);
+}
+
+GS_HD float gs_logf(float x) {
+    if (x != x) return x;
+    if (x < 0.0f) return u2f(0x7fc00000u);
+    if (x == 0.0f) return u2f(0xff800000u);
+    if (x == u2f(0x7f800000u)) return x;
+    int e_adj = 0;
+    if (x < 1.17549435e-38f) { x = x * 8388608.0f; e_adj = -23; }
+    const uint32_t u = f2u(x);
+    int e = (int)((u >> 23) & 0xffu) - 127 + e_adj;
+    float m = u2f((u & 0x007fffffu) | 0x3f800000u);
+    if (m > 1.41421353816986083984375f) { m = m * 0.5f; e += 1; }
+    const float f = m - 1.0f;
+    const float s = f / (2.0f + f);
+    const float s2 = s * s;
+    float p = fmaf(s2, 0.111111112f, 0.142857149f);
+    p = fmaf(p, s2, 0.2f);
+    p = fmaf(p, s2, 0.333333343f);
+    const float t = (s * s2) * p;
+    const float logm = 2.0f * s + 2.0f * t;
+    const float ef = (float)e;
+    return fmaf(ef, 0.693147182464599609375f, fmaf(ef, -1.904654323148236e-09f, logm));
+}
+
+GS_HD float gs_sigmoid(float x) { return 1.0f / (1.0f + gs_expf(-x)); }
+GS_HD float gs_logit(float x) { return -gs_logf(1.0f / x - 1.0f); }
+GS_HD float jl_clamp(float x, float lo, float hi) { return x > hi ? hi : (x < lo ? lo : x); }
+// Julia min(a, b) for floats: NaN if either argument is NaN
+GS_HD float fmin_jl(float a, float b) { return (a != a || b != b) ? a + b : (b < a ? b : a); }
+
+// float -> int32, saturating, NaN -> 0 (NaN / overflowing boxes become empty)
+GS_HD int32_t sat_i32(float v) {
+    if (v != v) return 0;
+    if (v >= 2147483520.0f) return INT32_MAX;
+    if (v <= -2147483648.0f) return INT32_MIN;
+    return (int32_t)v;
+}
+
+// SH constants SH_CONSTS_F64[i] (sh.jl:1-18) rounded to float, i 1-based; folds to a
+// literal when i is a compile-time constant.
+GS_HD float sh_c(int i) {
+    switch (i) {
+        case 1: return (float)0.28209479177387814;
+        case 2: return (float)0.4886025119029199;
+        case 3: return (float)0.4886025119029199;
+        case 4: return (float)0.4886025119029199;
+        case 5: return (float)1.0925484305920792;
+        case 6: return (float)-1.0925484305920792;
+        case 7: return (float)0.31539156525252005;
+        case 8: return (float)-1.0925484305920792;
+        case 9: return (float)0.5462742152960396;
+        case 10: return (float)-0.5900435899266435;
+        case 11: return (float)2.890611442640554;
+        case 12: return (float)-0.4570457994644658;
+        case 13: return (float)0.3731763325901154;
+        case 14: return (float)-0.4570457994644658;
+        case 15: return (float)1.445305721320277;
+        case 16: return (float)-0.5900435899266435;
+        default: return 0.0f;
+    }
+}
+
+// ---- launch geometry ---------------------------------------------------------------------
+constexpr int kSMs = 148;
+constexpr int kChunk = 4096;          // items per scan / sort tile
+constexpr int kChunkThreads = 256;
+constexpr int kChunkItems = kChunk / kChunkThreads;
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// ---- warp / block scans ---------------------------------------------------------------
+__device__ __forceinline__ int warp_inclusive_scan(int v) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += n;
+    }
+    return v;
+}
+
+// Exclusive block scan of one int per thread (blockDim.x a multiple of 32, <= 1024).
+// smem: >= 33 ints. Returns the exclusive prefix; *total receives the block sum.
+__device__ __forceinline__ int block_exclusive_scan(int v, int* smem, int* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nwarps = blockDim.x >> 5;
+    const int inc = warp_inclusive_scan(v);
+    if (lane == 31) smem[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+        const int w = lane < nwarps ? smem[lane] : 0;
+        const int wi = warp_inclusive_scan(w);
+        if (lane < nwarps) smem[lane] = wi - w;
+        if (lane == nwarps - 1) smem[32] = wi;
+    }
+    __syncthreads();
+    const int res = smem[warp] + inc - v;
+    *total = smem[32];
+    __syncthreads();
+    return res;
+}
+
+}  // namespace gs3d

@@ -1,0 +1,507 @@
+// forward.cu — render forward, render! GPU (forward_core.jl:196-314):
+//   k_keep_*       visibility mask + scan + compaction (F1, F2: forward_core.jl:326-386)
+//   k_project      per filtered Gaussian: mean, EWA conic, SH colour, tile rectangle (F3:
+//                  forward_core.jl:411-517)
+//   scan           duplicate counts -> offsets, D on the device (F4)
+//   k_dup_keys     tile << 32 | depth bits keys (F5: forward_core.jl:531-603)
+//   radix sort     (F6: radix_sort.cu)
+//   k_tiles_end    per-tile end of the sorted range (F7: forward_core.jl:676-734)
+//   k_raster       (F8 / F9: raster.cu)
+// F and D never leave the device unless the caller asks for them.
+#include "common.cuh"
+#include "internal.h"
+
+namespace gs3d {
+
+int launch_raster(const gs3d_render_outputs& out, const gs3d_camera& cam, const gs3d_tiling& til,
+                  const gs3d_render_options& opt, const gs3d_render_buffers& buf,
+                  cudaStream_t stream);
+
+namespace {
+
+// project_with_depth (cameras.jl:714-722)
+__device__ __forceinline__ void project_point(const gs3d_camera& c, float m0, float m1, float m2,
+                                              float& px, float& py, float& depth) {
+    const float* P = c.P;
+    const float h0 = P[0] * m0 + P[3] * m1 + P[6] * m2 + P[9];
+    const float h1 = P[1] * m0 + P[4] * m1 + P[7] * m2 + P[10];
+    const float h2 = P[2] * m0 + P[5] * m1 + P[8] * m2 + P[11];
+    depth = h2;
+    px = h0 / h2;
+    py = h1 / h2;
+}
+
+__device__ __forceinline__ bool keep_gaussian(const float4 mo, const gs3d_camera& cam,
+                                              const gs3d_render_options& opt) {
+    const float opacity = gs_sigmoid(mo.w);
+    bool keep = opacity >= opt.min_alpha;
+    if (keep) {
+        if (opt.clipping_mode == 1) {  // BoundaryFilter
+            float mx, my, depth;
+            project_point(cam, mo.x, mo.y, mo.z, mx, my, depth);
+            const bool on = opt.clip_x_min < mx && mx <= opt.clip_x_max && opt.clip_y_min < my &&
+                            my <= opt.clip_y_max;
+            keep = on && (cam.near_z < depth && depth <= cam.far_z) && opacity > opt.min_alpha;
+        } else {  // CovarianceBoundaryClamp: check_depth(get_mean_sv(g), camera)
+            const float* P = cam.P;
+            const float depth = P[2] * mo.x + P[5] * mo.y + P[8] * mo.z + P[11];
+            keep = cam.near_z < depth && depth <= cam.far_z;
+        }
+    }
+    return keep;
+}
+
+__global__ void __launch_bounds__(kChunkThreads) k_keep_upsweep(const float4* __restrict__ mo4,
+                                                                int n, gs3d_camera cam,
+                                                                gs3d_render_options opt,
+                                                                uint8_t* __restrict__ keep,
+                                                                int32_t* __restrict__ sums) {
+    __shared__ int sm[33];
+    const int64_t base = (int64_t)blockIdx.x * kChunk;
+    int cnt = 0;
+#pragma unroll 4
+    for (int k = 0; k < kChunkItems; ++k) {
+        const int64_t i = base + k * kChunkThreads + threadIdx.x;
+        if (i < n) {
+            const bool kp = keep_gaussian(mo4[i], cam, opt);
+            keep[i] = kp ? 1 : 0;
+            cnt += kp ? 1 : 0;
+        }
+    }
+    int total;
+    block_exclusive_scan(cnt, sm, &total);
+    if (threadIdx.x == 0) sums[blockIdx.x] = total;
+}
+
+__global__ void __launch_bounds__(kChunkThreads) k_keep_downsweep(const uint8_t* __restrict__ keep,
+                                                                  int n,
+                                                                  const int32_t* __restrict__ sums,
+                                                                  int32_t* __restrict__ keep_cs,
+                                                                  int32_t* __restrict__ f2g) {
+    __shared__ int sm[33];
+    const int64_t base = (int64_t)blockIdx.x * kChunk;
+    const int64_t mine = base + (int64_t)threadIdx.x * kChunkItems;
+    uint32_t flags = 0;
+    int s = 0;
+#pragma unroll
+    for (int k = 0; k < kChunkItems; ++k) {
+        const int64_t i = mine + k;
+        const uint32_t f = (i < n && keep[i]) ? 1u : 0u;
+        flags |= f << k;
+        s += (int)f;
+    }
+    int total;
+    int run = block_exclusive_scan(s, sm, &total) + sums[blockIdx.x];
+#pragma unroll
+    for (int k = 0; k < kChunkItems; ++k) {
+        const int64_t i = mine + k;
+        if (i < n) {
+            const int f = (flags >> k) & 1u;
+            run += f;
+            if (keep_cs) keep_cs[i] = run;
+            if (f) f2g[run - 1] = (int32_t)(i + 1);
+        }
+    }
+}
+
+// evaluate_sh_basis_function (sh.jl:123-149), i 1-based (constant after unrolling)
+__device__ __forceinline__ float sh_basis(int i, float x, float y, float z) {
+    switch (i) {
+        case 1: return sh_c(1);
+        case 2: return -y * sh_c(2);
+        case 3: return z * sh_c(3);
+        case 4: return -x * sh_c(4);
+        case 5: return x * y * sh_c(5);
+        case 6: return y * z * sh_c(6);
+        case 7: return (2.0f * (z * z) - x * x - y * y) * sh_c(7);
+        case 8: return x * z * sh_c(8);
+        case 9: return (x * x - y * y) * sh_c(9);
+        case 10: return y * (3.0f * (x * x) - y * y) * sh_c(10);
+        case 11: return x * y * z * sh_c(11);
+        case 12: return y * (4.0f * (z * z) - x * x - y * y) * sh_c(12);
+        case 13: return z * (2.0f * (z * z) - 3.0f * (x * x + y * y)) * sh_c(13);
+        case 14: return x * (4.0f * (z * z) - x * x - y * y) * sh_c(14);
+        case 15: return z * (x * x - y * y) * sh_c(15);
+        case 16: return x * (x * x - 3.0f * (y * y)) * sh_c(16);
+        default: return 0.0f;
+    }
+}
+
+// sh_coeffs_to_color (sh.jl:38-112) for one channel; hc = coefficient 1 of that channel
+template <int DEG>
+__device__ __forceinline__ float sh_channel(const float* hc, float x, float y, float z) {
+    float cc = sh_basis(1, x, y, z) * hc[0];
+    if (DEG >= 1) {
+        cc += (sh_basis(2, x, y, z) * hc[1] + sh_basis(3, x, y, z) * hc[2] +
+               sh_basis(4, x, y, z) * hc[3]);
+        if (DEG >= 2) {
+            cc += (sh_basis(5, x, y, z) * hc[4] + sh_basis(6, x, y, z) * hc[5] +
+                   sh_basis(7, x, y, z) * hc[6] + sh_basis(8, x, y, z) * hc[7] +
+                   sh_basis(9, x, y, z) * hc[8]);
+            if (DEG >= 3) {
+                cc += (sh_basis(10, x, y, z) * hc[9] + sh_basis(11, x, y, z) * hc[10] +
+                       sh_basis(12, x, y, z) * hc[11] + sh_basis(13, x, y, z) * hc[12] +
+                       sh_basis(14, x, y, z) * hc[13] + sh_basis(15, x, y, z) * hc[14] +
+                       sh_basis(16, x, y, z) * hc[15]);
+            }
+        }
+    }
+    cc += 0.5f;
+    if (cc < 0.0f) cc = 0.0f;
+    return cc;
+}
+
+struct ProjectArgs {
+    const float4* mo4;
+    const float* scal;
+    const float4* rot4;
+    const float* sh;
+    int sh_stride;  // (storage degree + 1)^2
+    const int32_t* f2g;
+    const int32_t* counts;
+    float* depths;
+    float* f2d;
+    int32_t* ranges;
+    int32_t* ntiles;
+};
+
+template <int DEG>
+__global__ void __launch_bounds__(256) k_project(const ProjectArgs a, const gs3d_camera cam,
+                                                 const gs3d_tiling til,
+                                                 const gs3d_render_options opt) {
+    const int F = a.counts[0];
+    for (int f = blockIdx.x * blockDim.x + threadIdx.x; f < F; f += gridDim.x * blockDim.x) {
+        const int gi = a.f2g[f] - 1;
+        const float4 mo = a.mo4[gi];
+        float opacity = gs_sigmoid(mo.w);
+        float mx, my, depth;
+        project_point(cam, mo.x, mo.y, mo.z, mx, my, depth);
+        float cu = mx, cv = my;
+        if (opt.clipping_mode == 0) {
+            cu = jl_clamp(mx, opt.clip_x_min, opt.clip_x_max);
+            cv = jl_clamp(my, opt.clip_y_min, opt.clip_y_max);
+        }
+        // get_linearized_projection_2d (cameras.jl:755-774)
+        const float* P = cam.P;
+        const float idepth = 1.0f / depth;
+        float J[2][3];
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+            J[0][j] = idepth * (P[0 + 3 * j] + (-cu) * P[2 + 3 * j]);
+            J[1][j] = idepth * (P[1 + 3 * j] + (-cv) * P[2 + 3 * j]);
+        }
+        // scale and rotation (gaussians.jl:1280-1331, misc.jl:133-141)
+        const float s0 = gs_expf(a.scal[3 * (size_t)gi]);
+        const float s1 = gs_expf(a.scal[3 * (size_t)gi + 1]);
+        const float s2 = gs_expf(a.scal[3 * (size_t)gi + 2]);
+        const float4 q = a.rot4[gi];
+        const float qss = q.x * q.x + q.y * q.y + q.z * q.z + q.w * q.w;
+        const float qs = sqrtf(2.0f * (1.0f / qss));
+        const float r = q.x * qs, x = q.y * qs, y = q.z * qs, z = q.w * qs;
+        const float R[3][3] = {{1.0f - (y * y + z * z), x * y - r * z, x * z + r * y},
+                               {x * y + r * z, 1.0f - (x * x + z * z), y * z - r * x},
+                               {x * z - r * y, y * z + r * x, 1.0f - (x * x + y * y)}};
+        const float s[3] = {s0, s1, s2};
+        float RS[3][3];
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+#pragma unroll
+            for (int j = 0; j < 3; ++j) RS[i][j] = R[i][j] * s[j];
+        float A[2][3];
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+            for (int k = 0; k < 3; ++k)
+                A[i][k] = J[i][0] * RS[0][k] + J[i][1] * RS[1][k] + J[i][2] * RS[2][k];
+        float c11 = A[0][0] * A[0][0] + A[0][1] * A[0][1] + A[0][2] * A[0][2];
+        const float c21 = A[1][0] * A[0][0] + A[1][1] * A[0][1] + A[1][2] * A[0][2];
+        float c22 = A[1][0] * A[1][0] + A[1][1] * A[1][1] + A[1][2] * A[1][2];
+        float undilated_det = 0.0f;
+        if (opt.use_antialiasing) undilated_det = fmaxf(c11 * c22 - c21 * c21, 0.0f);
+        c11 += opt.dilation_x;
+        c22 += opt.dilation_y;
+        const float icov_det = 1.0f / (c11 * c22 - c21 * c21);
+        if (opt.use_antialiasing)
+            opacity *= fmaxf(opt.antialiasing_min_factor, sqrtf(undilated_det * icov_det));
+
+        // _get_bbox_cts_px_cov + _get_bbox_discrete_px (forward_structs.jl:1303-1411)
+        bool empty = true;
+        int left = 0, top = 0, right = -1, bottom = -1;
+        if (opacity >= opt.min_alpha) {
+            const float gamma = 2.0f * gs_logf(opacity / opt.min_alpha);
+            const float xr = sqrtf(gamma * c11);
+            const float yr = sqrtf(gamma * c22);
+            left = max(1, sat_i32(ceilf((mx - xr) + 0.5f)));
+            top = max(1, sat_i32(ceilf((my - yr) + 0.5f)));
+            right = min(cam.width, sat_i32(rintf(mx + xr)));
+            bottom = min(cam.height, sat_i32(rintf(my + yr)));
+            empty = left > right || top > bottom;
+        }
+        // colour from the normalised view direction (sh.jl:38-112)
+        const float vx = mo.x - cam.position[0], vy = mo.y - cam.position[1],
+                    vz = mo.z - cam.position[2];
+        const float inv = 1.0f / sqrtf(vx * vx + vy * vy + vz * vz);
+        const float dx = vx * inv, dy = vy * inv, dz = vz * inv;
+        const float* h = a.sh + (size_t)gi * 3 * a.sh_stride;
+        constexpr int NC = (DEG + 1) * (DEG + 1);
+        float hc[3][NC];
+        if (NC == a.sh_stride && ((3 * NC) % 4) == 0 && (reinterpret_cast<uintptr_t>(a.sh) & 15) == 0) {
+            const float4* h4 = reinterpret_cast<const float4*>(h);
+#pragma unroll
+            for (int k = 0; k < (3 * NC) / 4; ++k) {
+                const float4 v = h4[k];
+                (&hc[0][0])[4 * k] = v.x; (&hc[0][0])[4 * k + 1] = v.y;
+                (&hc[0][0])[4 * k + 2] = v.z; (&hc[0][0])[4 * k + 3] = v.w;
+            }
+        } else {
+#pragma unroll
+            for (int c = 0; c < 3; ++c)
+#pragma unroll
+                for (int i = 0; i < NC; ++i) hc[c][i] = h[c * a.sh_stride + i];
+        }
+        const float col0 = sh_channel<DEG>(hc[0], dx, dy, dz);
+        const float col1 = sh_channel<DEG>(hc[1], dx, dy, dz);
+        const float col2 = sh_channel<DEG>(hc[2], dx, dy, dz);
+
+        a.depths[f] = depth;
+        float* rr = a.f2d + 9 * (size_t)f;
+        rr[0] = mx; rr[1] = my; rr[2] = opacity;
+        rr[3] = c22 * icov_det; rr[4] = -c21 * icov_det; rr[5] = c11 * icov_det;
+        rr[6] = col0; rr[7] = col1; rr[8] = col2;
+        int4 rect;
+        int count;
+        if (empty) {
+            rect = make_int4(1, 1, 0, 0);
+            count = 0;
+        } else {  // rectangle_to_tile_ids without clamping (forward_structs.jl:517-528)
+            rect.x = (left + til.tile_width - 1) / til.tile_width;
+            rect.y = (top + til.tile_height - 1) / til.tile_height;
+            rect.z = (right + til.tile_width - 1) / til.tile_width;
+            rect.w = (bottom + til.tile_height - 1) / til.tile_height;
+            count = (rect.z - rect.x + 1) * (rect.w - rect.y + 1);
+        }
+        reinterpret_cast<int4*>(a.ranges)[f] = rect;
+        a.ntiles[f] = count;
+    }
+}
+
+// fill_df2dgs_codes_and_dfgidx_to_fgidx_kernel! (forward_core.jl:531-603)
+__global__ void __launch_bounds__(256) k_dup_keys(const int32_t* __restrict__ counts,
+                                                  const int32_t* __restrict__ ntiles,
+                                                  const int32_t* __restrict__ ntiles_cs,
+                                                  const int4* __restrict__ ranges,
+                                                  const float* __restrict__ depths,
+                                                  int tiles_x, int64_t capacity,
+                                                  int64_t* __restrict__ codes,
+                                                  int32_t* __restrict__ dfg,
+                                                  int32_t* status) {
+    const int F = counts[0];
+    for (int f = blockIdx.x * blockDim.x + threadIdx.x; f < F; f += gridDim.x * blockDim.x) {
+        const int cnt = ntiles[f];
+        if (cnt == 0) continue;
+        int64_t d = (int64_t)ntiles_cs[f] - cnt;
+        if ((int64_t)ntiles_cs[f] > capacity) atomicOr(status, (int)GS3D_STATUS_DUP_OVERFLOW);
+        const int4 r = ranges[f];
+        const uint64_t dcode = (uint64_t)(int64_t)(int32_t)f2u(depths[f]);
+        for (int ty = r.y; ty <= r.w; ++ty) {
+            const int ycontrib = (ty - 1) * tiles_x;
+            for (int tx = r.x; tx <= r.z; ++tx, ++d) {
+                if (d >= capacity) continue;
+                const uint32_t tile = (uint32_t)(tx + ycontrib);
+                codes[d] = (int64_t)(((uint64_t)tile << 32) | dcode);
+                dfg[d] = f + 1;
+            }
+        }
+    }
+}
+
+// fill_tiles_end_sdfgidx_kernel! (forward_core.jl:676-734)
+__global__ void __launch_bounds__(256) k_tiles_end(const int32_t* __restrict__ counts,
+                                                   int64_t capacity,
+                                                   const int64_t* __restrict__ scodes,
+                                                   int nb_tiles, int32_t* __restrict__ tiles_end) {
+    const int64_t Draw = counts[1];
+    const int D = (int)(Draw < capacity ? Draw : capacity);
+    if (counts[0] == 0 || D == 0) return;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < D; i += gridDim.x * blockDim.x) {
+        const int cur = (int)((uint64_t)scodes[i] >> 32);
+        if (i == 0)
+            for (int t = 1; t < cur; ++t) tiles_end[t - 1] = 0;
+        if (i + 1 < D) {
+            const int nxt = (int)((uint64_t)scodes[i + 1] >> 32);
+            for (int t = cur; t < nxt; ++t) tiles_end[t - 1] = i + 1;
+        } else {
+            for (int t = cur; t <= nb_tiles; ++t) tiles_end[t - 1] = D;
+        }
+    }
+}
+
+int grid_for(int64_t items, int threads, int per_sm = 16) {
+    int64_t b = ceil_div(items, threads);
+    const int64_t cap = (int64_t)kSMs * per_sm;
+    if (b > cap) b = cap;
+    if (b < 1) b = 1;
+    return (int)b;
+}
+
+struct FwdLayout {
+    size_t sums, sort, total;
+};
+
+FwdLayout fwd_layout(int64_t capacity_n, int64_t capacity_dup) {
+    FwdLayout L;
+    size_t off = 0;
+    L.sums = off; off += scan_workspace_bytes(capacity_n > 0 ? capacity_n : 1);
+    L.sort = off; off += radix_sort_workspace_bytes(capacity_dup);
+    L.total = off;
+    return L;
+}
+
+int check_common(const gs3d_gaussians* g, const gs3d_camera* cam, const gs3d_tiling* til,
+                 const gs3d_render_options* opt) {
+    if (!g || !cam || !til || !opt) return invalid("NULL argument");
+    if (g->n < 0) return invalid("negative Gaussian count %d", g->n);
+    if (g->n > 0 && (!g->means_opacity_features || !g->scaling_features || !g->rotation_features ||
+                     !g->sh_coeffs))
+        return invalid("NULL Gaussian array");
+    if (g->sh_degree < 0 || g->sh_degree > 3) return invalid("storage SH degree %d", g->sh_degree);
+    if (opt->sh_degree < 0 || opt->sh_degree > g->sh_degree)
+        return invalid("render SH degree %d with storage degree %d", opt->sh_degree, g->sh_degree);
+    if (cam->width <= 0 || cam->height <= 0) return invalid("camera size %dx%d", cam->width, cam->height);
+    if (til->tile_width <= 0 || til->tile_height <= 0 ||
+        til->tile_width * til->tile_height > 512 || (til->tile_width * til->tile_height) % 32 != 0)
+        return invalid("tile %dx%d (need a multiple of 32 and <= 512 pixels)", til->tile_width,
+                       til->tile_height);
+    if ((int64_t)til->nb_tiles_x * til->tile_width < cam->width ||
+        (int64_t)til->nb_tiles_y * til->tile_height < cam->height || til->nb_tiles_x <= 0 ||
+        til->nb_tiles_y <= 0)
+        return invalid("tiling %dx%d of %dx%d does not cover %dx%d", til->nb_tiles_x,
+                       til->nb_tiles_y, til->tile_width, til->tile_height, cam->width, cam->height);
+    return GS3D_OK;
+}
+
+}  // namespace
+
+int check_render_common(const gs3d_gaussians* g, const gs3d_camera* cam, const gs3d_tiling* til,
+                        const gs3d_render_options* opt) {
+    return check_common(g, cam, til, opt);
+}
+
+}  // namespace gs3d
+
+using namespace gs3d;
+
+extern "C" {
+
+GS3D_API int gs3d_render_forward_workspace_size(int64_t capacity_n, int64_t capacity_dup,
+                                                int32_t nb_tiles, size_t* bytes) {
+    if (!bytes) return invalid("bytes is NULL");
+    if (capacity_n < 0 || capacity_dup < 0 || nb_tiles < 0) return invalid("negative capacity");
+    *bytes = fwd_layout(capacity_n, capacity_dup).total;
+    return GS3D_OK;
+}
+
+GS3D_API int gs3d_render_forward(const gs3d_render_outputs* outputs, const gs3d_gaussians* g,
+                                 const gs3d_camera* cam, const gs3d_tiling* til,
+                                 const gs3d_render_options* opt, gs3d_render_buffers* buf,
+                                 int32_t* host_counts, uint32_t flags, gs3d_stream_t stream_) {
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+    GS3D_RETURN_IF(check_common(g, cam, til, opt));
+    if (!outputs || !buf) return invalid("NULL outputs or buffers");
+    if (g->n > buf->capacity_n) return invalid("n = %d exceeds capacity_n = %lld", g->n, (long long)buf->capacity_n);
+    if (!buf->keep_gaussians || !buf->fgidx_to_gidx || !buf->depths ||
+        !buf->means2d_opacities_inverse_covariances_colors || !buf->intersected_tile_ranges ||
+        !buf->nb_overlapped_tiles || !buf->nb_overlapped_tiles_cs || !buf->df2dgs_codes ||
+        !buf->dfgidx_to_fgidx || !buf->sdf2dgs_codes || !buf->sdfgidx_to_fgidx ||
+        !buf->tiles_end_sdfgidx || !buf->device_counts)
+        return invalid("NULL render buffer array");
+    if (((uintptr_t)buf->intersected_tile_ranges & 15) || ((uintptr_t)g->means_opacity_features & 15) ||
+        ((uintptr_t)g->rotation_features & 15))
+        return invalid("tile ranges, means/opacity and rotation arrays must be 16-byte aligned");
+    const FwdLayout L = fwd_layout(buf->capacity_n, buf->capacity_dup);
+    if (!buf->workspace || buf->workspace_bytes < L.total)
+        return set_error("render workspace %zu bytes < %zu", buf->workspace_bytes, L.total),
+               GS3D_ERR_WORKSPACE;
+    unsigned char* ws = static_cast<unsigned char*>(buf->workspace);
+    int32_t* sums = reinterpret_cast<int32_t*>(ws + L.sums);
+    int32_t* counts = buf->device_counts;
+    const int n = g->n;
+    const int64_t cap_n = buf->capacity_n > 0 ? buf->capacity_n : 1;
+    const int nb_tiles = til->nb_tiles_x * til->nb_tiles_y;
+
+    GS3D_CUDA(cudaMemsetAsync(counts, 0, 4 * sizeof(int32_t), stream), "memset counts");
+    // F1 + F2
+    if (n > 0) {
+        const unsigned nch = (unsigned)ceil_div(n, kChunk);
+        k_keep_upsweep<<<nch, kChunkThreads, 0, stream>>>(
+            reinterpret_cast<const float4*>(g->means_opacity_features), n, *cam, *opt,
+            buf->keep_gaussians, sums);
+        GS3D_LAUNCHED("k_keep_upsweep");
+        GS3D_RETURN_IF(scan_spine(sums, cap_n, nullptr, n, counts + 0, stream));
+        k_keep_downsweep<<<nch, kChunkThreads, 0, stream>>>(buf->keep_gaussians, n, sums,
+                                                            buf->keep_gaussians_cs,
+                                                            buf->fgidx_to_gidx);
+        GS3D_LAUNCHED("k_keep_downsweep");
+    }
+    // F3
+    ProjectArgs pa;
+    pa.mo4 = reinterpret_cast<const float4*>(g->means_opacity_features);
+    pa.scal = g->scaling_features;
+    pa.rot4 = reinterpret_cast<const float4*>(g->rotation_features);
+    pa.sh = g->sh_coeffs;
+    pa.sh_stride = (g->sh_degree + 1) * (g->sh_degree + 1);
+    pa.f2g = buf->fgidx_to_gidx;
+    pa.counts = counts;
+    pa.depths = buf->depths;
+    pa.f2d = buf->means2d_opacities_inverse_covariances_colors;
+    pa.ranges = buf->intersected_tile_ranges;
+    pa.ntiles = buf->nb_overlapped_tiles;
+    const int pgrid = grid_for(n, 256, 8);
+    switch (opt->sh_degree) {
+        case 0: k_project<0><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
+        case 1: k_project<1><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
+        case 2: k_project<2><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
+        default: k_project<3><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
+    }
+    GS3D_LAUNCHED("k_project");
+    // F4
+    GS3D_RETURN_IF(inclusive_scan_i32(buf->nb_overlapped_tiles, buf->nb_overlapped_tiles_cs, cap_n,
+                                      counts + 0, 0, counts + 1, sums, stream));
+    // F5
+    k_dup_keys<<<grid_for(n, 256, 8), 256, 0, stream>>>(
+        counts, buf->nb_overlapped_tiles, buf->nb_overlapped_tiles_cs,
+        reinterpret_cast<const int4*>(buf->intersected_tile_ranges), buf->depths, til->nb_tiles_x,
+        buf->capacity_dup, buf->df2dgs_codes, buf->dfgidx_to_fgidx, counts + 2);
+    GS3D_LAUNCHED("k_dup_keys");
+    if (!(flags & GS3D_RENDER_NO_HOST_SYNC)) {
+        int32_t local[4];
+        int32_t* dst = host_counts ? host_counts : local;
+        GS3D_CUDA(cudaMemcpyAsync(dst, counts, 4 * sizeof(int32_t), cudaMemcpyDeviceToHost, stream),
+                  "copy counts");
+        GS3D_CUDA(cudaStreamSynchronize(stream), "sync counts");
+        if ((int64_t)dst[1] > buf->capacity_dup)
+            return set_error("%d duplicated keys exceed capacity_dup = %lld", dst[1],
+                             (long long)buf->capacity_dup),
+                   GS3D_ERR_CAPACITY;
+    }
+    // F6
+    int highest = 33;
+    for (int t = nb_tiles; t > 1; t >>= 1) ++highest;  // 33 + floor(log2(nb_tiles))
+    GS3D_RETURN_IF(radix_sort_pairs(ws + L.sort, L.total - L.sort, buf->df2dgs_codes,
+                                    buf->sdf2dgs_codes, buf->dfgidx_to_fgidx,
+                                    buf->sdfgidx_to_fgidx, buf->capacity_dup, counts + 1, 0, highest,
+                                    stream));
+    // F7
+    k_tiles_end<<<grid_for(buf->capacity_dup, 256, 8), 256, 0, stream>>>(
+        counts, buf->capacity_dup, buf->sdf2dgs_codes, nb_tiles, buf->tiles_end_sdfgidx);
+    GS3D_LAUNCHED("k_tiles_end");
+    // F8 / F9
+    GS3D_RETURN_IF(launch_raster(*outputs, *cam, *til, *opt, *buf, stream));
+    if ((flags & GS3D_RENDER_NO_HOST_SYNC) && host_counts)
+        GS3D_CUDA(cudaMemcpyAsync(host_counts, counts, 4 * sizeof(int32_t), cudaMemcpyDeviceToHost,
+                                  stream),
+                  "copy counts");
+    return GS3D_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,34 @@
+// internal.h — host-side interfaces shared between libgs3d translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+namespace gs3d {
+
+// Round a byte count up to 256 (every workspace region starts 256-byte aligned).
+inline size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
+
+// LSD radix sort of (int64 key, int32 value) pairs on bits [0, highest_key_bit), stable.
+// The item count is read from count_dev[0] on the device (clamped to capacity) when
+// count_dev is not NULL, else count_host is used. keys_in / values_in are not modified.
+size_t radix_sort_workspace_bytes(int64_t capacity);
+int radix_sort_pairs(void* ws, size_t ws_bytes, const int64_t* keys_in, int64_t* keys_out,
+                     const int32_t* values_in, int32_t* values_out, int64_t capacity,
+                     const int32_t* count_dev, int64_t count_host, int highest_key_bit,
+                     cudaStream_t stream);
+
+// Device-wide scans over int32 with the length on the device (len_dev[0]) or on the host.
+size_t scan_workspace_bytes(int64_t capacity);
+// inclusive scan of in[0, len) into out; the total is written to total_dev[0].
+int inclusive_scan_i32(const int32_t* in, int32_t* out, int64_t capacity, const int32_t* len_dev,
+                       int64_t len_host, int32_t* total_dev, void* ws, cudaStream_t stream);
+
+// Exclusive scan in place of the per-chunk sums of a chunked scan (chunk = 4096 items):
+// nchunks = ceil(len / 4096); the grand total goes to total_dev[0] (may be NULL).
+int scan_spine(int32_t* sums, int64_t capacity, const int32_t* len_dev, int64_t len_host,
+               int32_t* total_dev, cudaStream_t stream);
+
+int device_sm_count();
+
+}  // namespace gs3d

@@ -1,0 +1,169 @@
+// raster.cu — front-to-back tile alpha blend, render_tiles_kernel! (forward_core.jl:756-993).
+//
+// One CTA per tile (tile_width x tile_height threads, one pixel each). Lanes run down a
+// pixel column (v fastest) so a warp's RGB / T / index stores are contiguous in the
+// reference's column-major 3 x h x w and h x w images. The duplicated Gaussians of the tile
+// are staged BATCH = blockDim at a time in shared memory in the reference's precomputed
+// form (forward_core.jl:877-897): six quadratic-form coefficients with log(opacity)
+// absorbed, the colour and the depth. Per pixel the arithmetic and its order are the
+// reference's: alpha = min(max_alpha, exp(q)), skip alpha < min_alpha, stop when
+// T (1 - alpha) < min_transmittance.
+//
+// Beyond the reference: (a) q below log(min_alpha) - 0.01 skips the exponential (exp(q)
+// is then certainly below min_alpha, so the result is unchanged); (b) the whole CTA leaves
+// the batch loop once every pixel has stopped (__syncthreads_count); (c) a CTA reads the
+// duplicate and tile counts from device memory and draws the void image itself when there
+// is nothing to draw (render_void!, forward_structs.jl:743-757), so no host sync is needed.
+#include "common.cuh"
+#include "internal.h"
+
+namespace gs3d {
+
+namespace {
+
+struct RasterArgs {
+    const int32_t* sfgidx;      // sorted dup -> fgidx (1-based)
+    const int32_t* tiles_end;   // per tile, inclusive 1-based end
+    const float* f2d;           // 9 x F
+    const float* depths;        // F
+    const int32_t* counts;      // [0] F, [1] D
+    int64_t capacity_dup;
+    float* rgb;
+    float* trans;
+    float* depth_img;
+    int32_t* last;
+    int32_t width, height;
+    int32_t tile_w, tile_h, tiles_x;
+    float bg0, bg1, bg2;
+    float min_alpha, max_alpha, min_T, q_skip;
+};
+
+__global__ void __launch_bounds__(512) k_raster(const RasterArgs a) {
+    extern __shared__ __align__(16) float4 sm4[];
+    const int nthr = blockDim.x;
+    float4* sA = sm4;             // p1 p2 p3 p4
+    float4* sB = sm4 + nthr;      // p5 p6 r g
+    float2* sC = reinterpret_cast<float2*>(sm4 + 2 * nthr);  // b depth
+
+    const int t = threadIdx.x;
+    const int lv = t % a.tile_h, lu = t / a.tile_h;     // 0-based in tile, v fastest
+    const int txi = blockIdx.x, tyi = blockIdx.y;       // 0-based tile coordinates
+    const int u0 = txi * a.tile_w, v0 = tyi * a.tile_h;
+    const int U = u0 + lu + 1, V = v0 + lv + 1;         // 1-based pixel
+    const bool inside = U <= a.width && V <= a.height;
+    const size_t px = (size_t)(V - 1) + (size_t)a.height * (size_t)(U - 1);
+
+    const int F = a.counts[0];
+    const int64_t Draw = a.counts[1];
+    const int D = (int)(Draw < a.capacity_dup ? Draw : a.capacity_dup);
+    if (F == 0 || D == 0) {  // render_void!
+        if (inside) {
+            if (a.rgb) { a.rgb[3 * px] = a.bg0; a.rgb[3 * px + 1] = a.bg1; a.rgb[3 * px + 2] = a.bg2; }
+            if (a.trans) a.trans[px] = 1.0f;
+            if (a.depth_img) a.depth_img[px] = u2f(0x7f800000u);
+            if (a.last) a.last[px] = 0;
+        }
+        return;
+    }
+    const int tile = txi + tyi * a.tiles_x + 1;  // 1-based linear, x-contiguous
+    const int start = tile == 1 ? 0 : a.tiles_end[tile - 2];
+    const int end = a.tiles_end[tile - 1];
+
+    const float cu = (float)(lu + 1) - 0.5f, cv = (float)(lv + 1) - 0.5f;
+    const float uu = cu * cu, uv = cu * cv, vv = cv * cv;
+    float T = 1.0f, c0 = 0.0f, c1 = 0.0f, c2 = 0.0f, dep = 0.0f;
+    int32_t lastc = 0;
+    bool done = !inside;
+
+    for (int base = start; base < end; base += nthr) {
+        if (__syncthreads_count(!done) == 0) break;  // also guards shared-memory reuse
+        const int idx = base + t;
+        if (idx < end) {
+            const int fg = a.sfgidx[idx] - 1;
+            const float* r = a.f2d + 9 * (size_t)fg;
+            const float x = r[0], y = r[1], op = r[2];
+            const float ic11 = r[3], ic21 = r[4], ic22 = r[5];
+            const float du = x - (float)u0;
+            const float dv = y - (float)v0;
+            const float ic11_du = ic11 * du, ic21_du = ic21 * du, ic22_dv = ic22 * dv;
+            const float p1 = -0.5f * ic11, p2 = -0.5f * ic22, p3 = -ic21;
+            const float p4 = ic11_du + ic21 * dv;
+            const float p5 = ic21_du + ic22_dv;
+            const float p6 = -0.5f * (ic11_du * du + ic22_dv * dv) - ic21_du * dv + gs_logf(op);
+            sA[t] = make_float4(p1, p2, p3, p4);
+            sB[t] = make_float4(p5, p6, r[6], r[7]);
+            sC[t] = make_float2(r[8], a.depths[fg]);
+        }
+        __syncthreads();
+        if (!done) {
+            const int nb = min(nthr, end - base);
+            for (int j = 0; j < nb; ++j) {
+                const float4 A = sA[j];
+                const float4 B = sB[j];
+                const float q = A.x * uu + A.y * vv + A.z * uv + A.w * cu + B.x * cv + B.y;
+                if (q < a.q_skip) continue;
+                const float alpha = fmin_jl(a.max_alpha, gs_expf(q));
+                if (alpha < a.min_alpha) continue;
+                const float nT = T * (1.0f - alpha);
+                if (nT < a.min_T) { done = true; break; }
+                const float w = T * alpha;
+                const float2 C = sC[j];
+                c0 += w * B.z;
+                c1 += w * B.w;
+                c2 += w * C.x;
+                T = nT;
+                dep += w * C.y;
+                lastc = base + j + 1;
+            }
+        }
+    }
+    if (inside) {
+        if (a.rgb) {
+            a.rgb[3 * px] = c0 + T * a.bg0;
+            a.rgb[3 * px + 1] = c1 + T * a.bg1;
+            a.rgb[3 * px + 2] = c2 + T * a.bg2;
+        }
+        if (a.trans) a.trans[px] = T;
+        if (a.depth_img) a.depth_img[px] = dep;
+        if (a.last) a.last[px] = lastc;
+    }
+}
+
+}  // namespace
+
+int launch_raster(const gs3d_render_outputs& out, const gs3d_camera& cam, const gs3d_tiling& til,
+                  const gs3d_render_options& opt, const gs3d_render_buffers& buf,
+                  cudaStream_t stream) {
+    RasterArgs a;
+    a.sfgidx = buf.sdfgidx_to_fgidx;
+    a.tiles_end = buf.tiles_end_sdfgidx;
+    a.f2d = buf.means2d_opacities_inverse_covariances_colors;
+    a.depths = buf.depths;
+    a.counts = buf.device_counts;
+    a.capacity_dup = buf.capacity_dup;
+    a.rgb = out.rgb;
+    a.trans = out.transmittance;
+    a.depth_img = out.depth;
+    a.last = out.last_contributing_sdfgids;
+    a.width = cam.width;
+    a.height = cam.height;
+    a.tile_w = til.tile_width;
+    a.tile_h = til.tile_height;
+    a.tiles_x = til.nb_tiles_x;
+    a.bg0 = opt.background[0];
+    a.bg1 = opt.background[1];
+    a.bg2 = opt.background[2];
+    a.min_alpha = opt.min_alpha;
+    a.max_alpha = opt.max_alpha;
+    a.min_T = opt.min_transmittance;
+    // exp(q) < min_alpha for every q < log(min_alpha) - 0.01 (margin >> 2 ulp)
+    a.q_skip = opt.min_alpha > 0.0f ? gs_logf(opt.min_alpha) - 0.01f : -INFINITY;
+    const int nthr = til.tile_width * til.tile_height;
+    const size_t smem = (size_t)nthr * (2 * sizeof(float4) + sizeof(float2));
+    dim3 grid(til.nb_tiles_x, til.nb_tiles_y);
+    k_raster<<<grid, nthr, smem, stream>>>(a);
+    GS3D_LAUNCHED("k_raster");
+    return GS3D_OK;
+}
+
+}  // namespace gs3d

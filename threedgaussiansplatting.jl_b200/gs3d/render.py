@@ -1,0 +1,48 @@
+"""render! (forward_core.jl:196-314) through libgs3d.so."""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _abi
+from .structs import (GaussiansVector, PinholeCamera, RenderBuffers, RenderOptions,
+                      RenderOutputs, Tiling)
+
+
+def _stream_handle(stream: torch.cuda.Stream | None) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def render(outputs: RenderOutputs, gaussians: GaussiansVector, camera: PinholeCamera,
+           tiling: Tiling, options: RenderOptions, buffers: RenderBuffers,
+           stream: torch.cuda.Stream | None = None, host_sync: bool = True) -> RenderOutputs:
+    """Render `gaussians` for `camera` into `outputs` (in place), like the reference's
+    GPU `render!`. With `host_sync` the call waits once for the duplicate count and grows the
+    duplicate buffers when they are too small (the reference's set_nb_dfgaussians!);
+    without it nothing blocks and an overflow shows up in buffers.device_counts[2]."""
+    if gaussians.n > buffers.capacity_n:
+        raise ValueError(f"{gaussians.n} Gaussians exceed the buffers' capacity {buffers.capacity_n}")
+    lib = _abi.lib()
+    flags = 0 if host_sync else _abi.GS3D_RENDER_NO_HOST_SYNC
+    host = buffers.host_counts
+    hptr = C.c_void_p(host.data_ptr()) if host is not None else None
+    args = (outputs.to_c(), gaussians.to_c(), camera.to_c(), tiling.to_c(), options.to_c())
+    for _ in range(4):
+        b = buffers.to_c()
+        st = lib.gs3d_render_forward(C.byref(args[0]), C.byref(args[1]), C.byref(args[2]),
+                                     C.byref(args[3]), C.byref(args[4]), C.byref(b), hptr,
+                                     flags, C.c_void_p(_stream_handle(stream)))
+        if st == _abi.GS3D_ERR_CAPACITY:
+            buffers.grow_dup(int(host[1]) if host is not None else 2 * buffers.capacity_dup)
+            continue
+        _abi.check(st)
+        return outputs
+    raise RuntimeError("duplicate-key capacity did not converge")
+
+
+def counts(buffers: RenderBuffers) -> tuple[int, int]:
+    """(F, D) of the last render (reads device memory; synchronises)."""
+    c = buffers.device_counts.cpu()
+    return int(c[0]), int(c[1])
