@@ -207,6 +207,56 @@ def backward(g: NpGaussians, camera, tiling, options, fwd: dict, rgb_grad: np.nd
     return {k: v[:F] for k, v in o.items()}
 
 
+class NpMoments:
+    """Adam moments as numpy arrays: (n,3,2) (n,2) (n,3,2) (n,4,2) (n,3,S,2)."""
+
+    def __init__(self, mm, om, sm, rm, shm):
+        f = lambda a: np.ascontiguousarray(np.asarray(a, dtype=np.float32))
+        self.mm, self.om, self.sm, self.rm, self.shm = map(f, (mm, om, sm, rm, shm))
+
+    @classmethod
+    def from_moments(cls, m) -> "NpMoments":
+        return cls(*(t.detach().cpu().numpy() for t in m.tensors()))
+
+    @property
+    def sh_degree(self):
+        return int(round(np.sqrt(self.shm.shape[2]))) - 1
+
+    def to_c(self):
+        m = _abi.AdamMomentsC()
+        m.sh_degree = self.sh_degree
+        m.means_moments, m.opacity_features_moments = _p(self.mm), _p(self.om)
+        m.scaling_features_moments, m.rotation_features_moments = _p(self.sm), _p(self.rm)
+        m.sh_coeffs_moments = _p(self.shm)
+        return m
+
+    def copy(self):
+        return NpMoments(self.mm.copy(), self.om.copy(), self.sm.copy(), self.rm.copy(), self.shm.copy())
+
+
+def fgradients_c(grads: dict):
+    """FGradientsC over the numpy dict returned by backward() (3D parts only are read)."""
+    f = _abi.FGradientsC()
+    keep = {k: np.ascontiguousarray(v, np.float32) for k, v in grads.items()}
+    f.sh_degree = int(round(np.sqrt(keep["sh"].shape[2]))) - 1
+    f.mean2d_grads, f.opacity_grads = _p(keep["mean2d"]), _p(keep["opacity"])
+    f.licov2d_grads, f.color_grads = _p(keep["licov"]), _p(keep["color"])
+    f.mean3d_grads, f.opacity_feature_grads = _p(keep["mean3d"]), _p(keep["opacity_feature"])
+    f.scaling_features_grads, f.rotation_features_grads = _p(keep["scaling"]), _p(keep["rotation"])
+    f.sh_coeffs_grads = _p(keep["sh"])
+    return f, keep
+
+
+def adam(g: NpGaussians, m: NpMoments, grads: dict, fgidx_to_gidx: np.ndarray, params, bc1: float,
+         bc2: float) -> None:
+    """In-place sparse Adam step on (g, m); params is an _abi.AdamParamsC."""
+    f2g = np.ascontiguousarray(fgidx_to_gidx, np.int32)
+    fc, _keep = fgradients_c(grads)
+    gc, mc = g.to_c(), m.to_c()
+    assert lib().oracle_adam(C.byref(gc), C.byref(mc), C.byref(fc), _p(f2g), f2g.size,
+                             C.byref(params), bc1, bc2) == 0
+
+
 def sort_pairs(keys: np.ndarray, vals: np.ndarray, highest_key_bit: int):
     keys = np.ascontiguousarray(keys, np.int64)
     vals = np.ascontiguousarray(vals, np.int32)

@@ -1,0 +1,196 @@
+"""backward! and update! on the GPU against the CPU oracle.
+
+Bar: per-Gaussian gradients within 1e-3 relative L2 of the oracle (whose per-pair sums are
+exact doubles; the GPU sums float atomics in a different order), the reference's golden
+gradients at its own tolerance, and the Adam step bit-exact given identical gradients.
+"""
+import numpy as np
+import pytest
+import torch
+
+import gs3d
+from gs3d import RenderBuffers, RenderOptions, RenderOutputs, Tiling
+from gs3d.backward import FilteredGaussiansGradients, backward
+from gs3d.optimizer import AdamOptimizer, LearningRates, bias_corrections
+from gs3d.scene import SceneSpec, create_test_scene, look_at_camera, synthetic_gaussians
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+KEYS = ["mean2d", "opacity", "licov", "color", "mean3d", "opacity_feature", "scaling", "rotation", "sh"]
+
+
+def run_gpu(gv, cam, til, opt, rgb_grad, device, fix16=False):
+    g = gv.to(device)
+    out = RenderOutputs.create(cam.width, cam.height, device)
+    buf = RenderBuffers.create(g.n, til.nb_tiles, device)
+    gs3d.render(out, g, cam, til, opt, buf)
+    fg = FilteredGaussiansGradients.create(g.n, g.sh_degree, device)
+    backward(fg, torch.from_numpy(rgb_grad).to(device), out, g, cam, til, opt, buf, fix_sh16=fix16)
+    torch.cuda.synchronize()
+    F, _ = gs3d.counts(buf)
+    cpu = lambda t: t[:F].cpu().numpy()
+    grads = dict(mean2d=cpu(fg.mean2d_grads), opacity=cpu(fg.opacity_grads),
+                 licov=cpu(fg.licov2d_grads), color=cpu(fg.color_grads),
+                 mean3d=cpu(fg.mean3d_grads), opacity_feature=cpu(fg.opacity_feature_grads),
+                 scaling=cpu(fg.scaling_features_grads), rotation=cpu(fg.rotation_features_grads),
+                 sh=cpu(fg.sh_coeffs_grads))
+    return grads, (g, out, buf, fg)
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64).reshape(len(a), -1)
+    b = np.asarray(b, np.float64).reshape(len(b), -1)
+    total = np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30)
+    per = np.linalg.norm(a - b, axis=1) / np.maximum(np.linalg.norm(b, axis=1), 1e-30)
+    return total, per
+
+
+def check_grads(gpu, ref, tol=1e-3):
+    for k in KEYS:
+        total, per = rel_l2(gpu[k], ref[k])
+        assert total <= tol, (k, total)
+        # per Gaussian: relative L2 <= tol unless the gradient itself is negligible
+        norms = np.linalg.norm(np.asarray(ref[k], np.float64).reshape(len(per), -1), axis=1)
+        big = norms > 1e-3 * norms.max()
+        assert np.all(per[big] <= tol), (k, per[big].max(), np.count_nonzero(per[big] > tol))
+
+
+@pytest.mark.parametrize("deg", [0, 3])
+def test_backward_test_scene_golden(cuda, golden, deg):
+    gv, cams = create_test_scene(deg)
+    cam = cams[0]
+    opt = RenderOptions.for_camera(cam, deg)
+    til = Tiling.for_camera(cam, 16, 16)
+    ref_f = O.render(O.NpGaussians.from_vector(gv), cam, til, opt)
+    N = ref_f["rgb"].size
+    grad = (np.where(ref_f["rgb"] > 0.5, 1.0, -1.0) / N).astype(np.float32)
+    gpu, _ = run_gpu(gv, cam, til, opt, grad, cuda)
+    ref = O.backward(O.NpGaussians.from_vector(gv), cam, til, opt, ref_f, grad)
+    check_grads(gpu, ref)
+    gold = golden["backward_core"]["gradients"][str(deg)]
+    order = (deg + 1) ** 2
+    for i in range(3):
+        for mine, theirs in ((gpu["mean2d"][i], gold["means2d"][i]),
+                             (gpu["scaling"][i], gold["scaling_features"][i]),
+                             (gpu["opacity_feature"][i], gold["opacity_features"][i]),
+                             (gpu["sh"][i], np.array(gold["sh_coeffs"][i]).reshape(order, 3).T)):
+            theirs = np.asarray(theirs, np.float64)
+            if np.all(theirs == 0):
+                assert np.allclose(mine, theirs, atol=1e-3)
+            else:
+                assert np.allclose(mine, theirs, rtol=1e-2, atol=0)
+
+
+CASES = [
+    ("cfg0", SceneSpec(16_384, "uniform:1", -4.0, 0.5), 0, (256, 256, 60.0, (0, 0, 3)), None, {}, 3),
+    ("aa_bg", SceneSpec(16_384, "uniform:1", -4.0, 0.5), 5, (256, 256, 60.0, (0.3, 0.2, 2.5)), None,
+     dict(use_antialiasing=True, background=(0.2, 0.5, 0.9)), 3),
+    ("filter", SceneSpec(16_384, "uniform:1", -4.0, 0.5), 11, (256, 192, 60.0, (0, 0, 2.5)), None,
+     dict(clipping_mode=gs3d.FILTER), 2),
+    ("deg1_of3", SceneSpec(20_000, "uniform:1.5", -4.5, 0.5), 6, (320, 200, 70.0, (0, 1, 3)), None, {}, 1),
+    ("p720", SceneSpec(40_000, "uniform:3", -4.0, 0.6), 7, (1280, 720, 50.0, (0, 1.5, 6)), None, {}, 3),
+]
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
+@pytest.mark.parametrize("fix16", [False, True])
+def test_backward_random(cuda, case, fix16):
+    _, spec, seed, (w, h, fov, pos), tile, kw, deg = case
+    gv = synthetic_gaussians(spec, seed)
+    cam = look_at_camera(w, h, fov, pos)
+    opt = RenderOptions.for_camera(cam, deg, **kw)
+    til = Tiling.for_camera(cam, *(tile or (None, None)))
+    rng = np.random.default_rng(seed)
+    grad = rng.normal(0, 1e-5, size=(w, h, 3)).astype(np.float32)
+    gpu, _ = run_gpu(gv, cam, til, opt, grad, cuda, fix16)
+    g = O.NpGaussians.from_vector(gv)
+    ref_f = O.render(g, cam, til, opt)
+    ref = O.backward(g, cam, til, opt, ref_f, grad, flags=1 if fix16 else 0)
+    check_grads(gpu, ref)
+
+
+def test_adam_bit_exact(cuda):
+    spec = SceneSpec(16_384, "uniform:1", -4.0, 0.5)
+    gv = synthetic_gaussians(spec, 0)
+    cam = look_at_camera(256, 256, 60.0, (0, 0, 3))
+    opt = RenderOptions.for_camera(cam, 3)
+    til = Tiling.for_camera(cam)
+    grad = np.random.default_rng(1).normal(0, 1e-4, size=(256, 256, 3)).astype(np.float32)
+    gpu, (g, out, buf, fg) = run_gpu(gv, cam, til, opt, grad, cuda)
+    F, _ = gs3d.counts(buf)
+    # skip some filtered Gaussians, as ADC does (fgidx_to_gidx <= 0)
+    buf.fgidx_to_gidx[: F : 7] = 0
+    adam = AdamOptimizer(g, LearningRates(means=0.00016 * 3.3))
+    rng = np.random.default_rng(2)
+    for t in adam.moments.tensors():
+        t.copy_(torch.from_numpy(np.abs(rng.normal(0, 1e-4, size=tuple(t.shape))).astype(np.float32)))
+    adam.update_count = 5
+    before_g = O.NpGaussians.from_vector(g)
+    before_m = O.NpMoments.from_moments(adam.moments)
+    params = adam.params_c(3)
+    adam.update(fg, buf.fgidx_to_gidx, buf.device_counts, 3)
+    torch.cuda.synchronize()
+    bc1, bc2 = bias_corrections(adam.beta1, adam.beta2, 5)
+    O.adam(before_g, before_m, gpu, buf.fgidx_to_gidx[:F].cpu().numpy(), params, bc1, bc2)
+    after_g = O.NpGaussians.from_vector(g)
+    after_m = O.NpMoments.from_moments(adam.moments)
+    for a, b in zip((after_g.mo, after_g.sf, after_g.rf, after_g.sh),
+                    (before_g.mo, before_g.sf, before_g.rf, before_g.sh)):
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    for a, b in zip((after_m.mm, after_m.om, after_m.sm, after_m.rm, after_m.shm),
+                    (before_m.mm, before_m.om, before_m.sm, before_m.rm, before_m.shm)):
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    assert adam.update_count == 6
+
+
+def test_adam_reference_golden(cuda, golden):
+    """test/training.jl:181-257: beta1 = beta2 = 0.5, eps = 0, lr 1 (SH rest 10), t = 1,
+    parameters and moments of Gaussian k equal to k, gradients of filtered index k equal to k."""
+    tr = golden["training"]
+    n = 10
+    d = 1
+    f32 = dict(dtype=torch.float32, device=cuda)
+    # state after the reference's ADC step: Gaussian i holds the value of the old Gaussian it
+    # came from (ngidx_to_gidx), moments as the reference asserts them (zeros for splits and
+    # second clones)
+    k = torch.tensor(tr["ngidx_to_gidx"], **f32)
+    km = torch.tensor(tr["moments_after_adc"], **f32)
+    g = gs3d.GaussiansVector(k[:, None].repeat(1, 4).contiguous(), k[:, None].repeat(1, 3).contiguous(),
+                             k[:, None].repeat(1, 4).contiguous(),
+                             k[:, None, None].repeat(1, 3, (d + 1) ** 2).contiguous())
+    adam = AdamOptimizer(g, LearningRates(1.0, 1.0, 1.0, 1.0, 1.0, 10.0), beta1=0.5, beta2=0.5, epsilon=0.0)
+    for t in adam.moments.tensors():
+        t.copy_(km.view(-1, *([1] * (t.dim() - 1))).expand_as(t))
+    before = g.means_opacity_features.clone()
+    f2g = torch.tensor([int(x) for x in tr["adjusted_fgidx_to_gidx"]], dtype=torch.int32, device=cuda)
+    F = f2g.numel()
+    fg = FilteredGaussiansGradients.create(F, d, cuda)
+    kf = torch.arange(1, F + 1, **f32)
+    fg.mean3d_grads.copy_(kf[:, None].expand(F, 3))
+    fg.opacity_feature_grads.copy_(kf)
+    fg.scaling_features_grads.copy_(kf[:, None].expand(F, 3))
+    fg.rotation_features_grads.copy_(kf[:, None].expand(F, 4))
+    fg.sh_coeffs_grads.copy_(kf[:, None, None].expand(F, 3, 4))
+    counts = torch.tensor([F, 0, 0, 0], dtype=torch.int32, device=cuda)
+    adam.update(fg, f2g, counts, d)
+    torch.cuda.synchronize()
+
+    def expect(gidx, fgidx, lr=1.0):
+        m1h, m2h = gidx + fgidx, gidx + fgidx ** 2
+        return gidx - lr * m1h / np.sqrt(m2h), m1h / 2, m2h / 2
+
+    for ngidx, gidx, fgidx in tr["adam"]["checked"]:
+        i = ngidx - 1
+        p, m, v = expect(gidx, fgidx)
+        assert np.allclose(g.means_opacity_features[i].cpu().numpy(), p, rtol=1e-6)
+        assert np.allclose(adam.moments.means_moments[i].cpu().numpy(), np.array([[m, v]] * 3), rtol=1e-6)
+        assert np.allclose(adam.moments.opacity_features_moments[i].cpu().numpy(), [m, v], rtol=1e-6)
+        assert np.allclose(g.scaling_features[i].cpu().numpy(), p, rtol=1e-6)
+        assert np.allclose(g.rotation_features[i].cpu().numpy(), p, rtol=1e-6)
+        assert np.allclose(g.sh_coeffs[i, :, 0].cpu().numpy(), p, rtol=1e-6)
+        pr, mr, vr = expect(gidx, fgidx, 10.0)
+        assert np.allclose(g.sh_coeffs[i, :, 1:].cpu().numpy(), pr, rtol=1e-6)
+        assert np.allclose(adam.moments.sh_coeffs_moments[i, :, 1:].cpu().numpy()[..., 0], mr, rtol=1e-6)
+    for i in [int(x) for x in tr["splits_second_copies_ids"]]:
+        assert torch.equal(g.means_opacity_features[i - 1], before[i - 1])

@@ -1,0 +1,621 @@
+// backward.cu — backward! (backward_core.jl:37-72).
+//   k_zero_2d        zero_2d_grads! over the F filtered Gaussians (backward_structs.jl:250-257)
+//   k_bwd_raster     backward_render_tiles_kernel! (backward_core.jl:96-293): per pixel, back to
+//                    front from its last contributor, T recovered by division by (1 - alpha),
+//                    the reference's per-pair gradient formulas and order. The 9 per-pair
+//                    gradients are summed across the warp with register shuffles before one
+//                    lane issues the atomics (the reference issues 9 atomics per pixel-pair;
+//                    its TODO at backward_core.jl:282).
+//   k_bwd_project    backward_project_fgaussians_kernel! (backward_core.jl:309-452) with
+//                    compute_cov2d_lower_grad, Transposed_dsigma_dm / dv / dv_ds, DL_dR,
+//                    compute_normed_q_grad, compute_sh_coeffs_grad! and the colour/direction
+//                    Jacobian of sh.jl:175-267 (coefficient 15 in its last term unless
+//                    GS3D_BACKWARD_FIX_SH16).
+#include "common.cuh"
+#include "internal.h"
+
+namespace gs3d {
+
+int check_render_common(const gs3d_gaussians* g, const gs3d_camera* cam, const gs3d_tiling* til,
+                        const gs3d_render_options* opt);
+
+namespace {
+
+__global__ void __launch_bounds__(256) k_zero_2d(const int32_t* __restrict__ counts,
+                                                 float* __restrict__ m2, float* __restrict__ op,
+                                                 float* __restrict__ li, float* __restrict__ co) {
+    const int F = counts[0];
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < 3 * F; i += gridDim.x * blockDim.x) {
+        li[i] = 0.0f;
+        co[i] = 0.0f;
+        if (i < 2 * F) m2[i] = 0.0f;
+        if (i < F) op[i] = 0.0f;
+    }
+}
+
+struct BwdArgs {
+    const int32_t* sfgidx;
+    const int32_t* tiles_end;
+    const float* f2d;
+    const int32_t* counts;
+    int64_t capacity_dup;
+    const float* trans;
+    const int32_t* last;
+    const float* rgb_grad;
+    float* mean2d_g;
+    float* opacity_g;
+    float* licov_g;
+    float* color_g;
+    int32_t width, height, tile_w, tile_h, tiles_x;
+    float bg0, bg1, bg2, min_alpha, max_alpha, log_min_alpha;
+};
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__global__ void __launch_bounds__(512) k_bwd_raster(const BwdArgs a) {
+    extern __shared__ __align__(16) float4 sm4[];
+    const int nthr = blockDim.x;
+    float4* sA = sm4;                                    // x y opacity ic11
+    float4* sB = sm4 + nthr;                             // ic21 ic22 r g
+    float2* sC = reinterpret_cast<float2*>(sm4 + 2 * nthr);  // b q_threshold
+    int* sF = reinterpret_cast<int*>(sC + nthr);             // fgidx (0-based)
+    __shared__ int red[32];
+
+    const int F = a.counts[0];
+    const int64_t Draw = a.counts[1];
+    const int D = (int)(Draw < a.capacity_dup ? Draw : a.capacity_dup);
+    if (F == 0 || D == 0) return;
+
+    const int t = threadIdx.x;
+    const int lane = t & 31, warp = t >> 5;
+    const int lv = t % a.tile_h, lu = t / a.tile_h;
+    const int txi = blockIdx.x, tyi = blockIdx.y;
+    const int U = txi * a.tile_w + lu + 1, V = tyi * a.tile_h + lv + 1;
+    const bool inside = U <= a.width && V <= a.height;
+    const size_t px = (size_t)(V - 1) + (size_t)a.height * (size_t)(U - 1);
+    const int tile = txi + tyi * a.tiles_x + 1;
+    const int start = tile == 1 ? 0 : a.tiles_end[tile - 2];
+    const int end = a.tiles_end[tile - 1];
+
+    float T = 0.0f, g0 = 0.0f, g1 = 0.0f, g2 = 0.0f;
+    int lastc = 0;
+    if (inside) {
+        lastc = a.last[px];
+        T = a.trans[px];
+        g0 = a.rgb_grad[3 * px];
+        g1 = a.rgb_grad[3 * px + 1];
+        g2 = a.rgb_grad[3 * px + 2];
+    }
+    float p0 = T * a.bg0, p1 = T * a.bg1, p2 = T * a.bg2;
+    const float cpu = (float)U - 0.5f, cpv = (float)V - 0.5f;
+
+    // block / warp maxima of the last contributor (1-based sorted index)
+    int wlast = lastc;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) wlast = max(wlast, __shfl_xor_sync(0xffffffffu, wlast, o));
+    if (lane == 0) red[warp] = wlast;
+    __syncthreads();
+    int blast = 0;
+    for (int w = 0; w < (nthr >> 5); ++w) blast = max(blast, red[w]);
+    const int eff_end = min(end, blast);  // exclusive 0-based == inclusive 1-based
+
+    for (int bend = eff_end; bend > start; bend -= nthr) {
+        const int bstart = max(start, bend - nthr);
+        const int nb = bend - bstart;
+        __syncthreads();
+        if (t < nb) {
+            const int fg = a.sfgidx[bstart + t] - 1;
+            const float* r = a.f2d + 9 * (size_t)fg;
+            const float op = r[2];
+            sA[t] = make_float4(r[0], r[1], op, r[3]);
+            sB[t] = make_float4(r[4], r[5], r[6], r[7]);
+            // op * exp(q) < min_alpha whenever q < log(min_alpha) - log(op) - 0.01
+            const float thr = op > 0.0f ? a.log_min_alpha - gs_logf(op) - 0.01f : -INFINITY;
+            sC[t] = make_float2(r[8], thr);
+            sF[t] = fg;
+        }
+        __syncthreads();
+        const int jhi = min(nb, wlast - bstart) - 1;  // warp-uniform
+        for (int j = jhi; j >= 0; --j) {
+            const int idx1 = bstart + j + 1;
+            bool contrib = false;
+            float v0 = 0.f, v1 = 0.f, v2 = 0.f, v3 = 0.f, v4 = 0.f, v5 = 0.f, v6 = 0.f, v7 = 0.f, v8 = 0.f;
+            if (inside && idx1 <= lastc) {
+                const float4 A = sA[j];
+                const float4 B = sB[j];
+                const float2 Cc = sC[j];
+                const float du = cpu - A.x, dv = cpv - A.y;
+                const float ic11 = A.w, ic21 = B.x, ic22 = B.y;
+                const float q = -0.5f * (ic11 * (du * du) + ic22 * (dv * dv)) - ic21 * du * dv;
+                if (q >= Cc.y) {
+                    const float ge = gs_expf(q);
+                    const float alpha = fmin_jl(a.max_alpha, A.z * ge);
+                    if (alpha >= a.min_alpha) {
+                        contrib = true;
+                        const float inv1m = 1.0f / (1.0f - alpha);
+                        T *= inv1m;
+                        const float tc0 = T * B.z, tc1 = T * B.w, tc2 = T * Cc.x;
+                        p0 += alpha * tc0;
+                        p1 += alpha * tc1;
+                        p2 += alpha * tc2;
+                        const float ag = inv1m * (g0 * (tc0 - p0) + g1 * (tc1 - p1) + g2 * (tc2 - p2));
+                        const float aga = alpha * ag;
+                        const float sc = -0.5f * aga;
+                        const float g21 = sc * (dv * du);
+                        v0 = aga * (du * ic11 + dv * ic21);
+                        v1 = aga * (du * ic21 + dv * ic22);
+                        v2 = ge * ag;
+                        v3 = sc * (du * du);
+                        v4 = g21 + g21;
+                        v5 = sc * (dv * dv);
+                        const float ta = T * alpha;
+                        v6 = ta * g0;
+                        v7 = ta * g1;
+                        v8 = ta * g2;
+                    }
+                }
+            }
+            const unsigned mask = __ballot_sync(0xffffffffu, contrib);
+            if (mask == 0) continue;
+            const int fg = sF[j];
+            if (__popc(mask) == 1) {
+                if (contrib) {
+                    atomicAdd(a.mean2d_g + 2 * fg, v0);
+                    atomicAdd(a.mean2d_g + 2 * fg + 1, v1);
+                    atomicAdd(a.opacity_g + fg, v2);
+                    atomicAdd(a.licov_g + 3 * fg, v3);
+                    atomicAdd(a.licov_g + 3 * fg + 1, v4);
+                    atomicAdd(a.licov_g + 3 * fg + 2, v5);
+                    atomicAdd(a.color_g + 3 * fg, v6);
+                    atomicAdd(a.color_g + 3 * fg + 1, v7);
+                    atomicAdd(a.color_g + 3 * fg + 2, v8);
+                }
+            } else {
+                v0 = warp_sum(v0); v1 = warp_sum(v1); v2 = warp_sum(v2);
+                v3 = warp_sum(v3); v4 = warp_sum(v4); v5 = warp_sum(v5);
+                v6 = warp_sum(v6); v7 = warp_sum(v7); v8 = warp_sum(v8);
+                if (lane == 0) {
+                    atomicAdd(a.mean2d_g + 2 * fg, v0);
+                    atomicAdd(a.mean2d_g + 2 * fg + 1, v1);
+                    atomicAdd(a.opacity_g + fg, v2);
+                    atomicAdd(a.licov_g + 3 * fg, v3);
+                    atomicAdd(a.licov_g + 3 * fg + 1, v4);
+                    atomicAdd(a.licov_g + 3 * fg + 2, v5);
+                    atomicAdd(a.color_g + 3 * fg, v6);
+                    atomicAdd(a.color_g + 3 * fg + 1, v7);
+                    atomicAdd(a.color_g + 3 * fg + 2, v8);
+                }
+            }
+        }
+    }
+}
+
+// ---- projection backward -------------------------------------------------------------------
+__device__ __forceinline__ int low3(int i, int j) {
+    // column-major lower index of a symmetric 3x3: (0,0)0 (1,0)1 (2,0)2 (1,1)3 (2,1)4 (2,2)5
+    const int hi = i > j ? i : j, lo = i > j ? j : i;
+    return lo == 0 ? hi : (lo == 1 ? 2 + hi : 5);
+}
+
+__device__ __forceinline__ float sh_basis(int i, float x, float y, float z) {
+    switch (i) {
+        case 1: return sh_c(1);
+        case 2: return -y * sh_c(2);
+        case 3: return z * sh_c(3);
+        case 4: return -x * sh_c(4);
+        case 5: return x * y * sh_c(5);
+        case 6: return y * z * sh_c(6);
+        case 7: return (2.0f * (z * z) - x * x - y * y) * sh_c(7);
+        case 8: return x * z * sh_c(8);
+        case 9: return (x * x - y * y) * sh_c(9);
+        case 10: return y * (3.0f * (x * x) - y * y) * sh_c(10);
+        case 11: return x * y * z * sh_c(11);
+        case 12: return y * (4.0f * (z * z) - x * x - y * y) * sh_c(12);
+        case 13: return z * (2.0f * (z * z) - 3.0f * (x * x + y * y)) * sh_c(13);
+        case 14: return x * (4.0f * (z * z) - x * x - y * y) * sh_c(14);
+        case 15: return z * (x * x - y * y) * sh_c(15);
+        case 16: return x * (x * x - 3.0f * (y * y)) * sh_c(16);
+        default: return 0.0f;
+    }
+}
+
+struct BProjArgs {
+    const float4* mo4;
+    const float* scal;
+    const float4* rot4;
+    const float* sh;
+    int sh_stride;
+    const int32_t* f2g;
+    const float* f2d;
+    const int32_t* counts;
+    const float* mean2d_g;
+    const float* opacity_g;
+    const float* licov_g;
+    const float* color_g;
+    float* mean3d_g;
+    float* opf_g;
+    float* scale_g;
+    float* rot_g;
+    float* sh_g;
+    int sh_grad_stride;
+    int fix_sh16;
+};
+
+template <int DEG>
+__global__ void __launch_bounds__(128) k_bwd_project(const BProjArgs a, const gs3d_camera cam,
+                                                     const gs3d_render_options opt) {
+    const int F = a.counts[0];
+    float Ps[3][3];
+#pragma unroll
+    for (int i = 0; i < 3; ++i)
+#pragma unroll
+        for (int j = 0; j < 3; ++j) Ps[i][j] = cam.P[i + 3 * j];
+    const int L2I[3] = {0, 1, 1}, L2J[3] = {0, 0, 1};
+    const int L3I[6] = {0, 1, 2, 1, 2, 2}, L3J[6] = {0, 0, 0, 1, 1, 2};
+    constexpr int MAXO = (DEG + 1) * (DEG + 1);
+    for (int f = blockIdx.x * blockDim.x + threadIdx.x; f < F; f += gridDim.x * blockDim.x) {
+        const int gi = a.f2g[f] - 1;
+        const float* r = a.f2d + 9 * (size_t)f;
+        const float4 mo = a.mo4[gi];
+        const float orig_op = gs_sigmoid(mo.w);
+        const float depth = Ps[2][0] * mo.x + Ps[2][1] * mo.y + Ps[2][2] * mo.z + cam.P[11];
+        const float opac = opt.use_antialiasing ? r[2] : orig_op;
+        const float og = a.opacity_g[f];
+        a.opf_g[f] = opt.use_antialiasing ? og * opac * (1.0f - orig_op) : og * opac * (1.0f - opac);
+
+        // compute_cov2d_lower_grad (backward_core.jl:465-493)
+        const float ia = r[3], ib = r[4], id = r[5];
+        const float a_sq = ia * ia, ab = ia * ib, b_sq = ib * ib, bd = ib * id, d_sq = id * id, ad = ia * id;
+        const float ab2 = ab + ab, bd2 = bd + bd;
+        const float M[3][3] = {{a_sq, ab, b_sq}, {ab2, b_sq + ad, bd2}, {ib * ib, bd, d_sq}};
+        const float lg0 = a.licov_g[3 * (size_t)f], lg1 = a.licov_g[3 * (size_t)f + 1],
+                    lg2 = a.licov_g[3 * (size_t)f + 2];
+        float cg[3];
+#pragma unroll
+        for (int i = 0; i < 3; ++i) cg[i] = -(M[i][0] * lg0 + M[i][1] * lg1 + M[i][2] * lg2);
+        if (opt.use_antialiasing) {
+            const float Dx = opt.dilation_x, Dy = opt.dilation_y;
+            const float det = (ad - b_sq) * Dx * Dy;
+            const float b2 = ib + ib;
+            const float k = orig_op * og;
+            const float e0 = a_sq * Dx + b_sq * Dx - ia * det;
+            const float e1 = b2 * (ia * Dx + id * Dy - det);
+            const float e2 = b_sq * Dx + (id * id) * Dy - id * det;
+            cg[0] = cg[0] + k * e0;
+            cg[1] = cg[1] + k * e1;
+            cg[2] = cg[2] + k * e2;
+        }
+
+        // mean3d gradient from mean2d
+        const float mx = r[0], my = r[1];
+        float cmx = mx, cmy = my;
+        const bool clampmode = opt.clipping_mode == 0;
+        if (clampmode) {
+            cmx = jl_clamp(mx, opt.clip_x_min, opt.clip_x_max);
+            cmy = jl_clamp(my, opt.clip_y_min, opt.clip_y_max);
+        }
+        const float idepth = 1.0f / depth;
+        float J[2][3];
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+            J[0][j] = idepth * (Ps[0][j] + (-cmx) * Ps[2][j]);
+            J[1][j] = idepth * (Ps[1][j] + (-cmy) * Ps[2][j]);
+        }
+        const float gx = a.mean2d_g[2 * (size_t)f], gy = a.mean2d_g[2 * (size_t)f + 1];
+        float m3[3];
+        if (!clampmode) {
+#pragma unroll
+            for (int j = 0; j < 3; ++j) m3[j] = J[0][j] * gx + J[1][j] * gy;
+        } else {
+            const float t0 = gx, t1 = gy, t2 = -(mx * gx + my * gy);
+#pragma unroll
+            for (int j = 0; j < 3; ++j) m3[j] = idepth * (Ps[0][j] * t0 + Ps[1][j] * t1 + Ps[2][j] * t2);
+        }
+
+        // 3D covariance lower (V), scales, rotation
+        const float s[3] = {gs_expf(a.scal[3 * (size_t)gi]), gs_expf(a.scal[3 * (size_t)gi + 1]),
+                            gs_expf(a.scal[3 * (size_t)gi + 2])};
+        const float4 qf = a.rot4[gi];
+        float R[3][3];
+        {
+            const float qss = qf.x * qf.x + qf.y * qf.y + qf.z * qf.z + qf.w * qf.w;
+            const float qs = sqrtf(2.0f * (1.0f / qss));
+            const float rr = qf.x * qs, x = qf.y * qs, y = qf.z * qs, z = qf.w * qs;
+            R[0][0] = 1.0f - (y * y + z * z); R[0][1] = x * y - rr * z; R[0][2] = x * z + rr * y;
+            R[1][0] = x * y + rr * z; R[1][1] = 1.0f - (x * x + z * z); R[1][2] = y * z - rr * x;
+            R[2][0] = x * z - rr * y; R[2][1] = y * z + rr * x; R[2][2] = 1.0f - (x * x + y * y);
+        }
+        float V[6];
+        {
+            float RS[3][3];
+#pragma unroll
+            for (int i = 0; i < 3; ++i)
+#pragma unroll
+                for (int j = 0; j < 3; ++j) RS[i][j] = R[i][j] * s[j];
+#pragma unroll
+            for (int k = 0; k < 6; ++k) {
+                const int i = L3I[k], j = L3J[k];
+                V[k] = RS[i][0] * RS[j][0] + RS[i][1] * RS[j][1] + RS[i][2] * RS[j][2];
+            }
+        }
+        // mean3d gradient from cov2d (Transposed_dsigma_dm, backward_core.jl:789-922)
+        {
+            const float c2x = cmx + cmx, c2y = cmy + cmy;
+            float dlx = 1.0f, dly = 1.0f;
+            if (clampmode) {
+                dlx = (opt.clip_x_min < cmx && cmx <= opt.clip_x_max) ? 1.0f : 0.0f;
+                dly = (opt.clip_y_min < cmy && cmy <= opt.clip_y_max) ? 1.0f : 0.0f;
+            }
+            float dJ[2][3][3];
+#pragma unroll
+            for (int al = 0; al < 3; ++al) {
+                const float r0 = Ps[0][al] - c2x * Ps[2][al];
+                const float r1 = Ps[1][al] - c2y * Ps[2][al];
+                const float e0 = dlx * Ps[2][al];
+                const float e1 = dly * Ps[2][al];
+#pragma unroll
+                for (int k = 0; k < 3; ++k) {
+                    dJ[0][al][k] = e0 * Ps[0][k] + r0 * Ps[2][k];
+                    dJ[1][al][k] = e1 * Ps[1][k] + r1 * Ps[2][k];
+                }
+            }
+            const float sc = -(1.0f / (depth * depth));
+#pragma unroll
+            for (int k = 0; k < 3; ++k) {
+                float acc3 = 0.0f;
+#pragma unroll
+                for (int p = 0; p < 3; ++p) {
+                    const int i = L2I[p], j = L2J[p];
+                    float tt = 0.0f;
+#pragma unroll
+                    for (int al = 0; al < 3; ++al)
+#pragma unroll
+                        for (int be = 0; be < 3; ++be)
+                            tt = tt + V[low3(al, be)] * (dJ[i][al][k] * J[j][be] + J[i][al] * dJ[j][be][k]);
+                    acc3 = acc3 + tt * cg[p];
+                }
+                m3[k] = m3[k] + sc * acc3;
+            }
+        }
+        // mean3d gradient from the view-dependent colour
+        const float vx = mo.x - cam.position[0], vy = mo.y - cam.position[1], vz = mo.z - cam.position[2];
+        const float inv_vn = 1.0f / sqrtf(vx * vx + vy * vy + vz * vz);
+        const float nd0 = vx * inv_vn, nd1 = vy * inv_vn, nd2 = vz * inv_vn;
+        const float col[3] = {r[6], r[7], r[8]};
+        const float cgr[3] = {a.color_g[3 * (size_t)f], a.color_g[3 * (size_t)f + 1],
+                              a.color_g[3 * (size_t)f + 2]};
+        const float* h = a.sh + (size_t)gi * 3 * a.sh_stride;
+        float Jt[3][3] = {{0.f, 0.f, 0.f}, {0.f, 0.f, 0.f}, {0.f, 0.f, 0.f}};
+        if (DEG > 0) {
+            const float x = nd0, y = nd1, z = nd2;
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                if (col[c] <= 0.0f) continue;
+                const float* hc = h + c * MAXO;  // linear indexing with the options order (sh.jl:196)
+                float dy = -sh_c(2) * hc[1];
+                float dz = sh_c(3) * hc[2];
+                float dx = -sh_c(4) * hc[3];
+                if (DEG >= 2) {
+                    { const float q = sh_c(5) * hc[4]; dx += y * q; dy += x * q; }
+                    { const float q = sh_c(6) * hc[5]; dy += z * q; dz += y * q; }
+                    { const float q = sh_c(7) * hc[6]; dx -= 2.0f * x * q; dy -= 2.0f * y * q; dz += 4.0f * z * q; }
+                    { const float q = sh_c(8) * hc[7]; dx += z * q; dz += x * q; }
+                    { const float q = sh_c(9) * hc[8]; dx += 2.0f * x * q; dy -= 2.0f * y * q; }
+                    if (DEG >= 3) {
+                        { const float q = sh_c(10) * hc[9]; dx += 6.0f * x * y * q; dy += 3.0f * (x * x - y * y) * q; }
+                        { const float q = sh_c(11) * hc[10]; dx += y * z * q; dy += x * z * q; dz += x * y * q; }
+                        { const float q = sh_c(12) * hc[11];
+                          dx -= 2.0f * x * y * q;
+                          dy += (4.0f * (z * z) - x * x - 3.0f * (y * y)) * q;
+                          dz += 8.0f * y * z * q; }
+                        { const float q = sh_c(13) * hc[12];
+                          dx -= 6.0f * x * z * q;
+                          dy -= 6.0f * y * z * q;
+                          dz += 3.0f * (2.0f * (z * z) - x * x - y * y) * q; }
+                        { const float q = sh_c(14) * hc[13];
+                          dx += (4.0f * (z * z) - 3.0f * (x * x) - y * y) * q;
+                          dy -= 2.0f * x * y * q;
+                          dz += 8.0f * x * z * q; }
+                        { const float q = sh_c(15) * hc[14]; dx += 2.0f * x * z * q; dy -= 2.0f * y * z * q; dz += (x * x - y * y) * q; }
+                        { const float q = sh_c(16) * hc[a.fix_sh16 ? 15 : 14];
+                          dx += 3.0f * (x * x - y * y) * q;
+                          dy -= 6.0f * x * y * q; }
+                    }
+                }
+                Jt[0][c] = dx; Jt[1][c] = dy; Jt[2][c] = dz;
+            }
+        }
+        const float nd[3] = {nd0, nd1, nd2};
+        float ndg[3];
+#pragma unroll
+        for (int i = 0; i < 3; ++i) ndg[i] = Jt[i][0] * cgr[0] + Jt[i][1] * cgr[1] + Jt[i][2] * cgr[2];
+#pragma unroll
+        for (int i = 0; i < 3; ++i) {
+            float w = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 3; ++j) {
+                const float Nij = i == j ? 1.0f - nd[i] * nd[i] : -nd[i < j ? i : j] * nd[i < j ? j : i];
+                w = w + Nij * ndg[j];
+            }
+            m3[i] = m3[i] + inv_vn * w;
+        }
+        a.mean3d_g[3 * (size_t)f] = m3[0];
+        a.mean3d_g[3 * (size_t)f + 1] = m3[1];
+        a.mean3d_g[3 * (size_t)f + 2] = m3[2];
+
+        // scaling features: v gradient = Transposed_dsigma_dv(J) * cg
+        float vg[6];
+#pragma unroll
+        for (int jv = 0; jv < 6; ++jv) {
+            const int rr = L3I[jv], ss = L3J[jv];
+            float tt = 0.0f;
+#pragma unroll
+            for (int p = 0; p < 3; ++p) {
+                const int pp = L2I[p], qq = L2J[p];
+                float e = J[pp][rr] * J[qq][ss];
+                if (rr != ss) e = e + J[pp][ss] * J[qq][rr];
+                tt = tt + e * cg[p];
+            }
+            vg[jv] = tt;
+        }
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+            float tt = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 6; ++i) tt = tt + (s[j] * R[L3I[i]][j] * R[L3J[i]][j]) * vg[i];
+            a.scale_g[3 * (size_t)f + j] = (2.0f * tt) * s[j];
+        }
+        // rotation features
+        {
+            const float ssq[3] = {s[0] * s[0], s[1] * s[1], s[2] * s[2]};
+            float Rg[3][3];
+#pragma unroll
+            for (int k = 0; k < 3; ++k)
+#pragma unroll
+                for (int l = 0; l < 3; ++l) {
+                    float tt = vg[low3(k, k)] * R[k][l];
+#pragma unroll
+                    for (int i = 0; i < 3; ++i) tt = tt + vg[low3(i, k)] * R[i][l];
+                    Rg[k][l] = ssq[l] * tt;
+                }
+            const float qss = qf.x * qf.x + qf.y * qf.y + qf.z * qf.z + qf.w * qf.w;
+            const float inv_qn = 1.0f / sqrtf(qss);
+            const float nq[4] = {qf.x * inv_qn, qf.y * inv_qn, qf.z * inv_qn, qf.w * inv_qn};
+            const float rq = nq[0], xq = nq[1], yq = nq[2], zq = nq[3];
+            const float m2x = -(xq + xq), m2y = -(yq + yq), m2z = -(zq + zq);
+            const float A[4][3][3] = {
+                {{0.0f, -zq, yq}, {zq, 0.0f, -xq}, {-yq, xq, 0.0f}},
+                {{0.0f, yq, zq}, {yq, m2x, -rq}, {zq, rq, m2x}},
+                {{m2y, xq, rq}, {xq, 0.0f, zq}, {-rq, zq, m2y}},
+                {{m2z, -rq, xq}, {rq, m2z, yq}, {xq, yq, 0.0f}}};
+            float nqg[4];
+#pragma unroll
+            for (int t4 = 0; t4 < 4; ++t4) {
+                float dsum = 0.0f;
+#pragma unroll
+                for (int c3 = 0; c3 < 3; ++c3)
+#pragma unroll
+                    for (int r3 = 0; r3 < 3; ++r3) dsum = dsum + A[t4][r3][c3] * Rg[r3][c3];
+                nqg[t4] = 2.0f * dsum;
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float w = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float Nij = i == j ? 1.0f - nq[i] * nq[i] : -nq[i < j ? i : j] * nq[i < j ? j : i];
+                    w = w + Nij * nqg[j];
+                }
+                a.rot_g[4 * (size_t)f + i] = inv_qn * w;
+            }
+        }
+        // SH coefficients (compute_sh_coeffs_grad!, backward_core.jl:936-964)
+        float* shg = a.sh_g + (size_t)f * 3 * a.sh_grad_stride;
+#pragma unroll
+        for (int l = 0; l < 3; ++l) {
+            const bool live = col[l] >= 0.0f;
+#pragma unroll
+            for (int k = 1; k <= MAXO; ++k)
+                shg[(k - 1) + l * a.sh_grad_stride] = live ? cgr[l] * sh_basis(k, nd0, nd1, nd2) : 0.0f;
+        }
+    }
+}
+
+int grid_for(int64_t items, int threads, int per_sm) {
+    int64_t b = ceil_div(items, threads);
+    const int64_t cap = (int64_t)kSMs * per_sm;
+    if (b > cap) b = cap;
+    if (b < 1) b = 1;
+    return (int)b;
+}
+
+}  // namespace
+}  // namespace gs3d
+
+using namespace gs3d;
+
+extern "C" GS3D_API int gs3d_backward(const gs3d_fgradients* fg, const float* rgb_grad,
+                                      const gs3d_render_outputs* out, const gs3d_gaussians* g,
+                                      const gs3d_camera* cam, const gs3d_tiling* til,
+                                      const gs3d_render_options* opt,
+                                      const gs3d_render_buffers* buf, uint32_t flags,
+                                      gs3d_stream_t stream_) {
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+    GS3D_RETURN_IF(check_render_common(g, cam, til, opt));
+    if (!fg || !rgb_grad || !out || !buf) return invalid("NULL argument");
+    if (!out->transmittance || !out->last_contributing_sdfgids)
+        return invalid("backward needs the transmittance and last-contributor images");
+    if (!fg->mean2d_grads || !fg->opacity_grads || !fg->licov2d_grads || !fg->color_grads ||
+        !fg->mean3d_grads || !fg->opacity_feature_grads || !fg->scaling_features_grads ||
+        !fg->rotation_features_grads || !fg->sh_coeffs_grads)
+        return invalid("NULL gradient array");
+    if (fg->sh_degree < opt->sh_degree || fg->sh_degree > 3)
+        return invalid("gradient SH degree %d < render degree %d", fg->sh_degree, opt->sh_degree);
+    const int64_t cap_n = buf->capacity_n > 0 ? buf->capacity_n : 1;
+    k_zero_2d<<<grid_for(3 * cap_n, 256, 8), 256, 0, stream>>>(
+        buf->device_counts, fg->mean2d_grads, fg->opacity_grads, fg->licov2d_grads, fg->color_grads);
+    GS3D_LAUNCHED("k_zero_2d");
+
+    BwdArgs a;
+    a.sfgidx = buf->sdfgidx_to_fgidx;
+    a.tiles_end = buf->tiles_end_sdfgidx;
+    a.f2d = buf->means2d_opacities_inverse_covariances_colors;
+    a.counts = buf->device_counts;
+    a.capacity_dup = buf->capacity_dup;
+    a.trans = out->transmittance;
+    a.last = out->last_contributing_sdfgids;
+    a.rgb_grad = rgb_grad;
+    a.mean2d_g = fg->mean2d_grads;
+    a.opacity_g = fg->opacity_grads;
+    a.licov_g = fg->licov2d_grads;
+    a.color_g = fg->color_grads;
+    a.width = cam->width;
+    a.height = cam->height;
+    a.tile_w = til->tile_width;
+    a.tile_h = til->tile_height;
+    a.tiles_x = til->nb_tiles_x;
+    a.bg0 = opt->background[0];
+    a.bg1 = opt->background[1];
+    a.bg2 = opt->background[2];
+    a.min_alpha = opt->min_alpha;
+    a.max_alpha = opt->max_alpha;
+    a.log_min_alpha = opt->min_alpha > 0.0f ? gs_logf(opt->min_alpha) : -INFINITY;
+    const int nthr = til->tile_width * til->tile_height;
+    const size_t smem = (size_t)nthr * (2 * sizeof(float4) + sizeof(float2) + sizeof(int));
+    k_bwd_raster<<<dim3(til->nb_tiles_x, til->nb_tiles_y), nthr, smem, stream>>>(a);
+    GS3D_LAUNCHED("k_bwd_raster");
+
+    BProjArgs p;
+    p.mo4 = reinterpret_cast<const float4*>(g->means_opacity_features);
+    p.scal = g->scaling_features;
+    p.rot4 = reinterpret_cast<const float4*>(g->rotation_features);
+    p.sh = g->sh_coeffs;
+    p.sh_stride = (g->sh_degree + 1) * (g->sh_degree + 1);
+    p.f2g = buf->fgidx_to_gidx;
+    p.f2d = buf->means2d_opacities_inverse_covariances_colors;
+    p.counts = buf->device_counts;
+    p.mean2d_g = fg->mean2d_grads;
+    p.opacity_g = fg->opacity_grads;
+    p.licov_g = fg->licov2d_grads;
+    p.color_g = fg->color_grads;
+    p.mean3d_g = fg->mean3d_grads;
+    p.opf_g = fg->opacity_feature_grads;
+    p.scale_g = fg->scaling_features_grads;
+    p.rot_g = fg->rotation_features_grads;
+    p.sh_g = fg->sh_coeffs_grads;
+    p.sh_grad_stride = (fg->sh_degree + 1) * (fg->sh_degree + 1);
+    p.fix_sh16 = (flags & GS3D_BACKWARD_FIX_SH16) ? 1 : 0;
+    const int grid = grid_for(cap_n, 128, 16);
+    switch (opt->sh_degree) {
+        case 0: k_bwd_project<0><<<grid, 128, 0, stream>>>(p, *cam, *opt); break;
+        case 1: k_bwd_project<1><<<grid, 128, 0, stream>>>(p, *cam, *opt); break;
+        case 2: k_bwd_project<2><<<grid, 128, 0, stream>>>(p, *cam, *opt); break;
+        default: k_bwd_project<3><<<grid, 128, 0, stream>>>(p, *cam, *opt); break;
+    }
+    GS3D_LAUNCHED("k_bwd_project");
+    return GS3D_OK;
+}

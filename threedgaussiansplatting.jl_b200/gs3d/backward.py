@@ -1,0 +1,94 @@
+"""backward! (backward_core.jl:37-72) through libgs3d.so, and its gradient buffers
+(FilteredGaussiansGradientsVector, backward_structs.jl:1-29), indexed by filtered index."""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import torch
+
+from . import _abi
+from .render import _stream_handle
+from .structs import (GaussiansVector, PinholeCamera, RenderBuffers, RenderOptions,
+                      RenderOutputs, Tiling, _ptr)
+
+
+@dataclass
+class FilteredGaussiansGradients:
+    mean2d_grads: torch.Tensor             # (n, 2)
+    opacity_grads: torch.Tensor            # (n,)
+    licov2d_grads: torch.Tensor            # (n, 3)
+    color_grads: torch.Tensor              # (n, 3)
+    mean3d_grads: torch.Tensor             # (n, 3)
+    opacity_feature_grads: torch.Tensor    # (n,)
+    scaling_features_grads: torch.Tensor   # (n, 3)
+    rotation_features_grads: torch.Tensor  # (n, 4)
+    sh_coeffs_grads: torch.Tensor          # (n, 3, (d+1)^2)
+
+    @classmethod
+    def create(cls, capacity: int, sh_degree: int, device) -> "FilteredGaussiansGradients":
+        n = max(capacity, 1)
+        f = dict(dtype=torch.float32, device=device)
+        order = (sh_degree + 1) ** 2
+        return cls(torch.zeros((n, 2), **f), torch.zeros(n, **f), torch.zeros((n, 3), **f),
+                   torch.zeros((n, 3), **f), torch.zeros((n, 3), **f), torch.zeros(n, **f),
+                   torch.zeros((n, 3), **f), torch.zeros((n, 4), **f),
+                   torch.zeros((n, 3, order), **f))
+
+    @property
+    def capacity(self) -> int:
+        return self.mean2d_grads.shape[0]
+
+    @property
+    def sh_degree(self) -> int:
+        return int(round(self.sh_coeffs_grads.shape[2] ** 0.5)) - 1
+
+    def set_sh_degree(self, d: int) -> None:
+        """set_sh_degree! for gradients: grow the SH axis (new entries zero)."""
+        old = self.sh_coeffs_grads
+        new = torch.zeros((old.shape[0], 3, (d + 1) ** 2), dtype=old.dtype, device=old.device)
+        k = min(old.shape[2], new.shape[2])
+        new[:, :, :k] = old[:, :, :k]
+        self.sh_coeffs_grads = new
+
+    def resize(self, capacity: int) -> None:
+        """set_nb_gaussians! for gradients (contents are not kept)."""
+        fresh = FilteredGaussiansGradients.create(capacity, self.sh_degree,
+                                                  self.mean2d_grads.device)
+        self.__dict__.update(fresh.__dict__)
+
+    def to_c(self) -> _abi.FGradientsC:
+        f = _abi.FGradientsC()
+        f.sh_degree = self.sh_degree
+        f.mean2d_grads = _ptr(self.mean2d_grads)
+        f.opacity_grads = _ptr(self.opacity_grads)
+        f.licov2d_grads = _ptr(self.licov2d_grads)
+        f.color_grads = _ptr(self.color_grads)
+        f.mean3d_grads = _ptr(self.mean3d_grads)
+        f.opacity_feature_grads = _ptr(self.opacity_feature_grads)
+        f.scaling_features_grads = _ptr(self.scaling_features_grads)
+        f.rotation_features_grads = _ptr(self.rotation_features_grads)
+        f.sh_coeffs_grads = _ptr(self.sh_coeffs_grads)
+        return f
+
+
+def backward(fgradients: FilteredGaussiansGradients, rgb_image_grad: torch.Tensor,
+             outputs: RenderOutputs, gaussians: GaussiansVector, camera: PinholeCamera,
+             tiling: Tiling, options: RenderOptions, buffers: RenderBuffers,
+             fix_sh16: bool = False, stream: torch.cuda.Stream | None = None):
+    """Gradients of the loss w.r.t. the filtered Gaussians' parameters, from the gradient
+    image `rgb_image_grad` ((w, h, 3), i.e. 3 x h x w). The forward render must have run with
+    the same arguments. `fix_sh16` uses SH coefficient 16 in the last degree-3 term of the
+    colour/direction Jacobian; the default reproduces the reference (coefficient 15)."""
+    assert rgb_image_grad.is_contiguous() and rgb_image_grad.dtype == torch.float32
+    if fgradients.capacity < buffers.capacity_n:
+        raise ValueError("gradient buffers smaller than the render buffers")
+    lib = _abi.lib()
+    args = [fgradients.to_c(), outputs.to_c(), gaussians.to_c(), camera.to_c(), tiling.to_c(),
+            options.to_c(), buffers.to_c()]
+    flags = _abi.GS3D_BACKWARD_FIX_SH16 if fix_sh16 else 0
+    _abi.check(lib.gs3d_backward(C.byref(args[0]), C.c_void_p(rgb_image_grad.data_ptr()),
+                                 C.byref(args[1]), C.byref(args[2]), C.byref(args[3]),
+                                 C.byref(args[4]), C.byref(args[5]), C.byref(args[6]), flags,
+                                 C.c_void_p(_stream_handle(stream))))
+    return fgradients
