@@ -257,6 +257,60 @@ def adam(g: NpGaussians, m: NpMoments, grads: dict, fgidx_to_gidx: np.ndarray, p
                              C.byref(params), bc1, bc2) == 0
 
 
+def adc_stats(acc: np.ndarray, cnt: np.ndarray, mean2d_g: np.ndarray, fgidx_to_gidx: np.ndarray,
+              width: int, height: int) -> None:
+    m2 = np.ascontiguousarray(mean2d_g, np.float32)
+    f2g = np.ascontiguousarray(fgidx_to_gidx, np.int32)
+    assert acc.dtype == np.float32 and cnt.dtype == np.int32
+    lib().oracle_adc_stats(_p(acc), _p(cnt), _p(m2), _p(f2g), f2g.size, width, height)
+
+
+def adc_plan(g: NpGaussians, acc, cnt, params) -> dict:
+    n = g.n
+    out = dict(max_sf=np.zeros(n, np.float32), prune=np.zeros(n, np.uint8),
+               densify=np.zeros(n, np.uint8), clone=np.zeros(n, np.uint8),
+               counts=np.zeros(n, np.uint8), counts_cs=np.zeros(n, np.int32),
+               ngidx_to_gidx=np.zeros(2 * max(n, 1), np.int32))
+    gc = g.to_c()
+    acc = np.ascontiguousarray(acc, np.float32)
+    cnt = np.ascontiguousarray(cnt, np.int32)
+    new_n = lib().oracle_adc_plan(C.byref(gc), _p(acc), _p(cnt), C.byref(params), _p(out["max_sf"]),
+                                  _p(out["prune"]), _p(out["densify"]), _p(out["clone"]),
+                                  _p(out["counts"]), _p(out["counts_cs"]), _p(out["ngidx_to_gidx"]))
+    out["new_n"] = int(new_n)
+    out["ngidx_to_gidx"] = out["ngidx_to_gidx"][:new_n]
+    return out
+
+
+def adc_apply(g: NpGaussians, m: NpMoments, plan: dict, fgidx_to_gidx: np.ndarray | None,
+              log_split: float, seed: int):
+    """Returns (new NpGaussians, new NpMoments, retargeted fgidx_to_gidx)."""
+    nn = plan["new_n"]
+    S = g.sh.shape[2]
+    Sm = m.shm.shape[2]
+    ng = NpGaussians(np.zeros((nn, 4)), np.zeros((nn, 3)), np.zeros((nn, 4)), np.zeros((nn, 3, S)))
+    nm = NpMoments(np.zeros((nn, 3, 2)), np.zeros((nn, 2)), np.zeros((nn, 3, 2)), np.zeros((nn, 4, 2)),
+                   np.zeros((nn, 3, Sm, 2)))
+    f2g = np.ascontiguousarray(fgidx_to_gidx if fgidx_to_gidx is not None else np.zeros(0), np.int32).copy()
+    gc, mc, ngc, nmc = g.to_c(), m.to_c(), ng.to_c(), nm.to_c()
+    assert lib().oracle_adc_apply(C.byref(gc), C.byref(mc), C.byref(ngc), C.byref(nmc),
+                                  _p(plan["prune"]), _p(plan["densify"]), _p(plan["clone"]),
+                                  _p(plan["counts_cs"]), _p(f2g), f2g.size, log_split,
+                                  seed & 0xFFFFFFFFFFFFFFFF) == 0
+    return ng, nm, f2g
+
+
+def opacity_reset(g: NpGaussians, m: NpMoments, max_opacity: float) -> None:
+    gc, mc = g.to_c(), m.to_c()
+    lib().oracle_opacity_reset(C.byref(gc), C.byref(mc), max_opacity)
+
+
+def split_normals(seed: int, key: int) -> np.ndarray:
+    out = np.zeros(6, np.float32)
+    lib().oracle_split_normals(seed & 0xFFFFFFFFFFFFFFFF, key, _p(out))
+    return out
+
+
 def sort_pairs(keys: np.ndarray, vals: np.ndarray, highest_key_bit: int):
     keys = np.ascontiguousarray(keys, np.int64)
     vals = np.ascontiguousarray(vals, np.int32)

@@ -1,0 +1,192 @@
+"""Loss, densification and a whole training step on the GPU against the CPU oracle."""
+import numpy as np
+import pytest
+import torch
+
+import gs3d
+from gs3d import RenderOptions, Tiling, _abi
+from gs3d import adc as adc_mod
+from gs3d.loss import LossComputer
+from gs3d.optimizer import AdamMoments, bias_corrections
+from gs3d.scene import SceneSpec, look_at_camera, synthetic_gaussians, target_image
+from gs3d.training import Trainer, TrainingOptions
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("w,h,weight", [(64, 48, 0.2), (256, 256, 0.2), (333, 171, 0.5), (100, 80, 0.0)])
+def test_loss_matches_oracle(cuda, w, h, weight):
+    rng = np.random.default_rng(w * h)
+    K = rng.uniform(0, 1, (w, h, 3)).astype(np.float32)
+    K[: w // 2] = np.clip(K[: w // 2] * 0.3 + 0.2, 0, 1)  # some structure
+    I = rng.uniform(0, 1, (w, h, 3)).astype(np.float32)
+    I[5, 5] = K[5, 5]  # ties take the negative L1 branch
+    lc = LossComputer(w, h, cuda, weight)
+    grad = torch.empty((w, h, 3), dtype=torch.float32, device=cuda)
+    val = lc(torch.from_numpy(K).to(cuda), torch.from_numpy(I).to(cuda), grad).cpu().numpy()
+    ref, ref_grad = O.loss(K, I, weight)
+    np.testing.assert_allclose(val[:3], ref, rtol=2e-5, atol=1e-6)
+    g = grad.cpu().numpy()
+    assert np.abs(g - ref_grad).max() <= 1e-3 * np.abs(ref_grad).max()
+
+
+def _golden_adc_gpu(cuda, tr, prune, dens, clone):
+    n = 8
+    k = torch.arange(1, n + 1, dtype=torch.float32, device=cuda)
+    mo = k[:, None].repeat(1, 4).contiguous()
+    mo[:, 3] = torch.from_numpy(np.where(prune == 1, -10.0, 5.0).astype(np.float32)).to(cuda)
+    sf = torch.from_numpy(np.where(clone[:, None] == 1, -6.0, 0.0).repeat(3, 1).astype(np.float32)).to(cuda)
+    g = gs3d.GaussiansVector(mo, sf, k[:, None].repeat(1, 4).contiguous(),
+                             k[:, None, None].repeat(1, 3, 4).contiguous())
+    a = adc_mod.AdcBuffers.create(n, cuda)
+    a.accumulated_mean2d_grad_norms_ndc.copy_(torch.from_numpy((dens == 1).astype(np.float32)))
+    a.rendering_contribution_counts.fill_(1)
+    return g, a
+
+
+def test_adc_plan_apply_golden(cuda, golden):
+    tr = golden["training"]
+    prune = np.array(tr["should_prune"], np.uint8)
+    dens = np.array(tr["should_densify"], np.uint8)
+    clone = np.array(tr["should_clone"], np.uint8)
+    g, a = _golden_adc_gpu(cuda, tr, prune, dens, clone)
+    new_n = adc_mod.densify_prune_plan(a, g, 0.0002, 0.01, 0.005, 1e6, False)
+    assert new_n == 10
+    assert a.should_prune.cpu().numpy().tolist() == prune.tolist()
+    assert a.should_densify.cpu().numpy().tolist() == dens.tolist()
+    assert a.should_clone.cpu().numpy().tolist() == clone.tolist()
+    assert a.ngidx_to_gidx[:10].cpu().numpy().tolist() == [int(x) for x in tr["ngidx_to_gidx"]]
+    # the reference's apply test uses plain k-valued features; reuse its values here
+    k = torch.arange(1, 9, dtype=torch.float32, device=cuda)
+    g2 = gs3d.GaussiansVector(k[:, None].repeat(1, 4).contiguous(), k[:, None].repeat(1, 3).contiguous(),
+                              k[:, None].repeat(1, 4).contiguous(), k[:, None, None].repeat(1, 3, 4).contiguous())
+    m = AdamMoments.zeros(8, 1, cuda)
+    for t in m.tensors():
+        t.copy_(k.view(-1, *([1] * (t.dim() - 1))).expand_as(t))
+    f2g = torch.tensor([int(x) for x in tr["original_fgidx_to_gidx"]], dtype=torch.int32, device=cuda)
+    counts = torch.tensor([3, 0, 0, 0], dtype=torch.int32, device=cuda)
+    ng, nm = adc_mod.densify_apply(a, g2, m, 10, float(np.exp(np.float32(10.0))), 7, f2g, counts)
+    torch.cuda.synchronize()
+    assert f2g.cpu().numpy().tolist() == [int(x) for x in tr["adjusted_fgidx_to_gidx"]]
+    ids = [int(x) - 1 for x in tr["means_after_adc_ids"]]
+    assert np.array_equal(ng.means_opacity_features[ids, :3].cpu().numpy(),
+                          np.repeat(np.array(tr["means_after_adc"], np.float32)[:, None], 3, 1))
+    np.testing.assert_allclose(ng.scaling_features.cpu().numpy(),
+                               np.repeat(np.array(tr["scaling_after_adc"], np.float32)[:, None], 3, 1), rtol=1e-6)
+    want = np.array(tr["moments_after_adc"], np.float32)
+    for t in nm.tensors():
+        arr = t.cpu().numpy().reshape(10, -1)
+        assert np.array_equal(arr, np.repeat(want[:, None], arr.shape[1], 1))
+    # bit-exact against the oracle, split means included
+    go = O.NpGaussians.from_vector(g2)
+    mo_ = O.NpMoments.from_moments(m)
+    plan = dict(prune=prune, densify=dens, clone=clone,
+                counts_cs=np.cumsum((1 - prune) + dens).astype(np.int32), new_n=10)
+    ong, onm, of2g = O.adc_apply(go, mo_, plan, np.array(tr["original_fgidx_to_gidx"], np.int32),
+                                 float(np.log(np.float32(np.exp(np.float32(10.0))))), 7)
+    for a_, b_ in zip([t.cpu().numpy() for t in ng.tensors()], (ong.mo, ong.sf, ong.rf, ong.sh)):
+        assert np.array_equal(a_.view(np.uint32), b_.view(np.uint32))
+
+
+def test_adc_random_vs_oracle(cuda):
+    n = 50_000
+    gv = synthetic_gaussians(SceneSpec(n, "uniform:1", -4.0, 1.0), 3)
+    g = gv.to(cuda)
+    rng = np.random.default_rng(4)
+    a = adc_mod.AdcBuffers.create(n, cuda)
+    acc = rng.exponential(2e-4, n).astype(np.float32)
+    cnt = rng.integers(0, 4, n).astype(np.int32)
+    a.accumulated_mean2d_grad_norms_ndc.copy_(torch.from_numpy(acc))
+    a.rendering_contribution_counts.copy_(torch.from_numpy(cnt))
+    R = 3.3
+    new_n = adc_mod.densify_prune_plan(a, g, 0.0002, 0.01 * R, 0.005, 0.1 * R, True)
+    p = _abi.AdcParamsC()
+    p.densification_mean2d_grad_norm_threshold_ndc = 0.0002
+    p.densification_size_threshold = float(np.float32(0.01 * R))
+    p.pruning_min_opacity = 0.005
+    p.pruning_3d_max_scale = float(np.float32(0.1 * R))
+    p.use_max_scale_pruning = 1
+    go = O.NpGaussians.from_vector(gv)
+    plan = O.adc_plan(go, acc, cnt, p)
+    assert new_n == plan["new_n"]
+    for k, t in (("prune", a.should_prune), ("densify", a.should_densify), ("clone", a.should_clone),
+                 ("counts_cs", a.new_gaussian_counts_cs)):
+        assert np.array_equal(t.cpu().numpy(), plan[k]), k
+    assert np.array_equal(a.ngidx_to_gidx[:new_n].cpu().numpy(), plan["ngidx_to_gidx"])
+    m = AdamMoments.zeros(n, 3, cuda)
+    for t in m.tensors():
+        t.copy_(torch.from_numpy(rng.normal(0, 1, tuple(t.shape)).astype(np.float32)))
+    f2g_np = np.sort(rng.choice(n, 20_000, replace=False) + 1).astype(np.int32)
+    f2g = torch.from_numpy(f2g_np).to(cuda)
+    counts = torch.tensor([f2g_np.size, 0, 0, 0], dtype=torch.int32, device=cuda)
+    split = 1 / 1.6
+    ng, nm = adc_mod.densify_apply(a, g, m, new_n, split, 99, f2g, counts)
+    torch.cuda.synchronize()
+    ong, onm, of2g = O.adc_apply(go, O.NpMoments.from_moments(m), plan, f2g_np,
+                                 float(np.log(np.float32(split))), 99)
+    for x, y in zip([t.cpu().numpy() for t in ng.tensors()], (ong.mo, ong.sf, ong.rf, ong.sh)):
+        assert np.array_equal(x.view(np.uint32), y.view(np.uint32))
+    for x, y in zip([t.cpu().numpy() for t in nm.tensors()], (onm.mm, onm.om, onm.sm, onm.rm, onm.shm)):
+        assert np.array_equal(x, y)
+    assert np.array_equal(f2g.cpu().numpy(), of2g)
+
+
+def test_opacity_reset_vs_oracle(cuda):
+    gv = synthetic_gaussians(SceneSpec(10_000, "uniform:1", -4.0, 1.0, 0.0, 3.0), 5)
+    g = gv.to(cuda)
+    m = AdamMoments.zeros(g.n, 3, cuda)
+    m.opacity_features_moments.fill_(3.0)
+    adc_mod.opacity_reset(g, m, 0.01)
+    go = O.NpGaussians.from_vector(gv)
+    om = O.NpMoments.from_moments(AdamMoments.zeros(g.n, 3, "cpu"))
+    O.opacity_reset(go, om, 0.01)
+    assert np.array_equal(g.means_opacity_features.cpu().numpy(), go.mo)
+    assert torch.all(m.opacity_features_moments == 0)
+
+
+def _cfg0_trainer(cuda, nviews=1, seed=0):
+    gv = synthetic_gaussians(SceneSpec(16_384, "uniform:1", -4.0, 0.5), seed)
+    cams = [look_at_camera(256, 256, 60.0, (0, 0, 3))] * nviews
+    targets = [target_image(256, 256, 100 + i, cuda) for i in range(nviews)]
+    opts = TrainingOptions(scene_radius=3.3)
+    ro = RenderOptions.for_camera(cams[0], 3)
+    t = Trainer(gv.to(cuda), cams, targets, ro, Tiling.for_camera(cams[0]), opts)
+    return gv, cams, targets, ro, t
+
+
+def test_training_step_matches_oracle_chain(cuda):
+    gv, cams, targets, ro, t = _cfg0_trainer(cuda)
+    t.iteration_nb = 2000  # past the SH-degree increases, before any densify step
+    t.training_step()
+    torch.cuda.synchronize()
+    # oracle chain: render -> loss -> backward -> ADC stats -> Adam
+    g = O.NpGaussians.from_vector(gv)
+    til = Tiling.for_camera(cams[0])
+    f = O.render(g, cams[0], til, ro)
+    (loss, _, _), grad = O.loss(f["rgb"], targets[0].cpu().numpy(), 0.2)
+    b = O.backward(g, cams[0], til, ro, f, grad)
+    assert abs(float(t.last_loss[0]) - loss) <= 1e-5 * abs(loss)
+    p = t.optimizer.params_c(3)
+    p.update_count = 0
+    bc1, bc2 = bias_corrections(t.optimizer.beta1, t.optimizer.beta2, 0)
+    m = O.NpMoments.from_moments(AdamMoments.zeros(g.n, 3, "cpu"))
+    O.adam(g, m, b, f["fgidx_to_gidx"], p, bc1, bc2)
+    got = O.NpGaussians.from_vector(t.gaussians)
+    # first Adam step moves every touched parameter by ~lr * sign(grad): compare to that scale
+    for x, y, lr in ((got.mo[:, :3], g.mo[:, :3], p.lr_means), (got.mo[:, 3], g.mo[:, 3], p.lr_opacity_features),
+                     (got.sf, g.sf, p.lr_scaling_features), (got.rf, g.rf, p.lr_rotation_features),
+                     (got.sh[:, :, 1:], g.sh[:, :, 1:], p.lr_sh_rest)):
+        d = np.abs(x - y)
+        assert d.max() <= 2.01 * lr
+        assert np.mean(d <= 1e-6 + 1e-3 * lr) >= 0.999
+
+
+def test_trainer_loss_decreases(cuda):
+    _, _, _, _, t = _cfg0_trainer(cuda, nviews=1, seed=1)
+    t.iteration_nb = 3000
+    losses = []
+    for _ in range(40):
+        losses.append(float(t.training_step()[0]))
+    assert losses[-1] < losses[0]
+    assert t.optimizer.update_count == 40

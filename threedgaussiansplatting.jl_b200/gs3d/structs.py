@@ -272,6 +272,19 @@ class GaussiansVector:
         return (self.means_opacity_features, self.scaling_features, self.rotation_features,
                 self.sh_coeffs)
 
+    def set_sh_degree(self, d: int) -> None:
+        """set_sh_degree! (gaussians.jl): grow or shrink the SH axis; new coefficients are 0."""
+        old = self.sh_coeffs
+        new = torch.zeros((old.shape[0], 3, (d + 1) ** 2), dtype=old.dtype, device=old.device)
+        k = min(old.shape[2], new.shape[2])
+        new[:, :, :k] = old[:, :, :k]
+        self.sh_coeffs = new
+
+    def replace(self, other: "GaussiansVector") -> None:
+        """Take over `other`'s arrays (after densification)."""
+        (self.means_opacity_features, self.scaling_features, self.rotation_features,
+         self.sh_coeffs) = other.tensors()
+
     def to_c(self) -> _abi.GaussiansC:
         g = _abi.GaussiansC()
         g.n, g.sh_degree = self.n, self.sh_degree

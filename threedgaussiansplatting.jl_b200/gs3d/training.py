@@ -1,0 +1,207 @@
+"""Training orchestration of ThreeDGaussianSplatting.jl: TrainingOptions
+(training_structs.jl:43-228), Trainer and training_step! (training.jl:40-244) with the
+SH-degree increase, learning-rate annealing, densify/prune and opacity reset schedule
+(training.jl:253-459). Every compute step is a libgs3d.so call on one CUDA stream; the host
+only orders the calls (and, like the reference, reads n' back at a densify step)."""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from . import adc as adc_mod
+from .backward import FilteredGaussiansGradients, backward
+from .loss import LossComputer
+from .optimizer import AdamOptimizer, LearningRates
+from .render import render
+from .structs import GaussiansVector, PinholeCamera, RenderBuffers, RenderOptions, RenderOutputs, Tiling
+
+F32 = np.float32
+
+
+@dataclass
+class TrainingOptions:
+    """TrainingOptions with the reference defaults; radius-scaled values already scaled."""
+
+    scene_radius: float
+    nb_iterations: int = 30_000
+    loss_dssim_vs_L1_weight: float = 0.2
+    base_initial_means_lr: float = 0.00016
+    base_final_means_lr_rel_factor: float = 1 / 100
+    opacity_features_lr: float = 0.05
+    scaling_features_lr: float = 0.005
+    rotation_features_lr: float = 0.001
+    sh_coeffs_dc_lr: float = 0.0025
+    sh_coeffs_rest_lr_rel_factor: float = 1 / 20
+    nb_lr_annealing_steps: int | None = None
+    sh_degree_increase_interval: int = 1_000
+    opacity_reset_interval: int = 3_000
+    opacity_reset_start_iteration_nb: int = 0
+    opacity_reset_final_iteration_nb: int = 12_000
+    opacity_reset_max_value: float = 0.01
+    adc_interval: int = 100
+    adc_start_iteration_nb: int = 600
+    adc_final_iteration_nb: int = 14_900
+    densification_mean2d_grad_norm_threshold_ndc: float = 0.0002
+    base_densification_size_threshold: float = 0.01
+    splitting_scale_factor: float = 1 / (0.8 * 2)
+    pruning_min_opacity: float = 0.005
+    base_pruning_3d_max_scale: float = 0.1
+
+    def __post_init__(self):
+        if self.nb_lr_annealing_steps is None:
+            self.nb_lr_annealing_steps = self.nb_iterations
+        if not (self.scene_radius > 0):
+            raise ValueError("scene radius must be positive (the reference's _check_positive "
+                             "rejects a zero means learning rate)")
+
+    @property
+    def initial_means_lr(self) -> float:
+        return float(F32(self.base_initial_means_lr * self.scene_radius))
+
+    @property
+    def final_means_lr(self) -> float:
+        return float(F32(self.base_initial_means_lr * self.base_final_means_lr_rel_factor * self.scene_radius))
+
+    @property
+    def sh_coeffs_rest_lr(self) -> float:
+        return float(F32(self.sh_coeffs_dc_lr * self.sh_coeffs_rest_lr_rel_factor))
+
+    @property
+    def densification_size_threshold(self) -> float:
+        return float(F32(self.base_densification_size_threshold * self.scene_radius))
+
+    @property
+    def pruning_3d_max_scale(self) -> float:
+        return float(F32(self.base_pruning_3d_max_scale * self.scene_radius))
+
+    def learning_rates(self) -> LearningRates:
+        return LearningRates(self.initial_means_lr, self.opacity_features_lr, self.scaling_features_lr,
+                             self.rotation_features_lr, self.sh_coeffs_dc_lr, self.sh_coeffs_rest_lr)
+
+
+class Trainer:
+    """Trainer (training.jl:40-151). `targets[i]` is the ground-truth image of camera i as a
+    (w, h, 3) float32 tensor, on the device or in (pinned) host memory; host images are
+    copied to a device buffer at each step."""
+
+    def __init__(self, gaussians: GaussiansVector, cameras: list[PinholeCamera], targets,
+                 render_options: RenderOptions, tiling: Tiling, options: TrainingOptions,
+                 seed: int = 0, capacity_dup: int | None = None, adc_seed: int = 1234):
+        self.gaussians = gaussians
+        self.cameras = cameras
+        self.targets = targets
+        self.render_options = render_options
+        self.tiling = tiling
+        self.options = options
+        dev = gaussians.device
+        self.device = dev
+        cam0 = cameras[0]
+        self.width, self.height = cam0.width, cam0.height
+        self.render_buffers = RenderBuffers.create(gaussians.n, tiling.nb_tiles, dev, capacity_dup=capacity_dup)
+        self.render_outputs = RenderOutputs.create(self.width, self.height, dev)
+        self.rgb_image_grad = torch.empty((self.width, self.height, 3), dtype=torch.float32, device=dev)
+        self.gt_buffer = torch.empty((self.width, self.height, 3), dtype=torch.float32, device=dev)
+        self.loss = LossComputer(self.width, self.height, dev, options.loss_dssim_vs_L1_weight)
+        self.fgradients = FilteredGaussiansGradients.create(gaussians.n, gaussians.sh_degree, dev)
+        self.optimizer = AdamOptimizer(gaussians, options.learning_rates())
+        self.adc_buffers = adc_mod.AdcBuffers.create(gaussians.n, dev)
+        self.iteration_nb = 0
+        self.rng = np.random.default_rng(seed)
+        self.cameras_order = self.rng.permutation(len(cameras))
+        self.cameras_order_idx = -1
+        self.adc_seed = adc_seed
+        self.last_loss = None
+
+    # -- schedule pieces (training.jl:253-302) ---------------------------------------------
+    def current_camera_index(self) -> int:
+        return int(self.cameras_order[self.cameras_order_idx])
+
+    def maybe_increase_sh_degree(self) -> None:
+        if self.iteration_nb % self.options.sh_degree_increase_interval != 0:
+            return
+        d = self.gaussians.sh_degree
+        if d >= 3:
+            return
+        d += 1
+        self.render_options = self.render_options.with_sh_degree(d)
+        self.gaussians.set_sh_degree(d)
+        self.fgradients.set_sh_degree(d)
+        self.optimizer.moments.set_sh_degree(d)
+
+    def maybe_opacity_reset(self) -> None:
+        o = self.options
+        if (o.opacity_reset_start_iteration_nb <= self.iteration_nb <= o.opacity_reset_final_iteration_nb
+                and self.iteration_nb % o.opacity_reset_interval == 0):
+            adc_mod.opacity_reset(self.gaussians, self.optimizer.moments, o.opacity_reset_max_value)
+
+    def update_learning_rates(self) -> None:
+        o = self.options
+        x = F32((self.iteration_nb - 1) / F32(o.nb_lr_annealing_steps - 1)) if o.nb_lr_annealing_steps > 1 else F32(1)
+        x = F32(min(max(x, F32(0)), F32(1)))
+        lr = math.exp((1 - x) * math.log(o.initial_means_lr) + x * math.log(o.final_means_lr))
+        self.optimizer.lrs.means = float(F32(lr))
+
+    def maybe_densify_and_prune(self) -> bool:
+        o = self.options
+        if self.iteration_nb > o.adc_final_iteration_nb:
+            return False
+        rb = self.render_buffers
+        adc_mod.adc_stats(self.adc_buffers, self.fgradients, rb.fgidx_to_gidx, rb.device_counts,
+                          self.width, self.height)
+        if not (self.iteration_nb >= o.adc_start_iteration_nb and self.iteration_nb % o.adc_interval == 0):
+            return False
+        new_n = adc_mod.densify_prune_plan(
+            self.adc_buffers, self.gaussians, o.densification_mean2d_grad_norm_threshold_ndc,
+            o.densification_size_threshold, o.pruning_min_opacity, o.pruning_3d_max_scale,
+            self.iteration_nb > o.opacity_reset_interval)
+        ng, nm = adc_mod.densify_apply(self.adc_buffers, self.gaussians, self.optimizer.moments, new_n,
+                                       o.splitting_scale_factor, self.adc_seed + self.iteration_nb,
+                                       rb.fgidx_to_gidx, rb.device_counts)
+        self.gaussians.replace(ng)
+        self.optimizer.moments = nm
+        self.adc_buffers.set_nb_gaussians(new_n)
+        return True
+
+    def complete_adc_step(self) -> None:
+        n = self.gaussians.n
+        self.fgradients.resize(n)
+        rb = self.render_buffers
+        self.render_buffers = RenderBuffers.create(n, self.tiling.nb_tiles, self.device,
+                                                   capacity_dup=max(rb.capacity_dup, 4 * n))
+
+    # -- one iteration (training.jl:173-244) -----------------------------------------------
+    def target_for(self, idx: int) -> torch.Tensor:
+        t = self.targets[idx]
+        if t.device != self.device:
+            self.gt_buffer.copy_(t, non_blocking=True)
+            return self.gt_buffer
+        return t
+
+    def training_step(self) -> torch.Tensor:
+        """One iteration; returns the device tensor [loss, L1, DSSIM, -] (no host sync)."""
+        self.iteration_nb += 1
+        self.cameras_order_idx += 1
+        if self.cameras_order_idx >= len(self.cameras_order):
+            self.cameras_order = self.rng.permutation(len(self.cameras))
+            self.cameras_order_idx = 0
+        self.maybe_increase_sh_degree()
+        idx = self.current_camera_index()
+        cam = self.cameras[idx]
+        rb = self.render_buffers
+        render(self.render_outputs, self.gaussians, cam, self.tiling, self.render_options, rb)
+        gt = self.target_for(idx)
+        loss = self.loss(self.render_outputs.rgb, gt, self.rgb_image_grad)
+        backward(self.fgradients, self.rgb_image_grad, self.render_outputs, self.gaussians, cam,
+                 self.tiling, self.render_options, rb)
+        in_adc = self.maybe_densify_and_prune()
+        self.update_learning_rates()
+        self.optimizer.update(self.fgradients, rb.fgidx_to_gidx, rb.device_counts,
+                              self.render_options.sh_degree)
+        if in_adc:
+            self.complete_adc_step()
+        self.maybe_opacity_reset()
+        self.last_loss = loss
+        return loss
