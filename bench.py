@@ -1,0 +1,393 @@
+#!/usr/bin/env python3
+"""Benchmark of the 3DGS training hot path (render + L1/DSSIM loss + backward + Adam) on
+BASELINE.json's headline workload: 3M Gaussians at 1920x1080.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl gs3d|reference]
+
+Workload (synthetic, seeded; BASELINE.json config 4 with one view per GPU per step):
+3,000,000 Gaussians, means ~ N(0, 2^2 I), log-scales ~ N(-5.5, 0.6), opacity logits ~ N(1, 1.5),
+SH degree 3 (48 coefficients, DC ~ N(0, 0.3), rest ~ N(0, 0.05)); 256 pinhole cameras at
+1920x1080 (50 deg horizontal FOV) on a Fibonacci hemisphere of radius 5 looking at the
+origin; uniform [0, 1] target images. A step is one training iteration of the reference's
+training_step! (training.jl:173-244) per GPU: render!, loss, backward!, ADC statistics,
+learning-rate annealing and the Adam update, at iterations 3001.. (SH degree 3, between
+densify steps; densification happens once every 100 iterations and is not timed).
+N = 1 uses the reference's sparse Adam; N > 1 is multi-view data parallelism (one view per
+rank, dense gradient rows summed by an NCCL all-reduce, identical Adam on every rank), so the
+per-GPU work is fixed ("weak" scaling). Inputs are larger than L2 (2.1 GB of parameters and
+moments), so no L2 flush is needed between steps.
+
+`--impl reference` times the CPU restatement of the same training step (the reference has no
+runnable implementation here: it is Julia/CUDA.jl and Julia is not installed) on all host
+threads, rank 0 only, a time-bounded number of full steps.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+for _p in (str(REPO / "threedgaussiansplatting.jl_b200"), str(REPO)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "train iters/s and render frames/s, 3M Gaussians @1920x1080, 1/2/4/8 B200"
+UNIT = "train views/s"
+CONFIG_ID = 4
+START_ITERATION = 3000
+POOL = 8  # distinct target images (one per camera index modulo POOL)
+FALLBACK_HBM_GBS = 6650.0
+
+# kernels per profiled stage (for gpu_launches)
+KERNELS_PER_STAGE = {"keep_compact": 3, "project": 1, "dup_scan": 3, "dup_keys": 1, "tiles_end": 1,
+                     "raster": 1, "zero_2d": 1, "bwd_raster": 1, "bwd_project": 1, "loss": 3,
+                     "adc_stats": 1, "scatter_dense": 1, "adam_dense": 1, "adam": 1}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["gs3d", "reference"], default="gs3d")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--ref-budget-s", type=float, default=120.0)
+    return ap.parse_args()
+
+
+def measured_peaks() -> tuple[float, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.idx = device_index
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.idx)], stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.file.flush()
+        self.file.seek(0)
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.file.read().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                maxes.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        os.unlink(self.file.name)
+        return {"sm_mhz": statistics.median(sms) if sms else None,
+                "sm_max_mhz": max(maxes) if maxes else None, "samples": len(sms),
+                "reasons": sorted(reasons)}
+
+
+def build_workload(device, seed_offset=0):
+    import numpy as np
+    import torch
+    from gs3d import RenderOptions, Tiling
+    from gs3d.scene import CONFIGS, scene_radius, synthetic_gaussians
+    cfg = CONFIGS[CONFIG_ID]
+    gv = synthetic_gaussians(cfg["spec"], cfg["seed"])
+    cams = cfg["cameras"]()
+    w, h = cams[0].width, cams[0].height
+    gen = torch.Generator(device="cpu").manual_seed(1000 + seed_offset)
+    pool_host = [torch.rand((w, h, 3), generator=gen, dtype=torch.float32) for _ in range(POOL)]
+    ro = RenderOptions.for_camera(cams[0], 3)
+    til = Tiling.for_camera(cams[0])
+    return gv, cams, pool_host, ro, til, scene_radius(cams)
+
+
+def stage_bytes(stage: str, F: int, D: int, n: int, w: int, h: int, passes: int) -> float | None:
+    """Algorithmic bytes per launch (the per-unit figures of the hot-path analysis)."""
+    return {
+        "project": 300.0 * F,
+        "sort": 24.0 * passes * D,
+        "adam": 1656.0 * F,
+        "adam_dense": 1656.0 * F + 240.0 * n,
+        "bwd_project": 548.0 * F,
+        "keep_compact": 31.0 * n,
+        "dup_keys": 28.0 * F + 12.0 * D,
+        "raster": 40.0 * D + 20.0 * w * h,
+        "bwd_raster": 40.0 * D + 24.0 * w * h + 36.0 * F,
+        "loss": 12.0 * 3 * w * h + 4.0 * 9 * 3 * w * h * 2,
+    }.get(stage)
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    """The CPU restatement of the training step on all host threads (rank 0 only)."""
+    if rank != 0:
+        return
+    import numpy as np
+    from gs3d.optimizer import bias_corrections, LearningRates, AdamOptimizer  # noqa: F401
+    from gs3d import _abi
+    from gs3d.scene import CONFIGS, synthetic_gaussians
+    from gs3d.training import TrainingOptions
+    from gs3d import RenderOptions, Tiling
+    from gs3d.scene import scene_radius
+    from oracle import oracle as O
+    gv, cams, pool_host, ro, til, radius = build_workload("cpu")
+    threads = os.cpu_count() or 1
+    O.lib().oracle_set_threads(threads)
+    g = O.NpGaussians.from_vector(gv)
+    n = g.n
+    m = O.NpMoments(np.zeros((n, 3, 2)), np.zeros((n, 2)), np.zeros((n, 3, 2)), np.zeros((n, 4, 2)),
+                    np.zeros((n, 3, 16, 2)))
+    opts = TrainingOptions(scene_radius=radius)
+    rng = np.random.default_rng(0)
+    perm = rng.permutation(len(cams))
+    steps = 0
+    t0 = time.perf_counter()
+    while True:
+        cam_i = int(perm[steps % len(cams)])
+        cam = cams[cam_i]
+        target = pool_host[cam_i % POOL].numpy()
+        f = O.render(g, cam, til, ro)
+        (_, _, _), grad = O.loss(f["rgb"], target, opts.loss_dssim_vs_L1_weight)
+        b = O.backward(g, cam, til, ro, f, grad)
+        p = _abi.AdamParamsC()
+        lrs = opts.learning_rates()
+        p.lr_means, p.lr_opacity_features, p.lr_scaling_features = lrs.means, lrs.opacity_features, lrs.scaling_features
+        p.lr_rotation_features, p.lr_sh_dc, p.lr_sh_rest = lrs.rotation_features, lrs.sh_coeffs_dc, lrs.sh_coeffs_rest
+        p.beta1, p.beta2, p.epsilon, p.update_count, p.sh_degree = 0.9, 0.999, 1e-15, steps, 3
+        bc1, bc2 = bias_corrections(0.9, 0.999, steps)
+        O.adam(g, m, b, f["fgidx_to_gidx"], p, bc1, bc2)
+        steps += 1
+        el = time.perf_counter() - t0
+        if steps >= args.steps or el >= args.ref_budget_s:
+            break
+    value = steps / el
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps,
+            "warmup": 0, "ms_per_step": 1000 * el / steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": "3M Gaussians (config 4 scene), 1920x1080, 1 view per step, "
+                                   "render+L1/DSSIM+backward+Adam", "global_batch": 1,
+                       "parallelism": "cpu"},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"{steps} full training step(s) of the workload (time-bounded "
+                                       f"{args.ref_budget_s:.0f} s), CPU restatement of the reference's "
+                                       f"GPU-path arithmetic, {threads} threads"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline_leg(gv_cpu, cams, pool_host, ro, til, opts) -> dict:
+    """One full training step of the same workload through the CPU oracle (all host threads)."""
+    import numpy as np
+    from gs3d import _abi
+    from gs3d.optimizer import bias_corrections
+    from oracle import oracle as O
+    threads = os.cpu_count() or 1
+    O.lib().oracle_set_threads(threads)
+    g = O.NpGaussians.from_vector(gv_cpu)
+    n = g.n
+    m = O.NpMoments(np.zeros((n, 3, 2)), np.zeros((n, 2)), np.zeros((n, 3, 2)), np.zeros((n, 4, 2)),
+                    np.zeros((n, 3, 16, 2)))
+    cam = cams[0]
+    t0 = time.perf_counter()
+    f = O.render(g, cam, til, ro)
+    (_, _, _), grad = O.loss(f["rgb"], pool_host[0].numpy(), opts.loss_dssim_vs_L1_weight)
+    b = O.backward(g, cam, til, ro, f, grad)
+    p = _abi.AdamParamsC()
+    lrs = opts.learning_rates()
+    p.lr_means, p.lr_opacity_features, p.lr_scaling_features = lrs.means, lrs.opacity_features, lrs.scaling_features
+    p.lr_rotation_features, p.lr_sh_dc, p.lr_sh_rest = lrs.rotation_features, lrs.sh_coeffs_dc, lrs.sh_coeffs_rest
+    p.beta1, p.beta2, p.epsilon, p.update_count, p.sh_degree = 0.9, 0.999, 1e-15, 0, 3
+    bc1, bc2 = bias_corrections(0.9, 0.999, 0)
+    O.adam(g, m, b, f["fgidx_to_gidx"], p, bc1, bc2)
+    el = time.perf_counter() - t0
+    return {"value": 1.0 / el, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"1 full training step (render+loss+backward+Adam) of the same workload, camera 0, "
+                      f"CPU restatement of the reference's GPU-path arithmetic, {threads} threads, {el:.1f} s"}
+
+
+def main() -> None:
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    assert args.warmup >= 3, "at least 3 warm-up steps"
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import datetime
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=device)
+    import gs3d
+    from gs3d import _abi
+    from gs3d.dp import DataParallelTrainer
+    from gs3d.training import Trainer, TrainingOptions
+    gs3d.lib()
+
+    gv_cpu, cams, pool_host, ro, til, radius = build_workload(device)
+    opts = TrainingOptions(scene_radius=radius)
+    if START_ITERATION + args.warmup + 2 * args.steps + 8 >= START_ITERATION + 100:
+        opts.adc_interval = 10 ** 9  # keep densify steps out of every measured window
+    gv = gv_cpu.to(device)
+    pool_dev = [t.to(device) for t in pool_host]
+    targets_dev = [pool_dev[i % POOL] for i in range(len(cams))]
+    pool_pinned = [t.pin_memory() for t in pool_host]
+    targets_host = [pool_pinned[i % POOL] for i in range(len(cams))]
+    TrainerCls = DataParallelTrainer if world > 1 else Trainer
+    trainer = TrainerCls(gv, cams, targets_dev, ro, til, opts, seed=0,
+                         capacity_dup=8 * gv.n)
+    trainer.iteration_nb = START_ITERATION
+    stream = torch.cuda.current_stream()
+
+    for _ in range(args.warmup):
+        trainer.training_step()
+    torch.cuda.synchronize()
+    trainer.render_host_sync = False
+    F, D = (int(x) for x in trainer.render_buffers.device_counts[:2].cpu())
+
+    # ---- device-timed throughput, inputs resident in HBM ------------------------------
+    clocks = ClockSampler(local if "CUDA_VISIBLE_DEVICES" not in os.environ else local)
+    _abi.profile_enable(True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        trainer.training_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    if world > 1:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    prof = _abi.profile_report()
+    _abi.profile_enable(False)
+    status = int(trainer.render_buffers.device_counts[2].item())
+    if status & _abi.GS3D_STATUS_DUP_OVERFLOW:
+        raise RuntimeError("duplicate-key capacity overflow during the timed region")
+    ms_t = torch.tensor([ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    value = world * args.steps / (ms_max / 1000.0)
+
+    # ---- end to end through the public API: pinned host targets in, loss out ----------
+    e2e = None
+    if not args.no_e2e:
+        trainer.targets = targets_host
+        loss_host = torch.empty(4, dtype=torch.float32, pin_memory=True)
+        for _ in range(2):
+            loss_host.copy_(trainer.training_step(), non_blocking=True)
+            stream.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            loss_host.copy_(trainer.training_step(), non_blocking=True)
+            stream.synchronize()
+            float(loss_host[0])
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms2 = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
+        if world > 1:
+            dist.all_reduce(ms2, op=dist.ReduceOp.MAX)
+        w, h = cams[0].width, cams[0].height
+        e2e = {"value": world * args.steps / (float(ms2.item()) / 1000.0), "unit": UNIT,
+               "h2d_bytes_per_step": 3 * w * h * 4 * world, "d2h_bytes_per_step": 16 * world}
+
+    # ---- roofline of the dominant kernel ---------------------------------------------
+    peak, peak_kind = measured_peaks()
+    w, h = cams[0].width, cams[0].height
+    passes = math.ceil(til.highest_key_bit / 8)
+    stages = {}
+    for name, (cnt, tot) in prof.items():
+        avg = tot / max(cnt, 1)
+        b = stage_bytes(name, F, D, gv.n, w, h, passes)
+        stages[name] = {"launches": cnt, "avg_ms": round(avg, 4),
+                        "share": round(tot / max(sum(t for _, t in prof.values()), 1e-9), 4),
+                        "alg_GBps": round(b / (avg / 1000) / 1e9, 1) if b else None}
+    dominant = max(prof.items(), key=lambda kv: kv[1][1])[0]
+    dom = stages[dominant]
+    achieved = dom["alg_GBps"]
+    roofline = {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peak,
+                "peak_source": peak_kind, "unit": "GB/s",
+                "frac": round(achieved / peak, 4) if achieved else None,
+                "traffic": None}
+    gpu_launches = 0
+    for name, (cnt, _) in prof.items():
+        k = KERNELS_PER_STAGE.get(name, 1 + 3 * passes if name == "sort" else 1)
+        gpu_launches += cnt * k
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_leg(gv_cpu, cams, pool_host, ro, til, opts)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "3M Gaussians (BASELINE config 4 scene), 1920x1080, 1 view per GPU "
+                                   "per step: render + L1/DSSIM + backward + ADC stats + Adam",
+                       "global_batch": world, "views_per_gpu": 1, "resolution": [w, h],
+                       "n_gaussians": gv.n, "filtered_F": F, "duplicates_D": D,
+                       "tiles": [til.tile_width, til.tile_height],
+                       "parallelism": f"dp{world}" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (2.1 GB params+moments), no flush"},
+            "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk,
+            "gpu_launches": gpu_launches, "stages": stages,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -246,6 +246,24 @@ GS3D_API int gs3d_adam_step(
     const gs3d_fgradients* fgradients, const int32_t* fgidx_to_gidx,
     const int32_t* device_counts, const gs3d_adam_params* params, gs3d_stream_t stream);
 
+/* ---- multi-view data parallelism (no counterpart in the reference: it trains one view at a
+ * time on one GPU, training.jl:173-244). A dense gradient row of 60 floats per Gaussian:
+ * mean(3) opacity feature(1) scaling features(3) rotation features(4) SH (3 x 16,
+ * channel-major) touched(1). Rows from several views/ranks are summed (NCCL all-reduce), then
+ * gs3d_adam_step_dense applies the update! scalar rule to every touched Gaussian; with one view
+ * it equals gs3d_adam_step. */
+#define GS3D_DENSE_ROW 60
+
+/* Zero dense (n rows) and scatter the F-compact gradients of one view into it. */
+GS3D_API int gs3d_scatter_dense_grads(
+    const gs3d_fgradients* fgradients, const int32_t* fgidx_to_gidx,
+    const int32_t* device_counts, int32_t sh_degree, float* dense, int32_t n,
+    gs3d_stream_t stream);
+
+GS3D_API int gs3d_adam_step_dense(
+    const gs3d_gaussians* gaussians, const gs3d_adam_moments* moments, const float* dense,
+    const gs3d_adam_params* params, gs3d_stream_t stream);
+
 /* ---- loss: training.jl:196-217 (L1 + weight * DSSIM, with gradient) ----------------- */
 
 GS3D_API int gs3d_loss_workspace_size(int32_t width, int32_t height, size_t* bytes);
@@ -283,6 +301,13 @@ GS3D_API int gs3d_densify_apply(
     const int32_t* device_counts, float log_splitting_scale_factor, uint64_t seed,
     gs3d_stream_t stream);
 
+/* Dense-row counterpart of the fgidx_to_gidx retarget for multi-view data parallelism:
+ * dense_new (n' rows, GS3D_DENSE_ROW floats) gets the row of the original for the carried
+ * Gaussian and the first clone, zero rows otherwise. Run after gs3d_densify_prune_plan. */
+GS3D_API int gs3d_densify_remap_dense(
+    const gs3d_adc_buffers* adc, int32_t n_old, const float* dense_old, float* dense_new,
+    gs3d_stream_t stream);
+
 /* reset_opacities! (gaussians.jl:1093-1101) + zero_opacity_features_adam_moments!
  * (optimizer.jl:754-756). */
 GS3D_API int gs3d_opacity_reset(
@@ -292,6 +317,15 @@ GS3D_API int gs3d_opacity_reset(
 /* ---- misc ---------------------------------------------------------------------------- */
 GS3D_API const char* gs3d_last_error_string(void);
 GS3D_API int gs3d_version(void);
+
+/* Stage timers (no counterpart in the reference beyond its GUI render timer, gui.jl:358-373):
+ * when enabled, every entry point records CUDA events on its stream around each stage
+ * (keep_compact, project, dup_scan, dup_keys, sort, tiles_end, raster, zero_2d, bwd_raster,
+ * bwd_project, adam, loss, adc_stats). Enabling (or disabling) clears earlier records.
+ * gs3d_profile_report waits for the recorded events and writes "stage launches total_ms"
+ * lines. Host-thread unsafe; for measurement runs. */
+GS3D_API int gs3d_profile_enable(int enable);
+GS3D_API int gs3d_profile_report(char* buf, size_t len);
 
 #ifdef __cplusplus
 }

@@ -129,8 +129,8 @@ int oracle_backward(const gs3d_gaussians* gp, const gs3d_camera* camp, const gs3
     // B1 + B2 with double accumulators
     std::vector<double> acc((size_t)F * 9, 0.0);  // mean2d(2) opacity(1) licov(3) color(3)
     const int TW = til.tile_width, TH = til.tile_height;
-    for (int tyi = 1; tyi <= til.nb_tiles_y; ++tyi)
-        for (int txi = 1; txi <= til.nb_tiles_x; ++txi) {
+    parallel_for(0, (int64_t)til.nb_tiles_x * til.nb_tiles_y, [&](int64_t tl) {
+            const int txi = (int)(tl % til.nb_tiles_x) + 1, tyi = (int)(tl / til.nb_tiles_x) + 1;
             const int tile = txi + (tyi - 1) * til.nb_tiles_x;
             const int first = tile == 1 ? 1 : tiles_end[tile - 2] + 1;
             const int u0 = (txi - 1) * TW, v0 = (tyi - 1) * TH;
@@ -171,12 +171,13 @@ int oracle_backward(const gs3d_gaussians* gp, const gs3d_camera* camp, const gs3
                         const float m1 = aga * (du * ic21 + dv * ic22);
                         const float ta = T * alpha;
                         double* a = &acc[9 * (size_t)fg];
-                        a[0] += m0; a[1] += m1; a[2] += opg;
-                        a[3] += g11; a[4] += g21 + g21; a[5] += g22;
-                        a[6] += ta * gr[0]; a[7] += ta * gr[1]; a[8] += ta * gr[2];
+                        atomic_add(&a[0], m0); atomic_add(&a[1], m1); atomic_add(&a[2], opg);
+                        atomic_add(&a[3], g11); atomic_add(&a[4], g21 + g21); atomic_add(&a[5], g22);
+                        atomic_add(&a[6], ta * gr[0]); atomic_add(&a[7], ta * gr[1]);
+                        atomic_add(&a[8], ta * gr[2]);
                     }
                 }
-        }
+        });
     for (int f = 0; f < F; ++f) {
         const double* a = &acc[9 * (size_t)f];
         mean2d_g[2 * f] = (float)a[0]; mean2d_g[2 * f + 1] = (float)a[1];
@@ -193,7 +194,8 @@ int oracle_backward(const gs3d_gaussians* gp, const gs3d_camera* camp, const gs3
     const int MAXO = (deg + 1) * (deg + 1);
     const int S_store = (g.sh_degree + 1) * (g.sh_degree + 1);
     const int S_grad = (sh_grad_degree + 1) * (sh_grad_degree + 1);
-    for (int f = 0; f < F; ++f) {
+    parallel_for(0, F, [&](int64_t ff) {
+        const int f = (int)ff;
         const int gi = fgidx_to_gidx[f] - 1;
         const float* r = f2d + 9 * (size_t)f;
         const float* mo = g.means_opacity_features + 4 * (size_t)gi;
@@ -377,7 +379,7 @@ int oracle_backward(const gs3d_gaussians* gp, const gs3d_camera* camp, const gs3
                 for (int k = 1; k <= MAXO; ++k) shg[(k - 1) + l * S_grad] = 0.0f;
             }
         }
-    }
+    });
     return 0;
 }
 

@@ -302,13 +302,12 @@ int oracle_render(const gs3d_gaussians* gp, const gs3d_camera* camp, const gs3d_
     const int nb_tiles = til.nb_tiles_x * til.nb_tiles_y;
 
     // F1 + F2
+    parallel_for(0, n, [&](int64_t i) { keep[i] = keep_one(g, (int)i, cam, opt) ? 1 : 0; });
     int32_t cs = 0;
     for (int i = 0; i < n; ++i) {
-        const bool k = keep_one(g, i, cam, opt);
-        keep[i] = k ? 1 : 0;
-        cs += k ? 1 : 0;
+        cs += keep[i];
         if (keep_cs) keep_cs[i] = cs;
-        if (k) fgidx_to_gidx[cs - 1] = i + 1;
+        if (keep[i]) fgidx_to_gidx[cs - 1] = i + 1;
     }
     const int F = cs;
 
@@ -327,8 +326,7 @@ int oracle_render(const gs3d_gaussians* gp, const gs3d_camera* camp, const gs3d_
     if (F == 0) { render_void(); return 0; }
 
     // F3 + F4
-    int64_t D = 0;
-    for (int f = 0; f < F; ++f) {
+    parallel_for(0, F, [&](int64_t f) {
         const Projected p = project_one(g, fgidx_to_gidx[f] - 1, cam, til, opt);
         depths[f] = p.depth;
         float* r = f2d + 9 * (size_t)f;
@@ -336,7 +334,10 @@ int oracle_render(const gs3d_gaussians* gp, const gs3d_camera* camp, const gs3d_
         r[6] = p.col[0]; r[7] = p.col[1]; r[8] = p.col[2];
         for (int k = 0; k < 4; ++k) ranges[4 * (size_t)f + k] = p.rect[k];
         ntiles[f] = p.count;
-        D += p.count;
+    });
+    int64_t D = 0;
+    for (int f = 0; f < F; ++f) {
+        D += ntiles[f];
         ntiles_cs[f] = (int32_t)D;
     }
     counts[1] = D;
@@ -353,8 +354,8 @@ int oracle_render(const gs3d_gaussians* gp, const gs3d_camera* camp, const gs3d_
     oracle_tiles_end(scodes, D, nb_tiles, tiles_end);
     // F8: tile alpha blend (render_tiles_kernel!)
     const int TW = til.tile_width, TH = til.tile_height;
-    for (int tyi = 1; tyi <= til.nb_tiles_y; ++tyi)
-        for (int txi = 1; txi <= til.nb_tiles_x; ++txi) {
+    parallel_for(0, (int64_t)til.nb_tiles_x * til.nb_tiles_y, [&](int64_t tl) {
+            const int txi = (int)(tl % til.nb_tiles_x) + 1, tyi = (int)(tl / til.nb_tiles_x) + 1;
             const int tile = txi + (tyi - 1) * til.nb_tiles_x;
             const int start = tile == 1 ? 0 : tiles_end[tile - 2];
             const int end = tiles_end[tile - 1];
@@ -397,9 +398,11 @@ int oracle_render(const gs3d_gaussians* gp, const gs3d_camera* camp, const gs3d_
                     if (depth_img) depth_img[px] = dep;
                     if (last) last[px] = lastc;
                 }
-        }
+        });
     return 0;
 }
+
+void oracle_set_threads(int32_t n) { thread_count() = n < 1 ? 1 : n; }
 
 // Exposed for the oracle self-tests.
 float oracle_expf(float x) { return o_expf(x); }

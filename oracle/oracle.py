@@ -68,6 +68,8 @@ def lib():
         _LIB.oracle_logf.argtypes = [C.c_float]
         _LIB.oracle_split_normals.restype = None
         _LIB.oracle_split_normals.argtypes = [C.c_uint64, C.c_uint64, vp]
+        _LIB.oracle_set_threads.restype = None
+        _LIB.oracle_set_threads.argtypes = [C.c_int32]
         _LIB.oracle_compact.restype = C.c_int32
         _LIB.oracle_compact.argtypes = [vp, C.c_int64, vp, vp]
         _LIB.oracle_dup_keys.restype = C.c_int64

@@ -13,12 +13,59 @@
 // Both are accurate to about 1-2 ulp; tests/test_oracle_golden.py checks them against libm.
 // Compile with -ffp-contract=off: every a*b+c below is two roundings unless written fmaf.
 #pragma once
+#include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
 #include <climits>
+#include <thread>
+#include <vector>
 
 namespace oracle {
+
+// Host threads used by the loops whose iterations are independent (per Gaussian, per tile).
+// Results do not depend on the thread count except for the order of the backward pass's
+// double-precision sums.
+inline int& thread_count() { static int n = 1; return n; }
+
+template <class Fn>
+void parallel_for(int64_t begin, int64_t end, Fn fn) {
+    const int nt = thread_count();
+    if (nt <= 1 || end - begin < 64) {
+        for (int64_t i = begin; i < end; ++i) fn(i);
+        return;
+    }
+    std::atomic<int64_t> next(begin);
+    const int64_t chunk = std::max<int64_t>(1, (end - begin) / ((int64_t)nt * 32));
+    auto worker = [&]() {
+        for (;;) {
+            const int64_t s = next.fetch_add(chunk);
+            if (s >= end) break;
+            const int64_t e = std::min(end, s + chunk);
+            for (int64_t i = s; i < e; ++i) fn(i);
+        }
+    };
+    std::vector<std::thread> th;
+    for (int t = 1; t < nt; ++t) th.emplace_back(worker);
+    worker();
+    for (auto& t : th) t.join();
+}
+
+// a += v on a double shared between threads
+inline void atomic_add(double* a, double v) {
+    uint64_t old = __atomic_load_n(reinterpret_cast<uint64_t*>(a), __ATOMIC_RELAXED);
+    for (;;) {
+        double cur;
+        std::memcpy(&cur, &old, 8);
+        const double nv = cur + v;
+        uint64_t nb;
+        std::memcpy(&nb, &nv, 8);
+        if (__atomic_compare_exchange_n(reinterpret_cast<uint64_t*>(a), &old, nb, true,
+                                        __ATOMIC_RELAXED, __ATOMIC_RELAXED))
+            return;
+    }
+}
 
 static inline float bits_to_float(uint32_t u) { float f; std::memcpy(&f, &u, 4); return f; }
 static inline uint32_t float_to_bits(float f) { uint32_t u; std::memcpy(&u, &f, 4); return u; }

@@ -144,6 +144,39 @@ def test_adam_bit_exact(cuda):
     assert adam.update_count == 6
 
 
+def test_dense_adam_equals_sparse_adam(cuda):
+    """One view: scatter + dense Adam (the data-parallel path) == the sparse update! bit for bit."""
+    import ctypes as C
+    from gs3d import _abi
+    spec = SceneSpec(16_384, "uniform:1", -4.0, 0.5)
+    gv = synthetic_gaussians(spec, 0)
+    cam = look_at_camera(256, 256, 60.0, (0, 0, 3))
+    opt = RenderOptions.for_camera(cam, 3)
+    til = Tiling.for_camera(cam)
+    grad = np.random.default_rng(1).normal(0, 1e-4, size=(256, 256, 3)).astype(np.float32)
+    _, (g, out, buf, fg) = run_gpu(gv, cam, til, opt, grad, cuda)
+    F, _ = gs3d.counts(buf)
+    buf.fgidx_to_gidx[: F : 5] = 0
+    g2 = g.clone()
+    a1 = AdamOptimizer(g, LearningRates(means=0.001))
+    a2 = AdamOptimizer(g2, LearningRates(means=0.001))
+    a1.update(fg, buf.fgidx_to_gidx, buf.device_counts, 3)
+    dense = torch.empty((g2.n, 60), dtype=torch.float32, device=cuda)
+    lib = _abi.lib()
+    fc = fg.to_c()
+    _abi.check(lib.gs3d_scatter_dense_grads(C.byref(fc), C.c_void_p(buf.fgidx_to_gidx.data_ptr()),
+                                            C.c_void_p(buf.device_counts.data_ptr()), 3,
+                                            C.c_void_p(dense.data_ptr()), g2.n, None))
+    gc, mc, pc = g2.to_c(), a2.moments.to_c(), a2.params_c(3)
+    _abi.check(lib.gs3d_adam_step_dense(C.byref(gc), C.byref(mc), C.c_void_p(dense.data_ptr()),
+                                        C.byref(pc), None))
+    torch.cuda.synchronize()
+    for x, y in zip(g.tensors(), g2.tensors()):
+        assert torch.equal(x, y)
+    for x, y in zip(a1.moments.tensors(), a2.moments.tensors()):
+        assert torch.equal(x, y)
+
+
 def test_adam_reference_golden(cuda, golden):
     """test/training.jl:181-257: beta1 = beta2 = 0.5, eps = 0, lr 1 (SH rest 10), t = 1,
     parameters and moments of Gaussian k equal to k, gradients of filtered index k equal to k."""

@@ -2,6 +2,7 @@
 // native component, deps/cub_sort_pairs/cub_sort_pairs_wrapper.cu (sort_pairs and
 // determine_sort_pairs_temp_storage, same signatures, bound by forward_core.jl:629-659).
 #include <cstdarg>
+#include <vector>
 
 #include "common.cuh"
 #include "internal.h"
@@ -34,6 +35,45 @@ int invalid(const char* fmt, ...) {
     return GS3D_ERR_INVALID_ARGUMENT;
 }
 
+namespace {
+struct ProfRecord {
+    const char* stage;
+    cudaEvent_t start, stop;
+    bool closed;
+};
+bool g_prof_enabled = false;
+std::vector<ProfRecord> g_prof;
+std::vector<cudaEvent_t> g_event_pool;
+
+cudaEvent_t pool_event() {
+    if (!g_event_pool.empty()) {
+        cudaEvent_t e = g_event_pool.back();
+        g_event_pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+}
+}  // namespace
+
+void prof_begin(const char* stage, cudaStream_t stream) {
+    if (!g_prof_enabled) return;
+    ProfRecord r{stage, pool_event(), pool_event(), false};
+    cudaEventRecord(r.start, stream);
+    g_prof.push_back(r);
+}
+
+void prof_end(const char* stage, cudaStream_t stream) {
+    if (!g_prof_enabled) return;
+    for (auto it = g_prof.rbegin(); it != g_prof.rend(); ++it)
+        if (!it->closed && std::strcmp(it->stage, stage) == 0) {
+            cudaEventRecord(it->stop, stream);
+            it->closed = true;
+            return;
+        }
+}
+
 int device_sm_count() {
     int dev = 0, sms = kSMs;
     if (cudaGetDevice(&dev) == cudaSuccess)
@@ -50,6 +90,40 @@ extern "C" {
 GS3D_API const char* gs3d_last_error_string(void) { return g_error; }
 
 GS3D_API int gs3d_version(void) { return 1; }
+
+GS3D_API int gs3d_profile_enable(int enable) {
+    for (auto& r : g_prof) {
+        g_event_pool.push_back(r.start);
+        g_event_pool.push_back(r.stop);
+    }
+    g_prof.clear();
+    g_prof_enabled = enable != 0;
+    return GS3D_OK;
+}
+
+GS3D_API int gs3d_profile_report(char* buf, size_t len) {
+    if (!buf || len == 0) return invalid("NULL report buffer");
+    struct Acc { const char* stage; int n; double ms; };
+    std::vector<Acc> acc;
+    for (auto& r : g_prof) {
+        if (!r.closed) continue;
+        GS3D_CUDA(cudaEventSynchronize(r.stop), "profile event");
+        float ms = 0.0f;
+        GS3D_CUDA(cudaEventElapsedTime(&ms, r.start, r.stop), "profile elapsed");
+        auto it = std::find_if(acc.begin(), acc.end(),
+                               [&](const Acc& a) { return std::strcmp(a.stage, r.stage) == 0; });
+        if (it == acc.end()) acc.push_back({r.stage, 1, ms});
+        else { it->n += 1; it->ms += ms; }
+    }
+    size_t off = 0;
+    buf[0] = 0;
+    for (auto& a : acc) {
+        const int w = snprintf(buf + off, len - off, "%s %d %.6f\n", a.stage, a.n, a.ms);
+        if (w < 0 || (size_t)w >= len - off) break;
+        off += (size_t)w;
+    }
+    return GS3D_OK;
+}
 
 GS3D_API size_t determine_sort_pairs_temp_storage(const int64_t* keys_in, int64_t* keys_out,
                                                   const int32_t* values_in, int32_t* values_out,

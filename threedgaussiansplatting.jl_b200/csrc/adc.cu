@@ -245,6 +245,33 @@ __global__ void __launch_bounds__(128) k_adc_apply(const ApplyArgs a) {
     }
 }
 
+// Dense gradient rows after a densify step: the carried Gaussian and the first clone keep the
+// row of their original, every other new row is zero (untouched) — the dense counterpart of
+// adjust_fgidx_to_gidx_adc_kernel! (training.jl:514-541).
+__global__ void __launch_bounds__(256) k_remap_dense(const uint8_t* __restrict__ prune,
+                                                     const uint8_t* __restrict__ densify,
+                                                     const uint8_t* __restrict__ clone,
+                                                     const int32_t* __restrict__ counts_cs, int n,
+                                                     const float* __restrict__ dense_old,
+                                                     float* __restrict__ dense_new, int row) {
+    const int64_t total = (int64_t)n * row;
+    for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < total;
+         it += (int64_t)gridDim.x * blockDim.x) {
+        const int i = (int)(it / row);
+        const int c = (int)(it - (int64_t)i * row);
+        if (prune[i]) continue;
+        const int64_t last = (int64_t)counts_cs[i] - 1;
+        const float v = dense_old[it];
+        if (densify[i]) {
+            const int64_t first = last - 1;
+            dense_new[last * row + c] = 0.0f;
+            dense_new[first * row + c] = clone[i] ? v : 0.0f;
+        } else {
+            dense_new[last * row + c] = v;
+        }
+    }
+}
+
 __global__ void __launch_bounds__(256) k_opacity_reset(float* __restrict__ mo, float* __restrict__ om,
                                                        int n, float thr) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
@@ -275,6 +302,7 @@ GS3D_API int gs3d_adc_stats(const gs3d_adc_buffers* adc, const gs3d_fgradients* 
     if (!adc->accumulated_mean2d_grad_norms_ndc || !adc->rendering_contribution_counts)
         return invalid("NULL ADC statistics arrays");
     const double sqw4 = (double)width * width / 4.0, sqh4 = (double)height * height / 4.0;
+    ProfScope prof("adc_stats", reinterpret_cast<cudaStream_t>(stream_));
     k_adc_stats<<<kSMs * 8, 256, 0, reinterpret_cast<cudaStream_t>(stream_)>>>(
         adc->accumulated_mean2d_grad_norms_ndc, adc->rendering_contribution_counts,
         fg->mean2d_grads, fgidx_to_gidx, device_counts, sqw4, sqh4);
@@ -357,6 +385,18 @@ GS3D_API int gs3d_densify_apply(const gs3d_adc_buffers* adc, const gs3d_gaussian
     k_adc_apply<<<blocks_for(std::max(og->n, 1), 128, 16), 128, 0,
                   reinterpret_cast<cudaStream_t>(stream_)>>>(a);
     GS3D_LAUNCHED("k_adc_apply");
+    return GS3D_OK;
+}
+
+GS3D_API int gs3d_densify_remap_dense(const gs3d_adc_buffers* adc, int32_t n_old,
+                                      const float* dense_old, float* dense_new,
+                                      gs3d_stream_t stream_) {
+    if (!adc || !dense_old || !dense_new || n_old < 0) return invalid("NULL argument");
+    if (n_old == 0) return GS3D_OK;
+    k_remap_dense<<<kSMs * 8, 256, 0, reinterpret_cast<cudaStream_t>(stream_)>>>(
+        adc->should_prune, adc->should_densify, adc->should_clone, adc->new_gaussian_counts_cs,
+        n_old, dense_old, dense_new, GS3D_DENSE_ROW);
+    GS3D_LAUNCHED("k_remap_dense");
     return GS3D_OK;
 }
 

@@ -556,9 +556,13 @@ extern "C" GS3D_API int gs3d_backward(const gs3d_fgradients* fg, const float* rg
     if (fg->sh_degree < opt->sh_degree || fg->sh_degree > 3)
         return invalid("gradient SH degree %d < render degree %d", fg->sh_degree, opt->sh_degree);
     const int64_t cap_n = buf->capacity_n > 0 ? buf->capacity_n : 1;
-    k_zero_2d<<<grid_for(3 * cap_n, 256, 8), 256, 0, stream>>>(
-        buf->device_counts, fg->mean2d_grads, fg->opacity_grads, fg->licov2d_grads, fg->color_grads);
-    GS3D_LAUNCHED("k_zero_2d");
+    {
+        ProfScope prof("zero_2d", stream);
+        k_zero_2d<<<grid_for(3 * cap_n, 256, 8), 256, 0, stream>>>(
+            buf->device_counts, fg->mean2d_grads, fg->opacity_grads, fg->licov2d_grads,
+            fg->color_grads);
+        GS3D_LAUNCHED("k_zero_2d");
+    }
 
     BwdArgs a;
     a.sfgidx = buf->sdfgidx_to_fgidx;
@@ -586,8 +590,11 @@ extern "C" GS3D_API int gs3d_backward(const gs3d_fgradients* fg, const float* rg
     a.log_min_alpha = opt->min_alpha > 0.0f ? gs_logf(opt->min_alpha) : -INFINITY;
     const int nthr = til->tile_width * til->tile_height;
     const size_t smem = (size_t)nthr * (2 * sizeof(float4) + sizeof(float2) + sizeof(int));
-    k_bwd_raster<<<dim3(til->nb_tiles_x, til->nb_tiles_y), nthr, smem, stream>>>(a);
-    GS3D_LAUNCHED("k_bwd_raster");
+    {
+        ProfScope prof("bwd_raster", stream);
+        k_bwd_raster<<<dim3(til->nb_tiles_x, til->nb_tiles_y), nthr, smem, stream>>>(a);
+        GS3D_LAUNCHED("k_bwd_raster");
+    }
 
     BProjArgs p;
     p.mo4 = reinterpret_cast<const float4*>(g->means_opacity_features);
@@ -610,6 +617,7 @@ extern "C" GS3D_API int gs3d_backward(const gs3d_fgradients* fg, const float* rg
     p.sh_grad_stride = (fg->sh_degree + 1) * (fg->sh_degree + 1);
     p.fix_sh16 = (flags & GS3D_BACKWARD_FIX_SH16) ? 1 : 0;
     const int grid = grid_for(cap_n, 128, 16);
+    ProfScope prof("bwd_project", stream);
     switch (opt->sh_degree) {
         case 0: k_bwd_project<0><<<grid, 128, 0, stream>>>(p, *cam, *opt); break;
         case 1: k_bwd_project<1><<<grid, 128, 0, stream>>>(p, *cam, *opt); break;

@@ -432,6 +432,7 @@ GS3D_API int gs3d_render_forward(const gs3d_render_outputs* outputs, const gs3d_
     GS3D_CUDA(cudaMemsetAsync(counts, 0, 4 * sizeof(int32_t), stream), "memset counts");
     // F1 + F2
     if (n > 0) {
+        ProfScope prof("keep_compact", stream);
         const unsigned nch = (unsigned)ceil_div(n, kChunk);
         k_keep_upsweep<<<nch, kChunkThreads, 0, stream>>>(
             reinterpret_cast<const float4*>(g->means_opacity_features), n, *cam, *opt,
@@ -457,22 +458,31 @@ GS3D_API int gs3d_render_forward(const gs3d_render_outputs* outputs, const gs3d_
     pa.ranges = buf->intersected_tile_ranges;
     pa.ntiles = buf->nb_overlapped_tiles;
     const int pgrid = grid_for(n, 256, 8);
-    switch (opt->sh_degree) {
-        case 0: k_project<0><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
-        case 1: k_project<1><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
-        case 2: k_project<2><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
-        default: k_project<3><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
+    {
+        ProfScope prof("project", stream);
+        switch (opt->sh_degree) {
+            case 0: k_project<0><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
+            case 1: k_project<1><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
+            case 2: k_project<2><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
+            default: k_project<3><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
+        }
+        GS3D_LAUNCHED("k_project");
     }
-    GS3D_LAUNCHED("k_project");
     // F4
-    GS3D_RETURN_IF(inclusive_scan_i32(buf->nb_overlapped_tiles, buf->nb_overlapped_tiles_cs, cap_n,
-                                      counts + 0, 0, counts + 1, sums, stream));
+    {
+        ProfScope prof("dup_scan", stream);
+        GS3D_RETURN_IF(inclusive_scan_i32(buf->nb_overlapped_tiles, buf->nb_overlapped_tiles_cs,
+                                          cap_n, counts + 0, 0, counts + 1, sums, stream));
+    }
     // F5
-    k_dup_keys<<<grid_for(n, 256, 8), 256, 0, stream>>>(
-        counts, buf->nb_overlapped_tiles, buf->nb_overlapped_tiles_cs,
-        reinterpret_cast<const int4*>(buf->intersected_tile_ranges), buf->depths, til->nb_tiles_x,
-        buf->capacity_dup, buf->df2dgs_codes, buf->dfgidx_to_fgidx, counts + 2);
-    GS3D_LAUNCHED("k_dup_keys");
+    {
+        ProfScope prof("dup_keys", stream);
+        k_dup_keys<<<grid_for(n, 256, 8), 256, 0, stream>>>(
+            counts, buf->nb_overlapped_tiles, buf->nb_overlapped_tiles_cs,
+            reinterpret_cast<const int4*>(buf->intersected_tile_ranges), buf->depths,
+            til->nb_tiles_x, buf->capacity_dup, buf->df2dgs_codes, buf->dfgidx_to_fgidx, counts + 2);
+        GS3D_LAUNCHED("k_dup_keys");
+    }
     if (!(flags & GS3D_RENDER_NO_HOST_SYNC)) {
         int32_t local[4];
         int32_t* dst = host_counts ? host_counts : local;
@@ -487,16 +497,25 @@ GS3D_API int gs3d_render_forward(const gs3d_render_outputs* outputs, const gs3d_
     // F6
     int highest = 33;
     for (int t = nb_tiles; t > 1; t >>= 1) ++highest;  // 33 + floor(log2(nb_tiles))
-    GS3D_RETURN_IF(radix_sort_pairs(ws + L.sort, L.total - L.sort, buf->df2dgs_codes,
-                                    buf->sdf2dgs_codes, buf->dfgidx_to_fgidx,
-                                    buf->sdfgidx_to_fgidx, buf->capacity_dup, counts + 1, 0, highest,
-                                    stream));
+    {
+        ProfScope prof("sort", stream);
+        GS3D_RETURN_IF(radix_sort_pairs(ws + L.sort, L.total - L.sort, buf->df2dgs_codes,
+                                        buf->sdf2dgs_codes, buf->dfgidx_to_fgidx,
+                                        buf->sdfgidx_to_fgidx, buf->capacity_dup, counts + 1, 0,
+                                        highest, stream));
+    }
     // F7
-    k_tiles_end<<<grid_for(buf->capacity_dup, 256, 8), 256, 0, stream>>>(
-        counts, buf->capacity_dup, buf->sdf2dgs_codes, nb_tiles, buf->tiles_end_sdfgidx);
-    GS3D_LAUNCHED("k_tiles_end");
+    {
+        ProfScope prof("tiles_end", stream);
+        k_tiles_end<<<grid_for(buf->capacity_dup, 256, 8), 256, 0, stream>>>(
+            counts, buf->capacity_dup, buf->sdf2dgs_codes, nb_tiles, buf->tiles_end_sdfgidx);
+        GS3D_LAUNCHED("k_tiles_end");
+    }
     // F8 / F9
-    GS3D_RETURN_IF(launch_raster(*outputs, *cam, *til, *opt, *buf, stream));
+    {
+        ProfScope prof("raster", stream);
+        GS3D_RETURN_IF(launch_raster(*outputs, *cam, *til, *opt, *buf, stream));
+    }
     if ((flags & GS3D_RENDER_NO_HOST_SYNC) && host_counts)
         GS3D_CUDA(cudaMemcpyAsync(host_counts, counts, 4 * sizeof(int32_t), cudaMemcpyDeviceToHost,
                                   stream),

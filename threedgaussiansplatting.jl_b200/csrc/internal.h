@@ -31,4 +31,16 @@ int scan_spine(int32_t* sums, int64_t capacity, const int32_t* len_dev, int64_t 
 
 int device_sm_count();
 
+// Opt-in stage timers (gs3d_profile_enable): CUDA events recorded on the launching stream
+// around each stage; no effect when disabled.
+void prof_begin(const char* stage, cudaStream_t stream);
+void prof_end(const char* stage, cudaStream_t stream);
+
+struct ProfScope {
+    const char* stage;
+    cudaStream_t stream;
+    ProfScope(const char* s, cudaStream_t st) : stage(s), stream(st) { prof_begin(s, st); }
+    ~ProfScope() { prof_end(stage, stream); }
+};
+
 }  // namespace gs3d

@@ -255,6 +255,7 @@ GS3D_API int gs3d_loss_l1_dssim(const float* rendered, const float* target, int3
         for (int i = 0; i < 11; ++i) a.win[i] = (float)(g[i] / s);
     }
     const dim3 grid((width + TU - 1) / TU, (height + TV - 1) / TV);
+    ProfScope prof("loss", stream);
     k_ssim_forward<<<grid, LT, 0, stream>>>(a);
     GS3D_LAUNCHED("k_ssim_forward");
     k_ssim_backward<<<grid, LT, 0, stream>>>(a);

@@ -128,6 +128,10 @@ SIGNATURES = {
                                 C.c_uint32, C.c_void_p]),
     "gs3d_adam_step": (C.c_int, [P(GaussiansC), P(AdamMomentsC), P(FGradientsC), C.c_void_p,
                                  C.c_void_p, P(AdamParamsC), C.c_void_p]),
+    "gs3d_scatter_dense_grads": (C.c_int, [P(FGradientsC), C.c_void_p, C.c_void_p, C.c_int32,
+                                           C.c_void_p, C.c_int32, C.c_void_p]),
+    "gs3d_adam_step_dense": (C.c_int, [P(GaussiansC), P(AdamMomentsC), C.c_void_p, P(AdamParamsC),
+                                       C.c_void_p]),
     "gs3d_loss_workspace_size": (C.c_int, [C.c_int32, C.c_int32, P(C.c_size_t)]),
     "gs3d_loss_l1_dssim": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_float,
                                      C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
@@ -140,9 +144,28 @@ SIGNATURES = {
                                      P(GaussiansC), P(AdamMomentsC), C.c_void_p, C.c_void_p,
                                      C.c_float, C.c_uint64, C.c_void_p]),
     "gs3d_opacity_reset": (C.c_int, [P(GaussiansC), P(AdamMomentsC), C.c_float, C.c_void_p]),
+    "gs3d_densify_remap_dense": (C.c_int, [P(AdcBuffersC), C.c_int32, C.c_void_p, C.c_void_p,
+                                           C.c_void_p]),
     "gs3d_last_error_string": (C.c_char_p, []),
     "gs3d_version": (C.c_int, []),
+    "gs3d_profile_enable": (C.c_int, [C.c_int]),
+    "gs3d_profile_report": (C.c_int, [C.c_char_p, C.c_size_t]),
 }
+
+
+def profile_enable(on: bool = True) -> None:
+    check(lib().gs3d_profile_enable(1 if on else 0))
+
+
+def profile_report() -> dict[str, tuple[int, float]]:
+    """{stage: (launches, total_ms)} of the records since profile_enable (waits for them)."""
+    buf = C.create_string_buffer(1 << 16)
+    check(lib().gs3d_profile_report(buf, len(buf)))
+    out = {}
+    for line in buf.value.decode().splitlines():
+        name, n, ms = line.split()
+        out[name] = (int(n), float(ms))
+    return out
 
 _LIB = None
 

@@ -114,6 +114,9 @@ class Trainer:
         self.cameras_order_idx = -1
         self.adc_seed = adc_seed
         self.last_loss = None
+        # False: renders never block; a duplicate-key overflow is flagged in
+        # render_buffers.device_counts[2] instead of growing the buffers
+        self.render_host_sync = True
 
     # -- schedule pieces (training.jl:253-302) ---------------------------------------------
     def current_camera_index(self) -> int:
@@ -191,7 +194,8 @@ class Trainer:
         idx = self.current_camera_index()
         cam = self.cameras[idx]
         rb = self.render_buffers
-        render(self.render_outputs, self.gaussians, cam, self.tiling, self.render_options, rb)
+        render(self.render_outputs, self.gaussians, cam, self.tiling, self.render_options, rb,
+               host_sync=self.render_host_sync)
         gt = self.target_for(idx)
         loss = self.loss(self.render_outputs.rgb, gt, self.rgb_image_grad)
         backward(self.fgradients, self.rgb_image_grad, self.render_outputs, self.gaussians, cam,
