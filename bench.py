@@ -55,12 +55,14 @@ KERNELS_PER_STAGE = {"keep_compact": 3, "project": 1, "dup_scan": 3, "dup_keys":
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["gs3d", "reference"], default="gs3d")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--ref-budget-s", type=float, default=120.0)
+    ap.add_argument("--n-gaussians", type=int, default=None,
+                    help="override the Gaussian count (same distributions); for small profiling cases")
     return ap.parse_args()
 
 
@@ -125,13 +127,15 @@ class ClockSampler:
                 "reasons": sorted(reasons)}
 
 
-def build_workload(device, seed_offset=0):
+def build_workload(device, seed_offset=0, n_override=None):
     import numpy as np
     import torch
     from gs3d import RenderOptions, Tiling
     from gs3d.scene import CONFIGS, scene_radius, synthetic_gaussians
+    import dataclasses
     cfg = CONFIGS[CONFIG_ID]
-    gv = synthetic_gaussians(cfg["spec"], cfg["seed"])
+    spec = cfg["spec"] if not n_override else dataclasses.replace(cfg["spec"], n=int(n_override))
+    gv = synthetic_gaussians(spec, cfg["seed"])
     cams = cfg["cameras"]()
     w, h = cams[0].width, cams[0].height
     gen = torch.Generator(device="cpu").manual_seed(1000 + seed_offset)
@@ -169,7 +173,7 @@ def run_reference(args, rank: int, world: int) -> None:
     from gs3d import RenderOptions, Tiling
     from gs3d.scene import scene_radius
     from oracle import oracle as O
-    gv, cams, pool_host, ro, til, radius = build_workload("cpu")
+    gv, cams, pool_host, ro, til, radius = build_workload("cpu", n_override=args.n_gaussians)
     threads = os.cpu_count() or 1
     O.lib().oracle_set_threads(threads)
     g = O.NpGaussians.from_vector(gv)
@@ -269,7 +273,7 @@ def main() -> None:
     from gs3d.training import Trainer, TrainingOptions
     gs3d.lib()
 
-    gv_cpu, cams, pool_host, ro, til, radius = build_workload(device)
+    gv_cpu, cams, pool_host, ro, til, radius = build_workload(device, n_override=args.n_gaussians)
     opts = TrainingOptions(scene_radius=radius)
     if START_ITERATION + args.warmup + 2 * args.steps + 8 >= START_ITERATION + 100:
         opts.adc_interval = 10 ** 9  # keep densify steps out of every measured window

@@ -1,10 +1,11 @@
 // adam.cu — update!(opt, fgradients, Val(sh)) (optimizer.jl:964-1009) as ONE kernel.
 //
 // The reference launches five kernels (four component groups, then the SH coefficients:
-// optimizer.jl:1084-1127, :1165-1248), each walking the F filtered Gaussians. Here one
-// grid-stride kernel walks (filtered Gaussian, component) pairs, component-fastest, so a warp
-// touches consecutive scalars of one or two Gaussians: the F-compact gradients stream
-// contiguously and the scattered parameter / moment rows are read and written once.
+// optimizer.jl:1084-1127, :1165-1248), each walking the F filtered Gaussians. Here one kernel
+// gives each warp four filtered Gaussians at a time; lane s updates scalar slot s of each (SH
+// coefficients first, then mean, opacity feature, scales, rotation), so all lanes run the same
+// update with no divergence, the SH rows move as consecutive words, and every load of the four
+// Gaussians is in flight before the first update.
 // Per scalar the reference's update (scalar_adam_update, optimizer.jl:941-953):
 //   m1 <- b1 m1 + (1 - b1) g ; m2 <- b2 m2 + (1 - b2) g^2
 //   p  <- p - lr (m1 / (1 - b1^t)) / (sqrt(m2 / (1 - b2^t)) + eps),  t = update_count + 1
@@ -41,48 +42,114 @@ struct AdamArgs {
     int maxo;              // (render degree + 1)^2
     float lr_means, lr_op, lr_scale, lr_rot, lr_dc, lr_rest;
     float b1, b2, eps, bc1, bc2;
+    float rbc1, rbc2;      // RN(1 / bc): the bias-correction divisions as div_by_const
 };
 
 __device__ __forceinline__ void adam_scalar(float* p, float g, float* m, float lr, const AdamArgs& a) {
     const float nm1 = a.b1 * m[0] + (1.0f - a.b1) * g;
     const float nm2 = a.b2 * m[1] + (1.0f - a.b2) * (g * g);
-    const float h1 = nm1 / a.bc1;
-    const float h2 = nm2 / a.bc2;
+    const float h1 = div_by_const(nm1, a.bc1, a.rbc1);
+    const float h2 = div_by_const(nm2, a.bc2, a.rbc2);
     m[0] = nm1;
     m[1] = nm2;
     *p = *p - lr * h1 / (sqrtf(h2) + a.eps);
 }
 
-__global__ void __launch_bounds__(256) k_adam(const AdamArgs a) {
-    const int F = a.counts[0];
-    const int nc = 11 + 3 * a.maxo;
-    const int64_t total = (int64_t)F * nc;
-    for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < total;
-         it += (int64_t)gridDim.x * blockDim.x) {
-        const int f = (int)(it / nc);
-        const int c = (int)(it - (int64_t)f * nc);
-        const int gidx = a.f2g[f];
-        if (gidx <= 0) continue;
-        const size_t gi = (size_t)gidx - 1;
-        if (c < 3) {
-            adam_scalar(a.mo + 4 * gi + c, a.g_mean[3 * (size_t)f + c], a.mm + 6 * gi + 2 * c, a.lr_means, a);
-        } else if (c == 3) {
-            adam_scalar(a.mo + 4 * gi + 3, a.g_op[f], a.om + 2 * gi, a.lr_op, a);
-        } else if (c < 7) {
-            const int k = c - 4;
-            adam_scalar(a.sf + 3 * gi + k, a.g_scale[3 * (size_t)f + k], a.sm + 6 * gi + 2 * k, a.lr_scale, a);
-        } else if (c < 11) {
-            const int k = c - 7;
-            adam_scalar(a.rf + 4 * gi + k, a.g_rot[4 * (size_t)f + k], a.rm + 8 * gi + 2 * k, a.lr_rot, a);
+__device__ __forceinline__ void adam_reg(float& p, float g, float& m1, float& m2, float lr,
+                                         const AdamArgs& a) {
+    const float nm1 = a.b1 * m1 + (1.0f - a.b1) * g;
+    const float nm2 = a.b2 * m2 + (1.0f - a.b2) * (g * g);
+    const float h1 = div_by_const(nm1, a.bc1, a.rbc1);
+    const float h2 = div_by_const(nm2, a.bc2, a.rbc2);
+    m1 = nm1;
+    m2 = nm2;
+    p = p - lr * h1 / (sqrtf(h2) + a.eps);
+}
+
+// Scalar slot s of filtered Gaussian f / Gaussian gi: parameter, first moment (m2 follows),
+// gradient and learning rate (slot order as in k_adam_warp).
+template <int MAXO>
+__device__ __forceinline__ void adam_slot(const AdamArgs& a, int s, int64_t f, size_t gi, float*& p,
+                                          float*& m, const float*& g, float& lr) {
+    constexpr int NSH = 3 * MAXO;
+    if (s < NSH) {
+        const int ch = s / MAXO, i = s - ch * MAXO;
+        p = a.sh + gi * 3 * a.S + (size_t)(ch * a.S + i);
+        g = a.g_sh + (size_t)f * 3 * a.Sg + (size_t)(ch * a.Sg + i);
+        m = a.shm + 2 * (gi * 3 * a.Sm + (size_t)(ch * a.Sm + i));
+        lr = i == 0 ? a.lr_dc : a.lr_rest;
+    } else {
+        const int k = s - NSH;
+        if (k < 3) {
+            p = a.mo + 4 * gi + k; g = a.g_mean + 3 * (size_t)f + k; m = a.mm + 6 * gi + 2 * k; lr = a.lr_means;
+        } else if (k == 3) {
+            p = a.mo + 4 * gi + 3; g = a.g_op + f; m = a.om + 2 * gi; lr = a.lr_op;
+        } else if (k < 7) {
+            const int q = k - 4;
+            p = a.sf + 3 * gi + q; g = a.g_scale + 3 * (size_t)f + q; m = a.sm + 6 * gi + 2 * q; lr = a.lr_scale;
         } else {
-            const int k = c - 11;
-            const int ch = k / a.maxo, i = k - ch * a.maxo;
-            adam_scalar(a.sh + gi * 3 * a.S + (size_t)(ch * a.S + i),
-                        a.g_sh[(size_t)f * 3 * a.Sg + (size_t)(ch * a.Sg + i)],
-                        a.shm + gi * 6 * a.Sm + 2 * (size_t)(ch * a.Sm + i),
-                        i == 0 ? a.lr_dc : a.lr_rest, a);
+            const int q = k - 7;
+            p = a.rf + 4 * gi + q; g = a.g_rot + 4 * (size_t)f + q; m = a.rm + 8 * gi + 2 * q; lr = a.lr_rot;
         }
     }
+}
+
+// Four filtered Gaussians per warp iteration, every load issued before any update so that a
+// warp keeps up to 8 independent parameter / moment / gradient loads per lane in flight.
+template <int MAXO>
+__global__ void __launch_bounds__(256) k_adam_warp4(const AdamArgs a) {
+    constexpr int G = 4;
+    constexpr int NSLOT = 3 * MAXO + 11;
+    constexpr int R = (NSLOT + 31) / 32;
+    const int F = a.counts[0];
+    const int lane = threadIdx.x & 31;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t base = (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * G; base < F;
+         base += nwarps * G) {
+        const int64_t mine = base + (lane & (G - 1));
+        const int gl = (lane < G && mine < F) ? a.f2g[mine] : 0;
+        float* pp[G * R];
+        float* mp[G * R];
+        float pv[G * R], gv[G * R], lr[G * R];
+        float2 mv[G * R];
+        bool on[G * R];
+#pragma unroll
+        for (int k = 0; k < G; ++k) {
+            const int gidx = __shfl_sync(0xffffffffu, gl, k);
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int e = k * R + r;
+                const int s = r * 32 + lane;
+                on[e] = gidx > 0 && s < NSLOT;
+                if (on[e]) {
+                    const float* gp;
+                    adam_slot<MAXO>(a, s, base + k, (size_t)gidx - 1, pp[e], mp[e], gp, lr[e]);
+                    pv[e] = *pp[e];
+                    mv[e] = *reinterpret_cast<const float2*>(mp[e]);
+                    gv[e] = *gp;
+                }
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < G * R; ++e) {
+            if (!on[e]) continue;
+            adam_reg(pv[e], gv[e], mv[e].x, mv[e].y, lr[e], a);
+            *pp[e] = pv[e];
+            *reinterpret_cast<float2*>(mp[e]) = mv[e];
+        }
+    }
+}
+
+int launch_adam_warp(const AdamArgs& a, cudaStream_t stream) {
+    const int blocks = device_sm_count() * 8;
+    switch (a.maxo) {
+        case 1: k_adam_warp4<1><<<blocks, 256, 0, stream>>>(a); break;
+        case 4: k_adam_warp4<4><<<blocks, 256, 0, stream>>>(a); break;
+        case 9: k_adam_warp4<9><<<blocks, 256, 0, stream>>>(a); break;
+        default: k_adam_warp4<16><<<blocks, 256, 0, stream>>>(a); break;
+    }
+    GS3D_LAUNCHED("k_adam_warp4");
+    return GS3D_OK;
 }
 
 // Multi-view data parallelism: the F-compact gradients of one view are scattered into a
@@ -197,6 +264,8 @@ int make_args(const gs3d_gaussians* g, const gs3d_adam_moments* m, const gs3d_fg
     a.b1 = p->beta1; a.b2 = p->beta2; a.eps = p->epsilon;
     a.bc1 = adam_bias_correction(p->beta1, p->update_count);
     a.bc2 = adam_bias_correction(p->beta2, p->update_count);
+    a.rbc1 = 1.0f / a.bc1;
+    a.rbc2 = 1.0f / a.bc2;
     return GS3D_OK;
 }
 
@@ -210,10 +279,8 @@ extern "C" GS3D_API int gs3d_adam_step(const gs3d_gaussians* g, const gs3d_adam_
     if (!g || !m || !fg || !fgidx_to_gidx || !device_counts || !p) return invalid("NULL argument");
     AdamArgs a;
     GS3D_RETURN_IF(make_args(g, m, fg, fgidx_to_gidx, device_counts, p, a));
-    const int blocks = device_sm_count() * 8;
     ProfScope prof("adam", stream);
-    k_adam<<<blocks, 256, 0, stream>>>(a);
-    GS3D_LAUNCHED("k_adam");
+    GS3D_RETURN_IF(launch_adam_warp(a, stream));
     return GS3D_OK;
 }
 

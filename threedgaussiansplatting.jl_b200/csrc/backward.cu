@@ -46,23 +46,56 @@ struct BwdArgs {
     float* opacity_g;
     float* licov_g;
     float* color_g;
-    int32_t width, height, tile_w, tile_h, tiles_x;
+    int32_t width, height, tile_w, tile_h, tiles_x, compact;
     float bg0, bg1, bg2, min_alpha, max_alpha, log_min_alpha;
 };
 
-__device__ __forceinline__ float warp_sum(float v) {
+// Sum 9 per-lane values over the warp by recursive halving: at each of the five xor levels a
+// lane pair exchanges half of its remaining values, 12 shuffles in all. Afterwards the even
+// lanes hold complete sums, lane L the sum of value reduce9_index(L) (or padding).
+__device__ __forceinline__ float reduce9(const float (&v)[9], int lane) {
+    const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4, b1 = lane & 2;
+    float a[5];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
+    for (int k = 0; k < 5; ++k) {
+        const float hi = k + 5 < 9 ? v[k + 5] : 0.0f;
+        a[k] = (b4 ? hi : v[k]) + __shfl_xor_sync(0xffffffffu, b4 ? v[k] : hi, 16);
+    }
+    float b[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        const float hi = k + 3 < 5 ? a[k + 3] : 0.0f;
+        b[k] = (b3 ? hi : a[k]) + __shfl_xor_sync(0xffffffffu, b3 ? a[k] : hi, 8);
+    }
+    float c[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const float hi = k + 2 < 3 ? b[k + 2] : 0.0f;
+        c[k] = (b2 ? hi : b[k]) + __shfl_xor_sync(0xffffffffu, b2 ? b[k] : hi, 4);
+    }
+    const float d = (b1 ? c[1] : c[0]) + __shfl_xor_sync(0xffffffffu, b1 ? c[0] : c[1], 2);
+    return d + __shfl_xor_sync(0xffffffffu, d, 1);
+}
+
+// Value index whose total reduce9 leaves in lane L (even lanes), or -1 for padding.
+__device__ __forceinline__ int reduce9_index(int lane) {
+    const int b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1, b1 = (lane >> 1) & 1;
+    const int s3 = 2 * b2 + b1;
+    if (s3 >= 3) return -1;
+    const int s2 = 3 * b3 + s3;
+    if (s2 >= 5) return -1;
+    const int idx = 5 * b4 + s2;
+    return idx < 9 && (lane & 1) == 0 ? idx : -1;
 }
 
 __global__ void __launch_bounds__(512) k_bwd_raster(const BwdArgs a) {
     extern __shared__ __align__(16) float4 sm4[];
     const int nthr = blockDim.x;
-    float4* sA = sm4;                                    // x y opacity ic11
-    float4* sB = sm4 + nthr;                             // ic21 ic22 r g
-    float2* sC = reinterpret_cast<float2*>(sm4 + 2 * nthr);  // b q_threshold
-    int* sF = reinterpret_cast<int*>(sC + nthr);             // fgidx (0-based)
+    float4* sA = sm4;                                          // x y opacity ic11
+    float4* sB = sm4 + nthr;                                   // ic21 ic22 r g
+    float4* sC = sm4 + 2 * nthr;                               // b q_threshold cx cy
+    float2* sR = reinterpret_cast<float2*>(sm4 + 3 * nthr);    // box half-widths
+    int* sF = reinterpret_cast<int*>(sR + nthr);               // fgidx (0-based)
     __shared__ int red[32];
 
     const int F = a.counts[0];
@@ -72,9 +105,11 @@ __global__ void __launch_bounds__(512) k_bwd_raster(const BwdArgs a) {
 
     const int t = threadIdx.x;
     const int lane = t & 31, warp = t >> 5;
-    const int lv = t % a.tile_h, lu = t / a.tile_h;
+    int lu, lv;
+    tile_pixel(a.compact, a.tile_w, a.tile_h, t, lu, lv);
     const int txi = blockIdx.x, tyi = blockIdx.y;
-    const int U = txi * a.tile_w + lu + 1, V = tyi * a.tile_h + lv + 1;
+    const int u0 = txi * a.tile_w, v0 = tyi * a.tile_h;
+    const int U = u0 + lu + 1, V = v0 + lv + 1;
     const bool inside = U <= a.width && V <= a.height;
     const size_t px = (size_t)(V - 1) + (size_t)a.height * (size_t)(U - 1);
     const int tile = txi + tyi * a.tiles_x + 1;
@@ -92,11 +127,24 @@ __global__ void __launch_bounds__(512) k_bwd_raster(const BwdArgs a) {
     }
     float p0 = T * a.bg0, p1 = T * a.bg1, p2 = T * a.bg2;
     const float cpu = (float)U - 0.5f, cpv = (float)V - 0.5f;
+    const float wu0 = (float)__reduce_min_sync(0xffffffffu, (unsigned)lu) + 0.5f;
+    const float wu1 = (float)__reduce_max_sync(0xffffffffu, (unsigned)lu) + 0.5f;
+    const float wv0 = (float)__reduce_min_sync(0xffffffffu, (unsigned)lv) + 0.5f;
+    const float wv1 = (float)__reduce_max_sync(0xffffffffu, (unsigned)lv) + 0.5f;
 
-    // block / warp maxima of the last contributor (1-based sorted index)
-    int wlast = lastc;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) wlast = max(wlast, __shfl_xor_sync(0xffffffffu, wlast, o));
+    // this lane's share of the warp-reduced atomics: pointer and stride of value reduce9_index
+    const int vi = reduce9_index(lane);
+    float* vptr = nullptr;
+    int vstride = 0;
+    if (vi >= 0) {
+        if (vi < 2) { vptr = a.mean2d_g + vi; vstride = 2; }
+        else if (vi == 2) { vptr = a.opacity_g; vstride = 1; }
+        else if (vi < 6) { vptr = a.licov_g + (vi - 3); vstride = 3; }
+        else { vptr = a.color_g + (vi - 6); vstride = 3; }
+    }
+
+    // warp / block maxima of the last contributor (1-based sorted index)
+    const int wlast = (int)__reduce_max_sync(0xffffffffu, (unsigned)lastc);
     if (lane == 0) red[warp] = wlast;
     __syncthreads();
     int blast = 0;
@@ -111,83 +159,86 @@ __global__ void __launch_bounds__(512) k_bwd_raster(const BwdArgs a) {
             const int fg = a.sfgidx[bstart + t] - 1;
             const float* r = a.f2d + 9 * (size_t)fg;
             const float op = r[2];
+            const float lop = gs_logf(op);
             sA[t] = make_float4(r[0], r[1], op, r[3]);
             sB[t] = make_float4(r[4], r[5], r[6], r[7]);
             // op * exp(q) < min_alpha whenever q < log(min_alpha) - log(op) - 0.01
-            const float thr = op > 0.0f ? a.log_min_alpha - gs_logf(op) - 0.01f : -INFINITY;
-            sC[t] = make_float2(r[8], thr);
+            const float thr = op > 0.0f ? a.log_min_alpha - lop - 0.01f : -INFINITY;
+            sC[t] = make_float4(r[8], thr, r[0] - (float)u0, r[1] - (float)v0);
+            sR[t] = cull_box(r[3], r[4], r[5], lop, a.log_min_alpha);
             sF[t] = fg;
         }
         __syncthreads();
-        const int jhi = min(nb, wlast - bstart) - 1;  // warp-uniform
-        for (int j = jhi; j >= 0; --j) {
-            const int idx1 = bstart + j + 1;
-            bool contrib = false;
-            float v0 = 0.f, v1 = 0.f, v2 = 0.f, v3 = 0.f, v4 = 0.f, v5 = 0.f, v6 = 0.f, v7 = 0.f, v8 = 0.f;
-            if (inside && idx1 <= lastc) {
-                const float4 A = sA[j];
-                const float4 B = sB[j];
-                const float2 Cc = sC[j];
-                const float du = cpu - A.x, dv = cpv - A.y;
-                const float ic11 = A.w, ic21 = B.x, ic22 = B.y;
-                const float q = -0.5f * (ic11 * (du * du) + ic22 * (dv * dv)) - ic21 * du * dv;
-                if (q >= Cc.y) {
-                    const float ge = gs_expf(q);
-                    const float alpha = fmin_jl(a.max_alpha, A.z * ge);
-                    if (alpha >= a.min_alpha) {
-                        contrib = true;
-                        const float inv1m = 1.0f / (1.0f - alpha);
-                        T *= inv1m;
-                        const float tc0 = T * B.z, tc1 = T * B.w, tc2 = T * Cc.x;
-                        p0 += alpha * tc0;
-                        p1 += alpha * tc1;
-                        p2 += alpha * tc2;
-                        const float ag = inv1m * (g0 * (tc0 - p0) + g1 * (tc1 - p1) + g2 * (tc2 - p2));
-                        const float aga = alpha * ag;
-                        const float sc = -0.5f * aga;
-                        const float g21 = sc * (dv * du);
-                        v0 = aga * (du * ic11 + dv * ic21);
-                        v1 = aga * (du * ic21 + dv * ic22);
-                        v2 = ge * ag;
-                        v3 = sc * (du * du);
-                        v4 = g21 + g21;
-                        v5 = sc * (dv * dv);
-                        const float ta = T * alpha;
-                        v6 = ta * g0;
-                        v7 = ta * g1;
-                        v8 = ta * g2;
+        const int jend = min(nb, wlast - bstart);  // warp-uniform, exclusive
+        for (int c1 = jend; c1 > 0; c1 -= 32) {
+            const int c0 = max(0, c1 - 32);
+            const int j = c0 + lane;
+            bool rel = false;
+            if (j < c1) {
+                const float4 C = sC[j];
+                const float2 R = sR[j];
+                rel = C.z + R.x >= wu0 && C.z - R.x <= wu1 && C.w + R.y >= wv0 && C.w - R.y <= wv1;
+            }
+            unsigned mask = __ballot_sync(0xffffffffu, rel);
+            while (mask) {
+                const int hb = 31 - __clz(mask);
+                mask &= ~(1u << hb);
+                const int jj = c0 + hb;
+                bool contrib = false;
+                float v[9] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                if (inside && bstart + jj + 1 <= lastc) {
+                    const float4 A = sA[jj];
+                    const float4 B = sB[jj];
+                    const float4 Cc = sC[jj];
+                    const float du = cpu - A.x, dv = cpv - A.y;
+                    const float ic11 = A.w, ic21 = B.x, ic22 = B.y;
+                    const float q = -0.5f * (ic11 * (du * du) + ic22 * (dv * dv)) - ic21 * du * dv;
+                    if (q >= Cc.y) {
+                        const float ge = gs_expf(q);
+                        const float alpha = fmin_jl(a.max_alpha, A.z * ge);
+                        if (alpha >= a.min_alpha) {
+                            contrib = true;
+                            const float inv1m = 1.0f / (1.0f - alpha);
+                            T *= inv1m;
+                            const float tc0 = T * B.z, tc1 = T * B.w, tc2 = T * Cc.x;
+                            p0 += alpha * tc0;
+                            p1 += alpha * tc1;
+                            p2 += alpha * tc2;
+                            const float ag = inv1m * (g0 * (tc0 - p0) + g1 * (tc1 - p1) + g2 * (tc2 - p2));
+                            const float aga = alpha * ag;
+                            const float sc = -0.5f * aga;
+                            const float g21 = sc * (dv * du);
+                            v[0] = aga * (du * ic11 + dv * ic21);
+                            v[1] = aga * (du * ic21 + dv * ic22);
+                            v[2] = ge * ag;
+                            v[3] = sc * (du * du);
+                            v[4] = g21 + g21;
+                            v[5] = sc * (dv * dv);
+                            const float ta = T * alpha;
+                            v[6] = ta * g0;
+                            v[7] = ta * g1;
+                            v[8] = ta * g2;
+                        }
                     }
                 }
-            }
-            const unsigned mask = __ballot_sync(0xffffffffu, contrib);
-            if (mask == 0) continue;
-            const int fg = sF[j];
-            if (__popc(mask) == 1) {
-                if (contrib) {
-                    atomicAdd(a.mean2d_g + 2 * fg, v0);
-                    atomicAdd(a.mean2d_g + 2 * fg + 1, v1);
-                    atomicAdd(a.opacity_g + fg, v2);
-                    atomicAdd(a.licov_g + 3 * fg, v3);
-                    atomicAdd(a.licov_g + 3 * fg + 1, v4);
-                    atomicAdd(a.licov_g + 3 * fg + 2, v5);
-                    atomicAdd(a.color_g + 3 * fg, v6);
-                    atomicAdd(a.color_g + 3 * fg + 1, v7);
-                    atomicAdd(a.color_g + 3 * fg + 2, v8);
-                }
-            } else {
-                v0 = warp_sum(v0); v1 = warp_sum(v1); v2 = warp_sum(v2);
-                v3 = warp_sum(v3); v4 = warp_sum(v4); v5 = warp_sum(v5);
-                v6 = warp_sum(v6); v7 = warp_sum(v7); v8 = warp_sum(v8);
-                if (lane == 0) {
-                    atomicAdd(a.mean2d_g + 2 * fg, v0);
-                    atomicAdd(a.mean2d_g + 2 * fg + 1, v1);
-                    atomicAdd(a.opacity_g + fg, v2);
-                    atomicAdd(a.licov_g + 3 * fg, v3);
-                    atomicAdd(a.licov_g + 3 * fg + 1, v4);
-                    atomicAdd(a.licov_g + 3 * fg + 2, v5);
-                    atomicAdd(a.color_g + 3 * fg, v6);
-                    atomicAdd(a.color_g + 3 * fg + 1, v7);
-                    atomicAdd(a.color_g + 3 * fg + 2, v8);
+                const unsigned cmask = __ballot_sync(0xffffffffu, contrib);
+                if (cmask == 0) continue;
+                const int fg = sF[jj];
+                if (__popc(cmask) == 1) {
+                    if (contrib) {
+                        atomicAdd(a.mean2d_g + 2 * fg, v[0]);
+                        atomicAdd(a.mean2d_g + 2 * fg + 1, v[1]);
+                        atomicAdd(a.opacity_g + fg, v[2]);
+                        atomicAdd(a.licov_g + 3 * fg, v[3]);
+                        atomicAdd(a.licov_g + 3 * fg + 1, v[4]);
+                        atomicAdd(a.licov_g + 3 * fg + 2, v[5]);
+                        atomicAdd(a.color_g + 3 * fg, v[6]);
+                        atomicAdd(a.color_g + 3 * fg + 1, v[7]);
+                        atomicAdd(a.color_g + 3 * fg + 2, v[8]);
+                    }
+                } else {
+                    const float s = reduce9(v, lane);
+                    if (vi >= 0) atomicAdd(vptr + (size_t)vstride * fg, s);
                 }
             }
         }
@@ -246,7 +297,7 @@ struct BProjArgs {
 };
 
 template <int DEG>
-__global__ void __launch_bounds__(128) k_bwd_project(const BProjArgs a, const gs3d_camera cam,
+__global__ void __launch_bounds__(128, 6) k_bwd_project(const BProjArgs a, const gs3d_camera cam,
                                                      const gs3d_render_options opt) {
     const int F = a.counts[0];
     float Ps[3][3];
@@ -257,7 +308,18 @@ __global__ void __launch_bounds__(128) k_bwd_project(const BProjArgs a, const gs
     const int L2I[3] = {0, 1, 1}, L2J[3] = {0, 0, 1};
     const int L3I[6] = {0, 1, 2, 1, 2, 2}, L3J[6] = {0, 0, 0, 1, 1, 2};
     constexpr int MAXO = (DEG + 1) * (DEG + 1);
-    for (int f = blockIdx.x * blockDim.x + threadIdx.x; f < F; f += gridDim.x * blockDim.x) {
+    constexpr int NSH = 3 * MAXO;
+    // per-warp staging of the SH rows: the coefficients are loaded into it as float4, the
+    // Jacobian reads them from it, the SH gradients replace them and the warp then stores its
+    // 32 consecutive gradient rows with coalesced writes
+    __shared__ float stage[4][32][NSH + 1];
+    const int lane = threadIdx.x & 31;
+    float* mys = &stage[threadIdx.x >> 5][lane][0];
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t fb = (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * 32; fb < F;
+         fb += nwarps * 32) {
+      const int f = (int)fb + lane;
+      if (f < F) {
         const int gi = a.f2g[f] - 1;
         const float* r = a.f2d + 9 * (size_t)f;
         const float4 mo = a.mo4[gi];
@@ -389,13 +451,26 @@ __global__ void __launch_bounds__(128) k_bwd_project(const BProjArgs a, const gs
         const float cgr[3] = {a.color_g[3 * (size_t)f], a.color_g[3 * (size_t)f + 1],
                               a.color_g[3 * (size_t)f + 2]};
         const float* h = a.sh + (size_t)gi * 3 * a.sh_stride;
+        // the Jacobian reads coefficients 0 .. 3 MAXO - 1 of the row linearly (sh.jl:196)
+        if (DEG > 0) {
+            if ((NSH % 4) == 0 && (reinterpret_cast<uintptr_t>(h) & 15) == 0) {
+#pragma unroll
+                for (int k = 0; k < NSH / 4; ++k) {
+                    const float4 v4 = reinterpret_cast<const float4*>(h)[k];
+                    mys[4 * k] = v4.x; mys[4 * k + 1] = v4.y; mys[4 * k + 2] = v4.z; mys[4 * k + 3] = v4.w;
+                }
+            } else {
+#pragma unroll
+                for (int k = 0; k < NSH; ++k) mys[k] = h[k];
+            }
+        }
         float Jt[3][3] = {{0.f, 0.f, 0.f}, {0.f, 0.f, 0.f}, {0.f, 0.f, 0.f}};
         if (DEG > 0) {
             const float x = nd0, y = nd1, z = nd2;
 #pragma unroll
             for (int c = 0; c < 3; ++c) {
                 if (col[c] <= 0.0f) continue;
-                const float* hc = h + c * MAXO;  // linear indexing with the options order (sh.jl:196)
+                const float* hc = mys + c * MAXO;  // linear indexing with the options order (sh.jl:196)
                 float dy = -sh_c(2) * hc[1];
                 float dz = sh_c(3) * hc[2];
                 float dx = -sh_c(4) * hc[3];
@@ -513,15 +588,25 @@ __global__ void __launch_bounds__(128) k_bwd_project(const BProjArgs a, const gs
                 a.rot_g[4 * (size_t)f + i] = inv_qn * w;
             }
         }
-        // SH coefficients (compute_sh_coeffs_grad!, backward_core.jl:936-964)
-        float* shg = a.sh_g + (size_t)f * 3 * a.sh_grad_stride;
+        // SH coefficients (compute_sh_coeffs_grad!, backward_core.jl:936-964), staged
 #pragma unroll
         for (int l = 0; l < 3; ++l) {
             const bool live = col[l] >= 0.0f;
 #pragma unroll
             for (int k = 1; k <= MAXO; ++k)
-                shg[(k - 1) + l * a.sh_grad_stride] = live ? cgr[l] * sh_basis(k, nd0, nd1, nd2) : 0.0f;
+                mys[(k - 1) + l * MAXO] = live ? cgr[l] * sh_basis(k, nd0, nd1, nd2) : 0.0f;
         }
+      }
+      __syncwarp();
+      const int nrows = (int)min((int64_t)32, (int64_t)F - fb);
+      float* const warp_stage = &stage[threadIdx.x >> 5][0][0];
+      for (int e = lane; e < nrows * NSH; e += 32) {
+          const int row = e / NSH, rem = e - row * NSH;
+          const int c = rem / MAXO, k = rem - c * MAXO;
+          a.sh_g[(size_t)(fb + row) * 3 * a.sh_grad_stride + (size_t)(c * a.sh_grad_stride + k)] =
+              warp_stage[row * (NSH + 1) + rem];
+      }
+      __syncwarp();
     }
 }
 
@@ -582,6 +667,7 @@ extern "C" GS3D_API int gs3d_backward(const gs3d_fgradients* fg, const float* rg
     a.tile_w = til->tile_width;
     a.tile_h = til->tile_height;
     a.tiles_x = til->nb_tiles_x;
+    a.compact = compact_tiles(til->tile_width, til->tile_height);
     a.bg0 = opt->background[0];
     a.bg1 = opt->background[1];
     a.bg2 = opt->background[2];
@@ -589,7 +675,7 @@ extern "C" GS3D_API int gs3d_backward(const gs3d_fgradients* fg, const float* rg
     a.max_alpha = opt->max_alpha;
     a.log_min_alpha = opt->min_alpha > 0.0f ? gs_logf(opt->min_alpha) : -INFINITY;
     const int nthr = til->tile_width * til->tile_height;
-    const size_t smem = (size_t)nthr * (2 * sizeof(float4) + sizeof(float2) + sizeof(int));
+    const size_t smem = (size_t)nthr * (3 * sizeof(float4) + sizeof(float2) + sizeof(int));
     {
         ProfScope prof("bwd_raster", stream);
         k_bwd_raster<<<dim3(til->nb_tiles_x, til->nb_tiles_y), nthr, smem, stream>>>(a);

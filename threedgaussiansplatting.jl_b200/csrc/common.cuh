@@ -105,6 +105,19 @@ GS_HD float gs_logf(float x) {
     return fmaf(ef, 0.693147182464599609375f, fmaf(ef, -1.904654323148236e-09f, logm));
 }
 
+// x / b, correctly rounded, for a divisor b fixed for a whole launch with rb = RN(1/b) from
+// the host: q0 = RN(x rb), r = x - b q0 (exact with one FMA), q = RN(q0 + r rb) equals RN(x/b)
+// for normal operands (P. Markstein, "Computation of elementary functions on the IBM RISC
+// System/6000 processor", IBM J. Res. Dev. 34(1), 1990); tiny, huge or non-finite x take the
+// ordinary division.
+GS_HD float div_by_const(float x, float b, float rb) {
+    const float ax = fabsf(x);
+    if (!(ax >= 1e-25f && ax <= 1e25f)) return x / b;
+    const float q0 = x * rb;
+    const float r = fmaf(-b, q0, x);
+    return fmaf(r, rb, q0);
+}
+
 GS_HD float gs_sigmoid(float x) { return 1.0f / (1.0f + gs_expf(-x)); }
 GS_HD float gs_logit(float x) { return -gs_logf(1.0f / x - 1.0f); }
 GS_HD float jl_clamp(float x, float lo, float hi) { return x > hi ? hi : (x < lo ? lo : x); }
@@ -141,6 +154,43 @@ GS_HD float sh_c(int i) {
         case 16: return (float)-0.5900435899266435;
         default: return 0.0f;
     }
+}
+
+// ---- tile rasterisation helpers ---------------------------------------------------------
+// Pixels of a tile CTA: compact 4 (u) x 8 (v) blocks per warp when the tile allows (v fastest
+// inside a block, so a warp stores 4 runs of 8 consecutive pixels of the column-major
+// images), else pixel columns (v fastest).
+GS_HD int compact_tiles(int tw, int th) { return (tw % 4 == 0 && th % 8 == 0) ? 1 : 0; }
+
+__device__ __forceinline__ void tile_pixel(int compact, int tw, int th, int t, int& lu, int& lv) {
+    if (compact) {
+        const int w = t >> 5, lane = t & 31;
+        const int bpr = tw >> 2;
+        lu = (w % bpr) * 4 + (lane >> 3);
+        lv = (w / bpr) * 8 + (lane & 7);
+    } else {
+        lv = t % th;
+        lu = t / th;
+    }
+}
+
+// Half-widths (rx, ry) of the box, around the mean, outside which a Gaussian with conic
+// (ic11, ic21, ic22) and log-opacity lop has alpha < min_alpha at every point: the
+// alpha = min_alpha ellipse d'M d = 2 (lop - log(min_alpha)) widened by 0.1 in that form and by
+// 0.1% + 0.01 px, far beyond the rounding of either raster kernel's exponent. (+inf, +inf)
+// when the conic is degenerate or non-finite (never culled); (-inf, -inf) when no point can
+// reach min_alpha.
+__device__ __forceinline__ float2 cull_box(float ic11, float ic21, float ic22, float lop,
+                                           float log_min_alpha) {
+    const float det = ic11 * ic22 - ic21 * ic21;
+    const float gamma = 2.0f * (lop - log_min_alpha) + 0.1f;
+    const float inf = u2f(0x7f800000u);
+    if (!(det > 0.0f) || !(ic11 > 0.0f) || !(ic22 > 0.0f) || !(gamma == gamma) || gamma == inf ||
+        det == inf)
+        return make_float2(inf, inf);
+    if (gamma <= 0.0f) return make_float2(-inf, -inf);
+    return make_float2(sqrtf(gamma * ic22 / det) * 1.001f + 0.01f,
+                       sqrtf(gamma * ic11 / det) * 1.001f + 0.01f);
 }
 
 // ---- launch geometry ---------------------------------------------------------------------

@@ -1,19 +1,21 @@
 // raster.cu — front-to-back tile alpha blend, render_tiles_kernel! (forward_core.jl:756-993).
 //
-// One CTA per tile (tile_width x tile_height threads, one pixel each). Lanes run down a
-// pixel column (v fastest) so a warp's RGB / T / index stores are contiguous in the
-// reference's column-major 3 x h x w and h x w images. The duplicated Gaussians of the tile
-// are staged BATCH = blockDim at a time in shared memory in the reference's precomputed
-// form (forward_core.jl:877-897): six quadratic-form coefficients with log(opacity)
+// One CTA per tile (tile_width x tile_height threads, one pixel each). The duplicated Gaussians
+// of the tile are staged BATCH = blockDim at a time in shared memory in the reference's
+// precomputed form (forward_core.jl:877-897): six quadratic-form coefficients with log(opacity)
 // absorbed, the colour and the depth. Per pixel the arithmetic and its order are the
 // reference's: alpha = min(max_alpha, exp(q)), skip alpha < min_alpha, stop when
 // T (1 - alpha) < min_transmittance.
 //
-// Beyond the reference: (a) q below log(min_alpha) - 0.01 skips the exponential (exp(q)
-// is then certainly below min_alpha, so the result is unchanged); (b) the whole CTA leaves
-// the batch loop once every pixel has stopped (__syncthreads_count); (c) a CTA reads the
-// duplicate and tile counts from device memory and draws the void image itself when there
-// is nothing to draw (render_void!, forward_structs.jl:743-757), so no host sync is needed.
+// Work saved without changing any pixel's result:
+//   * warps cover compact 4 x 8 pixel blocks (when the tile allows; otherwise pixel columns),
+//     and each warp first tests 32 staged entries at once against its block with the entry's
+//     alpha >= min_alpha ellipse box (inflated by a safety margin), then evaluates only the
+//     entries that can reach one of its pixels, in order;
+//   * q below log(min_alpha) - 0.01 skips the exponential (exp(q) < min_alpha there);
+//   * the CTA leaves once every pixel has stopped (__syncthreads_count).
+// A CTA reads F and D from device memory and draws the void image itself when there is
+// nothing to draw (render_void!, forward_structs.jl:743-757), so no host sync is needed.
 #include "common.cuh"
 #include "internal.h"
 
@@ -34,22 +36,26 @@ struct RasterArgs {
     int32_t* last;
     int32_t width, height;
     int32_t tile_w, tile_h, tiles_x;
+    int32_t compact;            // 4 x 8 warp blocks
     float bg0, bg1, bg2;
-    float min_alpha, max_alpha, min_T, q_skip;
+    float min_alpha, max_alpha, min_T, q_skip, log_min_alpha;
 };
 
 __global__ void __launch_bounds__(512) k_raster(const RasterArgs a) {
     extern __shared__ __align__(16) float4 sm4[];
     const int nthr = blockDim.x;
-    float4* sA = sm4;             // p1 p2 p3 p4
-    float4* sB = sm4 + nthr;      // p5 p6 r g
-    float2* sC = reinterpret_cast<float2*>(sm4 + 2 * nthr);  // b depth
+    float4* sA = sm4;                 // p1 p2 p3 p4
+    float4* sB = sm4 + nthr;          // p5 p6 r g
+    float4* sC = sm4 + 2 * nthr;      // b depth cx cy
+    float2* sR = reinterpret_cast<float2*>(sm4 + 3 * nthr);  // box half-widths rx ry
 
     const int t = threadIdx.x;
-    const int lv = t % a.tile_h, lu = t / a.tile_h;     // 0-based in tile, v fastest
-    const int txi = blockIdx.x, tyi = blockIdx.y;       // 0-based tile coordinates
+    const int lane = t & 31;
+    int lu, lv;  // 0-based pixel in tile
+    tile_pixel(a.compact, a.tile_w, a.tile_h, t, lu, lv);
+    const int txi = blockIdx.x, tyi = blockIdx.y;
     const int u0 = txi * a.tile_w, v0 = tyi * a.tile_h;
-    const int U = u0 + lu + 1, V = v0 + lv + 1;         // 1-based pixel
+    const int U = u0 + lu + 1, V = v0 + lv + 1;
     const bool inside = U <= a.width && V <= a.height;
     const size_t px = (size_t)(V - 1) + (size_t)a.height * (size_t)(U - 1);
 
@@ -68,6 +74,12 @@ __global__ void __launch_bounds__(512) k_raster(const RasterArgs a) {
     const int tile = txi + tyi * a.tiles_x + 1;  // 1-based linear, x-contiguous
     const int start = tile == 1 ? 0 : a.tiles_end[tile - 2];
     const int end = a.tiles_end[tile - 1];
+
+    // the warp's pixel-centre rectangle in tile-local continuous coordinates
+    const float wu0 = (float)__reduce_min_sync(0xffffffffu, (unsigned)lu) + 0.5f;
+    const float wu1 = (float)__reduce_max_sync(0xffffffffu, (unsigned)lu) + 0.5f;
+    const float wv0 = (float)__reduce_min_sync(0xffffffffu, (unsigned)lv) + 0.5f;
+    const float wv1 = (float)__reduce_max_sync(0xffffffffu, (unsigned)lv) + 0.5f;
 
     const float cu = (float)(lu + 1) - 0.5f, cv = (float)(lv + 1) - 0.5f;
     const float uu = cu * cu, uv = cu * cv, vv = cv * cv;
@@ -89,31 +101,47 @@ __global__ void __launch_bounds__(512) k_raster(const RasterArgs a) {
             const float p1 = -0.5f * ic11, p2 = -0.5f * ic22, p3 = -ic21;
             const float p4 = ic11_du + ic21 * dv;
             const float p5 = ic21_du + ic22_dv;
-            const float p6 = -0.5f * (ic11_du * du + ic22_dv * dv) - ic21_du * dv + gs_logf(op);
+            const float lop = gs_logf(op);
+            const float p6 = -0.5f * (ic11_du * du + ic22_dv * dv) - ic21_du * dv + lop;
             sA[t] = make_float4(p1, p2, p3, p4);
             sB[t] = make_float4(p5, p6, r[6], r[7]);
-            sC[t] = make_float2(r[8], a.depths[fg]);
+            sC[t] = make_float4(r[8], a.depths[fg], du, dv);
+            sR[t] = cull_box(ic11, ic21, ic22, lop, a.log_min_alpha);
         }
         __syncthreads();
-        if (!done) {
+        if (__any_sync(0xffffffffu, !done)) {
             const int nb = min(nthr, end - base);
-            for (int j = 0; j < nb; ++j) {
-                const float4 A = sA[j];
-                const float4 B = sB[j];
-                const float q = A.x * uu + A.y * vv + A.z * uv + A.w * cu + B.x * cv + B.y;
-                if (q < a.q_skip) continue;
-                const float alpha = fmin_jl(a.max_alpha, gs_expf(q));
-                if (alpha < a.min_alpha) continue;
-                const float nT = T * (1.0f - alpha);
-                if (nT < a.min_T) { done = true; break; }
-                const float w = T * alpha;
-                const float2 C = sC[j];
-                c0 += w * B.z;
-                c1 += w * B.w;
-                c2 += w * C.x;
-                T = nT;
-                dep += w * C.y;
-                lastc = base + j + 1;
+            for (int ch = 0; ch < nb; ch += 32) {
+                const int j = ch + lane;
+                bool rel = false;
+                if (j < nb) {
+                    const float4 C = sC[j];
+                    const float2 R = sR[j];
+                    rel = C.z + R.x >= wu0 && C.z - R.x <= wu1 && C.w + R.y >= wv0 && C.w - R.y <= wv1;
+                }
+                unsigned mask = __ballot_sync(0xffffffffu, rel);
+                while (mask) {
+                    const int jj = ch + __ffs(mask) - 1;
+                    mask &= mask - 1;
+                    if (done) continue;
+                    const float4 A = sA[jj];
+                    const float4 B = sB[jj];
+                    const float q = A.x * uu + A.y * vv + A.z * uv + A.w * cu + B.x * cv + B.y;
+                    if (q < a.q_skip) continue;
+                    const float alpha = fmin_jl(a.max_alpha, gs_expf(q));
+                    if (alpha < a.min_alpha) continue;
+                    const float nT = T * (1.0f - alpha);
+                    if (nT < a.min_T) { done = true; continue; }
+                    const float w = T * alpha;
+                    const float4 C = sC[jj];
+                    c0 += w * B.z;
+                    c1 += w * B.w;
+                    c2 += w * C.x;
+                    T = nT;
+                    dep += w * C.y;
+                    lastc = base + jj + 1;
+                }
+                if (__all_sync(0xffffffffu, done)) break;
             }
         }
     }
@@ -150,6 +178,7 @@ int launch_raster(const gs3d_render_outputs& out, const gs3d_camera& cam, const 
     a.tile_w = til.tile_width;
     a.tile_h = til.tile_height;
     a.tiles_x = til.nb_tiles_x;
+    a.compact = compact_tiles(til.tile_width, til.tile_height);
     a.bg0 = opt.background[0];
     a.bg1 = opt.background[1];
     a.bg2 = opt.background[2];
@@ -157,9 +186,10 @@ int launch_raster(const gs3d_render_outputs& out, const gs3d_camera& cam, const 
     a.max_alpha = opt.max_alpha;
     a.min_T = opt.min_transmittance;
     // exp(q) < min_alpha for every q < log(min_alpha) - 0.01 (margin >> 2 ulp)
-    a.q_skip = opt.min_alpha > 0.0f ? gs_logf(opt.min_alpha) - 0.01f : -INFINITY;
+    a.log_min_alpha = opt.min_alpha > 0.0f ? gs_logf(opt.min_alpha) : -INFINITY;
+    a.q_skip = opt.min_alpha > 0.0f ? a.log_min_alpha - 0.01f : -INFINITY;
     const int nthr = til.tile_width * til.tile_height;
-    const size_t smem = (size_t)nthr * (2 * sizeof(float4) + sizeof(float2));
+    const size_t smem = (size_t)nthr * (3 * sizeof(float4) + sizeof(float2));
     dim3 grid(til.nb_tiles_x, til.nb_tiles_y);
     k_raster<<<grid, nthr, smem, stream>>>(a);
     GS3D_LAUNCHED("k_raster");
