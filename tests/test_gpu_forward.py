@@ -162,3 +162,39 @@ def test_sort_pairs_dropin(cuda, n, bits):
     ko, vo = _sort_gpu(keys, vals, bits, cuda)
     rk, rv = O.sort_pairs(keys, vals, bits)
     assert np.array_equal(ko, rk) and np.array_equal(vo, rv)
+
+
+def _reference_sort_lib():
+    """The reference's own CUB wrapper (deps/cub_sort_pairs/cub_sort_pairs_wrapper.cu),
+    compiled from the reference checkout by oracle/build.py into oracle/_ref/."""
+    from oracle.build import REF_LIB
+    if not REF_LIB.exists():
+        pytest.skip("reference CUB sort wrapper was not built (no reference checkout at build time)")
+    lib = C.CDLL(str(REF_LIB))
+    lib.determine_sort_pairs_temp_storage.restype = C.c_size_t
+    lib.determine_sort_pairs_temp_storage.argtypes = [C.c_void_p] * 4 + [C.c_int, C.c_int]
+    lib.sort_pairs.restype = None
+    lib.sort_pairs.argtypes = [C.c_void_p, C.c_size_t] + [C.c_void_p] * 4 + [C.c_int, C.c_int]
+    return lib
+
+
+@pytest.mark.parametrize("n,bits", [(5, 35), (4097, 44), (300_001, 46), (1_000_000, 64)])
+def test_sort_pairs_matches_reference_cub_wrapper(cuda, n, bits):
+    """Same inputs through the reference's CUB DeviceRadixSort wrapper and through libgs3d's
+    drop-in: identical keys and values (CUB's sort is stable, so the result is unique)."""
+    ref = _reference_sort_lib()
+    rng = np.random.default_rng(7 * n + bits)
+    keys = rng.integers(0, 1 << 62, n, dtype=np.int64)
+    keys[: n // 4] = keys[n // 2]
+    vals = rng.permutation(n).astype(np.int32)
+    ko, vo = _sort_gpu(keys, vals, bits, cuda)
+    k_in = torch.from_numpy(keys).to(cuda)
+    v_in = torch.from_numpy(vals).to(cuda)
+    k_out, v_out = torch.empty_like(k_in), torch.empty_like(v_in)
+    nbytes = ref.determine_sort_pairs_temp_storage(None, None, None, None, n, bits)
+    tmp = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=cuda)
+    torch.cuda.synchronize()
+    ref.sort_pairs(tmp.data_ptr(), nbytes, k_in.data_ptr(), k_out.data_ptr(), v_in.data_ptr(),
+                   v_out.data_ptr(), n, bits)
+    torch.cuda.synchronize()
+    assert np.array_equal(ko, k_out.cpu().numpy()) and np.array_equal(vo, v_out.cpu().numpy())
