@@ -207,6 +207,21 @@ GS3D_API int gs3d_sort_pairs_async(
     const int32_t* values_in, int32_t* values_out,
     int nb_items, int highest_key_bit, gs3d_stream_t stream);
 
+/* No counterpart in the reference (its sort always takes caller temp storage,
+ * forward_core.jl:629-659). gs3d_sort_pairs_async without temp storage: the scratch is a
+ * static device array inside libgs3d.so (13 MiB per device), so the call allocates nothing,
+ * for callers that cannot provide or allocate a temporary buffer. At most
+ * GS3D_SORT_NO_ALLOC_MAX_ITEMS pairs (larger calls return GS3D_ERR_INVALID_ARGUMENT and
+ * launch nothing). The scratch is shared by all calls on a device: calls whose work overlaps
+ * on the device race; calls on one stream do not. The first call with nb_items > 0 on a
+ * device does host-side setup (scratch address lookup, kernel attribute) and must come
+ * before any stream capture on that device. */
+#define GS3D_SORT_NO_ALLOC_MAX_ITEMS (1 << 20)
+GS3D_API int gs3d_sort_pairs_no_alloc(
+    const int64_t* keys_in, int64_t* keys_out,
+    const int32_t* values_in, int32_t* values_out,
+    int nb_items, int highest_key_bit, gs3d_stream_t stream);
+
 /* ---- render forward: render! GPU (forward_core.jl:196-314) -------------------------- */
 
 /* Bytes of render_buffers.workspace needed for these capacities. */

@@ -118,6 +118,8 @@ SIGNATURES = {
                           C.c_int, C.c_int]),
     "gs3d_sort_pairs_async": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p,
                                         C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
+    "gs3d_sort_pairs_no_alloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                           C.c_int, C.c_int, C.c_void_p]),
     "gs3d_render_forward_workspace_size": (C.c_int, [C.c_int64, C.c_int64, C.c_int32,
                                                      P(C.c_size_t)]),
     "gs3d_render_forward": (C.c_int, [P(RenderOutputsC), P(GaussiansC), P(Camera), P(TilingC),
