@@ -116,7 +116,9 @@ def test_backward_random(cuda, case, fix16):
     check_grads(gpu, ref)
 
 
-def test_adam_bit_exact(cuda):
+@pytest.mark.parametrize("deg", [0, 1, 2, 3])
+def test_adam_bit_exact(cuda, deg):
+    """Storage degree 3 with render degree deg: coefficients >= (deg + 1)^2 stay untouched."""
     spec = SceneSpec(16_384, "uniform:1", -4.0, 0.5)
     gv = synthetic_gaussians(spec, 0)
     cam = look_at_camera(256, 256, 60.0, (0, 0, 3))
@@ -134,8 +136,8 @@ def test_adam_bit_exact(cuda):
     adam.update_count = 5
     before_g = O.NpGaussians.from_vector(g)
     before_m = O.NpMoments.from_moments(adam.moments)
-    params = adam.params_c(3)
-    adam.update(fg, buf.fgidx_to_gidx, buf.device_counts, 3)
+    params = adam.params_c(deg)
+    adam.update(fg, buf.fgidx_to_gidx, buf.device_counts, deg)
     torch.cuda.synchronize()
     bc1, bc2 = bias_corrections(adam.beta1, adam.beta2, 5)
     O.adam(before_g, before_m, gpu, buf.fgidx_to_gidx[:F].cpu().numpy(), params, bc1, bc2)

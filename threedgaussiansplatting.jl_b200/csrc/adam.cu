@@ -2,7 +2,9 @@
 //
 // The reference launches five kernels (four component groups, then the SH coefficients:
 // optimizer.jl:1084-1127, :1165-1248), each walking the F filtered Gaussians. Here one kernel
-// gives each warp four filtered Gaussians at a time; lane s updates scalar slot s of each (SH
+// does all 59 parameters: k_adam_sh16 + k_adam_geom when every SH array has storage degree 3 (48 words per
+// Gaussian, moved as 16-byte units; the training configuration), else k_adam_warp4, which gives
+// each warp four filtered Gaussians at a time; lane s updates scalar slot s of each (SH
 // coefficients first, then mean, opacity feature, scales, rotation), so all lanes run the same
 // update with no divergence, the SH rows move as consecutive words, and every load of the four
 // Gaussians is in flight before the first update.
@@ -43,6 +45,7 @@ struct AdamArgs {
     float lr_means, lr_op, lr_scale, lr_rot, lr_dc, lr_rest;
     float b1, b2, eps, bc1, bc2;
     float rbc1, rbc2;      // RN(1 / bc): the bias-correction divisions as div_by_const
+    int64_t ncap;          // capacity of fgidx_to_gidx (the Gaussians' n): F is clamped to it
 };
 
 __device__ __forceinline__ void adam_scalar(float* p, float g, float* m, float lr, const AdamArgs& a) {
@@ -138,6 +141,99 @@ __global__ void __launch_bounds__(256) k_adam_warp4(const AdamArgs a) {
             *reinterpret_cast<float2*>(mp[e]) = mv[e];
         }
     }
+}
+
+// Storage degree 3 everywhere (Gaussians, moments, gradients): 48 SH words per Gaussian, so
+// every Gaussian's SH rows, moment rows and gradient rows are whole 16-byte units.
+//   k_adam_sh16: thread 12 f + c updates SH unit c of filtered Gaussian f, words 4c..4c+3 of
+//                the parameter row with their 8 interleaved moments and 4 gradients, as four
+//                16-byte loads; 12 consecutive threads cover one Gaussian's 192-byte row.
+//   k_adam_geom: one thread per filtered Gaussian for the 11 geometry scalars (mean, opacity
+//                feature, scales, rotation).
+// Grids are sized for the host-known n >= F, one item per thread, so the SMs keep as many
+// independent loads in flight as they hold threads (the SH kernel needs few registers and runs
+// at full occupancy). Same per-scalar update as above.
+__device__ __forceinline__ void adam4(float4& p, const float4& g, float4& m01, float4& m23,
+                                      float lr0, float lr, int nup, const AdamArgs& a) {
+    adam_reg(p.x, g.x, m01.x, m01.y, lr0, a);
+    if (nup > 1) adam_reg(p.y, g.y, m01.z, m01.w, lr, a);
+    if (nup > 2) adam_reg(p.z, g.z, m23.x, m23.y, lr, a);
+    if (nup > 3) adam_reg(p.w, g.w, m23.z, m23.w, lr, a);
+}
+
+__global__ void __launch_bounds__(256) k_adam_sh16(const AdamArgs a) {
+    // 32-bit indices: the host only takes this path when 12 n < 2^31
+    const uint32_t F = (uint32_t)max(0, min(a.counts[0], (int32_t)a.ncap));
+    const uint32_t it = blockIdx.x * blockDim.x + threadIdx.x;
+    if (it >= 12u * F) return;
+    const uint32_t f = it / 12u;
+    const int c = (int)(it - f * 12u);
+    const int i0 = 4 * (c & 3);  // coefficient index of the unit's first word
+    if (i0 >= a.maxo) return;
+    const int gidx = a.f2g[f];
+    if (gidx <= 0) return;
+    const size_t gi = (size_t)gidx - 1;
+    float4* pp = reinterpret_cast<float4*>(a.sh + gi * 48) + c;
+    float4* mp = reinterpret_cast<float4*>(a.shm + gi * 96) + 2 * c;
+    const float4 g = __ldg(reinterpret_cast<const float4*>(a.g_sh + (size_t)f * 48) + c);
+    float4 p = *pp, m01 = mp[0], m23 = mp[1];
+    const int nup = min(4, a.maxo - i0);
+    adam4(p, g, m01, m23, i0 == 0 ? a.lr_dc : a.lr_rest, a.lr_rest, nup, a);
+    *pp = p;
+    mp[0] = m01;
+    mp[1] = m23;
+}
+
+__global__ void __launch_bounds__(256) k_adam_geom(const AdamArgs a) {
+    const int64_t F = max((int64_t)0, min((int64_t)a.counts[0], a.ncap));
+    const int64_t f = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (f >= F) return;
+    const int gidx = a.f2g[f];
+    if (gidx <= 0) return;
+    const size_t gi = (size_t)gidx - 1;
+    float4* mop = reinterpret_cast<float4*>(a.mo) + gi;
+    float4* rfp = reinterpret_cast<float4*>(a.rf) + gi;
+    float2* mmp = reinterpret_cast<float2*>(a.mm) + 3 * gi;
+    float2* omp = reinterpret_cast<float2*>(a.om) + gi;
+    float2* smp = reinterpret_cast<float2*>(a.sm) + 3 * gi;
+    float4* rmp = reinterpret_cast<float4*>(a.rm) + 2 * gi;
+    float* sfp = a.sf + 3 * gi;
+    float4 mo = *mop, rf = *rfp, rm0 = rmp[0], rm1 = rmp[1];
+    float2 mm0 = mmp[0], mm1 = mmp[1], mm2 = mmp[2], om = *omp;
+    float2 sm0 = smp[0], sm1 = smp[1], sm2 = smp[2];
+    float s0 = sfp[0], s1 = sfp[1], s2 = sfp[2];
+    const float gm0 = __ldg(a.g_mean + 3 * f), gm1 = __ldg(a.g_mean + 3 * f + 1),
+                gm2 = __ldg(a.g_mean + 3 * f + 2), go = __ldg(a.g_op + f);
+    const float gs0 = __ldg(a.g_scale + 3 * f), gs1 = __ldg(a.g_scale + 3 * f + 1),
+                gs2 = __ldg(a.g_scale + 3 * f + 2);
+    const float4 gr = __ldg(reinterpret_cast<const float4*>(a.g_rot) + f);
+    adam_reg(mo.x, gm0, mm0.x, mm0.y, a.lr_means, a);
+    adam_reg(mo.y, gm1, mm1.x, mm1.y, a.lr_means, a);
+    adam_reg(mo.z, gm2, mm2.x, mm2.y, a.lr_means, a);
+    adam_reg(mo.w, go, om.x, om.y, a.lr_op, a);
+    adam_reg(s0, gs0, sm0.x, sm0.y, a.lr_scale, a);
+    adam_reg(s1, gs1, sm1.x, sm1.y, a.lr_scale, a);
+    adam_reg(s2, gs2, sm2.x, sm2.y, a.lr_scale, a);
+    adam_reg(rf.x, gr.x, rm0.x, rm0.y, a.lr_rot, a);
+    adam_reg(rf.y, gr.y, rm0.z, rm0.w, a.lr_rot, a);
+    adam_reg(rf.z, gr.z, rm1.x, rm1.y, a.lr_rot, a);
+    adam_reg(rf.w, gr.w, rm1.z, rm1.w, a.lr_rot, a);
+    *mop = mo;
+    *rfp = rf;
+    rmp[0] = rm0;
+    rmp[1] = rm1;
+    mmp[0] = mm0; mmp[1] = mm1; mmp[2] = mm2;
+    *omp = om;
+    smp[0] = sm0; smp[1] = sm1; smp[2] = sm2;
+    sfp[0] = s0; sfp[1] = s1; sfp[2] = s2;
+}
+
+bool aligned(const void* p, uintptr_t b) { return (reinterpret_cast<uintptr_t>(p) & (b - 1)) == 0; }
+
+bool flat16_ok(const AdamArgs& a, int64_t n) {
+    return n > 0 && 12 * n < ((int64_t)1 << 31) && a.S == 16 && a.Sm == 16 && a.Sg == 16 && aligned(a.sh, 16) && aligned(a.shm, 16) &&
+           aligned(a.g_sh, 16) && aligned(a.mo, 16) && aligned(a.rf, 16) && aligned(a.rm, 16) &&
+           aligned(a.g_rot, 16) && aligned(a.mm, 8) && aligned(a.om, 8) && aligned(a.sm, 8);
 }
 
 int launch_adam_warp(const AdamArgs& a, cudaStream_t stream) {
@@ -280,6 +376,14 @@ extern "C" GS3D_API int gs3d_adam_step(const gs3d_gaussians* g, const gs3d_adam_
     AdamArgs a;
     GS3D_RETURN_IF(make_args(g, m, fg, fgidx_to_gidx, device_counts, p, a));
     ProfScope prof("adam", stream);
+    if (flat16_ok(a, g->n)) {
+        a.ncap = g->n;
+        k_adam_sh16<<<(unsigned)ceil_div(12 * (int64_t)g->n, 256), 256, 0, stream>>>(a);
+        GS3D_LAUNCHED("k_adam_sh16");
+        k_adam_geom<<<(unsigned)ceil_div((int64_t)g->n, 256), 256, 0, stream>>>(a);
+        GS3D_LAUNCHED("k_adam_geom");
+        return GS3D_OK;
+    }
     GS3D_RETURN_IF(launch_adam_warp(a, stream));
     return GS3D_OK;
 }
