@@ -182,6 +182,30 @@ def test_training_step_matches_oracle_chain(cuda):
         assert np.mean(d <= 1e-6 + 1e-3 * lr) >= 0.999
 
 
+def test_host_targets_prefetched_match_device_targets(cuda):
+    """Pinned host targets, uploaded one step ahead on a copy stream, give the same training
+    run as device-resident targets (5 views, 12 steps: re-shuffles included): every step's
+    [loss, L1, DSSIM] agree. The backward's float atomics make two runs differ in the last
+    bits (and Adam with epsilon 1e-15 turns a near-zero gradient's sign flip into a full step),
+    so parameters are not compared and the losses have a tolerance, far below what a wrong or
+    stale target would change (the targets are independent random images)."""
+    runs = []
+    for on_host in (False, True):
+        gv = synthetic_gaussians(SceneSpec(16_384, "uniform:1", -4.0, 0.5), 3)
+        cams = [look_at_camera(256, 256, 60.0, (0.2 * i, 0, 3)) for i in range(5)]
+        targets = [target_image(256, 256, 200 + i, cuda) for i in range(5)]
+        if on_host:
+            targets = [x.cpu().pin_memory() for x in targets]
+        ro = RenderOptions.for_camera(cams[0], 3)
+        t = Trainer(gv.to(cuda), cams, targets, ro, Tiling.for_camera(cams[0]),
+                    TrainingOptions(scene_radius=3.3), seed=7)
+        t.iteration_nb = 3000
+        losses = [t.training_step().clone() for _ in range(12)]
+        torch.cuda.synchronize()
+        runs.append(torch.stack(losses)[:, :3].cpu())
+    assert torch.allclose(runs[0], runs[1], rtol=1e-5, atol=0), (runs[0], runs[1])
+
+
 def test_trainer_loss_decreases(cuda):
     _, _, _, _, t = _cfg0_trainer(cuda, nviews=1, seed=1)
     t.iteration_nb = 3000

@@ -2,6 +2,7 @@
 // native component, deps/cub_sort_pairs/cub_sort_pairs_wrapper.cu (sort_pairs and
 // determine_sort_pairs_temp_storage, same signatures, bound by forward_core.jl:629-659).
 #include <cstdarg>
+#include <cstdlib>
 #include <vector>
 
 #include "common.cuh"

@@ -194,8 +194,8 @@ __global__ void __launch_bounds__(512) k_bwd_raster(const BwdArgs a) {
                     const float ic11 = A.w, ic21 = B.x, ic22 = B.y;
                     const float q = -0.5f * (ic11 * (du * du) + ic22 * (dv * dv)) - ic21 * du * dv;
                     if (q >= Cc.y) {
-                        const float ge = gs_expf(q);
-                        const float alpha = fmin_jl(a.max_alpha, A.z * ge);
+                        const float ge = gs_expf_blend(q);
+                        const float alpha = min_hi(a.max_alpha, A.z * ge);
                         if (alpha >= a.min_alpha) {
                             contrib = true;
                             const float inv1m = 1.0f / (1.0f - alpha);
@@ -678,7 +678,8 @@ extern "C" GS3D_API int gs3d_backward(const gs3d_fgradients* fg, const float* rg
     const size_t smem = (size_t)nthr * (3 * sizeof(float4) + sizeof(float2) + sizeof(int));
     {
         ProfScope prof("bwd_raster", stream);
-        k_bwd_raster<<<dim3(til->nb_tiles_x, til->nb_tiles_y), nthr, smem, stream>>>(a);
+        const dim3 grid(til->nb_tiles_x, til->nb_tiles_y);
+        k_bwd_raster<<<grid, nthr, smem, stream>>>(a);
         GS3D_LAUNCHED("k_bwd_raster");
     }
 

@@ -82,6 +82,25 @@ GS_HD float gs_expf(float x) {
     return (p * u2f((uint32_t)(k1 + 127) << 23)) * u2f((uint32_t)(k2 + 127) << 23);
 }
 
+// gs_expf for the alpha-blend exponents, bit for bit: for -80 <= x <= 0.5 the result p 2^k is a
+// normal number, so gs_expf's two exact scalings by 2^(k/2) and 2^(k - k/2) equal one exact
+// scaling by 2^k; outside that range (and for NaN) it is gs_expf itself.
+GS_HD float gs_expf_blend(float x) {
+    if (!(x >= -80.0f && x <= 0.5f)) return gs_expf(x);
+    const float k = rintf(x * 1.44269502162933349609375f);
+    float r = fmaf(-k, 0.693147182464599609375f, x);
+    r = fmaf(-k, -1.904654323148236e-09f, r);
+    float p = 1.98412698e-04f;
+    p = fmaf(p, r, 1.38888892e-03f);
+    p = fmaf(p, r, 8.33333377e-03f);
+    p = fmaf(p, r, 4.16666679e-02f);
+    p = fmaf(p, r, 1.66666672e-01f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    return p * u2f((uint32_t)((int)k + 127) << 23);
+}
+
 GS_HD float gs_logf(float x) {
     if (x != x) return x;
     if (x < 0.0f) return u2f(0x7fc00000u);
@@ -123,6 +142,9 @@ GS_HD float gs_logit(float x) { return -gs_logf(1.0f / x - 1.0f); }
 GS_HD float jl_clamp(float x, float lo, float hi) { return x > hi ? hi : (x < lo ? lo : x); }
 // Julia min(a, b) for floats: NaN if either argument is NaN
 GS_HD float fmin_jl(float a, float b) { return (a != a || b != b) ? a + b : (b < a ? b : a); }
+// fmin_jl(hi, x) for a hi that is not NaN (callers check): a NaN x fails the comparison and
+// stays NaN, every other x gives the same value.
+GS_HD float min_hi(float hi, float x) { return x > hi ? hi : x; }
 
 // float -> int32, saturating, NaN -> 0 (NaN / overflowing boxes become empty)
 GS_HD int32_t sat_i32(float v) {
@@ -173,6 +195,81 @@ __device__ __forceinline__ void tile_pixel(int compact, int tw, int th, int t, i
         lu = t / th;
     }
 }
+
+// Lane groups of a warp for the rasterisers: GS consecutive lanes (GS = 8, 16 or 32) share one
+// rectangle of pixels and walk, in order, only the staged Gaussians whose cull box reaches that
+// rectangle, independently of the warp's other groups. Small Gaussians then cost a smaller
+// share of the warp. With compact tiles a warp covers a 4 (u) x 8 (v) pixel block split into
+// groups of GW x GH pixels (32: 4 x 8, 16: 4 x 4, 8: 2 x 4); otherwise GS is 32 and the warp
+// covers pixel columns (tile_pixel).
+template <int GS>
+struct PixelGroups {
+    static constexpr int GW = GS == 8 ? 2 : 4;
+    static constexpr int GH = GS == 32 ? 8 : 4;
+    static constexpr int NGU = 4 / GW, NGV = 8 / GH, NG = NGU * NGV;
+    static_assert(GS == 8 || GS == 16 || GS == 32, "group size");
+    int group;
+    float r_u0, r_u1, r_v0, r_v1;  // GS == 32: the warp's pixel-centre rectangle
+    float b_u, b_v;                // GS < 32: centre of the warp block's first pixel
+
+    // Pixel (lu, lv), 0-based in the tile, of thread t; GS < 32 needs compact tiles.
+    __device__ __forceinline__ PixelGroups(int compact, int tw, int th, int t, int& lu, int& lv) {
+        const int lane = t & 31;
+        if (GS == 32) {
+            tile_pixel(compact, tw, th, t, lu, lv);
+            group = 0;
+            r_u0 = (float)__reduce_min_sync(0xffffffffu, (unsigned)lu) + 0.5f;
+            r_u1 = (float)__reduce_max_sync(0xffffffffu, (unsigned)lu) + 0.5f;
+            r_v0 = (float)__reduce_min_sync(0xffffffffu, (unsigned)lv) + 0.5f;
+            r_v1 = (float)__reduce_max_sync(0xffffffffu, (unsigned)lv) + 0.5f;
+            b_u = b_v = 0.0f;
+        } else {
+            const int w = t >> 5, bpr = tw >> 2;
+            const int bu = (w % bpr) * 4, bv = (w / bpr) * 8;
+            group = lane / GS;
+            const int i = lane % GS;
+            lu = bu + (group % NGU) * GW + i / GH;
+            lv = bv + (group / NGU) * GH + i % GH;
+            b_u = (float)bu + 0.5f;
+            b_v = (float)bv + 0.5f;
+            r_u0 = r_u1 = r_v0 = r_v1 = 0.0f;
+        }
+    }
+
+    // Ballot of this lane's group: which of the warp's 32 candidate entries (one per lane,
+    // `valid` with box [eu0, eu1] x [ev0, ev1] in tile-local continuous coordinates) overlap
+    // the group's pixel-centre rectangle.
+    __device__ __forceinline__ unsigned relevant(bool valid, float eu0, float eu1, float ev0,
+                                                 float ev1) const {
+        if (GS == 32)
+            return __ballot_sync(0xffffffffu,
+                                 valid && eu1 >= r_u0 && eu0 <= r_u1 && ev1 >= r_v0 && ev0 <= r_v1);
+        bool ou[NGU], ov[NGV];
+#pragma unroll
+        for (int k = 0; k < NGU; ++k) {
+            const float u0 = b_u + (float)(k * GW);
+            ou[k] = eu1 >= u0 && eu0 <= u0 + (float)(GW - 1);
+        }
+#pragma unroll
+        for (int k = 0; k < NGV; ++k) {
+            const float v0 = b_v + (float)(k * GH);
+            ov[k] = ev1 >= v0 && ev0 <= v0 + (float)(GH - 1);
+        }
+        unsigned mine = 0;
+#pragma unroll
+        for (int g = 0; g < NG; ++g) {
+            const unsigned b = __ballot_sync(0xffffffffu, valid && ou[g % NGU] && ov[g / NGU]);
+            if (g == group) mine = b;
+        }
+        return mine;
+    }
+
+    // Iterations a warp needs to walk every group's mask.
+    __device__ __forceinline__ static int iterations(unsigned mask) {
+        if (GS == 32) return __popc(mask);
+        return (int)__reduce_max_sync(0xffffffffu, (unsigned)__popc(mask));
+    }
+};
 
 // Half-widths (rx, ry) of the box, around the mean, outside which a Gaussian with conic
 // (ic11, ic21, ic22) and log-opacity lop has alpha < min_alpha at every point: the

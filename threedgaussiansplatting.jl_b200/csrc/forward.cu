@@ -368,6 +368,9 @@ int check_common(const gs3d_gaussians* g, const gs3d_camera* cam, const gs3d_til
     if (opt->sh_degree < 0 || opt->sh_degree > g->sh_degree)
         return invalid("render SH degree %d with storage degree %d", opt->sh_degree, g->sh_degree);
     if (cam->width <= 0 || cam->height <= 0) return invalid("camera size %dx%d", cam->width, cam->height);
+    if (opt->max_alpha != opt->max_alpha || opt->min_alpha != opt->min_alpha ||
+        opt->min_transmittance != opt->min_transmittance)
+        return invalid("NaN alpha / transmittance threshold in the render options");
     if (til->tile_width <= 0 || til->tile_height <= 0 ||
         til->tile_width * til->tile_height > 512 || (til->tile_width * til->tile_height) % 32 != 0)
         return invalid("tile %dx%d (need a multiple of 32 and <= 512 pixels)", til->tile_width,

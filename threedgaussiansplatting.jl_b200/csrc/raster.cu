@@ -8,10 +8,11 @@
 // T (1 - alpha) < min_transmittance.
 //
 // Work saved without changing any pixel's result:
-//   * warps cover compact 4 x 8 pixel blocks (when the tile allows; otherwise pixel columns),
-//     and each warp first tests 32 staged entries at once against its block with the entry's
-//     alpha >= min_alpha ellipse box (inflated by a safety margin), then evaluates only the
-//     entries that can reach one of its pixels, in order;
+//   * warps cover compact 4 x 8 pixel blocks (when the tile allows; otherwise pixel columns)
+//     made of two 16-lane groups of 4 x 4 pixels (PixelGroups); 32 staged entries at a time
+//     are tested against each group's block with the entry's alpha >= min_alpha ellipse box
+//     (inflated by a safety margin), and each group then evaluates, in order, only the
+//     entries that can reach one of its pixels;
 //   * q below log(min_alpha) - 0.01 skips the exponential (exp(q) < min_alpha there);
 //   * the CTA leaves once every pixel has stopped (__syncthreads_count).
 // A CTA reads F and D from device memory and draws the void image itself when there is
@@ -41,6 +42,7 @@ struct RasterArgs {
     float min_alpha, max_alpha, min_T, q_skip, log_min_alpha;
 };
 
+template <int GS>
 __global__ void __launch_bounds__(512) k_raster(const RasterArgs a) {
     extern __shared__ __align__(16) float4 sm4[];
     const int nthr = blockDim.x;
@@ -52,7 +54,7 @@ __global__ void __launch_bounds__(512) k_raster(const RasterArgs a) {
     const int t = threadIdx.x;
     const int lane = t & 31;
     int lu, lv;  // 0-based pixel in tile
-    tile_pixel(a.compact, a.tile_w, a.tile_h, t, lu, lv);
+    const PixelGroups<GS> pg(a.compact, a.tile_w, a.tile_h, t, lu, lv);
     const int txi = blockIdx.x, tyi = blockIdx.y;
     const int u0 = txi * a.tile_w, v0 = tyi * a.tile_h;
     const int U = u0 + lu + 1, V = v0 + lv + 1;
@@ -74,12 +76,6 @@ __global__ void __launch_bounds__(512) k_raster(const RasterArgs a) {
     const int tile = txi + tyi * a.tiles_x + 1;  // 1-based linear, x-contiguous
     const int start = tile == 1 ? 0 : a.tiles_end[tile - 2];
     const int end = a.tiles_end[tile - 1];
-
-    // the warp's pixel-centre rectangle in tile-local continuous coordinates
-    const float wu0 = (float)__reduce_min_sync(0xffffffffu, (unsigned)lu) + 0.5f;
-    const float wu1 = (float)__reduce_max_sync(0xffffffffu, (unsigned)lu) + 0.5f;
-    const float wv0 = (float)__reduce_min_sync(0xffffffffu, (unsigned)lv) + 0.5f;
-    const float wv1 = (float)__reduce_max_sync(0xffffffffu, (unsigned)lv) + 0.5f;
 
     const float cu = (float)(lu + 1) - 0.5f, cv = (float)(lv + 1) - 0.5f;
     const float uu = cu * cu, uv = cu * cv, vv = cv * cv;
@@ -113,14 +109,18 @@ __global__ void __launch_bounds__(512) k_raster(const RasterArgs a) {
             const int nb = min(nthr, end - base);
             for (int ch = 0; ch < nb; ch += 32) {
                 const int j = ch + lane;
-                bool rel = false;
-                if (j < nb) {
+                const bool valid = j < nb;
+                float eu0 = 0.0f, eu1 = 0.0f, ev0 = 0.0f, ev1 = 0.0f;
+                if (valid) {
                     const float4 C = sC[j];
                     const float2 R = sR[j];
-                    rel = C.z + R.x >= wu0 && C.z - R.x <= wu1 && C.w + R.y >= wv0 && C.w - R.y <= wv1;
+                    eu0 = C.z - R.x; eu1 = C.z + R.x;
+                    ev0 = C.w - R.y; ev1 = C.w + R.y;
                 }
-                unsigned mask = __ballot_sync(0xffffffffu, rel);
-                while (mask) {
+                unsigned mask = pg.relevant(valid, eu0, eu1, ev0, ev1);
+                const int iters = PixelGroups<GS>::iterations(mask);
+                for (int it = 0; it < iters; ++it) {
+                    if (!mask) continue;
                     const int jj = ch + __ffs(mask) - 1;
                     mask &= mask - 1;
                     if (done) continue;
@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(512) k_raster(const RasterArgs a) {
                     const float4 B = sB[jj];
                     const float q = A.x * uu + A.y * vv + A.z * uv + A.w * cu + B.x * cv + B.y;
                     if (q < a.q_skip) continue;
-                    const float alpha = fmin_jl(a.max_alpha, gs_expf(q));
+                    const float alpha = min_hi(a.max_alpha, gs_expf_blend(q));
                     if (alpha < a.min_alpha) continue;
                     const float nT = T * (1.0f - alpha);
                     if (nT < a.min_T) { done = true; continue; }
@@ -191,7 +191,10 @@ int launch_raster(const gs3d_render_outputs& out, const gs3d_camera& cam, const 
     const int nthr = til.tile_width * til.tile_height;
     const size_t smem = (size_t)nthr * (3 * sizeof(float4) + sizeof(float2));
     dim3 grid(til.nb_tiles_x, til.nb_tiles_y);
-    k_raster<<<grid, nthr, smem, stream>>>(a);
+    // Compact tiles: 16-lane groups (4 x 4 pixels), measured fastest on the 1080p training
+    // workload (8 lanes: equal, 32: 6% slower); other tiles: whole warps over pixel columns.
+    if (a.compact) k_raster<16><<<grid, nthr, smem, stream>>>(a);
+    else k_raster<32><<<grid, nthr, smem, stream>>>(a);
     GS3D_LAUNCHED("k_raster");
     return GS3D_OK;
 }

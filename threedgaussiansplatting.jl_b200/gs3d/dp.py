@@ -50,6 +50,9 @@ class DataParallelTrainer(Trainer):
     def current_camera_index(self) -> int:
         return view_index(self.step_index, self.rank, self.world, self.perm, len(self.cameras))
 
+    def peek_camera_index(self, ahead: int) -> int:
+        return view_index(self.step_index + ahead, self.rank, self.world, self.perm, len(self.cameras))
+
     def training_step(self) -> torch.Tensor:
         lib = _abi.lib()
         self.iteration_nb += 1
@@ -59,7 +62,11 @@ class DataParallelTrainer(Trainer):
         rb = self.render_buffers
         render(self.render_outputs, self.gaussians, cam, self.tiling, self.render_options, rb,
                host_sync=self.render_host_sync)
-        loss = self.loss(self.render_outputs.rgb, self.target_for(idx), self.rgb_image_grad)
+        gt = self.target_for(idx)
+        loss = self.loss(self.render_outputs.rgb, gt, self.rgb_image_grad)
+        if gt is self._gt_buffers[self._gt_slot]:
+            self._gt_free[self._gt_slot].record(torch.cuda.current_stream(self.device))
+        self.prefetch_target()
         backward(self.fgradients, self.rgb_image_grad, self.render_outputs, self.gaussians, cam,
                  self.tiling, self.render_options, rb)
         o = self.options

@@ -103,7 +103,15 @@ class Trainer:
         self.render_buffers = RenderBuffers.create(gaussians.n, tiling.nb_tiles, dev, capacity_dup=capacity_dup)
         self.render_outputs = RenderOutputs.create(self.width, self.height, dev)
         self.rgb_image_grad = torch.empty((self.width, self.height, 3), dtype=torch.float32, device=dev)
-        self.gt_buffer = torch.empty((self.width, self.height, 3), dtype=torch.float32, device=dev)
+        # host targets: two device buffers, filled on a copy stream one step ahead
+        self._gt_buffers = [torch.empty((self.width, self.height, 3), dtype=torch.float32, device=dev)
+                            for _ in range(2)]
+        self._gt_ready = [torch.cuda.Event() for _ in range(2)] if dev.type == "cuda" else None
+        self._gt_free = [torch.cuda.Event() for _ in range(2)] if dev.type == "cuda" else None
+        self._gt_slot = 0
+        self._prefetched = None
+        self._copy_stream = None
+        self._next_orders = []
         self.loss = LossComputer(self.width, self.height, dev, options.loss_dssim_vs_L1_weight)
         self.fgradients = FilteredGaussiansGradients.create(gaussians.n, gaussians.sh_degree, dev)
         self.optimizer = AdamOptimizer(gaussians, options.learning_rates())
@@ -177,19 +185,68 @@ class Trainer:
 
     # -- one iteration (training.jl:173-244) -----------------------------------------------
     def target_for(self, idx: int) -> torch.Tensor:
+        """Device copy of camera idx's target. Host targets are uploaded on a side stream one
+        step ahead (prefetch_target), into one of two device buffers, so the copy overlaps the
+        previous step's kernels; a target that was not prefetched is copied here."""
         t = self.targets[idx]
-        if t.device != self.device:
-            self.gt_buffer.copy_(t, non_blocking=True)
-            return self.gt_buffer
-        return t
+        if t.device == self.device:
+            return t
+        stream = torch.cuda.current_stream(self.device)
+        pf = self._prefetched
+        if pf is not None and pf[0] == idx and pf[1] is t:
+            _, _, slot = pf
+            stream.wait_event(self._gt_ready[slot])
+        else:
+            slot = self._gt_slot ^ 1
+            stream.wait_event(self._gt_free[slot])
+            self._gt_buffers[slot].copy_(t, non_blocking=True)
+        self._prefetched = None
+        self._gt_slot = slot
+        return self._gt_buffers[slot]
+
+    def advance_camera(self) -> None:
+        """Next camera of the shuffled order, re-shuffled after every pass over the cameras
+        (training.jl:174-178)."""
+        self.cameras_order_idx += 1
+        if self.cameras_order_idx >= len(self.cameras_order):
+            self.cameras_order = (self._next_orders.pop(0) if self._next_orders
+                                  else self.rng.permutation(len(self.cameras)))
+            self.cameras_order_idx = 0
+
+    def peek_camera_index(self, ahead: int) -> int:
+        """Camera of the step `ahead` steps after the current one (drawing the coming
+        permutations from the same generator, in the same order, as training_step would)."""
+        pos = self.cameras_order_idx + ahead
+        order = self.cameras_order
+        k = 0
+        while pos >= len(order):
+            pos -= len(order)
+            if k == len(self._next_orders):
+                self._next_orders.append(self.rng.permutation(len(self.cameras)))
+            order = self._next_orders[k]
+            k += 1
+        return int(order[pos])
+
+    def prefetch_target(self) -> None:
+        """Start the upload of the next step's host target on the copy stream."""
+        idx = self.peek_camera_index(1)
+        t = self.targets[idx]
+        if t.device == self.device:
+            return
+        slot = self._gt_slot ^ 1
+        if self._copy_stream is None:
+            self._copy_stream = torch.cuda.Stream(self.device)
+        cs = self._copy_stream
+        cs.wait_event(self._gt_free[slot])
+        with torch.cuda.stream(cs):
+            self._gt_buffers[slot].copy_(t, non_blocking=True)
+            self._gt_ready[slot].record(cs)
+        self._prefetched = (idx, t, slot)
 
     def training_step(self) -> torch.Tensor:
         """One iteration; returns the device tensor [loss, L1, DSSIM, -] (no host sync)."""
         self.iteration_nb += 1
-        self.cameras_order_idx += 1
-        if self.cameras_order_idx >= len(self.cameras_order):
-            self.cameras_order = self.rng.permutation(len(self.cameras))
-            self.cameras_order_idx = 0
+        self.advance_camera()
         self.maybe_increase_sh_degree()
         idx = self.current_camera_index()
         cam = self.cameras[idx]
@@ -198,6 +255,9 @@ class Trainer:
                host_sync=self.render_host_sync)
         gt = self.target_for(idx)
         loss = self.loss(self.render_outputs.rgb, gt, self.rgb_image_grad)
+        if gt is self._gt_buffers[self._gt_slot]:
+            self._gt_free[self._gt_slot].record(torch.cuda.current_stream(self.device))
+        self.prefetch_target()
         backward(self.fgradients, self.rgb_image_grad, self.render_outputs, self.gaussians, cam,
                  self.tiling, self.render_options, rb)
         in_adc = self.maybe_densify_and_prune()
