@@ -15,7 +15,8 @@ from oracle import oracle as O
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("w,h,weight", [(64, 48, 0.2), (256, 256, 0.2), (333, 171, 0.5), (100, 80, 0.0)])
+@pytest.mark.parametrize("w,h,weight", [(64, 48, 0.2), (256, 256, 0.2), (333, 171, 0.5), (100, 80, 0.0),
+                                        (1920, 1080, 0.2), (9, 7, 0.2)])
 def test_loss_matches_oracle(cuda, w, h, weight):
     rng = np.random.default_rng(w * h)
     K = rng.uniform(0, 1, (w, h, 3)).astype(np.float32)

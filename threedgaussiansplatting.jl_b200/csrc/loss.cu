@@ -9,6 +9,12 @@
 // i.e. three more zero-padded blurs of per-pixel partials (the window is symmetric).
 // Two tiled kernels (forward maps + partials; backward blurs + gradient) and a fixed-order
 // final reduction, so the loss value is deterministic.
+//
+// Both kernels stage a 16 (u) x 32 (v) tile with its 5-pixel halo in shared memory (all three
+// channels at once, read as the contiguous runs of the interleaved images) and blur with
+// sliding windows held in registers: a thread makes 4 consecutive outputs of the vertical pass
+// from 14 staged inputs, and 2 consecutive outputs of the horizontal pass from 12, every tap a
+// fused multiply-add.
 #include <cmath>
 
 #include "common.cuh"
@@ -23,6 +29,11 @@ constexpr int HALO = 5;
 constexpr int RV = TV + 2 * HALO; // 42
 constexpr int RU = TU + 2 * HALO; // 26
 constexpr int LT = 256;           // threads
+constexpr int RVP = RV + 1;       // padded staged row: the warp's 4 columns x 8 runs hit distinct banks
+constexpr int TVP = TV + 1;       // padded row of the vertical pass's output
+constexpr int VR = 4;             // vertical-pass outputs per thread
+constexpr int UR = 2;             // horizontal-pass outputs per thread
+static_assert(RU * (TV / VR) <= LT && TV * (TU / UR) == LT, "pass work must fit one round");
 
 struct LossArgs {
     const float* K;   // 3 x h x w  (index 3 (v + h u) + c)
@@ -37,71 +48,123 @@ struct LossArgs {
     double invN;
 };
 
-__global__ void __launch_bounds__(LT) k_ssim_forward(const LossArgs a) {
-    __shared__ float sx[RU][RV];
-    __shared__ float sy[RU][RV];
-    __shared__ float tmp[5][RU][TV];
+// Stage the (RU x RV) halo region of the interleaved images K and I, all three channels, into
+// sx / sy [c][uu][vv], zero outside the image. Every load of a thread is issued before its
+// first shared-memory store, so each thread keeps 2 NST loads in flight.
+constexpr int NST = (RU * 3 * RV + LT - 1) / LT;
+
+__device__ __forceinline__ void stage_rgb2(const float* __restrict__ K, const float* __restrict__ I,
+                                           float (*sx)[RU][RVP], float (*sy)[RU][RVP], int u0,
+                                           int v0, int W, int H) {
+    float xk[NST], yk[NST];
+#pragma unroll
+    for (int k = 0; k < NST; ++k) {
+        const int i = threadIdx.x + k * LT;
+        const int uu = i / (3 * RV);
+        const int r = i - uu * (3 * RV);
+        const int vv = r / 3, c = r - 3 * vv;
+        const int u = u0 + uu - HALO, v = v0 + vv - HALO;
+        const bool in = i < RU * 3 * RV && u >= 0 && u < W && v >= 0 && v < H;
+        const size_t p = in ? 3 * ((size_t)v + (size_t)H * u) + c : 0;
+        xk[k] = in ? __ldg(K + p) : 0.0f;
+        yk[k] = in ? __ldg(I + p) : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < NST; ++k) {
+        const int i = threadIdx.x + k * LT;
+        if (i >= RU * 3 * RV) continue;
+        const int uu = i / (3 * RV);
+        const int r = i - uu * (3 * RV);
+        const int vv = r / 3, c = r - 3 * vv;
+        sx[c][uu][vv] = xk[k];
+        sy[c][uu][vv] = yk[k];
+    }
+}
+
+__global__ void __launch_bounds__(LT, 4) k_ssim_forward(const LossArgs a) {
+    __shared__ float sx[3][RU][RVP];
+    __shared__ float sy[3][RU][RVP];
+    __shared__ float tmp[5][RU][TVP];
     __shared__ float red[LT / 32];
     const int u0 = blockIdx.x * TU, v0 = blockIdx.y * TV;
     const int t = threadIdx.x;
-    float ssim_acc = 0.0f;
     const size_t plane = (size_t)a.W * a.H;
+    stage_rgb2(a.K, a.I, sx, sy, u0, v0, a.W, a.H);
+    float ssim_acc = 0.0f;
     for (int c = 0; c < 3; ++c) {
-        __syncthreads();
-        for (int i = t; i < RU * RV; i += LT) {
-            const int uu = i / RV, vv = i % RV;
-            const int u = u0 + uu - HALO, v = v0 + vv - HALO;
-            float x = 0.0f, y = 0.0f;
-            if (u >= 0 && u < a.W && v >= 0 && v < a.H) {
-                const size_t p = 3 * ((size_t)v + (size_t)a.H * u) + c;
-                x = a.K[p];
-                y = a.I[p];
+        __syncthreads();  // staging done / previous channel's tmp consumed
+        if (t < RU * (TV / VR)) {  // vertical pass: column uu, rows vo .. vo + VR - 1
+            const int uu = t / (TV / VR), vo = (t % (TV / VR)) * VR;
+            float acc[5][VR];
+#pragma unroll
+            for (int m = 0; m < 5; ++m)
+#pragma unroll
+                for (int o = 0; o < VR; ++o) acc[m][o] = 0.0f;
+#pragma unroll
+            for (int j = 0; j < VR + 10; ++j) {
+                const float x = sx[c][uu][vo + j], y = sy[c][uu][vo + j];
+                const float xx = x * x, yy = y * y, xy = x * y;
+#pragma unroll
+                for (int o = 0; o < VR; ++o) {
+                    const int k = j - o;
+                    if (k < 0 || k > 10) continue;
+                    const float wk = a.win[k];
+                    acc[0][o] = fmaf(wk, x, acc[0][o]);
+                    acc[1][o] = fmaf(wk, y, acc[1][o]);
+                    acc[2][o] = fmaf(wk, xx, acc[2][o]);
+                    acc[3][o] = fmaf(wk, yy, acc[3][o]);
+                    acc[4][o] = fmaf(wk, xy, acc[4][o]);
+                }
             }
-            sx[uu][vv] = x;
-            sy[uu][vv] = y;
+#pragma unroll
+            for (int m = 0; m < 5; ++m)
+#pragma unroll
+                for (int o = 0; o < VR; ++o) tmp[m][uu][vo + o] = acc[m][o];
         }
         __syncthreads();
-        for (int i = t; i < RU * TV; i += LT) {  // blur along v
-            const int uu = i / TV, v = i % TV;
-            float m0 = 0.f, m1 = 0.f, m2 = 0.f, m3 = 0.f, m4 = 0.f;
+        {  // horizontal pass: row v, columns uo .. uo + UR - 1; SSIM and its partials
+            const int v = t % TV, uo = (t / TV) * UR;
+            float acc[5][UR];
 #pragma unroll
-            for (int k = 0; k < 11; ++k) {
-                const float x = sx[uu][v + k], y = sy[uu][v + k], wk = a.win[k];
-                m0 += wk * x;
-                m1 += wk * y;
-                m2 += wk * (x * x);
-                m3 += wk * (y * y);
-                m4 += wk * (x * y);
-            }
-            tmp[0][uu][v] = m0; tmp[1][uu][v] = m1; tmp[2][uu][v] = m2;
-            tmp[3][uu][v] = m3; tmp[4][uu][v] = m4;
-        }
-        __syncthreads();
-        for (int i = t; i < TU * TV; i += LT) {  // blur along u, SSIM and partials
-            const int uu = i / TV, v = i % TV;
-            const int u = u0 + uu, vg = v0 + v;
-            if (u >= a.W || vg >= a.H) continue;
-            float ux = 0.f, uy = 0.f, exx = 0.f, eyy = 0.f, exy = 0.f;
+            for (int m = 0; m < 5; ++m)
 #pragma unroll
-            for (int k = 0; k < 11; ++k) {
-                const float wk = a.win[k];
-                ux += wk * tmp[0][uu + k][v];
-                uy += wk * tmp[1][uu + k][v];
-                exx += wk * tmp[2][uu + k][v];
-                eyy += wk * tmp[3][uu + k][v];
-                exy += wk * tmp[4][uu + k][v];
+                for (int o = 0; o < UR; ++o) acc[m][o] = 0.0f;
+#pragma unroll
+            for (int j = 0; j < UR + 10; ++j) {
+                float q[5];
+#pragma unroll
+                for (int m = 0; m < 5; ++m) q[m] = tmp[m][uo + j][v];
+#pragma unroll
+                for (int o = 0; o < UR; ++o) {
+                    const int k = j - o;
+                    if (k < 0 || k > 10) continue;
+                    const float wk = a.win[k];
+#pragma unroll
+                    for (int m = 0; m < 5; ++m) acc[m][o] = fmaf(wk, q[m], acc[m][o]);
+                }
             }
-            const float C1 = 0.0001f, C2 = 0.0009f;
-            const float vx = exx - ux * ux, vy = eyy - uy * uy, vxy = exy - ux * uy;
-            const float A1 = 2.0f * ux * uy + C1, A2 = 2.0f * vxy + C2;
-            const float B1 = ux * ux + uy * uy + C1, B2 = vx + vy + C2;
-            const float iB = 1.0f / (B1 * B2);
-            const float S = A1 * A2 * iB;
-            ssim_acc += S;
-            const size_t pp = (size_t)vg + (size_t)a.H * u;
-            a.dmaps[(0 * 3 + c) * plane + pp] = 2.0f * uy * (A2 - A1) * iB - 2.0f * ux * S * (1.0f / B1 - 1.0f / B2);
-            a.dmaps[(1 * 3 + c) * plane + pp] = -S / B2;
-            a.dmaps[(2 * 3 + c) * plane + pp] = 2.0f * A1 * iB;
+            const int vg = v0 + v;
+#pragma unroll
+            for (int o = 0; o < UR; ++o) {
+                const int u = u0 + uo + o;
+                if (u >= a.W || vg >= a.H) continue;
+                const float ux = acc[0][o], uy = acc[1][o];
+                const float C1 = 0.0001f, C2 = 0.0009f;
+                const float vx = fmaf(-ux, ux, acc[2][o]), vy = fmaf(-uy, uy, acc[3][o]);
+                const float vxy = fmaf(-ux, uy, acc[4][o]);
+                const float A1 = fmaf(2.0f * ux, uy, C1), A2 = fmaf(2.0f, vxy, C2);
+                const float B1 = fmaf(ux, ux, fmaf(uy, uy, C1)), B2 = vx + vy + C2;
+                const float iB = 1.0f / (B1 * B2);
+                const float S = A1 * A2 * iB;
+                ssim_acc += S;
+                // dS/dmu_x = 2 uy (A2 - A1) / (B1 B2) - 2 ux S (1/B1 - 1/B2),
+                // dS/dE[x^2] = -S / B2, dS/dE[xy] = 2 A1 / (B1 B2)
+                const size_t pp = (size_t)vg + (size_t)a.H * u;
+                a.dmaps[(0 * 3 + c) * plane + pp] =
+                    2.0f * iB * fmaf(uy, A2 - A1, -ux * S * (B2 - B1));
+                a.dmaps[(1 * 3 + c) * plane + pp] = -S * B1 * iB;
+                a.dmaps[(2 * 3 + c) * plane + pp] = 2.0f * A1 * iB;
+            }
         }
     }
 #pragma unroll
@@ -115,56 +178,108 @@ __global__ void __launch_bounds__(LT) k_ssim_forward(const LossArgs a) {
     }
 }
 
-__global__ void __launch_bounds__(LT) k_ssim_backward(const LossArgs a) {
-    __shared__ float sd[3][RU][RV];
-    __shared__ float tmp[3][RU][TV];
+__global__ void __launch_bounds__(LT, 4) k_ssim_backward(const LossArgs a) {
+    __shared__ float sd[3][RU][RVP];
+    __shared__ float tmp[3][RU][TVP];
     __shared__ float red[LT / 32];
     const int u0 = blockIdx.x * TU, v0 = blockIdx.y * TV;
     const int t = threadIdx.x;
     const size_t plane = (size_t)a.W * a.H;
+    const int v = t % TV, uo = (t / TV) * UR;  // this thread's horizontal-pass outputs
+    const int vg = v0 + v;
     float l1_acc = 0.0f;
+    const float ginv = (float)a.invN;
     for (int c = 0; c < 3; ++c) {
-        __syncthreads();
-        for (int i = t; i < RU * RV; i += LT) {
-            const int uu = i / RV, vv = i % RV;
-            const int u = u0 + uu - HALO, v = v0 + vv - HALO;
-            const bool in = u >= 0 && u < a.W && v >= 0 && v < a.H;
-            const size_t pp = (size_t)v + (size_t)a.H * u;
+        // K and I of this channel at the thread's output pixels, loaded ahead of the blurs
+        float xs[UR], ys[UR];
 #pragma unroll
-            for (int m = 0; m < 3; ++m) sd[m][uu][vv] = in ? a.dmaps[(m * 3 + c) * plane + pp] : 0.0f;
+        for (int o = 0; o < UR; ++o) {
+            const int u = u0 + uo + o;
+            const bool in = u < a.W && vg < a.H;
+            const size_t p = in ? 3 * ((size_t)vg + (size_t)a.H * u) + c : 0;
+            xs[o] = in ? __ldg(a.K + p) : 0.0f;
+            ys[o] = in ? __ldg(a.I + p) : 0.0f;
         }
-        __syncthreads();
-        for (int i = t; i < RU * TV; i += LT) {
-            const int uu = i / TV, v = i % TV;
-            float m0 = 0.f, m1 = 0.f, m2 = 0.f;
+        __syncthreads();  // previous channel's sd / tmp consumed
+        {  // the three partial maps of channel c, all loads of a thread in flight together
+            float d[NST];
 #pragma unroll
-            for (int k = 0; k < 11; ++k) {
-                const float wk = a.win[k];
-                m0 += wk * sd[0][uu][v + k];
-                m1 += wk * sd[1][uu][v + k];
-                m2 += wk * sd[2][uu][v + k];
+            for (int k = 0; k < NST; ++k) {
+                const int i = t + k * LT;
+                const int m = i / (RU * RV);
+                const int r = i - m * (RU * RV);
+                const int uu = r / RV, vv = r - RV * uu;
+                const int u = u0 + uu - HALO, vs = v0 + vv - HALO;
+                const bool in = i < 3 * RU * RV && u >= 0 && u < a.W && vs >= 0 && vs < a.H;
+                d[k] = in ? __ldg(a.dmaps + (m * 3 + c) * plane + (size_t)vs + (size_t)a.H * u)
+                          : 0.0f;
             }
-            tmp[0][uu][v] = m0; tmp[1][uu][v] = m1; tmp[2][uu][v] = m2;
+#pragma unroll
+            for (int k = 0; k < NST; ++k) {
+                const int i = t + k * LT;
+                if (i >= 3 * RU * RV) continue;
+                const int m = i / (RU * RV);
+                const int r = i - m * (RU * RV);
+                const int uu = r / RV, vv = r - RV * uu;
+                sd[m][uu][vv] = d[k];
+            }
         }
         __syncthreads();
-        for (int i = t; i < TU * TV; i += LT) {
-            const int uu = i / TV, v = i % TV;
-            const int u = u0 + uu, vg = v0 + v;
+        if (t < RU * (TV / VR)) {  // vertical pass
+            const int uu = t / (TV / VR), vo = (t % (TV / VR)) * VR;
+            float acc[3][VR];
+#pragma unroll
+            for (int m = 0; m < 3; ++m)
+#pragma unroll
+                for (int o = 0; o < VR; ++o) acc[m][o] = 0.0f;
+#pragma unroll
+            for (int j = 0; j < VR + 10; ++j) {
+                float q[3];
+#pragma unroll
+                for (int m = 0; m < 3; ++m) q[m] = sd[m][uu][vo + j];
+#pragma unroll
+                for (int o = 0; o < VR; ++o) {
+                    const int k = j - o;
+                    if (k < 0 || k > 10) continue;
+                    const float wk = a.win[k];
+#pragma unroll
+                    for (int m = 0; m < 3; ++m) acc[m][o] = fmaf(wk, q[m], acc[m][o]);
+                }
+            }
+#pragma unroll
+            for (int m = 0; m < 3; ++m)
+#pragma unroll
+                for (int o = 0; o < VR; ++o) tmp[m][uu][vo + o] = acc[m][o];
+        }
+        __syncthreads();
+        float acc[3][UR];
+#pragma unroll
+        for (int m = 0; m < 3; ++m)
+#pragma unroll
+            for (int o = 0; o < UR; ++o) acc[m][o] = 0.0f;
+#pragma unroll
+        for (int j = 0; j < UR + 10; ++j) {  // horizontal pass
+            float q[3];
+#pragma unroll
+            for (int m = 0; m < 3; ++m) q[m] = tmp[m][uo + j][v];
+#pragma unroll
+            for (int o = 0; o < UR; ++o) {
+                const int k = j - o;
+                if (k < 0 || k > 10) continue;
+                const float wk = a.win[k];
+#pragma unroll
+                for (int m = 0; m < 3; ++m) acc[m][o] = fmaf(wk, q[m], acc[m][o]);
+            }
+        }
+        // dL/dK(p) of this channel: L1 part + weight * (-(b0 + 2 K(p) b1 + I(p) b2) / N)
+#pragma unroll
+        for (int o = 0; o < UR; ++o) {
+            const int u = u0 + uo + o;
             if (u >= a.W || vg >= a.H) continue;
-            float b0 = 0.f, b1 = 0.f, b2 = 0.f;
-#pragma unroll
-            for (int k = 0; k < 11; ++k) {
-                const float wk = a.win[k];
-                b0 += wk * tmp[0][uu + k][v];
-                b1 += wk * tmp[1][uu + k][v];
-                b2 += wk * tmp[2][uu + k][v];
-            }
-            const size_t p = 3 * ((size_t)vg + (size_t)a.H * u) + c;
-            const float x = a.K[p], y = a.I[p];
-            const float dS = b0 + 2.0f * x * b1 + y * b2;
-            const float gd = -dS * (float)a.invN;
+            const float x = xs[o], y = ys[o];
+            const float dS = fmaf(2.0f * x, acc[1][o], fmaf(y, acc[2][o], acc[0][o]));
             const float gl = x > y ? a.l1w : -a.l1w;
-            a.grad[p] = gl + a.weight * gd;
+            a.grad[3 * ((size_t)vg + (size_t)a.H * u) + c] = fmaf(a.weight, -dS * ginv, gl);
             l1_acc += fabsf(x - y);
         }
     }
