@@ -2,7 +2,10 @@
 //   k_zero_2d        zero_2d_grads! over the F filtered Gaussians (backward_structs.jl:250-257)
 //   k_bwd_raster     backward_render_tiles_kernel! (backward_core.jl:96-293): per pixel, back to
 //                    front from its last contributor, T recovered by division by (1 - alpha),
-//                    the reference's per-pair gradient formulas and order. The 9 per-pair
+//                    the reference's per-pair gradient formulas (contracted into fused
+//                    multiply-adds, with the fast exponential and reciprocal intrinsics: the
+//                    gradients are float-atomic sums, compared within a tolerance, and the
+//                    set of pairs taken is decided exactly). The 9 per-pair
 //                    gradients are summed across the warp with register shuffles before one
 //                    lane issues the atomics (the reference issues 9 atomics per pixel-pair;
 //                    its TODO at backward_core.jl:282).
@@ -192,28 +195,37 @@ __global__ void __launch_bounds__(512) k_bwd_raster(const BwdArgs a) {
                     const float4 Cc = sC[jj];
                     const float du = cpu - A.x, dv = cpv - A.y;
                     const float ic11 = A.w, ic21 = B.x, ic22 = B.y;
-                    const float q = -0.5f * (ic11 * (du * du) + ic22 * (dv * dv)) - ic21 * du * dv;
+                    const float du2 = du * du, dv2 = dv * dv, duv = du * dv;
+                    const float q = fmaf(-0.5f, fmaf(ic11, du2, ic22 * dv2), -ic21 * duv);
                     if (q >= Cc.y) {
-                        const float ge = gs_expf_blend(q);
-                        const float alpha = min_hi(a.max_alpha, A.z * ge);
+                        // __expf (within 8 ulp for |q| < 6); where alpha falls within 4e-6
+                        // (relative) of min_alpha the exact exponential decides, so the
+                        // pairs taken are those the forward blended
+                        float ge = __expf(q);
+                        float alpha = min_hi(a.max_alpha, A.z * ge);
+                        if (fabsf(alpha - a.min_alpha) <= 4e-6f * a.min_alpha) {
+                            ge = gs_expf_blend(q);
+                            alpha = min_hi(a.max_alpha, A.z * ge);
+                        }
                         if (alpha >= a.min_alpha) {
                             contrib = true;
-                            const float inv1m = 1.0f / (1.0f - alpha);
+                            const float inv1m = __fdividef(1.0f, 1.0f - alpha);
                             T *= inv1m;
                             const float tc0 = T * B.z, tc1 = T * B.w, tc2 = T * Cc.x;
-                            p0 += alpha * tc0;
-                            p1 += alpha * tc1;
-                            p2 += alpha * tc2;
-                            const float ag = inv1m * (g0 * (tc0 - p0) + g1 * (tc1 - p1) + g2 * (tc2 - p2));
+                            p0 = fmaf(alpha, tc0, p0);
+                            p1 = fmaf(alpha, tc1, p1);
+                            p2 = fmaf(alpha, tc2, p2);
+                            const float ag =
+                                inv1m * fmaf(g0, tc0 - p0, fmaf(g1, tc1 - p1, g2 * (tc2 - p2)));
                             const float aga = alpha * ag;
                             const float sc = -0.5f * aga;
-                            const float g21 = sc * (dv * du);
-                            v[0] = aga * (du * ic11 + dv * ic21);
-                            v[1] = aga * (du * ic21 + dv * ic22);
+                            const float g21 = sc * duv;
+                            v[0] = aga * fmaf(du, ic11, dv * ic21);
+                            v[1] = aga * fmaf(du, ic21, dv * ic22);
                             v[2] = ge * ag;
-                            v[3] = sc * (du * du);
+                            v[3] = sc * du2;
                             v[4] = g21 + g21;
-                            v[5] = sc * (dv * dv);
+                            v[5] = sc * dv2;
                             const float ta = T * alpha;
                             v[6] = ta * g0;
                             v[7] = ta * g1;
