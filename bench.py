@@ -295,7 +295,10 @@ def main() -> None:
     F, D = (int(x) for x in trainer.render_buffers.device_counts[:2].cpu())
 
     # ---- device-timed throughput, inputs resident in HBM ------------------------------
-    clocks = ClockSampler(local if "CUDA_VISIBLE_DEVICES" not in os.environ else local)
+    # nvidia-smi numbers GPUs physically: map this rank's device through CUDA_VISIBLE_DEVICES
+    visible = [v.strip() for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+    smi_index = visible[local] if local < len(visible) and visible[local].isdigit() else str(local)
+    clocks = ClockSampler(smi_index)
     _abi.profile_enable(True)
     if world > 1:
         dist.barrier()
