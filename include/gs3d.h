@@ -263,11 +263,27 @@ GS3D_API int gs3d_adam_step(
 
 /* ---- multi-view data parallelism (no counterpart in the reference: it trains one view at a
  * time on one GPU, training.jl:173-244). A dense gradient row of 60 floats per Gaussian:
- * mean(3) opacity feature(1) scaling features(3) rotation features(4) SH (3 x 16,
- * channel-major) touched(1). Rows from several views/ranks are summed (NCCL all-reduce), then
- * gs3d_adam_step_dense applies the update! scalar rule to every touched Gaussian; with one view
- * it equals gs3d_adam_step. */
+ * SH (3 x 16, channel-major; 16-byte aligned) at 0, mean(3) at 48, opacity feature(1) at 51,
+ * scaling features(3) at 52, rotation features(4) at 55, touched(1) at 59. Rows from several
+ * views/ranks are summed (NCCL), then gs3d_adam_step_dense applies the update! scalar rule to
+ * every touched Gaussian; with one view it equals gs3d_adam_step. */
 #define GS3D_DENSE_ROW 60
+
+/* gs3d_backward with the 3D gradients written straight into dense rows (n rows, zeroed here,
+ * touched flags set) instead of the F-compact 3D arrays of fgradients, which may be NULL; the
+ * 2D arrays are filled as by gs3d_backward. */
+GS3D_API int gs3d_backward_dense(
+    const gs3d_fgradients* fgradients, const float* rgb_image_grad,
+    const gs3d_render_outputs* outputs, const gs3d_gaussians* gaussians,
+    const gs3d_camera* camera, const gs3d_tiling* tiling,
+    const gs3d_render_options* options, const gs3d_render_buffers* buffers,
+    uint32_t flags, float* dense, int32_t n, gs3d_stream_t stream);
+
+/* gs3d_adam_step_dense over the Gaussians [g_begin, g_end) only, whose rows start at dense[0]
+ * (a rank's shard of reduce-scattered rows). */
+GS3D_API int gs3d_adam_step_dense_range(
+    const gs3d_gaussians* gaussians, const gs3d_adam_moments* moments, const float* dense,
+    int32_t g_begin, int32_t g_end, const gs3d_adam_params* params, gs3d_stream_t stream);
 
 /* Zero dense (n rows) and scatter the F-compact gradients of one view into it. */
 GS3D_API int gs3d_scatter_dense_grads(

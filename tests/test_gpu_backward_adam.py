@@ -235,3 +235,96 @@ def test_adam_reference_golden(cuda, golden):
         assert np.allclose(adam.moments.sh_coeffs_moments[i, :, 1:].cpu().numpy()[..., 0], mr, rtol=1e-6)
     for i in [int(x) for x in tr["splits_second_copies_ids"]]:
         assert torch.equal(g.means_opacity_features[i - 1], before[i - 1])
+
+
+def _scatter_rows(fg, buf, n, deg, device):
+    import ctypes as C
+    from gs3d import _abi
+    dense = torch.empty((n, 60), dtype=torch.float32, device=device)
+    fc = fg.to_c()
+    _abi.check(_abi.lib().gs3d_scatter_dense_grads(
+        C.byref(fc), C.c_void_p(buf.fgidx_to_gidx.data_ptr()), C.c_void_p(buf.device_counts.data_ptr()),
+        deg, C.c_void_p(dense.data_ptr()), n, None))
+    return dense
+
+
+@pytest.mark.parametrize("deg", [1, 3])
+def test_backward_dense_rows_match_scattered_gradients(cuda, deg):
+    """gs3d_backward_dense writes each filtered Gaussian's 3D gradients into its dense row (and
+    the touched flag); scattering gs3d_backward's F-compact gradients gives the same rows (the
+    float-atomic 2D sums differ in the last bits between the two runs)."""
+    from gs3d.backward import backward_dense
+    spec = SceneSpec(16_384, "uniform:1", -4.0, 0.5)
+    gv = synthetic_gaussians(spec, 4)
+    cam = look_at_camera(256, 256, 60.0, (0, 0, 3))
+    opt = RenderOptions.for_camera(cam, deg)
+    til = Tiling.for_camera(cam)
+    grad = np.random.default_rng(3).normal(0, 1e-4, size=(256, 256, 3)).astype(np.float32)
+    _, (g, out, buf, fg) = run_gpu(gv, cam, til, opt, grad, cuda)
+    want = _scatter_rows(fg, buf, g.n, deg, cuda)
+    dense = torch.full((g.n + 5, 60), 7.0, dtype=torch.float32, device=cuda)  # zeroed by the call
+    backward_dense(fg, torch.from_numpy(grad).to(cuda), out, g, cam, til, opt, buf, dense)
+    torch.cuda.synchronize()
+    got = dense[: g.n]
+    assert torch.equal(got[:, 59], want[:, 59]) and torch.all(dense[g.n:] == 0)
+    d = (got - want).abs()
+    assert d.max() <= 1e-5 * want.abs().max() + 1e-12, d.max()
+    assert torch.linalg.norm(got - want) <= 1e-5 * torch.linalg.norm(want)
+
+
+def test_dense_adam_range_split_equals_full(cuda):
+    """Two calls over [0, k) and [k, n) with the matching row slices == one call over [0, n)."""
+    import ctypes as C
+    from gs3d import _abi
+    spec = SceneSpec(16_384, "uniform:1", -4.0, 0.5)
+    gv = synthetic_gaussians(spec, 0)
+    cam = look_at_camera(256, 256, 60.0, (0, 0, 3))
+    opt = RenderOptions.for_camera(cam, 3)
+    til = Tiling.for_camera(cam)
+    grad = np.random.default_rng(1).normal(0, 1e-4, size=(256, 256, 3)).astype(np.float32)
+    _, (g, out, buf, fg) = run_gpu(gv, cam, til, opt, grad, cuda)
+    dense = _scatter_rows(fg, buf, g.n, 3, cuda)
+    g2 = g.clone()
+    a1 = AdamOptimizer(g, LearningRates(means=0.001))
+    a2 = AdamOptimizer(g2, LearningRates(means=0.001))
+    lib = _abi.lib()
+    gc, mc, pc = g.to_c(), a1.moments.to_c(), a1.params_c(3)
+    _abi.check(lib.gs3d_adam_step_dense(C.byref(gc), C.byref(mc), C.c_void_p(dense.data_ptr()),
+                                        C.byref(pc), None))
+    gc2, mc2, pc2 = g2.to_c(), a2.moments.to_c(), a2.params_c(3)
+    k = 5001
+    for lo, hi in ((0, k), (k, g2.n)):
+        part = dense[lo:hi].contiguous()
+        _abi.check(lib.gs3d_adam_step_dense_range(C.byref(gc2), C.byref(mc2), C.c_void_p(part.data_ptr()),
+                                                  lo, hi, C.byref(pc2), None))
+    torch.cuda.synchronize()
+    for x, y in zip(g.tensors(), g2.tensors()):
+        assert torch.equal(x, y)
+    for x, y in zip(a1.moments.tensors(), a2.moments.tensors()):
+        assert torch.equal(x, y)
+
+
+def test_dense_adam_equals_sparse_adam_storage_degree_1(cuda):
+    """The generic dense kernel (storage degree below 3) against the sparse update!, bit for bit."""
+    import ctypes as C
+    from gs3d import _abi
+    spec = SceneSpec(16_384, "uniform:1", -4.0, 0.5, sh_degree=1)
+    gv = synthetic_gaussians(spec, 2)
+    cam = look_at_camera(256, 256, 60.0, (0, 0, 3))
+    opt = RenderOptions.for_camera(cam, 1)
+    til = Tiling.for_camera(cam)
+    grad = np.random.default_rng(5).normal(0, 1e-4, size=(256, 256, 3)).astype(np.float32)
+    _, (g, out, buf, fg) = run_gpu(gv, cam, til, opt, grad, cuda)
+    dense = _scatter_rows(fg, buf, g.n, 1, cuda)
+    g2 = g.clone()
+    a1 = AdamOptimizer(g, LearningRates(means=0.001))
+    a2 = AdamOptimizer(g2, LearningRates(means=0.001))
+    a1.update(fg, buf.fgidx_to_gidx, buf.device_counts, 1)
+    gc, mc, pc = g2.to_c(), a2.moments.to_c(), a2.params_c(1)
+    _abi.check(_abi.lib().gs3d_adam_step_dense(C.byref(gc), C.byref(mc), C.c_void_p(dense.data_ptr()),
+                                               C.byref(pc), None))
+    torch.cuda.synchronize()
+    for x, y in zip(g.tensors(), g2.tensors()):
+        assert torch.equal(x, y)
+    for x, y in zip(a1.moments.tensors(), a2.moments.tensors()):
+        assert torch.equal(x, y)

@@ -215,3 +215,19 @@ def test_trainer_loss_decreases(cuda):
         losses.append(float(t.training_step()[0]))
     assert losses[-1] < losses[0]
     assert t.optimizer.update_count == 40
+
+
+def test_data_parallel_trainer_one_rank_matches_trainer(cuda):
+    """DataParallelTrainer without a process group (the dense-row path: gs3d_backward_dense +
+    gs3d_adam_step_dense) follows the sparse Trainer's training run (one view, 8 steps)."""
+    from gs3d.dp import DataParallelTrainer
+    runs = []
+    for cls in (Trainer, DataParallelTrainer):
+        gv = synthetic_gaussians(SceneSpec(16_384, "uniform:1", -4.0, 0.5), 9)
+        cams = [look_at_camera(256, 256, 60.0, (0, 0, 3))]
+        ro = RenderOptions.for_camera(cams[0], 3)
+        t = cls(gv.to(cuda), cams, [target_image(256, 256, 300, cuda)], ro, Tiling.for_camera(cams[0]),
+                TrainingOptions(scene_radius=3.3), seed=7)
+        t.iteration_nb = 3000
+        runs.append(torch.stack([t.training_step().clone() for _ in range(8)])[:, :3].cpu())
+    assert torch.allclose(runs[0], runs[1], rtol=1e-5, atol=0), (runs[0], runs[1])

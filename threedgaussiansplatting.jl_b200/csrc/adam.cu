@@ -248,12 +248,14 @@ int launch_adam_warp(const AdamArgs& a, cudaStream_t stream) {
     return GS3D_OK;
 }
 
-// Multi-view data parallelism: the F-compact gradients of one view are scattered into a
-// dense row per Gaussian, kDenseRow floats: mean(3) opacity(1) scale(3) rotation(4)
-// SH(3 x 16, channel-major) touched(1). Rows are summed across ranks (NCCL all-reduce),
-// then k_adam_dense steps every touched Gaussian with the summed gradient.
-constexpr int kDenseRow = 60;
-constexpr int kDenseTouched = 59;
+// Multi-view data parallelism: the gradients of one view are written into a dense row per
+// Gaussian (by gs3d_backward_dense directly, or scattered from the F-compact arrays by
+// k_scatter_dense), kDenseRow floats: SH 3 x 16 channel-major at 0 (16-byte aligned),
+// mean 48, opacity feature 51, scaling features 52, rotation features 55, touched flag 59.
+// Rows are summed across ranks (NCCL), then the dense kernels step every touched Gaussian of
+// a range [g_begin, g_end) whose rows start at dense[0], with the summed gradients.
+constexpr int kDenseRow = GS3D_DENSE_ROW;
+constexpr int kDMean = 48, kDOpacity = 51, kDScale = 52, kDRot = 55, kDTouched = 59;
 
 __global__ void __launch_bounds__(256) k_scatter_dense(const AdamArgs a, float* __restrict__ dense) {
     const int F = a.counts[0];
@@ -266,51 +268,118 @@ __global__ void __launch_bounds__(256) k_scatter_dense(const AdamArgs a, float* 
         const int gidx = a.f2g[f];
         if (gidx <= 0) continue;
         float* row = dense + (size_t)(gidx - 1) * kDenseRow;
-        if (c == nc) { row[kDenseTouched] = 1.0f; continue; }
+        if (c == nc) { row[kDTouched] = 1.0f; continue; }
         float v;
         int col;
-        if (c < 3) { v = a.g_mean[3 * (size_t)f + c]; col = c; }
-        else if (c == 3) { v = a.g_op[f]; col = 3; }
-        else if (c < 7) { v = a.g_scale[3 * (size_t)f + (c - 4)]; col = c; }
-        else if (c < 11) { v = a.g_rot[4 * (size_t)f + (c - 7)]; col = c; }
+        if (c < 3) { v = a.g_mean[3 * (size_t)f + c]; col = kDMean + c; }
+        else if (c == 3) { v = a.g_op[f]; col = kDOpacity; }
+        else if (c < 7) { v = a.g_scale[3 * (size_t)f + (c - 4)]; col = kDScale + (c - 4); }
+        else if (c < 11) { v = a.g_rot[4 * (size_t)f + (c - 7)]; col = kDRot + (c - 7); }
         else {
             const int k = c - 11, ch = k / a.maxo, i = k - ch * a.maxo;
             v = a.g_sh[(size_t)f * 3 * a.Sg + (size_t)(ch * a.Sg + i)];
-            col = 11 + ch * 16 + i;
+            col = ch * 16 + i;
         }
         row[col] = v;
     }
 }
 
+// Any storage degree: one thread per (Gaussian, scalar slot).
 __global__ void __launch_bounds__(256) k_adam_dense(const AdamArgs a, const float* __restrict__ dense,
-                                                    int n) {
+                                                    int64_t g_begin, int64_t g_end) {
     const int nc = 11 + 3 * a.maxo;
-    const int64_t total = (int64_t)n * nc;
+    const int64_t total = (g_end - g_begin) * nc;
     for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < total;
          it += (int64_t)gridDim.x * blockDim.x) {
-        const int g = (int)(it / nc);
-        const int c = (int)(it - (int64_t)g * nc);
-        const float* row = dense + (size_t)g * kDenseRow;
-        if (!(row[kDenseTouched] > 0.0f)) continue;
-        const size_t gi = (size_t)g;
+        const int64_t lr_ = it / nc;
+        const int c = (int)(it - lr_ * nc);
+        const float* row = dense + (size_t)lr_ * kDenseRow;
+        if (!(row[kDTouched] > 0.0f)) continue;
+        const size_t gi = (size_t)(g_begin + lr_);
         if (c < 3) {
-            adam_scalar(a.mo + 4 * gi + c, row[c], a.mm + 6 * gi + 2 * c, a.lr_means, a);
+            adam_scalar(a.mo + 4 * gi + c, row[kDMean + c], a.mm + 6 * gi + 2 * c, a.lr_means, a);
         } else if (c == 3) {
-            adam_scalar(a.mo + 4 * gi + 3, row[3], a.om + 2 * gi, a.lr_op, a);
+            adam_scalar(a.mo + 4 * gi + 3, row[kDOpacity], a.om + 2 * gi, a.lr_op, a);
         } else if (c < 7) {
             const int k = c - 4;
-            adam_scalar(a.sf + 3 * gi + k, row[c], a.sm + 6 * gi + 2 * k, a.lr_scale, a);
+            adam_scalar(a.sf + 3 * gi + k, row[kDScale + k], a.sm + 6 * gi + 2 * k, a.lr_scale, a);
         } else if (c < 11) {
             const int k = c - 7;
-            adam_scalar(a.rf + 4 * gi + k, row[c], a.rm + 8 * gi + 2 * k, a.lr_rot, a);
+            adam_scalar(a.rf + 4 * gi + k, row[kDRot + k], a.rm + 8 * gi + 2 * k, a.lr_rot, a);
         } else {
             const int k = c - 11;
             const int ch = k / a.maxo, i = k - ch * a.maxo;
-            adam_scalar(a.sh + gi * 3 * a.S + (size_t)(ch * a.S + i), row[11 + ch * 16 + i],
+            adam_scalar(a.sh + gi * 3 * a.S + (size_t)(ch * a.S + i), row[ch * 16 + i],
                         a.shm + gi * 6 * a.Sm + 2 * (size_t)(ch * a.Sm + i),
                         i == 0 ? a.lr_dc : a.lr_rest, a);
         }
     }
+}
+
+// Storage degree 3 (the k_adam_sh16 / k_adam_geom forms over dense rows): thread
+// 12 (g - g_begin) + c updates SH unit c of Gaussian g from the row's 16-byte unit c.
+__global__ void __launch_bounds__(256) k_adam_dense_sh16(const AdamArgs a,
+                                                         const float* __restrict__ dense,
+                                                         int64_t g_begin, int64_t g_end) {
+    const int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (it >= 12 * (g_end - g_begin)) return;
+    const int64_t lr_ = it / 12;
+    const int c = (int)(it - lr_ * 12);
+    const int i0 = 4 * (c & 3);
+    if (i0 >= a.maxo) return;
+    const float* row = dense + (size_t)lr_ * kDenseRow;
+    if (!(__ldg(row + kDTouched) > 0.0f)) return;
+    const size_t gi = (size_t)(g_begin + lr_);
+    float4* pp = reinterpret_cast<float4*>(a.sh + gi * 48) + c;
+    float4* mp = reinterpret_cast<float4*>(a.shm + gi * 96) + 2 * c;
+    const float4 g = __ldg(reinterpret_cast<const float4*>(row) + c);
+    float4 p = *pp, m01 = mp[0], m23 = mp[1];
+    adam4(p, g, m01, m23, i0 == 0 ? a.lr_dc : a.lr_rest, a.lr_rest, min(4, a.maxo - i0), a);
+    *pp = p;
+    mp[0] = m01;
+    mp[1] = m23;
+}
+
+__global__ void __launch_bounds__(256) k_adam_dense_geom(const AdamArgs a,
+                                                         const float* __restrict__ dense,
+                                                         int64_t g_begin, int64_t g_end) {
+    const int64_t lr_ = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (lr_ >= g_end - g_begin) return;
+    const float4* row4 = reinterpret_cast<const float4*>(dense + (size_t)lr_ * kDenseRow);
+    const float4 r12 = __ldg(row4 + 12), r13 = __ldg(row4 + 13), r14 = __ldg(row4 + 14);
+    // r12: mean x y z, opacity; r13: scale 0 1 2, rotation 0; r14: rotation 1 2 3, touched
+    if (!(r14.w > 0.0f)) return;
+    const size_t gi = (size_t)(g_begin + lr_);
+    float4* mop = reinterpret_cast<float4*>(a.mo) + gi;
+    float4* rfp = reinterpret_cast<float4*>(a.rf) + gi;
+    float2* mmp = reinterpret_cast<float2*>(a.mm) + 3 * gi;
+    float2* omp = reinterpret_cast<float2*>(a.om) + gi;
+    float2* smp = reinterpret_cast<float2*>(a.sm) + 3 * gi;
+    float4* rmp = reinterpret_cast<float4*>(a.rm) + 2 * gi;
+    float* sfp = a.sf + 3 * gi;
+    float4 mo = *mop, rf = *rfp, rm0 = rmp[0], rm1 = rmp[1];
+    float2 mm0 = mmp[0], mm1 = mmp[1], mm2 = mmp[2], om = *omp;
+    float2 sm0 = smp[0], sm1 = smp[1], sm2 = smp[2];
+    float s0 = sfp[0], s1 = sfp[1], s2 = sfp[2];
+    adam_reg(mo.x, r12.x, mm0.x, mm0.y, a.lr_means, a);
+    adam_reg(mo.y, r12.y, mm1.x, mm1.y, a.lr_means, a);
+    adam_reg(mo.z, r12.z, mm2.x, mm2.y, a.lr_means, a);
+    adam_reg(mo.w, r12.w, om.x, om.y, a.lr_op, a);
+    adam_reg(s0, r13.x, sm0.x, sm0.y, a.lr_scale, a);
+    adam_reg(s1, r13.y, sm1.x, sm1.y, a.lr_scale, a);
+    adam_reg(s2, r13.z, sm2.x, sm2.y, a.lr_scale, a);
+    adam_reg(rf.x, r13.w, rm0.x, rm0.y, a.lr_rot, a);
+    adam_reg(rf.y, r14.x, rm0.z, rm0.w, a.lr_rot, a);
+    adam_reg(rf.z, r14.y, rm1.x, rm1.y, a.lr_rot, a);
+    adam_reg(rf.w, r14.z, rm1.z, rm1.w, a.lr_rot, a);
+    *mop = mo;
+    *rfp = rf;
+    rmp[0] = rm0;
+    rmp[1] = rm1;
+    mmp[0] = mm0; mmp[1] = mm1; mmp[2] = mm2;
+    *omp = om;
+    smp[0] = sm0; smp[1] = sm1; smp[2] = sm2;
+    sfp[0] = s0; sfp[1] = s1; sfp[2] = s2;
 }
 
 }  // namespace
@@ -407,15 +476,38 @@ extern "C" GS3D_API int gs3d_scatter_dense_grads(const gs3d_fgradients* fg,
     return GS3D_OK;
 }
 
-extern "C" GS3D_API int gs3d_adam_step_dense(const gs3d_gaussians* g, const gs3d_adam_moments* m,
-                                             const float* dense, const gs3d_adam_params* p,
-                                             gs3d_stream_t stream_) {
+extern "C" GS3D_API int gs3d_adam_step_dense_range(const gs3d_gaussians* g,
+                                                   const gs3d_adam_moments* m, const float* dense,
+                                                   int32_t g_begin, int32_t g_end,
+                                                   const gs3d_adam_params* p,
+                                                   gs3d_stream_t stream_) {
     cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
     if (!g || !m || !dense || !p) return invalid("NULL argument");
+    if (g_begin < 0 || g_end < g_begin || g_end > g->n)
+        return invalid("Gaussian range [%d, %d) of n = %d", g_begin, g_end, g->n);
     AdamArgs a;
     GS3D_RETURN_IF(make_args(g, m, nullptr, nullptr, nullptr, p, a));
+    if (g_end == g_begin) return GS3D_OK;
     ProfScope prof("adam_dense", stream);
-    k_adam_dense<<<device_sm_count() * 8, 256, 0, stream>>>(a, dense, g->n);
-    GS3D_LAUNCHED("k_adam_dense");
+    const int64_t cnt = (int64_t)g_end - g_begin;
+    const bool flat = a.S == 16 && a.Sm == 16 && aligned(dense, 16) && aligned(a.sh, 16) &&
+                      aligned(a.shm, 16) && aligned(a.mo, 16) && aligned(a.rf, 16) &&
+                      aligned(a.rm, 16) && aligned(a.mm, 8) && aligned(a.om, 8) && aligned(a.sm, 8);
+    if (flat) {
+        k_adam_dense_sh16<<<(unsigned)ceil_div(12 * cnt, 256), 256, 0, stream>>>(a, dense, g_begin, g_end);
+        GS3D_LAUNCHED("k_adam_dense_sh16");
+        k_adam_dense_geom<<<(unsigned)ceil_div(cnt, 256), 256, 0, stream>>>(a, dense, g_begin, g_end);
+        GS3D_LAUNCHED("k_adam_dense_geom");
+    } else {
+        k_adam_dense<<<device_sm_count() * 8, 256, 0, stream>>>(a, dense, g_begin, g_end);
+        GS3D_LAUNCHED("k_adam_dense");
+    }
     return GS3D_OK;
+}
+
+extern "C" GS3D_API int gs3d_adam_step_dense(const gs3d_gaussians* g, const gs3d_adam_moments* m,
+                                             const float* dense, const gs3d_adam_params* p,
+                                             gs3d_stream_t stream) {
+    if (!g) return invalid("NULL argument");
+    return gs3d_adam_step_dense_range(g, m, dense, 0, g->n, p, stream);
 }

@@ -306,7 +306,15 @@ struct BProjArgs {
     float* sh_g;
     int sh_grad_stride;
     int fix_sh16;
+    // NULL, or dense gradient rows indexed by Gaussian (kDenseRow floats, layout in gs3d.h):
+    // the 3D gradients then go to row gidx instead of the F-compact arrays above
+    float* dense;
 };
+
+// Dense gradient row (GS3D_DENSE_ROW): SH 3 x 16 channel-major at 0, mean 48, opacity feature
+// 51, scaling features 52, rotation features 55, touched flag 59.
+constexpr int kDenseRow = GS3D_DENSE_ROW;
+constexpr int kDMean = 48, kDOpacity = 51, kDScale = 52, kDRot = 55, kDTouched = 59;
 
 template <int DEG>
 __global__ void __launch_bounds__(128, 6) k_bwd_project(const BProjArgs a, const gs3d_camera cam,
@@ -331,15 +339,22 @@ __global__ void __launch_bounds__(128, 6) k_bwd_project(const BProjArgs a, const
     for (int64_t fb = (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * 32; fb < F;
          fb += nwarps * 32) {
       const int f = (int)fb + lane;
-      if (f < F) {
-        const int gi = a.f2g[f] - 1;
+      const int gi = f < F ? a.f2g[f] - 1 : -1;
+      if (gi >= 0) {
+        float* const drow = a.dense ? a.dense + (size_t)gi * kDenseRow : nullptr;
         const float* r = a.f2d + 9 * (size_t)f;
         const float4 mo = a.mo4[gi];
         const float orig_op = gs_sigmoid(mo.w);
         const float depth = Ps[2][0] * mo.x + Ps[2][1] * mo.y + Ps[2][2] * mo.z + cam.P[11];
         const float opac = opt.use_antialiasing ? r[2] : orig_op;
         const float og = a.opacity_g[f];
-        a.opf_g[f] = opt.use_antialiasing ? og * opac * (1.0f - orig_op) : og * opac * (1.0f - opac);
+        const float opf = opt.use_antialiasing ? og * opac * (1.0f - orig_op) : og * opac * (1.0f - opac);
+        if (drow) {
+            drow[kDOpacity] = opf;
+            drow[kDTouched] = 1.0f;
+        } else {
+            a.opf_g[f] = opf;
+        }
 
         // compute_cov2d_lower_grad (backward_core.jl:465-493)
         const float ia = r[3], ib = r[4], id = r[5];
@@ -530,9 +545,10 @@ __global__ void __launch_bounds__(128, 6) k_bwd_project(const BProjArgs a, const
             }
             m3[i] = m3[i] + inv_vn * w;
         }
-        a.mean3d_g[3 * (size_t)f] = m3[0];
-        a.mean3d_g[3 * (size_t)f + 1] = m3[1];
-        a.mean3d_g[3 * (size_t)f + 2] = m3[2];
+        float* const m3out = drow ? drow + kDMean : a.mean3d_g + 3 * (size_t)f;
+        m3out[0] = m3[0];
+        m3out[1] = m3[1];
+        m3out[2] = m3[2];
 
         // scaling features: v gradient = Transposed_dsigma_dv(J) * cg
         float vg[6];
@@ -554,7 +570,7 @@ __global__ void __launch_bounds__(128, 6) k_bwd_project(const BProjArgs a, const
             float tt = 0.0f;
 #pragma unroll
             for (int i = 0; i < 6; ++i) tt = tt + (s[j] * R[L3I[i]][j] * R[L3J[i]][j]) * vg[i];
-            a.scale_g[3 * (size_t)f + j] = (2.0f * tt) * s[j];
+            (drow ? drow + kDScale : a.scale_g + 3 * (size_t)f)[j] = (2.0f * tt) * s[j];
         }
         // rotation features
         {
@@ -597,7 +613,7 @@ __global__ void __launch_bounds__(128, 6) k_bwd_project(const BProjArgs a, const
                     const float Nij = i == j ? 1.0f - nq[i] * nq[i] : -nq[i < j ? i : j] * nq[i < j ? j : i];
                     w = w + Nij * nqg[j];
                 }
-                a.rot_g[4 * (size_t)f + i] = inv_qn * w;
+                (drow ? drow + kDRot : a.rot_g + 4 * (size_t)f)[i] = inv_qn * w;
             }
         }
         // SH coefficients (compute_sh_coeffs_grad!, backward_core.jl:936-964), staged
@@ -612,11 +628,21 @@ __global__ void __launch_bounds__(128, 6) k_bwd_project(const BProjArgs a, const
       __syncwarp();
       const int nrows = (int)min((int64_t)32, (int64_t)F - fb);
       float* const warp_stage = &stage[threadIdx.x >> 5][0][0];
-      for (int e = lane; e < nrows * NSH; e += 32) {
-          const int row = e / NSH, rem = e - row * NSH;
-          const int c = rem / MAXO, k = rem - c * MAXO;
-          a.sh_g[(size_t)(fb + row) * 3 * a.sh_grad_stride + (size_t)(c * a.sh_grad_stride + k)] =
-              warp_stage[row * (NSH + 1) + rem];
+      if (a.dense) {  // row `row` of the warp goes to dense row gidx (skipped when gidx <= 0)
+          for (int e = lane; e < 32 * NSH; e += 32) {
+              const int row = e / NSH, rem = e - row * NSH;
+              const int grow = __shfl_sync(0xffffffffu, gi, row);
+              if (row >= nrows || grow < 0) continue;
+              const int c = rem / MAXO, k = rem - c * MAXO;
+              a.dense[(size_t)grow * kDenseRow + (size_t)(c * 16 + k)] = warp_stage[row * (NSH + 1) + rem];
+          }
+      } else {
+          for (int e = lane; e < nrows * NSH; e += 32) {
+              const int row = e / NSH, rem = e - row * NSH;
+              const int c = rem / MAXO, k = rem - c * MAXO;
+              a.sh_g[(size_t)(fb + row) * 3 * a.sh_grad_stride + (size_t)(c * a.sh_grad_stride + k)] =
+                  warp_stage[row * (NSH + 1) + rem];
+          }
       }
       __syncwarp();
     }
@@ -635,24 +661,33 @@ int grid_for(int64_t items, int threads, int per_sm) {
 
 using namespace gs3d;
 
-extern "C" GS3D_API int gs3d_backward(const gs3d_fgradients* fg, const float* rgb_grad,
-                                      const gs3d_render_outputs* out, const gs3d_gaussians* g,
-                                      const gs3d_camera* cam, const gs3d_tiling* til,
-                                      const gs3d_render_options* opt,
-                                      const gs3d_render_buffers* buf, uint32_t flags,
-                                      gs3d_stream_t stream_) {
-    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+namespace {
+
+// backward! with the 3D gradients into the F-compact arrays of fg (dense == NULL) or into
+// dense rows indexed by Gaussian (rows zeroed here first, touched flags set).
+int backward_impl(const gs3d_fgradients* fg, const float* rgb_grad,
+                  const gs3d_render_outputs* out, const gs3d_gaussians* g, const gs3d_camera* cam,
+                  const gs3d_tiling* til, const gs3d_render_options* opt,
+                  const gs3d_render_buffers* buf, uint32_t flags, float* dense, int32_t n_dense,
+                  cudaStream_t stream) {
     GS3D_RETURN_IF(check_render_common(g, cam, til, opt));
     if (!fg || !rgb_grad || !out || !buf) return invalid("NULL argument");
     if (!out->transmittance || !out->last_contributing_sdfgids)
         return invalid("backward needs the transmittance and last-contributor images");
-    if (!fg->mean2d_grads || !fg->opacity_grads || !fg->licov2d_grads || !fg->color_grads ||
-        !fg->mean3d_grads || !fg->opacity_feature_grads || !fg->scaling_features_grads ||
-        !fg->rotation_features_grads || !fg->sh_coeffs_grads)
+    if (!fg->mean2d_grads || !fg->opacity_grads || !fg->licov2d_grads || !fg->color_grads)
+        return invalid("NULL 2D gradient array");
+    if (!dense && (!fg->mean3d_grads || !fg->opacity_feature_grads || !fg->scaling_features_grads ||
+                   !fg->rotation_features_grads || !fg->sh_coeffs_grads))
         return invalid("NULL gradient array");
-    if (fg->sh_degree < opt->sh_degree || fg->sh_degree > 3)
+    if (dense && n_dense < g->n) return invalid("dense rows %d < n = %d", n_dense, g->n);
+    if (!dense && (fg->sh_degree < opt->sh_degree || fg->sh_degree > 3))
         return invalid("gradient SH degree %d < render degree %d", fg->sh_degree, opt->sh_degree);
     const int64_t cap_n = buf->capacity_n > 0 ? buf->capacity_n : 1;
+    if (dense) {
+        ProfScope prof("zero_dense", stream);
+        GS3D_CUDA(cudaMemsetAsync(dense, 0, (size_t)n_dense * kDenseRow * sizeof(float), stream),
+                  "zero dense rows");
+    }
     {
         ProfScope prof("zero_2d", stream);
         k_zero_2d<<<grid_for(3 * cap_n, 256, 8), 256, 0, stream>>>(
@@ -715,6 +750,7 @@ extern "C" GS3D_API int gs3d_backward(const gs3d_fgradients* fg, const float* rg
     p.sh_g = fg->sh_coeffs_grads;
     p.sh_grad_stride = (fg->sh_degree + 1) * (fg->sh_degree + 1);
     p.fix_sh16 = (flags & GS3D_BACKWARD_FIX_SH16) ? 1 : 0;
+    p.dense = dense;
     const int grid = grid_for(cap_n, 128, 16);
     ProfScope prof("bwd_project", stream);
     switch (opt->sh_degree) {
@@ -725,4 +761,28 @@ extern "C" GS3D_API int gs3d_backward(const gs3d_fgradients* fg, const float* rg
     }
     GS3D_LAUNCHED("k_bwd_project");
     return GS3D_OK;
+}
+
+}  // namespace
+
+extern "C" GS3D_API int gs3d_backward(const gs3d_fgradients* fg, const float* rgb_grad,
+                                      const gs3d_render_outputs* out, const gs3d_gaussians* g,
+                                      const gs3d_camera* cam, const gs3d_tiling* til,
+                                      const gs3d_render_options* opt,
+                                      const gs3d_render_buffers* buf, uint32_t flags,
+                                      gs3d_stream_t stream) {
+    return backward_impl(fg, rgb_grad, out, g, cam, til, opt, buf, flags, nullptr, 0,
+                         reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" GS3D_API int gs3d_backward_dense(const gs3d_fgradients* fg, const float* rgb_grad,
+                                            const gs3d_render_outputs* out,
+                                            const gs3d_gaussians* g, const gs3d_camera* cam,
+                                            const gs3d_tiling* til,
+                                            const gs3d_render_options* opt,
+                                            const gs3d_render_buffers* buf, uint32_t flags,
+                                            float* dense, int32_t n, gs3d_stream_t stream) {
+    if (!dense) return invalid("NULL dense rows");
+    return backward_impl(fg, rgb_grad, out, g, cam, til, opt, buf, flags, dense, n,
+                         reinterpret_cast<cudaStream_t>(stream));
 }

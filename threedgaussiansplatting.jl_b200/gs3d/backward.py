@@ -92,3 +92,27 @@ def backward(fgradients: FilteredGaussiansGradients, rgb_image_grad: torch.Tenso
                                  C.byref(args[4]), C.byref(args[5]), C.byref(args[6]), flags,
                                  C.c_void_p(_stream_handle(stream))))
     return fgradients
+
+
+def backward_dense(fgradients: FilteredGaussiansGradients, rgb_image_grad: torch.Tensor,
+                   outputs: RenderOutputs, gaussians: GaussiansVector, camera: PinholeCamera,
+                   tiling: Tiling, options: RenderOptions, buffers: RenderBuffers,
+                   dense: torch.Tensor, fix_sh16: bool = False,
+                   stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """backward() with the 3D gradients written into `dense` ((rows >= n, GS3D_DENSE_ROW)
+    float32, zeroed here) at each Gaussian's row instead of the F-compact 3D arrays; the 2D
+    gradients still go to `fgradients`."""
+    assert rgb_image_grad.is_contiguous() and rgb_image_grad.dtype == torch.float32
+    assert dense.is_contiguous() and dense.dtype == torch.float32 and dense.shape[1] == 60
+    if fgradients.capacity < buffers.capacity_n:
+        raise ValueError("gradient buffers smaller than the render buffers")
+    lib = _abi.lib()
+    args = [fgradients.to_c(), outputs.to_c(), gaussians.to_c(), camera.to_c(), tiling.to_c(),
+            options.to_c(), buffers.to_c()]
+    flags = _abi.GS3D_BACKWARD_FIX_SH16 if fix_sh16 else 0
+    _abi.check(lib.gs3d_backward_dense(C.byref(args[0]), C.c_void_p(rgb_image_grad.data_ptr()),
+                                       C.byref(args[1]), C.byref(args[2]), C.byref(args[3]),
+                                       C.byref(args[4]), C.byref(args[5]), C.byref(args[6]), flags,
+                                       C.c_void_p(dense.data_ptr()), dense.shape[0],
+                                       C.c_void_p(_stream_handle(stream))))
+    return dense

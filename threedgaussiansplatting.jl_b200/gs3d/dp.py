@@ -1,9 +1,9 @@
 """Multi-view data-parallel training: one process per GPU, model replicated.
 
-Each rank renders and back-propagates its own view of the step; the F-compact gradients are
-scattered into dense rows (gs3d_scatter_dense_grads), summed across ranks with one
-all-reduce over NCCL (torch.distributed), and every rank applies the identical Adam update to
-the union of touched Gaussians (gs3d_adam_step_dense). With one rank this is exactly the
+Each rank renders and back-propagates its own view of the step with the 3D gradients written
+straight into dense rows indexed by Gaussian (gs3d_backward_dense), the rows are summed across
+ranks with one all-reduce over NCCL (torch.distributed), and every rank applies the identical
+Adam update to the union of touched Gaussians (gs3d_adam_step_dense). With one rank this is exactly the
 reference's sparse update. Densify steps all-reduce the statistics first, so every rank makes
 the same decisions, and remap the dense rows like the reference retargets fgidx_to_gidx.
 Views: a permutation of the cameras drawn from a seed shared by all ranks; at step k rank r
@@ -18,7 +18,7 @@ import torch.distributed as dist
 
 from . import _abi
 from . import adc as adc_mod
-from .backward import backward
+from .backward import backward_dense
 from .render import _stream_handle, render
 from .training import Trainer
 
@@ -67,16 +67,10 @@ class DataParallelTrainer(Trainer):
         if gt is self._gt_buffers[self._gt_slot]:
             self._gt_free[self._gt_slot].record(torch.cuda.current_stream(self.device))
         self.prefetch_target()
-        backward(self.fgradients, self.rgb_image_grad, self.render_outputs, self.gaussians, cam,
-                 self.tiling, self.render_options, rb)
+        backward_dense(self.fgradients, self.rgb_image_grad, self.render_outputs, self.gaussians,
+                       cam, self.tiling, self.render_options, rb, self.dense)
         o = self.options
         stream = C.c_void_p(_stream_handle(None))
-        fg = self.fgradients.to_c()
-        _abi.check(lib.gs3d_scatter_dense_grads(C.byref(fg), C.c_void_p(rb.fgidx_to_gidx.data_ptr()),
-                                                C.c_void_p(rb.device_counts.data_ptr()),
-                                                self.render_options.sh_degree,
-                                                C.c_void_p(self.dense.data_ptr()), self.gaussians.n,
-                                                stream))
         self._allreduce(self.dense)
         in_adc = False
         if self.iteration_nb <= o.adc_final_iteration_nb:
