@@ -1,0 +1,86 @@
+"""Host logic of the data-parallel trainer on CPU: two gloo ranks, no GPU.
+
+Checks the shard arithmetic, the view assignment, and that the collectives the trainer
+issues on its padded storage (reduce-scatter of gradient rows into each rank's own slice,
+all-gather of each rank's slice of a parameter array; in place over NCCL, from a copy here)
+give the summed rows and the replicated arrays."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from gs3d.dp import DENSE_ROW, shard_range, view_index
+
+
+def test_shard_ranges_partition_the_gaussians():
+    for n in (1, 2, 7, 8, 9, 1000, 313_001):
+        for world in (1, 2, 3, 4, 8):
+            covered = []
+            for r in range(world):
+                S, lo, hi = shard_range(n, world, r)
+                assert S * world >= n and (S - 1) * world < n or n < world
+                covered.extend(range(lo, hi))
+            assert covered == list(range(n)), (n, world)
+
+
+def test_views_of_a_step_are_distinct():
+    perm = np.random.default_rng(0).permutation(256)
+    for world in (2, 4, 8):
+        for step in range(100):
+            views = {view_index(step, r, world, perm, 256) for r in range(world)}
+            assert len(views) == world
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        n = 11
+        S, lo, hi = shard_range(n, world, rank)
+        rows = S * world
+        # each rank's dense rows: rank-dependent values, padding rows zero
+        dense = torch.zeros((rows, DENSE_ROW))
+        dense[:n] = torch.arange(n * DENSE_ROW, dtype=torch.float32).view(n, DENSE_ROW) * (rank + 1)
+        flat = dense.view(-1)
+        per = S * DENSE_ROW
+        dist.reduce_scatter_tensor(flat[rank * per:(rank + 1) * per], flat.clone(), op=dist.ReduceOp.SUM)
+        total = sum(r + 1 for r in range(world))
+        want = torch.arange(n * DENSE_ROW, dtype=torch.float32).view(n, DENSE_ROW) * total
+        ok_rs = torch.equal(dense[lo:hi], want[lo:hi])
+        # parameter array: each rank writes its own slice, the all-gather replicates all
+        base = torch.full((rows, 4), -1.0)
+        base[lo:hi] = torch.arange(lo, hi, dtype=torch.float32)[:, None] + 0.5
+        fb = base.view(-1)
+        per4 = fb.numel() // world
+        dist.all_gather_into_tensor(fb, fb[rank * per4:(rank + 1) * per4].clone())
+        ok_ag = torch.equal(base[:n], torch.arange(n, dtype=torch.float32)[:, None].expand(n, 4) + 0.5)
+        q.put((rank, ok_rs, ok_ag))
+        dist.destroy_process_group()
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, repr(e), None))
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_sharded_collectives_on_padded_storage(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, ok_rs, ok_ag in results:
+        assert ok_rs is True and ok_ag is True, (rank, ok_rs, ok_ag)
