@@ -13,9 +13,10 @@ training_step! (training.jl:173-244) per GPU: render!, loss, backward!, ADC stat
 learning-rate annealing and the Adam update, at iterations 3001.. (SH degree 3, between
 densify steps; densification happens once every 100 iterations and is not timed).
 N = 1 uses the reference's sparse Adam; N > 1 is multi-view data parallelism (one view per
-rank, dense gradient rows summed by an NCCL all-reduce, identical Adam on every rank), so the
-per-GPU work is fixed ("weak" scaling). Inputs are larger than L2 (2.1 GB of parameters and
-moments), so no L2 flush is needed between steps.
+rank; dense gradient rows reduce-scattered over NCCL, each rank updates its 1/N of the
+Gaussians, parameters all-gathered), so the per-GPU work is fixed ("weak" scaling). Inputs
+are larger than L2 (2.1 GB of parameters and moments), so no L2 flush is needed between steps.
+The line also carries the render-only throughput (frames/s) of the same scene and cameras.
 
 `--impl reference` times the CPU restatement of the same training step (the reference has no
 runnable implementation here: it is Julia/CUDA.jl and Julia is not installed) on all host
@@ -49,7 +50,8 @@ FALLBACK_HBM_GBS = 6650.0
 # kernels per profiled stage (for gpu_launches)
 KERNELS_PER_STAGE = {"keep_compact": 3, "project": 1, "dup_scan": 3, "dup_keys": 1, "tiles_end": 1,
                      "raster": 1, "zero_2d": 1, "bwd_raster": 1, "bwd_project": 1, "loss": 3,
-                     "adc_stats": 1, "scatter_dense": 1, "adam_dense": 1, "adam": 1}
+                     "adc_stats": 1, "scatter_dense": 1, "adam_dense": 2, "adam": 2,
+                     "zero_dense": 0}
 
 
 def parse():
@@ -161,6 +163,18 @@ def stage_bytes(stage: str, F: int, D: int, n: int, w: int, h: int, passes: int)
     }.get(stage)
 
 
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one launch, from ncu captures of
+# the 1M-Gaussian case of this workload (profiles/k_*_1M_1080p.md), as a fraction of that
+# launch's algorithmic bytes; the full-size traffic is that fraction of the full-size bytes
+# (traffic grows with the same units).
+NCU_TRAFFIC_FRACTION = {
+    # 114.40 MB read + 6.12 MB write at F = 992,004, D = 943,223, 1920x1080
+    "bwd_raster": 120.52e6 / (40.0 * 943_223 + 24.0 * 2_073_600 + 36.0 * 992_004),
+    # 39.42 MB read + 8.89 MB write
+    "raster": 48.31e6 / (40.0 * 943_223 + 20.0 * 2_073_600),
+}
+
+
 def run_reference(args, rank: int, world: int) -> None:
     """The CPU restatement of the training step on all host threads (rank 0 only)."""
     if rank != 0:
@@ -231,22 +245,28 @@ def cpu_baseline_leg(gv_cpu, cams, pool_host, ro, til, opts) -> dict:
     n = g.n
     m = O.NpMoments(np.zeros((n, 3, 2)), np.zeros((n, 2)), np.zeros((n, 3, 2)), np.zeros((n, 4, 2)),
                     np.zeros((n, 3, 16, 2)))
-    cam = cams[0]
-    t0 = time.perf_counter()
-    f = O.render(g, cam, til, ro)
-    (_, _, _), grad = O.loss(f["rgb"], pool_host[0].numpy(), opts.loss_dssim_vs_L1_weight)
-    b = O.backward(g, cam, til, ro, f, grad)
     p = _abi.AdamParamsC()
     lrs = opts.learning_rates()
     p.lr_means, p.lr_opacity_features, p.lr_scaling_features = lrs.means, lrs.opacity_features, lrs.scaling_features
     p.lr_rotation_features, p.lr_sh_dc, p.lr_sh_rest = lrs.rotation_features, lrs.sh_coeffs_dc, lrs.sh_coeffs_rest
-    p.beta1, p.beta2, p.epsilon, p.update_count, p.sh_degree = 0.9, 0.999, 1e-15, 0, 3
-    bc1, bc2 = bias_corrections(0.9, 0.999, 0)
-    O.adam(g, m, b, f["fgidx_to_gidx"], p, bc1, bc2)
+    p.beta1, p.beta2, p.epsilon, p.sh_degree = 0.9, 0.999, 1e-15, 3
+    t0 = time.perf_counter()
+    steps = 0
+    while steps < 6 and (steps == 0 or time.perf_counter() - t0 < 10.0):  # about 10 s of work
+        cam = cams[steps % len(cams)]
+        f = O.render(g, cam, til, ro)
+        (_, _, _), grad = O.loss(f["rgb"], pool_host[steps % len(pool_host)].numpy(),
+                                 opts.loss_dssim_vs_L1_weight)
+        b = O.backward(g, cam, til, ro, f, grad)
+        p.update_count = steps
+        bc1, bc2 = bias_corrections(0.9, 0.999, steps)
+        O.adam(g, m, b, f["fgidx_to_gidx"], p, bc1, bc2)
+        steps += 1
     el = time.perf_counter() - t0
-    return {"value": 1.0 / el, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"1 full training step (render+loss+backward+Adam) of the same workload, camera 0, "
-                      f"CPU restatement of the reference's GPU-path arithmetic, {threads} threads, {el:.1f} s"}
+    return {"value": steps / el, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{steps} full training steps (render+loss+backward+Adam) of the same workload, "
+                      f"cameras 0..{steps - 1}, CPU restatement of the reference's GPU-path arithmetic, "
+                      f"{threads} threads, {el:.1f} s"}
 
 
 def main() -> None:
@@ -350,6 +370,31 @@ def main() -> None:
         e2e = {"value": world * args.steps / (float(ms2.item()) / 1000.0), "unit": UNIT,
                "h2d_bytes_per_step": 3 * w * h * 4 * world, "d2h_bytes_per_step": 16 * world}
 
+    # ---- render-only throughput (the metric's "render frames/s"): same scene and cameras,
+    # each rank renders its own frames, device-timed, max over ranks --------------------------
+    from gs3d import render as gs_render
+    rb = trainer.render_buffers
+    for k in range(3):
+        gs_render(trainer.render_outputs, trainer.gaussians, cams[k % len(cams)], trainer.tiling,
+                  trainer.render_options, rb, host_sync=False)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for k in range(args.steps):
+        gs_render(trainer.render_outputs, trainer.gaussians, cams[(k * world + rank) % len(cams)],
+                  trainer.tiling, trainer.render_options, rb, host_sync=False)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if int(rb.device_counts[2].item()) & _abi.GS3D_STATUS_DUP_OVERFLOW:
+        raise RuntimeError("duplicate-key capacity overflow during the render timing")
+    ms3 = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(ms3, op=dist.ReduceOp.MAX)
+    render_fps = {"value": world * args.steps / (float(ms3.item()) / 1000.0), "unit": "frames/s",
+                  "ms_per_frame": float(ms3.item()) / args.steps,
+                  "workload": "forward render only, same scene, 1920x1080, one frame per GPU per step"}
+
     # ---- roofline of the dominant kernel ---------------------------------------------
     peak, peak_kind = measured_peaks()
     w, h = cams[0].width, cams[0].height
@@ -364,10 +409,15 @@ def main() -> None:
     dominant = max(prof.items(), key=lambda kv: kv[1][1])[0]
     dom = stages[dominant]
     achieved = dom["alg_GBps"]
+    dom_bytes = stage_bytes(dominant, F, D, gv.n, w, h, passes)
+    traffic = (round(NCU_TRAFFIC_FRACTION[dominant] * dom_bytes / 1e9, 4)
+               if dominant in NCU_TRAFFIC_FRACTION and dom_bytes else None)
     roofline = {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peak,
                 "peak_source": peak_kind, "unit": "GB/s",
                 "frac": round(achieved / peak, 4) if achieved else None,
-                "traffic": None}
+                "traffic": traffic, "traffic_unit": "GB per launch",
+                "limiter": ("FP32 issue (ncu: ~83% issue-active, <2% DRAM)"
+                            if dominant in ("raster", "bwd_raster") else "HBM")}
     gpu_launches = 0
     for name, (cnt, _) in prof.items():
         k = KERNELS_PER_STAGE.get(name, 1 + 3 * passes if name == "sort" else 1)
@@ -387,7 +437,7 @@ def main() -> None:
                        "tiles": [til.tile_width, til.tile_height],
                        "parallelism": f"dp{world}" if world > 1 else "single",
                        "l2": "inputs larger than L2 (2.1 GB params+moments), no flush"},
-            "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk,
+            "e2e": e2e, "render": render_fps, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk,
             "gpu_launches": gpu_launches, "stages": stages,
         }
         print(json.dumps(line), flush=True)
