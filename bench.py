@@ -51,7 +51,7 @@ FALLBACK_HBM_GBS = 6650.0
 KERNELS_PER_STAGE = {"keep_compact": 3, "project": 1, "dup_scan": 3, "dup_keys": 1, "tiles_end": 1,
                      "raster": 1, "zero_2d": 1, "bwd_raster": 1, "bwd_project": 1, "loss": 3,
                      "adc_stats": 1, "scatter_dense": 1, "adam_dense": 2, "adam": 2,
-                     "zero_dense": 0}
+                     "zero_dense": 0, "tile_count": 3, "sort": 2}
 
 
 def parse():
@@ -151,7 +151,8 @@ def stage_bytes(stage: str, F: int, D: int, n: int, w: int, h: int, passes: int)
     """Algorithmic bytes per launch (the per-unit figures of the hot-path analysis)."""
     return {
         "project": 300.0 * F,
-        "sort": 24.0 * passes * D,
+        "sort": 20.0 * F + 28.0 * D,          # scatter (rect, depth; key) + segment sort (key; code, value)
+        "tile_count": 16.0 * F,              # tile rectangles
         "adam": 1656.0 * F,
         "adam_dense": 1656.0 * F + 240.0 * n,
         "bwd_project": 548.0 * F,
@@ -420,7 +421,7 @@ def main() -> None:
                             if dominant in ("raster", "bwd_raster") else "HBM")}
     gpu_launches = 0
     for name, (cnt, _) in prof.items():
-        k = KERNELS_PER_STAGE.get(name, 1 + 3 * passes if name == "sort" else 1)
+        k = KERNELS_PER_STAGE.get(name, 1)
         gpu_launches += cnt * k
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -46,6 +46,7 @@ typedef struct CUstream_st* gs3d_stream_t; /* ABI-compatible with cudaStream_t *
 
 /* render flags */
 #define GS3D_RENDER_NO_HOST_SYNC 1u /* never block: D is checked on the device only      */
+#define GS3D_RENDER_REFERENCE_ORDER 2u /* F4-F7 as the reference stages them (see below)   */
 
 /* backward flags */
 #define GS3D_BACKWARD_FIX_SH16 1u /* use coefficient 16 in the degree-3 direction Jacobian
@@ -230,6 +231,13 @@ GS3D_API int gs3d_render_forward_workspace_size(
 
 /* Filter (F1), compact (F2), project (F3), count + scan duplicates (F4), write keys (F5),
  * sort (F6), tile ranges (F7), alpha-blend (F8) or fill the void image (F9).
+ * By default F4-F7 run as a tile-bucket sort: per-tile counts and their scan give
+ * tiles_end_sdfgidx, and each tile's entries are sorted by (depth bits, filtered index) in
+ * shared memory, which yields sdf2dgs_codes, sdfgidx_to_fgidx and tiles_end_sdfgidx identical
+ * to the reference's stable sort; df2dgs_codes is then scratch, and dfgidx_to_fgidx and
+ * nb_overlapped_tiles_cs are not written. With GS3D_RENDER_REFERENCE_ORDER those three are
+ * filled as the reference fills them (scan, keys in filtered order, stable radix sort).
+ * The camera needs 0 <= near_z < far_z.
  * F and D are written to render_buffers.device_counts[0..1]; when host_counts is not NULL
  * they are also copied there (pinned memory; valid after the stream reaches this point).
  * Without GS3D_RENDER_NO_HOST_SYNC the call waits once for D and returns

@@ -103,8 +103,7 @@ __global__ void __launch_bounds__(512) k_bwd_raster(const BwdArgs a) {
 
     const int F = a.counts[0];
     const int64_t Draw = a.counts[1];
-    const int D = (int)(Draw < a.capacity_dup ? Draw : a.capacity_dup);
-    if (F == 0 || D == 0) return;
+    if (F == 0 || Draw == 0 || Draw > a.capacity_dup) return;  // nothing drawn (or overflow)
 
     const int t = threadIdx.x;
     const int lane = t & 31, warp = t >> 5;

@@ -348,11 +348,15 @@ struct FwdLayout {
     size_t sums, sort, total;
 };
 
-FwdLayout fwd_layout(int64_t capacity_n, int64_t capacity_dup) {
+// scan sums, then one region used either by the radix sort (reference-order pipeline) or by
+// the tile-bucket sort
+FwdLayout fwd_layout(int64_t capacity_n, int64_t capacity_dup, int nb_tiles) {
     FwdLayout L;
     size_t off = 0;
     L.sums = off; off += scan_workspace_bytes(capacity_n > 0 ? capacity_n : 1);
-    L.sort = off; off += radix_sort_workspace_bytes(capacity_dup);
+    L.sort = off;
+    off += std::max(radix_sort_workspace_bytes(capacity_dup),
+                    tile_sort_workspace_bytes(capacity_dup, nb_tiles > 0 ? nb_tiles : 1));
     L.total = off;
     return L;
 }
@@ -368,6 +372,10 @@ int check_common(const gs3d_gaussians* g, const gs3d_camera* cam, const gs3d_til
     if (opt->sh_degree < 0 || opt->sh_degree > g->sh_degree)
         return invalid("render SH degree %d with storage degree %d", opt->sh_degree, g->sh_degree);
     if (cam->width <= 0 || cam->height <= 0) return invalid("camera size %dx%d", cam->width, cam->height);
+    // depths of kept Gaussians exceed near_z; a negative near plane would let negative depths
+    // into the keys, whose sign bit the reference's key layout does not order
+    if (!(cam->near_z >= 0.0f) || !(cam->far_z > cam->near_z))
+        return invalid("clip planes near %g, far %g (need 0 <= near < far)", cam->near_z, cam->far_z);
     if (opt->max_alpha != opt->max_alpha || opt->min_alpha != opt->min_alpha ||
         opt->min_transmittance != opt->min_transmittance)
         return invalid("NaN alpha / transmittance threshold in the render options");
@@ -400,7 +408,7 @@ GS3D_API int gs3d_render_forward_workspace_size(int64_t capacity_n, int64_t capa
                                                 int32_t nb_tiles, size_t* bytes) {
     if (!bytes) return invalid("bytes is NULL");
     if (capacity_n < 0 || capacity_dup < 0 || nb_tiles < 0) return invalid("negative capacity");
-    *bytes = fwd_layout(capacity_n, capacity_dup).total;
+    *bytes = fwd_layout(capacity_n, capacity_dup, nb_tiles).total;
     return GS3D_OK;
 }
 
@@ -421,7 +429,8 @@ GS3D_API int gs3d_render_forward(const gs3d_render_outputs* outputs, const gs3d_
     if (((uintptr_t)buf->intersected_tile_ranges & 15) || ((uintptr_t)g->means_opacity_features & 15) ||
         ((uintptr_t)g->rotation_features & 15))
         return invalid("tile ranges, means/opacity and rotation arrays must be 16-byte aligned");
-    const FwdLayout L = fwd_layout(buf->capacity_n, buf->capacity_dup);
+    const FwdLayout L = fwd_layout(buf->capacity_n, buf->capacity_dup,
+                                   til->nb_tiles_x * til->nb_tiles_y);
     if (!buf->workspace || buf->workspace_bytes < L.total)
         return set_error("render workspace %zu bytes < %zu", buf->workspace_bytes, L.total),
                GS3D_ERR_WORKSPACE;
@@ -471,7 +480,45 @@ GS3D_API int gs3d_render_forward(const gs3d_render_outputs* outputs, const gs3d_
         }
         GS3D_LAUNCHED("k_project");
     }
-    // F4
+    if (!(flags & GS3D_RENDER_REFERENCE_ORDER) && nb_tiles <= tile_sort_max_tiles()) {
+        // F4 - F7 as a tile-bucket sort (tile_sort.cu): same sorted arrays and tile ends
+        const int4* ranges = reinterpret_cast<const int4*>(buf->intersected_tile_ranges);
+        {
+            ProfScope prof("tile_count", stream);
+            GS3D_RETURN_IF(tile_sort_count(ws + L.sort, L.total - L.sort, counts, ranges, cap_n,
+                                           til->nb_tiles_x, nb_tiles, buf->capacity_dup,
+                                           buf->tiles_end_sdfgidx, stream));
+        }
+        if (!(flags & GS3D_RENDER_NO_HOST_SYNC)) {
+            int32_t local[4];
+            int32_t* dst = host_counts ? host_counts : local;
+            GS3D_CUDA(cudaMemcpyAsync(dst, counts, 4 * sizeof(int32_t), cudaMemcpyDeviceToHost,
+                                      stream),
+                      "copy counts");
+            GS3D_CUDA(cudaStreamSynchronize(stream), "sync counts");
+            if ((int64_t)dst[1] > buf->capacity_dup)
+                return set_error("%d duplicated keys exceed capacity_dup = %lld", dst[1],
+                                 (long long)buf->capacity_dup),
+                       GS3D_ERR_CAPACITY;
+        }
+        {
+            ProfScope prof("sort", stream);
+            GS3D_RETURN_IF(tile_sort_order(ws + L.sort, counts, ranges, buf->depths, cap_n,
+                                           til->nb_tiles_x, nb_tiles, buf->capacity_dup,
+                                           buf->tiles_end_sdfgidx, buf->df2dgs_codes,
+                                           buf->sdf2dgs_codes, buf->sdfgidx_to_fgidx, stream));
+        }
+        {
+            ProfScope prof("raster", stream);
+            GS3D_RETURN_IF(launch_raster(*outputs, *cam, *til, *opt, *buf, stream));
+        }
+        if ((flags & GS3D_RENDER_NO_HOST_SYNC) && host_counts)
+            GS3D_CUDA(cudaMemcpyAsync(host_counts, counts, 4 * sizeof(int32_t),
+                                      cudaMemcpyDeviceToHost, stream),
+                      "copy counts");
+        return GS3D_OK;
+    }
+    // reference order: F4
     {
         ProfScope prof("dup_scan", stream);
         GS3D_RETURN_IF(inclusive_scan_i32(buf->nb_overlapped_tiles, buf->nb_overlapped_tiles_cs,

@@ -18,6 +18,19 @@ int radix_sort_pairs(void* ws, size_t ws_bytes, const int64_t* keys_in, int64_t*
                      const int32_t* count_dev, int64_t count_host, int highest_key_bit,
                      cudaStream_t stream);
 
+// Tile-bucket sort of the duplicated keys (tile_sort.cu). tile_sort_count writes the per-tile
+// inclusive ends into tiles_end and D into counts[1] (status bit on overflow);
+// tile_sort_order then fills the sorted keys and values. The counts F / D are read on the device.
+size_t tile_sort_workspace_bytes(int64_t capacity_dup, int nb_tiles);
+int tile_sort_max_tiles();  // more tiles than this take the reference-order pipeline
+int tile_sort_count(void* ws, size_t ws_bytes, int32_t* counts, const int4* ranges,
+                    int64_t capacity_n, int tiles_x, int nb_tiles, int64_t capacity_dup,
+                    int32_t* tiles_end, cudaStream_t stream);
+int tile_sort_order(void* ws, const int32_t* counts, const int4* ranges, const float* depths,
+                    int64_t capacity_n, int tiles_x, int nb_tiles, int64_t capacity_dup,
+                    const int32_t* tiles_end, int64_t* keys_scratch, int64_t* sorted_codes,
+                    int32_t* sorted_vals, cudaStream_t stream);
+
 // Device-wide scans over int32 with the length on the device (len_dev[0]) or on the host.
 size_t scan_workspace_bytes(int64_t capacity);
 // inclusive scan of in[0, len) into out; the total is written to total_dev[0].

@@ -63,8 +63,9 @@ __global__ void __launch_bounds__(512) k_raster(const RasterArgs a) {
 
     const int F = a.counts[0];
     const int64_t Draw = a.counts[1];
-    const int D = (int)(Draw < a.capacity_dup ? Draw : a.capacity_dup);
-    if (F == 0 || D == 0) {  // render_void!
+    // render_void! when there is nothing to draw, and also when the duplicated keys overflowed
+    // the buffers (flagged in counts[2]; the sorted arrays and tile ends are then not valid)
+    if (F == 0 || Draw == 0 || Draw > a.capacity_dup) {
         if (inside) {
             if (a.rgb) { a.rgb[3 * px] = a.bg0; a.rgb[3 * px + 1] = a.bg1; a.rgb[3 * px + 2] = a.bg2; }
             if (a.trans) a.trans[px] = 1.0f;

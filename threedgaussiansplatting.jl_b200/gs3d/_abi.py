@@ -18,6 +18,7 @@ GS3D_ERR_WORKSPACE = -4
 GS3D_ERR_UNSUPPORTED = -5
 GS3D_STATUS_DUP_OVERFLOW = 1
 GS3D_RENDER_NO_HOST_SYNC = 1
+GS3D_RENDER_REFERENCE_ORDER = 2
 GS3D_BACKWARD_FIX_SH16 = 1
 
 f32p = C.POINTER(C.c_float)

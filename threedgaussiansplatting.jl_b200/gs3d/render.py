@@ -17,15 +17,21 @@ def _stream_handle(stream: torch.cuda.Stream | None) -> int:
 
 def render(outputs: RenderOutputs, gaussians: GaussiansVector, camera: PinholeCamera,
            tiling: Tiling, options: RenderOptions, buffers: RenderBuffers,
-           stream: torch.cuda.Stream | None = None, host_sync: bool = True) -> RenderOutputs:
+           stream: torch.cuda.Stream | None = None, host_sync: bool = True,
+           reference_order: bool = False) -> RenderOutputs:
     """Render `gaussians` for `camera` into `outputs` (in place), like the reference's
     GPU `render!`. With `host_sync` the call waits once for the duplicate count and grows the
     duplicate buffers when they are too small (the reference's set_nb_dfgaussians!);
-    without it nothing blocks and an overflow shows up in buffers.device_counts[2]."""
+    without it nothing blocks and an overflow shows up in buffers.device_counts[2].
+    `reference_order` also fills the unsorted duplicate arrays and the duplicate-count scan
+    as the reference does (GS3D_RENDER_REFERENCE_ORDER); the sorted arrays, tile ends and
+    images are the same either way."""
     if gaussians.n > buffers.capacity_n:
         raise ValueError(f"{gaussians.n} Gaussians exceed the buffers' capacity {buffers.capacity_n}")
     lib = _abi.lib()
     flags = 0 if host_sync else _abi.GS3D_RENDER_NO_HOST_SYNC
+    if reference_order:
+        flags |= _abi.GS3D_RENDER_REFERENCE_ORDER
     host = buffers.host_counts
     hptr = C.c_void_p(host.data_ptr()) if host is not None else None
     args = (outputs.to_c(), gaussians.to_c(), camera.to_c(), tiling.to_c(), options.to_c())
