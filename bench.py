@@ -169,10 +169,12 @@ def stage_bytes(stage: str, F: int, D: int, n: int, w: int, h: int, passes: int)
 # launch's algorithmic bytes; the full-size traffic is that fraction of the full-size bytes
 # (traffic grows with the same units).
 NCU_TRAFFIC_FRACTION = {
-    # 114.40 MB read + 6.12 MB write at F = 992,004, D = 943,223, 1920x1080
-    "bwd_raster": 120.52e6 / (40.0 * 943_223 + 24.0 * 2_073_600 + 36.0 * 992_004),
-    # 39.42 MB read + 8.89 MB write
-    "raster": 48.31e6 / (40.0 * 943_223 + 20.0 * 2_073_600),
+    # 114.26 MB read + 6.23 MB write at F = 992,004, D = 943,223, 1920x1080
+    "bwd_raster": 120.49e6 / (40.0 * 943_223 + 24.0 * 2_073_600 + 36.0 * 992_004),
+    # 39.40 MB read + 9.17 MB write
+    "raster": 48.57e6 / (40.0 * 943_223 + 20.0 * 2_073_600),
+    # k_adam_sh16 766.31 MB read + 516.67 MB write, k_adam_geom 179.64 MB + 74.07 MB
+    "adam": (766.31e6 + 516.67e6 + 179.64e6 + 74.07e6) / (1656.0 * 992_004),
 }
 
 
