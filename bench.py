@@ -288,8 +288,12 @@ def main() -> None:
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     if world > 1:
+        # NCCL on high-priority streams: its blocks are scheduled ahead of the compute kernels'
+        # as SM slots free up, so the chunked reduce-scatters overlap the projection backward
+        opts = dist.ProcessGroupNCCL.Options()
+        opts.is_high_priority_stream = True
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=device)
+                                device_id=device, pg_options=opts)
     import gs3d
     from gs3d import _abi
     from gs3d.dp import DataParallelTrainer

@@ -287,6 +287,23 @@ GS3D_API int gs3d_backward_dense(
     const gs3d_render_options* options, const gs3d_render_buffers* buffers,
     uint32_t flags, float* dense, int32_t n, gs3d_stream_t stream);
 
+/* gs3d_backward_dense in two phases, so that the rows of one range of Gaussians can be
+ * exchanged while the next range is computed: gs3d_backward_raster fills the 2D arrays of
+ * fgradients (B1, B2); gs3d_backward_project_dense then runs B3/B4 for the filtered Gaussians
+ * whose 0-based index is in [g_begin, g_end), writing row gidx - g_begin of dense_rows (rows
+ * are not zeroed here: the caller zeroes them, touched flags are set). */
+GS3D_API int gs3d_backward_raster(
+    const gs3d_fgradients* fgradients, const float* rgb_image_grad,
+    const gs3d_render_outputs* outputs, const gs3d_gaussians* gaussians,
+    const gs3d_camera* camera, const gs3d_tiling* tiling,
+    const gs3d_render_options* options, const gs3d_render_buffers* buffers,
+    uint32_t flags, gs3d_stream_t stream);
+GS3D_API int gs3d_backward_project_dense(
+    const gs3d_fgradients* fgradients, const gs3d_gaussians* gaussians,
+    const gs3d_camera* camera, const gs3d_tiling* tiling,
+    const gs3d_render_options* options, const gs3d_render_buffers* buffers,
+    uint32_t flags, float* dense_rows, int32_t g_begin, int32_t g_end, gs3d_stream_t stream);
+
 /* gs3d_adam_step_dense over the Gaussians [g_begin, g_end) only, whose rows start at dense[0]
  * (a rank's shard of reduce-scattered rows). */
 GS3D_API int gs3d_adam_step_dense_range(

@@ -13,7 +13,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from gs3d.dp import DENSE_ROW, shard_range, view_index
+from gs3d.dp import CHUNKS, DENSE_ROW, chunk_layout, shard_range, view_index
 
 
 def test_shard_ranges_partition_the_gaussians():
@@ -25,6 +25,20 @@ def test_shard_ranges_partition_the_gaussians():
                 assert S * world >= n and (S - 1) * world < n or n < world
                 covered.extend(range(lo, hi))
             assert covered == list(range(n)), (n, world)
+
+
+def test_chunk_ownership_partitions_the_gaussians():
+    """Rank r owns [c C + r S, c C + (r + 1) S) of every chunk c; together they cover [0, n)."""
+    for n in (1, 5, 8, 9, 1000, 313_001):
+        for world in (1, 2, 3, 8):
+            S, C_ = chunk_layout(n, world, CHUNKS)
+            assert C_ == S * world and CHUNKS * C_ >= n
+            covered = []
+            for c in range(CHUNKS):
+                for r in range(world):
+                    lo = c * C_ + r * S
+                    covered.extend(range(min(lo, n), min(lo + S, n)))
+            assert sorted(covered) == list(range(n)), (n, world)
 
 
 def test_views_of_a_step_are_distinct():
@@ -46,23 +60,28 @@ def _worker(rank, world, port, q):
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
         dist.init_process_group("gloo", rank=rank, world_size=world)
         n = 11
-        S, lo, hi = shard_range(n, world, rank)
-        rows = S * world
+        S, C_ = chunk_layout(n, world, CHUNKS)
+        rows = CHUNKS * C_
         # each rank's dense rows: rank-dependent values, padding rows zero
         dense = torch.zeros((rows, DENSE_ROW))
         dense[:n] = torch.arange(n * DENSE_ROW, dtype=torch.float32).view(n, DENSE_ROW) * (rank + 1)
-        flat = dense.view(-1)
-        per = S * DENSE_ROW
-        dist.reduce_scatter_tensor(flat[rank * per:(rank + 1) * per], flat.clone(), op=dist.ReduceOp.SUM)
         total = sum(r + 1 for r in range(world))
-        want = torch.arange(n * DENSE_ROW, dtype=torch.float32).view(n, DENSE_ROW) * total
-        ok_rs = torch.equal(dense[lo:hi], want[lo:hi])
-        # parameter array: each rank writes its own slice, the all-gather replicates all
+        want = torch.zeros((rows, DENSE_ROW))
+        want[:n] = torch.arange(n * DENSE_ROW, dtype=torch.float32).view(n, DENSE_ROW) * total
+        ok_rs = True
         base = torch.full((rows, 4), -1.0)
-        base[lo:hi] = torch.arange(lo, hi, dtype=torch.float32)[:, None] + 0.5
-        fb = base.view(-1)
-        per4 = fb.numel() // world
-        dist.all_gather_into_tensor(fb, fb[rank * per4:(rank + 1) * per4].clone())
+        for c in range(CHUNKS):  # per chunk: reduce-scatter into the owners' sub-ranges
+            flat = dense[c * C_:(c + 1) * C_].reshape(-1)
+            per = S * DENSE_ROW
+            dist.reduce_scatter_tensor(flat[rank * per:(rank + 1) * per], flat.clone(), op=dist.ReduceOp.SUM)
+            lo = c * C_ + rank * S
+            ok_rs = ok_rs and torch.equal(dense[lo:lo + S], want[lo:lo + S])
+            base[lo:lo + S] = torch.arange(lo, lo + S, dtype=torch.float32)[:, None] + 0.5
+        ok_ag = True
+        for c in range(CHUNKS):  # per chunk: all-gather each owner's sub-range of a parameter array
+            fb = base[c * C_:(c + 1) * C_].reshape(-1)
+            per4 = fb.numel() // world
+            dist.all_gather_into_tensor(fb, fb[rank * per4:(rank + 1) * per4].clone())
         ok_ag = torch.equal(base[:n], torch.arange(n, dtype=torch.float32)[:, None].expand(n, 4) + 0.5)
         q.put((rank, ok_rs, ok_ag))
         dist.destroy_process_group()

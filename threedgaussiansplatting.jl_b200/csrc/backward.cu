@@ -306,8 +306,10 @@ struct BProjArgs {
     int sh_grad_stride;
     int fix_sh16;
     // NULL, or dense gradient rows indexed by Gaussian (kDenseRow floats, layout in gs3d.h):
-    // the 3D gradients then go to row gidx instead of the F-compact arrays above
+    // the 3D gradients then go to row gidx - g_begin instead of the F-compact arrays above
     float* dense;
+    // only filtered Gaussians whose 0-based Gaussian index is in [g_begin, g_end) are done
+    int32_t g_begin, g_end;
 };
 
 // Dense gradient row (GS3D_DENSE_ROW): SH 3 x 16 channel-major at 0, mean 48, opacity feature
@@ -338,9 +340,10 @@ __global__ void __launch_bounds__(128, 6) k_bwd_project(const BProjArgs a, const
     for (int64_t fb = (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * 32; fb < F;
          fb += nwarps * 32) {
       const int f = (int)fb + lane;
-      const int gi = f < F ? a.f2g[f] - 1 : -1;
+      const int gi0 = f < F ? a.f2g[f] - 1 : -1;
+      const int gi = (gi0 >= a.g_begin && gi0 < a.g_end) ? gi0 : -1;
       if (gi >= 0) {
-        float* const drow = a.dense ? a.dense + (size_t)gi * kDenseRow : nullptr;
+        float* const drow = a.dense ? a.dense + (size_t)(gi - a.g_begin) * kDenseRow : nullptr;
         const float* r = a.f2d + 9 * (size_t)f;
         const float4 mo = a.mo4[gi];
         const float orig_op = gs_sigmoid(mo.w);
@@ -627,10 +630,11 @@ __global__ void __launch_bounds__(128, 6) k_bwd_project(const BProjArgs a, const
       __syncwarp();
       const int nrows = (int)min((int64_t)32, (int64_t)F - fb);
       float* const warp_stage = &stage[threadIdx.x >> 5][0][0];
-      if (a.dense) {  // row `row` of the warp goes to dense row gidx (skipped when gidx <= 0)
+      if (a.dense) {  // row `row` of the warp goes to dense row gidx - g_begin (if in range)
+          const int rel = gi >= 0 ? gi - a.g_begin : -1;
           for (int e = lane; e < 32 * NSH; e += 32) {
               const int row = e / NSH, rem = e - row * NSH;
-              const int grow = __shfl_sync(0xffffffffu, gi, row);
+              const int grow = __shfl_sync(0xffffffffu, rel, row);
               if (row >= nrows || grow < 0) continue;
               const int c = rem / MAXO, k = rem - c * MAXO;
               a.dense[(size_t)grow * kDenseRow + (size_t)(c * 16 + k)] = warp_stage[row * (NSH + 1) + rem];
@@ -662,72 +666,79 @@ using namespace gs3d;
 
 namespace {
 
-// backward! with the 3D gradients into the F-compact arrays of fg (dense == NULL) or into
-// dense rows indexed by Gaussian (rows zeroed here first, touched flags set).
+constexpr unsigned kPhaseRaster = 1u, kPhaseProject = 2u;
+
+// backward! in phases: kPhaseRaster = B1 + B2 (the 2D gradients), kPhaseProject = B3 + B4 for
+// the filtered Gaussians with index in [g_begin, g_end), with the 3D gradients into the
+// F-compact arrays of fg (dense == NULL) or into dense rows (row gidx - g_begin; zeroed here
+// first when zero_rows > 0: rows [0, zero_rows) of dense).
 int backward_impl(const gs3d_fgradients* fg, const float* rgb_grad,
                   const gs3d_render_outputs* out, const gs3d_gaussians* g, const gs3d_camera* cam,
                   const gs3d_tiling* til, const gs3d_render_options* opt,
-                  const gs3d_render_buffers* buf, uint32_t flags, float* dense, int32_t n_dense,
-                  cudaStream_t stream) {
+                  const gs3d_render_buffers* buf, uint32_t flags, unsigned phases, float* dense,
+                  int32_t zero_rows, int32_t g_begin, int32_t g_end, cudaStream_t stream) {
     GS3D_RETURN_IF(check_render_common(g, cam, til, opt));
-    if (!fg || !rgb_grad || !out || !buf) return invalid("NULL argument");
-    if (!out->transmittance || !out->last_contributing_sdfgids)
-        return invalid("backward needs the transmittance and last-contributor images");
+    if (!fg || !buf) return invalid("NULL argument");
+    if ((phases & kPhaseRaster) &&
+        (!rgb_grad || !out || !out->transmittance || !out->last_contributing_sdfgids))
+        return invalid("backward needs the gradient image, transmittance and last-contributor images");
     if (!fg->mean2d_grads || !fg->opacity_grads || !fg->licov2d_grads || !fg->color_grads)
         return invalid("NULL 2D gradient array");
-    if (!dense && (!fg->mean3d_grads || !fg->opacity_feature_grads || !fg->scaling_features_grads ||
-                   !fg->rotation_features_grads || !fg->sh_coeffs_grads))
+    const bool compact_out = (phases & kPhaseProject) && !dense;
+    if (compact_out && (!fg->mean3d_grads || !fg->opacity_feature_grads ||
+                        !fg->scaling_features_grads || !fg->rotation_features_grads ||
+                        !fg->sh_coeffs_grads))
         return invalid("NULL gradient array");
-    if (dense && n_dense < g->n) return invalid("dense rows %d < n = %d", n_dense, g->n);
-    if (!dense && (fg->sh_degree < opt->sh_degree || fg->sh_degree > 3))
+    if (g_begin < 0 || g_end < g_begin) return invalid("Gaussian range [%d, %d)", g_begin, g_end);
+    if (compact_out && (fg->sh_degree < opt->sh_degree || fg->sh_degree > 3))
         return invalid("gradient SH degree %d < render degree %d", fg->sh_degree, opt->sh_degree);
     const int64_t cap_n = buf->capacity_n > 0 ? buf->capacity_n : 1;
-    if (dense) {
+    if (dense && zero_rows > 0) {
         ProfScope prof("zero_dense", stream);
-        GS3D_CUDA(cudaMemsetAsync(dense, 0, (size_t)n_dense * kDenseRow * sizeof(float), stream),
+        GS3D_CUDA(cudaMemsetAsync(dense, 0, (size_t)zero_rows * kDenseRow * sizeof(float), stream),
                   "zero dense rows");
     }
-    {
-        ProfScope prof("zero_2d", stream);
-        k_zero_2d<<<grid_for(3 * cap_n, 256, 8), 256, 0, stream>>>(
-            buf->device_counts, fg->mean2d_grads, fg->opacity_grads, fg->licov2d_grads,
-            fg->color_grads);
-        GS3D_LAUNCHED("k_zero_2d");
-    }
-
-    BwdArgs a;
-    a.sfgidx = buf->sdfgidx_to_fgidx;
-    a.tiles_end = buf->tiles_end_sdfgidx;
-    a.f2d = buf->means2d_opacities_inverse_covariances_colors;
-    a.counts = buf->device_counts;
-    a.capacity_dup = buf->capacity_dup;
-    a.trans = out->transmittance;
-    a.last = out->last_contributing_sdfgids;
-    a.rgb_grad = rgb_grad;
-    a.mean2d_g = fg->mean2d_grads;
-    a.opacity_g = fg->opacity_grads;
-    a.licov_g = fg->licov2d_grads;
-    a.color_g = fg->color_grads;
-    a.width = cam->width;
-    a.height = cam->height;
-    a.tile_w = til->tile_width;
-    a.tile_h = til->tile_height;
-    a.tiles_x = til->nb_tiles_x;
-    a.compact = compact_tiles(til->tile_width, til->tile_height);
-    a.bg0 = opt->background[0];
-    a.bg1 = opt->background[1];
-    a.bg2 = opt->background[2];
-    a.min_alpha = opt->min_alpha;
-    a.max_alpha = opt->max_alpha;
-    a.log_min_alpha = opt->min_alpha > 0.0f ? gs_logf(opt->min_alpha) : -INFINITY;
-    const int nthr = til->tile_width * til->tile_height;
-    const size_t smem = (size_t)nthr * (3 * sizeof(float4) + sizeof(float2) + sizeof(int));
-    {
+    if (phases & kPhaseRaster) {
+        {
+            ProfScope prof("zero_2d", stream);
+            k_zero_2d<<<grid_for(3 * cap_n, 256, 8), 256, 0, stream>>>(
+                buf->device_counts, fg->mean2d_grads, fg->opacity_grads, fg->licov2d_grads,
+                fg->color_grads);
+            GS3D_LAUNCHED("k_zero_2d");
+        }
+        BwdArgs a;
+        a.sfgidx = buf->sdfgidx_to_fgidx;
+        a.tiles_end = buf->tiles_end_sdfgidx;
+        a.f2d = buf->means2d_opacities_inverse_covariances_colors;
+        a.counts = buf->device_counts;
+        a.capacity_dup = buf->capacity_dup;
+        a.trans = out->transmittance;
+        a.last = out->last_contributing_sdfgids;
+        a.rgb_grad = rgb_grad;
+        a.mean2d_g = fg->mean2d_grads;
+        a.opacity_g = fg->opacity_grads;
+        a.licov_g = fg->licov2d_grads;
+        a.color_g = fg->color_grads;
+        a.width = cam->width;
+        a.height = cam->height;
+        a.tile_w = til->tile_width;
+        a.tile_h = til->tile_height;
+        a.tiles_x = til->nb_tiles_x;
+        a.compact = compact_tiles(til->tile_width, til->tile_height);
+        a.bg0 = opt->background[0];
+        a.bg1 = opt->background[1];
+        a.bg2 = opt->background[2];
+        a.min_alpha = opt->min_alpha;
+        a.max_alpha = opt->max_alpha;
+        a.log_min_alpha = opt->min_alpha > 0.0f ? gs_logf(opt->min_alpha) : -INFINITY;
+        const int nthr = til->tile_width * til->tile_height;
+        const size_t smem = (size_t)nthr * (3 * sizeof(float4) + sizeof(float2) + sizeof(int));
         ProfScope prof("bwd_raster", stream);
         const dim3 grid(til->nb_tiles_x, til->nb_tiles_y);
         k_bwd_raster<<<grid, nthr, smem, stream>>>(a);
         GS3D_LAUNCHED("k_bwd_raster");
     }
+    if (!(phases & kPhaseProject)) return GS3D_OK;
 
     BProjArgs p;
     p.mo4 = reinterpret_cast<const float4*>(g->means_opacity_features);
@@ -750,6 +761,8 @@ int backward_impl(const gs3d_fgradients* fg, const float* rgb_grad,
     p.sh_grad_stride = (fg->sh_degree + 1) * (fg->sh_degree + 1);
     p.fix_sh16 = (flags & GS3D_BACKWARD_FIX_SH16) ? 1 : 0;
     p.dense = dense;
+    p.g_begin = g_begin;
+    p.g_end = g_end;
     const int grid = grid_for(cap_n, 128, 16);
     ProfScope prof("bwd_project", stream);
     switch (opt->sh_degree) {
@@ -770,7 +783,8 @@ extern "C" GS3D_API int gs3d_backward(const gs3d_fgradients* fg, const float* rg
                                       const gs3d_render_options* opt,
                                       const gs3d_render_buffers* buf, uint32_t flags,
                                       gs3d_stream_t stream) {
-    return backward_impl(fg, rgb_grad, out, g, cam, til, opt, buf, flags, nullptr, 0,
+    return backward_impl(fg, rgb_grad, out, g, cam, til, opt, buf, flags,
+                         kPhaseRaster | kPhaseProject, nullptr, 0, 0, INT32_MAX,
                          reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -782,6 +796,32 @@ extern "C" GS3D_API int gs3d_backward_dense(const gs3d_fgradients* fg, const flo
                                             const gs3d_render_buffers* buf, uint32_t flags,
                                             float* dense, int32_t n, gs3d_stream_t stream) {
     if (!dense) return invalid("NULL dense rows");
-    return backward_impl(fg, rgb_grad, out, g, cam, til, opt, buf, flags, dense, n,
+    if (!g || n < g->n) return invalid("dense rows %d < n", n);
+    return backward_impl(fg, rgb_grad, out, g, cam, til, opt, buf, flags,
+                         kPhaseRaster | kPhaseProject, dense, n, 0, g->n,
                          reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" GS3D_API int gs3d_backward_raster(const gs3d_fgradients* fg, const float* rgb_grad,
+                                             const gs3d_render_outputs* out,
+                                             const gs3d_gaussians* g, const gs3d_camera* cam,
+                                             const gs3d_tiling* til,
+                                             const gs3d_render_options* opt,
+                                             const gs3d_render_buffers* buf, uint32_t flags,
+                                             gs3d_stream_t stream) {
+    return backward_impl(fg, rgb_grad, out, g, cam, til, opt, buf, flags, kPhaseRaster, nullptr,
+                         0, 0, 0, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" GS3D_API int gs3d_backward_project_dense(const gs3d_fgradients* fg,
+                                                    const gs3d_gaussians* g, const gs3d_camera* cam,
+                                                    const gs3d_tiling* til,
+                                                    const gs3d_render_options* opt,
+                                                    const gs3d_render_buffers* buf, uint32_t flags,
+                                                    float* dense_rows, int32_t g_begin,
+                                                    int32_t g_end, gs3d_stream_t stream) {
+    if (!dense_rows) return invalid("NULL dense rows");
+    if (!g || g_end > g->n) return invalid("Gaussian range end %d > n", g_end);
+    return backward_impl(fg, nullptr, nullptr, g, cam, til, opt, buf, flags, kPhaseProject,
+                         dense_rows, 0, g_begin, g_end, reinterpret_cast<cudaStream_t>(stream));
 }

@@ -140,6 +140,12 @@ SIGNATURES = {
                                       C.c_uint32, C.c_void_p, C.c_int32, C.c_void_p]),
     "gs3d_adam_step_dense_range": (C.c_int, [P(GaussiansC), P(AdamMomentsC), C.c_void_p, C.c_int32,
                                              C.c_int32, P(AdamParamsC), C.c_void_p]),
+    "gs3d_backward_raster": (C.c_int, [P(FGradientsC), C.c_void_p, P(RenderOutputsC), P(GaussiansC),
+                                       P(Camera), P(TilingC), P(RenderOptionsC), P(RenderBuffersC),
+                                       C.c_uint32, C.c_void_p]),
+    "gs3d_backward_project_dense": (C.c_int, [P(FGradientsC), P(GaussiansC), P(Camera), P(TilingC),
+                                              P(RenderOptionsC), P(RenderBuffersC), C.c_uint32,
+                                              C.c_void_p, C.c_int32, C.c_int32, C.c_void_p]),
     "gs3d_loss_workspace_size": (C.c_int, [C.c_int32, C.c_int32, P(C.c_size_t)]),
     "gs3d_loss_l1_dssim": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_float,
                                      C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),

@@ -94,6 +94,41 @@ def backward(fgradients: FilteredGaussiansGradients, rgb_image_grad: torch.Tenso
     return fgradients
 
 
+def backward_raster(fgradients: FilteredGaussiansGradients, rgb_image_grad: torch.Tensor,
+                    outputs: RenderOutputs, gaussians: GaussiansVector, camera: PinholeCamera,
+                    tiling: Tiling, options: RenderOptions, buffers: RenderBuffers,
+                    fix_sh16: bool = False, stream: torch.cuda.Stream | None = None):
+    """First phase of backward(): the 2D gradients only (B1, B2)."""
+    assert rgb_image_grad.is_contiguous() and rgb_image_grad.dtype == torch.float32
+    lib = _abi.lib()
+    args = [fgradients.to_c(), outputs.to_c(), gaussians.to_c(), camera.to_c(), tiling.to_c(),
+            options.to_c(), buffers.to_c()]
+    flags = _abi.GS3D_BACKWARD_FIX_SH16 if fix_sh16 else 0
+    _abi.check(lib.gs3d_backward_raster(C.byref(args[0]), C.c_void_p(rgb_image_grad.data_ptr()),
+                                        C.byref(args[1]), C.byref(args[2]), C.byref(args[3]),
+                                        C.byref(args[4]), C.byref(args[5]), C.byref(args[6]), flags,
+                                        C.c_void_p(_stream_handle(stream))))
+    return fgradients
+
+
+def backward_project_dense(fgradients: FilteredGaussiansGradients, gaussians: GaussiansVector,
+                           camera: PinholeCamera, tiling: Tiling, options: RenderOptions,
+                           buffers: RenderBuffers, dense_rows: torch.Tensor, g_begin: int,
+                           g_end: int, fix_sh16: bool = False,
+                           stream: torch.cuda.Stream | None = None) -> None:
+    """Second phase: 3D gradients of the filtered Gaussians with index in [g_begin, g_end)
+    into row gidx - g_begin of `dense_rows` (a view starting at row g_begin; not zeroed here)."""
+    assert dense_rows.is_contiguous() and dense_rows.dtype == torch.float32
+    lib = _abi.lib()
+    args = [fgradients.to_c(), gaussians.to_c(), camera.to_c(), tiling.to_c(), options.to_c(),
+            buffers.to_c()]
+    flags = _abi.GS3D_BACKWARD_FIX_SH16 if fix_sh16 else 0
+    _abi.check(lib.gs3d_backward_project_dense(
+        C.byref(args[0]), C.byref(args[1]), C.byref(args[2]), C.byref(args[3]), C.byref(args[4]),
+        C.byref(args[5]), flags, C.c_void_p(dense_rows.data_ptr()), int(g_begin), int(g_end),
+        C.c_void_p(_stream_handle(stream))))
+
+
 def backward_dense(fgradients: FilteredGaussiansGradients, rgb_image_grad: torch.Tensor,
                    outputs: RenderOutputs, gaussians: GaussiansVector, camera: PinholeCamera,
                    tiling: Tiling, options: RenderOptions, buffers: RenderBuffers,

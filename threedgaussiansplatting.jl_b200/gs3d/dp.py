@@ -1,15 +1,21 @@
 """Multi-view data-parallel training: one process per GPU.
 
 Each rank renders and back-propagates its own view of the step with the 3D gradients written
-straight into dense rows indexed by Gaussian (gs3d_backward_dense). The optimizer step is
-sharded over the ranks: the rows are summed with one NCCL reduce-scatter, rank r applies the
-Adam update to the touched Gaussians of its range [r S, (r + 1) S) (S = ceil(n / world)) with
-gs3d_adam_step_dense_range, and the updated parameters are all-gathered, so the parameters are
-identical on every rank after each step while each rank keeps its own range's moments current.
-Parameters, moments and rows live in storage padded to world * S rows so that both
-collectives run in place. A densify step all-gathers the moments, all-reduces the rows and
-the statistics, and every rank then makes the same decisions and the full dense update, as
-the reference retargets fgidx_to_gidx. With one rank this is the reference's sparse update.
+straight into dense rows indexed by Gaussian (no scatter pass). The optimizer step is sharded
+over the ranks and pipelined over `chunks` ranges of Gaussians: chunk c holds rows
+[c C, (c + 1) C), C = world * S, and rank r owns the sub-range [c C + r S, c C + (r + 1) S) of
+every chunk. For each chunk in turn the projection backward writes its rows
+(gs3d_backward_project_dense) and an in-place NCCL reduce-scatter sums them into the owners'
+sub-ranges while the next chunk's rows are computed; then, chunk by chunk, each rank applies
+the Adam update to the touched Gaussians of its sub-range (gs3d_adam_step_dense_range) and
+in-place all-gathers of the four parameter arrays replicate the result while the next chunk
+is updated. Parameters are identical on every rank after each step; each rank keeps its own
+sub-ranges' moments current. Parameters, moments and rows live in storage padded to
+chunks * C rows so that every collective runs in place. A densify step all-gathers the
+moments, all-reduces the rows and the statistics, and every rank then makes the same
+decisions and the full update, as the reference retargets fgidx_to_gidx. With one rank this
+is the reference's sparse update. `optimizer_step="replicated"` instead all-reduces each chunk's
+rows and lets every rank apply the full update (no parameter exchange; measured slower).
 Views: a permutation of the cameras drawn from a seed shared by all ranks; at step k rank r
 takes entry (k * world + r) mod #cameras.
 """
@@ -19,14 +25,16 @@ import ctypes as C
 
 import torch
 import torch.distributed as dist
+from torch.distributed.distributed_c10d import _coalescing_manager
 
 from . import _abi
 from . import adc as adc_mod
-from .backward import backward_dense
+from .backward import backward_dense, backward_project_dense, backward_raster
 from .render import _stream_handle, render
 from .training import Trainer
 
 DENSE_ROW = 60
+CHUNKS = 4
 
 
 def view_index(step: int, rank: int, world: int, perm, ncams: int) -> int:
@@ -37,27 +45,45 @@ def view_index(step: int, rank: int, world: int, perm, ncams: int) -> int:
 
 
 def shard_range(n: int, world: int, rank: int) -> tuple[int, int, int]:
-    """(S, begin, end): shard size and this rank's Gaussian range."""
+    """(S, begin, end) of an unchunked split: shard size and this rank's Gaussian range."""
     S = max(1, -(-n // world))
     return S, min(n, rank * S), min(n, (rank + 1) * S)
 
 
+def chunk_layout(n: int, world: int, chunks: int) -> tuple[int, int]:
+    """(S, C): per-rank sub-range size and chunk size (C = world * S, chunks * C >= n)."""
+    S = max(1, -(-n // (chunks * world)))
+    return S, S * world
+
+
 class DataParallelTrainer(Trainer):
-    def __init__(self, *args, group=None, **kw):
+    """`optimizer_step`: "sharded" (reduce-scatter rows, Adam on the rank's sub-ranges,
+    all-gather parameters) or "replicated" (all-reduce rows chunk by chunk, the full Adam update
+    on every rank, no parameter exchange)."""
+
+    def __init__(self, *args, group=None, optimizer_step: str = "sharded", chunks: int | None = None,
+                 **kw):
         super().__init__(*args, **kw)
+        if optimizer_step not in ("sharded", "replicated"):
+            raise ValueError(f"optimizer_step {optimizer_step!r}")
+        self.optimizer_step = optimizer_step
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        # pipeline depth (measured at 3M Gaussians: 4 chunks best up to 4 ranks; with 8 ranks
+        # each rank's share of a chunk gets small, 2 chunks)
+        self.chunks = int(chunks) if chunks else (CHUNKS if self.world <= 4 else 2)
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.step_index = 0
         self.perm = self.rng.permutation(len(self.cameras))
         self._bases = {}
         self.dense = None
+        self._side = None
         self._ensure_padded()
 
     # -- padded storage -------------------------------------------------------------------
     def _padded_rows(self) -> int:
-        S, _, _ = shard_range(self.gaussians.n, self.world, self.rank)
-        return S * self.world
+        _, C_ = chunk_layout(self.gaussians.n, self.world, self.chunks)
+        return self.chunks * C_
 
     def _pad(self, key: str, t: torch.Tensor, rows: int) -> torch.Tensor:
         """t as the leading n rows of a (rows, ...) base tensor (reused when t already is)."""
@@ -85,15 +111,20 @@ class DataParallelTrainer(Trainer):
         if self.dense is None or self.dense.shape[0] != rows:
             self.dense = torch.zeros((rows, DENSE_ROW), dtype=torch.float32, device=self.device)
 
-    def _all_gather_rows(self, keys) -> None:
-        """In-place all-gather of each padded array's shards."""
+    def _gather_chunk(self, keys, c: int, async_op: bool):
+        """In-place all-gather of chunk c of each padded array (rank r's sub-range to all), as
+        one NCCL group."""
         if self.world <= 1:
-            return
-        for key in keys:
-            flat = self._bases[key].view(-1)
-            per = flat.numel() // self.world
-            dist.all_gather_into_tensor(flat, flat[self.rank * per:(self.rank + 1) * per],
-                                        group=self.group)
+            return []
+        S, C_ = chunk_layout(self.gaussians.n, self.world, self.chunks)
+        with _coalescing_manager(group=self.group, device=self.device, async_ops=async_op) as cm:
+            for key in keys:
+                base = self._bases[key]
+                flat = base[c * C_:(c + 1) * C_].reshape(-1)
+                per = flat.numel() // self.world
+                dist.all_gather_into_tensor(flat, flat[self.rank * per:(self.rank + 1) * per],
+                                            group=self.group)
+        return [cm] if async_op else []
 
     def _allreduce(self, t: torch.Tensor) -> None:
         if self.world > 1:
@@ -111,6 +142,20 @@ class DataParallelTrainer(Trainer):
         self.iteration_nb += 1
         self.maybe_increase_sh_degree()
         self._ensure_padded()
+        compute = torch.cuda.current_stream(self.device)
+        o = self.options
+        in_adc = (self.iteration_nb <= o.adc_final_iteration_nb and
+                  self.iteration_nb >= o.adc_start_iteration_nb and
+                  self.iteration_nb % o.adc_interval == 0)
+        # zero the rows on a side stream while the forward runs
+        if self._side is None:
+            self._side = torch.cuda.Stream(self.device)
+        self._side.wait_stream(compute)
+        with torch.cuda.stream(self._side):
+            self.dense.zero_()
+        zeroed = torch.cuda.Event()
+        zeroed.record(self._side)
+
         idx = self.current_camera_index()
         cam = self.cameras[idx]
         rb = self.render_buffers
@@ -119,40 +164,90 @@ class DataParallelTrainer(Trainer):
         gt = self.target_for(idx)
         loss = self.loss(self.render_outputs.rgb, gt, self.rgb_image_grad)
         if gt is self._gt_buffers[self._gt_slot]:
-            self._gt_free[self._gt_slot].record(torch.cuda.current_stream(self.device))
+            self._gt_free[self._gt_slot].record(compute)
         self.prefetch_target()
-        backward_dense(self.fgradients, self.rgb_image_grad, self.render_outputs, self.gaussians,
-                       cam, self.tiling, self.render_options, rb, self.dense)
-        o = self.options
+        backward_raster(self.fgradients, self.rgb_image_grad, self.render_outputs, self.gaussians,
+                        cam, self.tiling, self.render_options, rb)
+        compute.wait_event(zeroed)
         stream = C.c_void_p(_stream_handle(None))
-        in_adc = False
-        if self.iteration_nb <= o.adc_final_iteration_nb:
+        n = self.gaussians.n
+        S, C_ = chunk_layout(n, self.world, self.chunks)
+        if in_adc:
+            backward_project_dense(self.fgradients, self.gaussians, cam, self.tiling,
+                                   self.render_options, rb, self.dense, 0, n)
             adc_mod.adc_stats(self.adc_buffers, self.fgradients, rb.fgidx_to_gidx, rb.device_counts,
                               self.width, self.height)
-            in_adc = self.iteration_nb >= o.adc_start_iteration_nb and self.iteration_nb % o.adc_interval == 0
-        self.update_learning_rates()
-        params = self.optimizer.params_c(self.render_options.sh_degree)
-        if in_adc:
+            self.update_learning_rates()
+            params = self.optimizer.params_c(self.render_options.sh_degree)
             # every rank needs every moment and the summed rows: the update is not sharded
-            self._all_gather_rows(("mm", "om", "sm", "rm", "shm"))
+            if self.optimizer_step == "sharded":
+                for c in range(self.chunks):
+                    self._gather_chunk(("mm", "om", "sm", "rm", "shm"), c, async_op=False)
             self._allreduce(self.dense)
             self._densify()
             g, m = self.gaussians.to_c(), self.optimizer.moments.to_c()
             _abi.check(lib.gs3d_adam_step_dense(C.byref(g), C.byref(m), C.c_void_p(self.dense.data_ptr()),
                                                 C.byref(params), stream))
-        else:
-            n = self.gaussians.n
-            S, lo, hi = shard_range(n, self.world, self.rank)
-            if self.world > 1:
-                flat = self.dense.view(-1)
-                per = S * DENSE_ROW
-                dist.reduce_scatter_tensor(flat[self.rank * per:(self.rank + 1) * per], flat,
-                                           op=dist.ReduceOp.SUM, group=self.group)
+        elif self.optimizer_step == "replicated" or self.world == 1:
+            # chunk c: its rows, then their all-reduce while chunk c + 1 is computed; then the
+            # full update of chunk c on every rank while the later chunks are still exchanged
+            ar = []
+            for c in range(self.chunks):
+                lo, hi = c * C_, min((c + 1) * C_, n)
+                if lo < hi:
+                    backward_project_dense(self.fgradients, self.gaussians, cam, self.tiling,
+                                           self.render_options, rb, self.dense[lo:], lo, hi)
+                if self.world > 1:
+                    ar.append(dist.all_reduce(self.dense[c * C_:(c + 1) * C_], op=dist.ReduceOp.SUM,
+                                              group=self.group, async_op=True))
+            if self.iteration_nb <= o.adc_final_iteration_nb:
+                adc_mod.adc_stats(self.adc_buffers, self.fgradients, rb.fgidx_to_gidx, rb.device_counts,
+                                  self.width, self.height)
+            self.update_learning_rates()
+            params = self.optimizer.params_c(self.render_options.sh_degree)
             g, m = self.gaussians.to_c(), self.optimizer.moments.to_c()
-            rows = self.dense[lo:]
-            _abi.check(lib.gs3d_adam_step_dense_range(C.byref(g), C.byref(m), C.c_void_p(rows.data_ptr()),
-                                                      lo, hi, C.byref(params), stream))
-            self._all_gather_rows(("mo", "sf", "rf", "sh"))
+            for c in range(self.chunks):
+                if ar:
+                    ar[c].wait()
+                lo, hi = c * C_, min((c + 1) * C_, n)
+                if lo < hi:
+                    _abi.check(lib.gs3d_adam_step_dense_range(C.byref(g), C.byref(m),
+                                                              C.c_void_p(self.dense[lo:].data_ptr()), lo, hi,
+                                                              C.byref(params), stream))
+        else:
+            # chunk c: its rows, then the reduce-scatter of those rows while chunk c + 1 is computed
+            rs = []
+            for c in range(self.chunks):
+                lo, hi = c * C_, min((c + 1) * C_, n)
+                if lo < hi:
+                    backward_project_dense(self.fgradients, self.gaussians, cam, self.tiling,
+                                           self.render_options, rb, self.dense[lo:], lo, hi)
+                if self.world > 1:
+                    flat = self.dense[c * C_:(c + 1) * C_].reshape(-1)
+                    per = S * DENSE_ROW
+                    rs.append(dist.reduce_scatter_tensor(flat[self.rank * per:(self.rank + 1) * per], flat,
+                                                         op=dist.ReduceOp.SUM, group=self.group,
+                                                         async_op=True))
+            if self.iteration_nb <= o.adc_final_iteration_nb:
+                adc_mod.adc_stats(self.adc_buffers, self.fgradients, rb.fgidx_to_gidx, rb.device_counts,
+                                  self.width, self.height)
+            self.update_learning_rates()
+            params = self.optimizer.params_c(self.render_options.sh_degree)
+            g, m = self.gaussians.to_c(), self.optimizer.moments.to_c()
+            ag = []
+            for c in range(self.chunks):
+                if rs:
+                    rs[c].wait()
+                lo = c * C_ + self.rank * S
+                hi = min(lo + S, n)
+                if lo < hi:
+                    rows = self.dense[lo:]
+                    _abi.check(lib.gs3d_adam_step_dense_range(C.byref(g), C.byref(m),
+                                                              C.c_void_p(rows.data_ptr()), lo, hi,
+                                                              C.byref(params), stream))
+                ag.extend(self._gather_chunk(("mo", "sf", "rf", "sh"), c, async_op=True))
+            for w in ag:
+                w.wait()
         self.optimizer.update_count += 1
         if in_adc:
             self.complete_adc_step()
