@@ -65,6 +65,10 @@ def parse():
     ap.add_argument("--ref-budget-s", type=float, default=120.0)
     ap.add_argument("--n-gaussians", type=int, default=None,
                     help="override the Gaussian count (same distributions); for small profiling cases")
+    ap.add_argument("--dp-exchange", choices=["factored", "dense"], default="factored",
+                    help="N > 1: gradient rows exchanged as factored rows (16 floats per Gaussian) "
+                         "or dense rows (60)")
+    ap.add_argument("--dp-chunks", type=int, default=None, help="N > 1: pipeline depth")
     return ap.parse_args()
 
 
@@ -147,15 +151,21 @@ def build_workload(device, seed_offset=0, n_override=None):
     return gv, cams, pool_host, ro, til, scene_radius(cams)
 
 
-def stage_bytes(stage: str, F: int, D: int, n: int, w: int, h: int, passes: int) -> float | None:
-    """Algorithmic bytes per launch (the per-unit figures of the hot-path analysis)."""
+def stage_bytes(stage: str, F: int, D: int, n: int, w: int, h: int, passes: int,
+                world: int = 1, factored: bool = True) -> float | None:
+    """Algorithmic bytes of one step of a stage on one rank (the per-unit figures of the
+    hot-path analysis). Adam: 1416 B of parameters and moments read and written per Gaussian
+    plus its gradients: 44 B of geometry gradients, the colour gradients and projected colours
+    (24 B) from which the SH gradients are rebuilt, the fgidx_to_gidx entry; data parallel: the
+    rank's n / world Gaussians with a 48 B geometry row and a 16 B colour row per view
+    (factored) or a 240 B dense row."""
     return {
         "project": 300.0 * F,
         "sort": 20.0 * F + 28.0 * D,          # scatter (rect, depth; key) + segment sort (key; code, value)
         "tile_count": 16.0 * F,              # tile rectangles
-        "adam": 1656.0 * F,
-        "adam_dense": 1656.0 * F + 240.0 * n,
-        "bwd_project": 548.0 * F,
+        "adam": 1488.0 * F,
+        "adam_dense": (1416.0 + (48.0 + 16.0 * world if factored else 240.0)) * n / world,
+        "bwd_project": 356.0 * F,
         "keep_compact": 31.0 * n,
         "dup_keys": 28.0 * F + 12.0 * D,
         "raster": 40.0 * D + 20.0 * w * h,
@@ -173,8 +183,6 @@ NCU_TRAFFIC_FRACTION = {
     "bwd_raster": 120.49e6 / (40.0 * 943_223 + 24.0 * 2_073_600 + 36.0 * 992_004),
     # 39.40 MB read + 9.17 MB write
     "raster": 48.57e6 / (40.0 * 943_223 + 20.0 * 2_073_600),
-    # k_adam_sh16 766.31 MB read + 516.67 MB write, k_adam_geom 179.64 MB + 74.07 MB
-    "adam": (766.31e6 + 516.67e6 + 179.64e6 + 74.07e6) / (1656.0 * 992_004),
 }
 
 
@@ -309,9 +317,12 @@ def main() -> None:
     targets_dev = [pool_dev[i % POOL] for i in range(len(cams))]
     pool_pinned = [t.pin_memory() for t in pool_host]
     targets_host = [pool_pinned[i % POOL] for i in range(len(cams))]
-    TrainerCls = DataParallelTrainer if world > 1 else Trainer
-    trainer = TrainerCls(gv, cams, targets_dev, ro, til, opts, seed=0,
-                         capacity_dup=8 * gv.n)
+    if world > 1:
+        trainer = DataParallelTrainer(gv, cams, targets_dev, ro, til, opts, seed=0,
+                                      capacity_dup=8 * gv.n, chunks=args.dp_chunks,
+                                      factored=args.dp_exchange == "factored")
+    else:
+        trainer = Trainer(gv, cams, targets_dev, ro, til, opts, seed=0, capacity_dup=8 * gv.n)
     trainer.iteration_nb = START_ITERATION
     stream = torch.cuda.current_stream()
 
@@ -407,16 +418,19 @@ def main() -> None:
     w, h = cams[0].width, cams[0].height
     passes = math.ceil(til.highest_key_bit / 8)
     stages = {}
+    factored = world > 1 and args.dp_exchange == "factored"
     for name, (cnt, tot) in prof.items():
         avg = tot / max(cnt, 1)
-        b = stage_bytes(name, F, D, gv.n, w, h, passes)
+        b = stage_bytes(name, F, D, gv.n, w, h, passes, world, factored)
+        b = b * args.steps / cnt if b and cnt else b  # per launch (chunked stages: a share)
         stages[name] = {"launches": cnt, "avg_ms": round(avg, 4),
                         "share": round(tot / max(sum(t for _, t in prof.values()), 1e-9), 4),
                         "alg_GBps": round(b / (avg / 1000) / 1e9, 1) if b else None}
     dominant = max(prof.items(), key=lambda kv: kv[1][1])[0]
     dom = stages[dominant]
     achieved = dom["alg_GBps"]
-    dom_bytes = stage_bytes(dominant, F, D, gv.n, w, h, passes)
+    dom_bytes = stage_bytes(dominant, F, D, gv.n, w, h, passes, world, factored)
+    dom_bytes = dom_bytes * args.steps / prof[dominant][0] if dom_bytes else dom_bytes
     traffic = (round(NCU_TRAFFIC_FRACTION[dominant] * dom_bytes / 1e9, 4)
                if dominant in NCU_TRAFFIC_FRACTION and dom_bytes else None)
     roofline = {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peak,
@@ -443,6 +457,8 @@ def main() -> None:
                        "n_gaussians": gv.n, "filtered_F": F, "duplicates_D": D,
                        "tiles": [til.tile_width, til.tile_height],
                        "parallelism": f"dp{world}" if world > 1 else "single",
+                       **({"dp_exchange": args.dp_exchange, "dp_chunks": trainer.chunks}
+                          if world > 1 else {}),
                        "l2": "inputs larger than L2 (2.1 GB params+moments), no flush"},
             "e2e": e2e, "render": render_fps, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk,
             "gpu_launches": gpu_launches, "stages": stages,

@@ -51,6 +51,8 @@ typedef struct CUstream_st* gs3d_stream_t; /* ABI-compatible with cudaStream_t *
 /* backward flags */
 #define GS3D_BACKWARD_FIX_SH16 1u /* use coefficient 16 in the degree-3 direction Jacobian
                                      (the reference reads coefficient 15: sh.jl:249)     */
+#define GS3D_BACKWARD_SKIP_SH_GRADS 2u /* leave sh_coeffs_grads unwritten: for an update by
+                                     gs3d_adam_step_rebuild_sh, which recomputes them      */
 
 /* ---- POD parameter structs ---------------------------------------------------------- */
 
@@ -269,6 +271,22 @@ GS3D_API int gs3d_adam_step(
     const gs3d_fgradients* fgradients, const int32_t* fgidx_to_gidx,
     const int32_t* device_counts, const gs3d_adam_params* params, gs3d_stream_t stream);
 
+/* gs3d_adam_step with the SH gradients recomputed instead of read: for filtered Gaussian f the
+ * gradient of coefficient k of channel c is live_c * color_grads[f][c] * basis_k(d), d the unit
+ * direction from camera_position (HOST memory, 3 floats: the camera the backward ran for) to
+ * the Gaussian's mean, live_c = (the projected colour of channel c, float 6 + c of row f of
+ * projected, the render buffers' means2d_opacities_inverse_covariances_colors) >= 0: the
+ * expression gs3d_backward evaluates (compute_sh_coeffs_grad!, backward_core.jl:936-964), so
+ * the update equals gs3d_adam_step after gs3d_backward bit for bit as long as the Gaussians are
+ * unchanged between the backward and this call (not across a densify step). The backward may
+ * then run with GS3D_BACKWARD_SKIP_SH_GRADS. Needs SH storage degree 3 and 16-byte aligned
+ * arrays. */
+GS3D_API int gs3d_adam_step_rebuild_sh(
+    const gs3d_gaussians* gaussians, const gs3d_adam_moments* moments,
+    const gs3d_fgradients* fgradients, const int32_t* fgidx_to_gidx,
+    const int32_t* device_counts, const float* projected, const float* camera_position,
+    const gs3d_adam_params* params, gs3d_stream_t stream);
+
 /* ---- multi-view data parallelism (no counterpart in the reference: it trains one view at a
  * time on one GPU, training.jl:173-244). A dense gradient row of 60 floats per Gaussian:
  * SH (3 x 16, channel-major; 16-byte aligned) at 0, mean(3) at 48, opacity feature(1) at 51,
@@ -319,6 +337,39 @@ GS3D_API int gs3d_scatter_dense_grads(
 GS3D_API int gs3d_adam_step_dense(
     const gs3d_gaussians* gaussians, const gs3d_adam_moments* moments, const float* dense,
     const gs3d_adam_params* params, gs3d_stream_t stream);
+
+/* Factored rows: the dense row with its 48 SH gradients replaced by their factors. The SH
+ * gradient of one view is the outer product of the 3 colour gradients (each zero where the
+ * colour was clamped) with the 16 SH basis values of the view direction (compute_sh_coeffs_grad!,
+ * backward_core.jl:936-964), so a view needs to send only its colour gradients; the owner of a
+ * Gaussian rebuilds the sum over views from the cameras' positions. Geometry row: the dense row's
+ * floats 48..59 (mean, opacity feature, scaling, rotation, touched), summed over views like dense
+ * rows. Colour row (one per view, not summed): colour gradients 0..2 and flags at 3,
+ * 1 + 2 live0 + 4 live1 + 8 live2 where the Gaussian is filtered in that view, else 0. */
+#define GS3D_GEOM_ROW 12
+#define GS3D_COLOUR_ROW 4
+#define GS3D_MAX_FACTORED_VIEWS 64
+
+/* gs3d_backward_project_dense writing factored rows: geometry row and colour row
+ * gidx - g_begin for the filtered Gaussians with index in [g_begin, g_end) (rows are not zeroed
+ * here; colour_rows 16-byte aligned). */
+GS3D_API int gs3d_backward_project_factored(
+    const gs3d_fgradients* fgradients, const gs3d_gaussians* gaussians,
+    const gs3d_camera* camera, const gs3d_tiling* tiling,
+    const gs3d_render_options* options, const gs3d_render_buffers* buffers,
+    uint32_t flags, float* geom_rows, float* colour_rows, int32_t g_begin, int32_t g_end,
+    gs3d_stream_t stream);
+
+/* gs3d_adam_step_dense_range from factored rows: geom_rows holds the summed geometry rows of
+ * [g_begin, g_end); colour_rows the colour rows of n_views views (1 .. GS3D_MAX_FACTORED_VIEWS),
+ * view v's row for Gaussian g at row v * view_stride + g - g_begin; view_positions (HOST memory,
+ * 3 floats per view) the camera positions the views were rendered from. The SH gradient is
+ * rebuilt as the sum over the views in order v = 0, 1, ... (with one view: the gradient
+ * gs3d_backward writes, bit for bit). Needs SH storage degree 3 and 16-byte aligned arrays. */
+GS3D_API int gs3d_adam_step_factored_range(
+    const gs3d_gaussians* gaussians, const gs3d_adam_moments* moments, const float* geom_rows,
+    const float* colour_rows, int32_t n_views, int64_t view_stride, const float* view_positions,
+    int32_t g_begin, int32_t g_end, const gs3d_adam_params* params, gs3d_stream_t stream);
 
 /* ---- loss: training.jl:196-217 (L1 + weight * DSSIM, with gradient) ----------------- */
 

@@ -13,7 +13,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from gs3d.dp import CHUNKS, DENSE_ROW, chunk_layout, shard_range, view_index
+from gs3d.dp import (CHUNKS, COLOUR_ROW, DENSE_ROW, GEOM_ROW, chunk_layout, exchange_factored_chunk,
+                     shard_range, view_index)
 
 
 def test_shard_ranges_partition_the_gaussians():
@@ -103,3 +104,55 @@ def test_sharded_collectives_on_padded_storage(world):
         assert p.exitcode == 0
     for rank, ok_rs, ok_ag in results:
         assert ok_rs is True and ok_ag is True, (rank, ok_rs, ok_ag)
+
+
+def _factored_worker(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        n = 13
+        S, C_ = chunk_layout(n, world, CHUNKS)
+        rows = CHUNKS * C_
+        ar = torch.arange(n, dtype=torch.float32)
+        geom = torch.zeros((rows, GEOM_ROW))
+        geom[:n] = (ar[:, None] * GEOM_ROW + torch.arange(GEOM_ROW)) * (rank + 1)
+        colour = torch.zeros((rows, COLOUR_ROW))
+        colour[:n] = ar[:, None] * 10 + torch.arange(COLOUR_ROW) + 1000 * rank
+        total = sum(r + 1 for r in range(world))
+        want_geom = (ar[:, None] * GEOM_ROW + torch.arange(GEOM_ROW)) * total
+        ok = True
+        for c in range(CHUNKS):
+            recv = torch.full((world, S, COLOUR_ROW), -7.0)
+            for w in exchange_factored_chunk(geom, colour, recv, c, S, C_, rank, in_place=False):
+                w.wait()
+            lo = c * C_ + rank * S
+            hi = min(lo + S, n)
+            if lo < hi:
+                ok = ok and torch.equal(geom[lo:hi], want_geom[lo:hi])
+                for src in range(world):  # slot src: rank src's colour rows of this sub-range
+                    want = ar[lo:hi, None] * 10 + torch.arange(COLOUR_ROW) + 1000 * src
+                    ok = ok and torch.equal(recv[src, : hi - lo], want)
+                    ok = ok and bool(torch.all(recv[src, hi - lo:] == 0))
+        q.put((rank, ok))
+        dist.destroy_process_group()
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, repr(e)))
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_factored_exchange_on_padded_storage(world):
+    """Geometry rows summed into each owner's sub-range; every view's colour rows of that
+    sub-range delivered to the owner in rank order (the order the owner rebuilds the SH
+    gradients in); padding rows arrive as zeros."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_factored_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, ok in results:
+        assert ok is True, (rank, ok)

@@ -328,3 +328,129 @@ def test_dense_adam_equals_sparse_adam_storage_degree_1(cuda):
         assert torch.equal(x, y)
     for x, y in zip(a1.moments.tensors(), a2.moments.tensors()):
         assert torch.equal(x, y)
+
+
+def test_factored_rows_rebuild_dense_rows_over_views(cuda):
+    """Three views of one scene. Per view, the factored rows (gs3d_backward_project_factored)
+    hold the dense rows' geometry part bit for bit and the colour gradients with their live
+    flags; the update from the views' summed geometry rows and their colour rows
+    (gs3d_adam_step_factored_range, SH gradients rebuilt from the camera positions) equals the
+    dense update from the summed dense rows, bit for bit, over two Gaussian ranges."""
+    import ctypes as C
+    from gs3d import _abi
+    from gs3d.backward import backward_project_dense, backward_project_factored, backward_raster
+    spec = SceneSpec(16_384, "uniform:1", -4.0, 0.5)
+    g = synthetic_gaussians(spec, 5).to(cuda)
+    n = g.n
+    k = 6007
+    dsum = gsum = None
+    colours = []
+    positions = []
+    for v, pos in enumerate([(0, 0, 3), (2.0, 0.5, 2.2), (-1.5, 1.0, 2.5)]):
+        cam = look_at_camera(256, 256, 60.0, pos)
+        opt = RenderOptions.for_camera(cam, 3)
+        til = Tiling.for_camera(cam)
+        out = RenderOutputs.create(cam.width, cam.height, cuda)
+        buf = RenderBuffers.create(n, til.nb_tiles, cuda)
+        gs3d.render(out, g, cam, til, opt, buf)
+        fg = FilteredGaussiansGradients.create(n, 3, cuda)
+        grad = np.random.default_rng(10 + v).normal(0, 1e-4, size=(256, 256, 3)).astype(np.float32)
+        backward_raster(fg, torch.from_numpy(grad).to(cuda), out, g, cam, til, opt, buf)
+        dense = torch.zeros((n, 60), dtype=torch.float32, device=cuda)
+        geom = torch.zeros((n, 12), dtype=torch.float32, device=cuda)
+        colour = torch.zeros((n, 4), dtype=torch.float32, device=cuda)
+        for lo, hi in ((0, k), (k, n)):
+            backward_project_dense(fg, g, cam, til, opt, buf, dense[lo:], lo, hi)
+            backward_project_factored(fg, g, cam, til, opt, buf, geom[lo:], colour[lo:], lo, hi)
+        torch.cuda.synchronize()
+        assert torch.equal(geom, dense[:, 48:60])
+        touched = dense[:, 59] > 0
+        assert int(touched.sum()) > n // 4
+        assert torch.equal(colour[:, 3] > 0, touched)
+        fl = colour[touched, 3].to(torch.int32)
+        assert torch.all((fl & 1) == 1) and torch.all(fl <= 15)
+        # a colour row reproduces its dense row's SH gradients: cg * basis(k = 1) on live channels
+        c0 = (float(np.float32(0.28209479177387814)) * colour[touched, :3].double()).float()
+        live = torch.stack([(fl >> (1 + c)) & 1 for c in range(3)], 1).bool()
+        assert torch.equal(torch.where(live, c0, torch.zeros_like(c0)), dense[touched][:, [0, 16, 32]])
+        dsum = dense if dsum is None else dsum + dense
+        gsum = geom if gsum is None else gsum + geom
+        colours.append(colour)
+        positions.append(cam.position)
+    g2 = g.clone()
+    a1 = AdamOptimizer(g, LearningRates(means=0.001))
+    a2 = AdamOptimizer(g2, LearningRates(means=0.001))
+    a1.update_count = a2.update_count = 4
+    lib = _abi.lib()
+    gc, mc, pc = g.to_c(), a1.moments.to_c(), a1.params_c(3)
+    _abi.check(lib.gs3d_adam_step_dense(C.byref(gc), C.byref(mc), C.c_void_p(dsum.data_ptr()),
+                                        C.byref(pc), None))
+    views = torch.stack(colours).contiguous()  # (3, n, 4): view stride n rows
+    pos = np.ascontiguousarray(np.stack(positions).astype(np.float32))
+    gc2, mc2, pc2 = g2.to_c(), a2.moments.to_c(), a2.params_c(3)
+    for lo, hi in ((0, k), (k, n)):
+        vpart = views[:, lo:hi].contiguous()
+        _abi.check(lib.gs3d_adam_step_factored_range(
+            C.byref(gc2), C.byref(mc2), C.c_void_p(gsum[lo:].data_ptr()), C.c_void_p(vpart.data_ptr()),
+            3, hi - lo, pos.ctypes.data_as(C.POINTER(C.c_float)), lo, hi, C.byref(pc2), None))
+    torch.cuda.synchronize()
+    for x, y in zip(g.tensors(), g2.tensors()):
+        assert torch.equal(x, y)
+    for x, y in zip(a1.moments.tensors(), a2.moments.tensors()):
+        assert torch.equal(x, y)
+
+
+def test_factored_adam_rejects_bad_arguments(cuda):
+    import ctypes as C
+    from gs3d import _abi
+    g = synthetic_gaussians(SceneSpec(1024, "uniform:1", -4.0, 0.5), 0).to(cuda)
+    a = AdamOptimizer(g, LearningRates(means=0.001))
+    geom = torch.zeros((g.n, 12), dtype=torch.float32, device=cuda)
+    col = torch.zeros((g.n, 4), dtype=torch.float32, device=cuda)
+    pos = (C.c_float * 3)(0.0, 0.0, 3.0)
+    gc, mc, pc = g.to_c(), a.moments.to_c(), a.params_c(3)
+    lib = _abi.lib()
+    call = lambda nv, stride, lo, hi: lib.gs3d_adam_step_factored_range(
+        C.byref(gc), C.byref(mc), C.c_void_p(geom.data_ptr()), C.c_void_p(col.data_ptr()), nv, stride,
+        pos, lo, hi, C.byref(pc), None)
+    assert call(0, g.n, 0, g.n) == _abi.GS3D_ERR_INVALID_ARGUMENT
+    assert call(_abi.GS3D_MAX_FACTORED_VIEWS + 1, g.n, 0, g.n) == _abi.GS3D_ERR_INVALID_ARGUMENT
+    assert call(1, g.n - 1, 0, g.n) == _abi.GS3D_ERR_INVALID_ARGUMENT
+    assert call(1, g.n, 0, g.n + 1) == _abi.GS3D_ERR_INVALID_ARGUMENT
+    assert call(1, g.n, 0, g.n) == _abi.GS3D_OK
+    torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("deg", [0, 1, 2, 3])
+def test_rebuilt_sh_update_equals_sparse_update(cuda, deg):
+    """gs3d_backward with GS3D_BACKWARD_SKIP_SH_GRADS leaves the SH gradients untouched and
+    gs3d_adam_step_rebuild_sh, recomputing them from the colour gradients, the projected colours
+    and the camera position, gives gs3d_adam_step's update bit for bit (render degree `deg`,
+    storage degree 3, some filtered Gaussians skipped)."""
+    spec = SceneSpec(16_384, "uniform:1", -4.0, 0.5)
+    gv = synthetic_gaussians(spec, 6)
+    cam = look_at_camera(256, 256, 60.0, (0.4, -0.3, 3))
+    opt = RenderOptions.for_camera(cam, deg)
+    til = Tiling.for_camera(cam)
+    grad = np.random.default_rng(7).normal(0, 1e-4, size=(256, 256, 3)).astype(np.float32)
+    _, (g, out, buf, fg) = run_gpu(gv, cam, til, opt, grad, cuda)
+    F, _ = gs3d.counts(buf)
+    buf.fgidx_to_gidx[: F : 7] = 0
+    fg2 = FilteredGaussiansGradients.create(g.n, 3, cuda)
+    fg2.sh_coeffs_grads.fill_(3.0)
+    backward(fg2, torch.from_numpy(grad).to(cuda), out, g, cam, til, opt, buf, skip_sh_grads=True)
+    torch.cuda.synchronize()
+    assert torch.all(fg2.sh_coeffs_grads == 3.0)
+    g2 = g.clone()
+    a1 = AdamOptimizer(g, LearningRates(means=0.001))
+    a2 = AdamOptimizer(g2, LearningRates(means=0.001))
+    a1.update_count = a2.update_count = 2
+    a1.update(fg, buf.fgidx_to_gidx, buf.device_counts, deg)
+    # the same colour gradients as the first backward (the 2D sums of the second run may differ
+    # in the last bits): the rebuilt update reads fg
+    a2.update_rebuild_sh(fg, buf.fgidx_to_gidx, buf.device_counts, buf.f2d, cam.position, deg)
+    torch.cuda.synchronize()
+    for x, y in zip(g.tensors(), g2.tensors()):
+        assert torch.equal(x, y)
+    for x, y in zip(a1.moments.tensors(), a2.moments.tensors()):
+        assert torch.equal(x, y)

@@ -217,12 +217,16 @@ def test_trainer_loss_decreases(cuda):
     assert t.optimizer.update_count == 40
 
 
-def test_data_parallel_trainer_one_rank_matches_trainer(cuda):
-    """DataParallelTrainer without a process group (the dense-row path: gs3d_backward_dense +
-    gs3d_adam_step_dense) follows the sparse Trainer's training run (one view, 8 steps)."""
+@pytest.mark.parametrize("factored", [False, True])
+def test_data_parallel_trainer_one_rank_matches_trainer(cuda, factored):
+    """DataParallelTrainer without a process group (dense rows: gs3d_backward_project_dense +
+    gs3d_adam_step_dense_range; factored rows: gs3d_backward_project_factored +
+    gs3d_adam_step_factored_range) follows the sparse Trainer's training run (one view, 8 steps)."""
+    from functools import partial
+
     from gs3d.dp import DataParallelTrainer
     runs = []
-    for cls in (Trainer, DataParallelTrainer):
+    for cls in (Trainer, partial(DataParallelTrainer, factored=factored)):
         gv = synthetic_gaussians(SceneSpec(16_384, "uniform:1", -4.0, 0.5), 9)
         cams = [look_at_camera(256, 256, 60.0, (0, 0, 3))]
         ro = RenderOptions.for_camera(cams[0], 3)

@@ -161,6 +161,62 @@ __device__ __forceinline__ void adam4(float4& p, const float4& g, float4& m01, f
     if (nup > 3) adam_reg(p.w, g.w, m23.z, m23.w, lr, a);
 }
 
+template <int Q>
+__device__ __forceinline__ float4 sh_basis4(float x, float y, float z) {
+    return make_float4(sh_basis(4 * Q + 1, x, y, z), sh_basis(4 * Q + 2, x, y, z),
+                       sh_basis(4 * Q + 3, x, y, z), sh_basis(4 * Q + 4, x, y, z));
+}
+
+// SH gradients of coefficients 4q + 1 .. 4q + 4 (1-based) of one colour channel for one view,
+// as the projection backward computes them (compute_sh_coeffs_grad!, backward_core.jl:936-964):
+// live ? cg * basis_k(d) : 0, d = normalize(mean - camera position), same operations.
+__device__ __forceinline__ float4 sh_grad_unit(int q, float cg, bool live, const float4& mo,
+                                               float px, float py, float pz) {
+    const float vx = mo.x - px, vy = mo.y - py, vz = mo.z - pz;
+    const float inv_vn = 1.0f / sqrtf(vx * vx + vy * vy + vz * vz);
+    const float nd0 = vx * inv_vn, nd1 = vy * inv_vn, nd2 = vz * inv_vn;
+    float4 b;
+    switch (q) {
+        case 0: b = sh_basis4<0>(nd0, nd1, nd2); break;
+        case 1: b = sh_basis4<1>(nd0, nd1, nd2); break;
+        case 2: b = sh_basis4<2>(nd0, nd1, nd2); break;
+        default: b = sh_basis4<3>(nd0, nd1, nd2); break;
+    }
+    return live ? make_float4(cg * b.x, cg * b.y, cg * b.z, cg * b.w)
+                : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+}
+
+// k_adam_sh16 with the unit's SH gradients recomputed from the filtered Gaussian's colour
+// gradient (fgradients' color_grads), its projected colour (row f of the render buffers'
+// projected array, floats 6..8: live where >= 0) and the camera position; runs before
+// k_adam_geom, which updates the means it reads.
+__global__ void __launch_bounds__(256) k_adam_sh16_rebuild(const AdamArgs a,
+                                                           const float* __restrict__ color_g,
+                                                           const float* __restrict__ projected,
+                                                           float px, float py, float pz) {
+    const uint32_t F = (uint32_t)max(0, min(a.counts[0], (int32_t)a.ncap));
+    const uint32_t it = blockIdx.x * blockDim.x + threadIdx.x;
+    if (it >= 12u * F) return;
+    const uint32_t f = it / 12u;
+    const int c = (int)(it - f * 12u);
+    const int ch = c >> 2, q = c & 3, i0 = 4 * q;
+    if (i0 >= a.maxo) return;
+    const int gidx = a.f2g[f];
+    if (gidx <= 0) return;
+    const size_t gi = (size_t)gidx - 1;
+    const float4 mo = reinterpret_cast<const float4*>(a.mo)[gi];
+    const float cg = __ldg(color_g + 3 * (size_t)f + ch);
+    const bool live = __ldg(projected + 9 * (size_t)f + 6 + ch) >= 0.0f;
+    const float4 g = sh_grad_unit(q, cg, live, mo, px, py, pz);
+    float4* pp = reinterpret_cast<float4*>(a.sh + gi * 48) + c;
+    float4* mp = reinterpret_cast<float4*>(a.shm + gi * 96) + 2 * c;
+    float4 p = *pp, m01 = mp[0], m23 = mp[1];
+    adam4(p, g, m01, m23, i0 == 0 ? a.lr_dc : a.lr_rest, a.lr_rest, min(4, a.maxo - i0), a);
+    *pp = p;
+    mp[0] = m01;
+    mp[1] = m23;
+}
+
 __global__ void __launch_bounds__(256) k_adam_sh16(const AdamArgs a) {
     // 32-bit indices: the host only takes this path when 12 n < 2^31
     const uint32_t F = (uint32_t)max(0, min(a.counts[0], (int32_t)a.ncap));
@@ -230,10 +286,15 @@ __global__ void __launch_bounds__(256) k_adam_geom(const AdamArgs a) {
 
 bool aligned(const void* p, uintptr_t b) { return (reinterpret_cast<uintptr_t>(p) & (b - 1)) == 0; }
 
-bool flat16_ok(const AdamArgs& a, int64_t n) {
-    return n > 0 && 12 * n < ((int64_t)1 << 31) && a.S == 16 && a.Sm == 16 && a.Sg == 16 && aligned(a.sh, 16) && aligned(a.shm, 16) &&
-           aligned(a.g_sh, 16) && aligned(a.mo, 16) && aligned(a.rf, 16) && aligned(a.rm, 16) &&
+// The k_adam_sh16 / k_adam_geom layout, apart from the SH gradients.
+bool flat16_params_ok(const AdamArgs& a, int64_t n) {
+    return n > 0 && 12 * n < ((int64_t)1 << 31) && a.S == 16 && a.Sm == 16 && aligned(a.sh, 16) &&
+           aligned(a.shm, 16) && aligned(a.mo, 16) && aligned(a.rf, 16) && aligned(a.rm, 16) &&
            aligned(a.g_rot, 16) && aligned(a.mm, 8) && aligned(a.om, 8) && aligned(a.sm, 8);
+}
+
+bool flat16_ok(const AdamArgs& a, int64_t n) {
+    return flat16_params_ok(a, n) && a.Sg == 16 && aligned(a.g_sh, 16);
 }
 
 int launch_adam_warp(const AdamArgs& a, cudaStream_t stream) {
@@ -256,6 +317,7 @@ int launch_adam_warp(const AdamArgs& a, cudaStream_t stream) {
 // a range [g_begin, g_end) whose rows start at dense[0], with the summed gradients.
 constexpr int kDenseRow = GS3D_DENSE_ROW;
 constexpr int kDMean = 48, kDOpacity = 51, kDScale = 52, kDRot = 55, kDTouched = 59;
+constexpr int kGeomRow = GS3D_GEOM_ROW;
 
 __global__ void __launch_bounds__(256) k_scatter_dense(const AdamArgs a, float* __restrict__ dense) {
     const int F = a.counts[0];
@@ -340,13 +402,15 @@ __global__ void __launch_bounds__(256) k_adam_dense_sh16(const AdamArgs a,
     mp[1] = m23;
 }
 
+// Geometry part of a row: 12 floats at `geom` + (g - g_begin) * stride (the dense row's last 12,
+// stride kDenseRow, or a factored geometry row, stride kGeomRow).
 __global__ void __launch_bounds__(256) k_adam_dense_geom(const AdamArgs a,
-                                                         const float* __restrict__ dense,
+                                                         const float* __restrict__ geom, int stride,
                                                          int64_t g_begin, int64_t g_end) {
     const int64_t lr_ = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (lr_ >= g_end - g_begin) return;
-    const float4* row4 = reinterpret_cast<const float4*>(dense + (size_t)lr_ * kDenseRow);
-    const float4 r12 = __ldg(row4 + 12), r13 = __ldg(row4 + 13), r14 = __ldg(row4 + 14);
+    const float4* row4 = reinterpret_cast<const float4*>(geom + (size_t)lr_ * stride);
+    const float4 r12 = __ldg(row4), r13 = __ldg(row4 + 1), r14 = __ldg(row4 + 2);
     // r12: mean x y z, opacity; r13: scale 0 1 2, rotation 0; r14: rotation 1 2 3, touched
     if (!(r14.w > 0.0f)) return;
     const size_t gi = (size_t)(g_begin + lr_);
@@ -380,6 +444,57 @@ __global__ void __launch_bounds__(256) k_adam_dense_geom(const AdamArgs a,
     *omp = om;
     smp[0] = sm0; smp[1] = sm1; smp[2] = sm2;
     sfp[0] = s0; sfp[1] = s1; sfp[2] = s2;
+}
+
+// Factored rows (sharded multi-view step): the SH gradient of Gaussian g is rebuilt from the
+// colour rows of the views, sum over v = 0 .. nv - 1 of live_c(v) cg_c(v) basis_k(d_v), d_v the
+// unit direction from camera v to the Gaussian's mean, each term the expression the projection
+// backward uses for one view (compute_sh_coeffs_grad!, backward_core.jl:936-964), the terms added
+// in view order starting from the first view that filtered the Gaussian (one view: the
+// single-view gradient bit for bit). Thread 12 (g - g_begin) + c updates SH unit c; it reads the
+// mean, so it runs before k_adam_dense_geom updates it.
+struct ViewPositions {
+    float p[GS3D_MAX_FACTORED_VIEWS][3];
+};
+
+__global__ void __launch_bounds__(256) k_adam_factored_sh16(const AdamArgs a,
+                                                            const float* __restrict__ geom,
+                                                            const float4* __restrict__ colour,
+                                                            int nv, int64_t view_stride,
+                                                            const ViewPositions vp,
+                                                            int64_t g_begin, int64_t g_end) {
+    const int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (it >= 12 * (g_end - g_begin)) return;
+    const int64_t lr_ = it / 12;
+    const int c = (int)(it - lr_ * 12);
+    const int ch = c >> 2, q = c & 3, i0 = 4 * q;
+    if (i0 >= a.maxo) return;
+    if (!(__ldg(geom + (size_t)lr_ * kGeomRow + (kGeomRow - 1)) > 0.0f)) return;
+    const size_t gi = (size_t)(g_begin + lr_);
+    const float4 mo = reinterpret_cast<const float4*>(a.mo)[gi];
+    float4 g = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    bool first = true;
+    for (int v = 0; v < nv; ++v) {
+        const float4 cr = __ldg(colour + (size_t)v * view_stride + lr_);
+        if (!(cr.w > 0.0f)) continue;  // not filtered in view v
+        const int fl = (int)cr.w;
+        const bool live = ((fl >> (1 + ch)) & 1) != 0;
+        const float cg = ch == 0 ? cr.x : (ch == 1 ? cr.y : cr.z);
+        const float4 t = sh_grad_unit(q, cg, live, mo, vp.p[v][0], vp.p[v][1], vp.p[v][2]);
+        if (first) {
+            g = t;
+            first = false;
+        } else {
+            g.x = g.x + t.x; g.y = g.y + t.y; g.z = g.z + t.z; g.w = g.w + t.w;
+        }
+    }
+    float4* pp = reinterpret_cast<float4*>(a.sh + gi * 48) + c;
+    float4* mp = reinterpret_cast<float4*>(a.shm + gi * 96) + 2 * c;
+    float4 p = *pp, m01 = mp[0], m23 = mp[1];
+    adam4(p, g, m01, m23, i0 == 0 ? a.lr_dc : a.lr_rest, a.lr_rest, min(4, a.maxo - i0), a);
+    *pp = p;
+    mp[0] = m01;
+    mp[1] = m23;
 }
 
 }  // namespace
@@ -496,7 +611,8 @@ extern "C" GS3D_API int gs3d_adam_step_dense_range(const gs3d_gaussians* g,
     if (flat) {
         k_adam_dense_sh16<<<(unsigned)ceil_div(12 * cnt, 256), 256, 0, stream>>>(a, dense, g_begin, g_end);
         GS3D_LAUNCHED("k_adam_dense_sh16");
-        k_adam_dense_geom<<<(unsigned)ceil_div(cnt, 256), 256, 0, stream>>>(a, dense, g_begin, g_end);
+        k_adam_dense_geom<<<(unsigned)ceil_div(cnt, 256), 256, 0, stream>>>(a, dense + kDMean, kDenseRow,
+                                                                            g_begin, g_end);
         GS3D_LAUNCHED("k_adam_dense_geom");
     } else {
         k_adam_dense<<<device_sm_count() * 8, 256, 0, stream>>>(a, dense, g_begin, g_end);
@@ -510,4 +626,61 @@ extern "C" GS3D_API int gs3d_adam_step_dense(const gs3d_gaussians* g, const gs3d
                                              gs3d_stream_t stream) {
     if (!g) return invalid("NULL argument");
     return gs3d_adam_step_dense_range(g, m, dense, 0, g->n, p, stream);
+}
+
+extern "C" GS3D_API int gs3d_adam_step_factored_range(
+    const gs3d_gaussians* g, const gs3d_adam_moments* m, const float* geom_rows,
+    const float* colour_rows, int32_t n_views, int64_t view_stride, const float* view_positions,
+    int32_t g_begin, int32_t g_end, const gs3d_adam_params* p, gs3d_stream_t stream_) {
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+    if (!g || !m || !geom_rows || !colour_rows || !view_positions || !p) return invalid("NULL argument");
+    if (g_begin < 0 || g_end < g_begin || g_end > g->n)
+        return invalid("Gaussian range [%d, %d) of n = %d", g_begin, g_end, g->n);
+    if (n_views < 1 || n_views > GS3D_MAX_FACTORED_VIEWS)
+        return invalid("%d views (1 .. %d)", n_views, GS3D_MAX_FACTORED_VIEWS);
+    if (view_stride < (int64_t)g_end - g_begin) return invalid("view stride %lld < range", (long long)view_stride);
+    AdamArgs a;
+    GS3D_RETURN_IF(make_args(g, m, nullptr, nullptr, nullptr, p, a));
+    if (!(a.S == 16 && a.Sm == 16 && aligned(geom_rows, 16) && aligned(colour_rows, 16) &&
+          aligned(a.sh, 16) && aligned(a.shm, 16) && aligned(a.mo, 16) && aligned(a.rf, 16) &&
+          aligned(a.rm, 16) && aligned(a.mm, 8) && aligned(a.om, 8) && aligned(a.sm, 8)))
+        return invalid("factored Adam needs storage degree 3 and 16-byte aligned arrays");
+    if (g_end == g_begin) return GS3D_OK;
+    ViewPositions vp{};
+    for (int v = 0; v < n_views; ++v)
+        for (int k = 0; k < 3; ++k) vp.p[v][k] = view_positions[3 * v + k];
+    ProfScope prof("adam_dense", stream);
+    const int64_t cnt = (int64_t)g_end - g_begin;
+    k_adam_factored_sh16<<<(unsigned)ceil_div(12 * cnt, 256), 256, 0, stream>>>(
+        a, geom_rows, reinterpret_cast<const float4*>(colour_rows), n_views, view_stride, vp, g_begin, g_end);
+    GS3D_LAUNCHED("k_adam_factored_sh16");
+    k_adam_dense_geom<<<(unsigned)ceil_div(cnt, 256), 256, 0, stream>>>(a, geom_rows, kGeomRow, g_begin, g_end);
+    GS3D_LAUNCHED("k_adam_dense_geom");
+    return GS3D_OK;
+}
+
+extern "C" GS3D_API int gs3d_adam_step_rebuild_sh(const gs3d_gaussians* g, const gs3d_adam_moments* m,
+                                                  const gs3d_fgradients* fg,
+                                                  const int32_t* fgidx_to_gidx,
+                                                  const int32_t* device_counts,
+                                                  const float* projected,
+                                                  const float* camera_position,
+                                                  const gs3d_adam_params* p, gs3d_stream_t stream_) {
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+    if (!g || !m || !fg || !fgidx_to_gidx || !device_counts || !projected || !camera_position || !p)
+        return invalid("NULL argument");
+    if (!fg->color_grads) return invalid("NULL colour gradients");
+    AdamArgs a;
+    GS3D_RETURN_IF(make_args(g, m, fg, fgidx_to_gidx, device_counts, p, a));
+    // the SH gradients are not read: only the other arrays need the flat layout
+    if (!flat16_params_ok(a, g->n))
+        return invalid("rebuilt SH update needs storage degree 3 and aligned arrays");
+    ProfScope prof("adam", stream);
+    a.ncap = g->n;
+    k_adam_sh16_rebuild<<<(unsigned)ceil_div(12 * (int64_t)g->n, 256), 256, 0, stream>>>(
+        a, fg->color_grads, projected, camera_position[0], camera_position[1], camera_position[2]);
+    GS3D_LAUNCHED("k_adam_sh16_rebuild");
+    k_adam_geom<<<(unsigned)ceil_div((int64_t)g->n, 256), 256, 0, stream>>>(a);
+    GS3D_LAUNCHED("k_adam_geom");
+    return GS3D_OK;
 }

@@ -263,28 +263,6 @@ __device__ __forceinline__ int low3(int i, int j) {
     return lo == 0 ? hi : (lo == 1 ? 2 + hi : 5);
 }
 
-__device__ __forceinline__ float sh_basis(int i, float x, float y, float z) {
-    switch (i) {
-        case 1: return sh_c(1);
-        case 2: return -y * sh_c(2);
-        case 3: return z * sh_c(3);
-        case 4: return -x * sh_c(4);
-        case 5: return x * y * sh_c(5);
-        case 6: return y * z * sh_c(6);
-        case 7: return (2.0f * (z * z) - x * x - y * y) * sh_c(7);
-        case 8: return x * z * sh_c(8);
-        case 9: return (x * x - y * y) * sh_c(9);
-        case 10: return y * (3.0f * (x * x) - y * y) * sh_c(10);
-        case 11: return x * y * z * sh_c(11);
-        case 12: return y * (4.0f * (z * z) - x * x - y * y) * sh_c(12);
-        case 13: return z * (2.0f * (z * z) - 3.0f * (x * x + y * y)) * sh_c(13);
-        case 14: return x * (4.0f * (z * z) - x * x - y * y) * sh_c(14);
-        case 15: return z * (x * x - y * y) * sh_c(15);
-        case 16: return x * (x * x - 3.0f * (y * y)) * sh_c(16);
-        default: return 0.0f;
-    }
-}
-
 struct BProjArgs {
     const float4* mo4;
     const float* scal;
@@ -305,17 +283,25 @@ struct BProjArgs {
     float* sh_g;
     int sh_grad_stride;
     int fix_sh16;
+    int skip_sh;  // GS3D_BACKWARD_SKIP_SH_GRADS: no SH gradients (F-compact output only)
     // NULL, or dense gradient rows indexed by Gaussian (kDenseRow floats, layout in gs3d.h):
     // the 3D gradients then go to row gidx - g_begin instead of the F-compact arrays above
     float* dense;
+    // NULL, or the factored rows (dense == NULL): geometry row gidx - g_begin (kGeomRow floats,
+    // the dense row's last 12) and colour row gidx - g_begin (the three colour gradients and
+    // the flags 1 + 2 live0 + 4 live1 + 8 live2) instead of the SH gradients
+    float* geom;
+    float4* colour;
     // only filtered Gaussians whose 0-based Gaussian index is in [g_begin, g_end) are done
     int32_t g_begin, g_end;
 };
 
 // Dense gradient row (GS3D_DENSE_ROW): SH 3 x 16 channel-major at 0, mean 48, opacity feature
 // 51, scaling features 52, rotation features 55, touched flag 59.
+// Offsets below are relative to the geometry part (dense row + 48, or the factored geometry row).
 constexpr int kDenseRow = GS3D_DENSE_ROW;
-constexpr int kDMean = 48, kDOpacity = 51, kDScale = 52, kDRot = 55, kDTouched = 59;
+constexpr int kDGeom = 48, kGeomRow = GS3D_GEOM_ROW;
+constexpr int kDMean = 0, kDOpacity = 3, kDScale = 4, kDRot = 7, kDTouched = 11;
 
 template <int DEG>
 __global__ void __launch_bounds__(128, 6) k_bwd_project(const BProjArgs a, const gs3d_camera cam,
@@ -343,7 +329,8 @@ __global__ void __launch_bounds__(128, 6) k_bwd_project(const BProjArgs a, const
       const int gi0 = f < F ? a.f2g[f] - 1 : -1;
       const int gi = (gi0 >= a.g_begin && gi0 < a.g_end) ? gi0 : -1;
       if (gi >= 0) {
-        float* const drow = a.dense ? a.dense + (size_t)(gi - a.g_begin) * kDenseRow : nullptr;
+        float* const drow = a.dense ? a.dense + (size_t)(gi - a.g_begin) * kDenseRow + kDGeom
+                                    : a.geom ? a.geom + (size_t)(gi - a.g_begin) * kGeomRow : nullptr;
         const float* r = a.f2d + 9 * (size_t)f;
         const float4 mo = a.mo4[gi];
         const float orig_op = gs_sigmoid(mo.w);
@@ -618,19 +605,28 @@ __global__ void __launch_bounds__(128, 6) k_bwd_project(const BProjArgs a, const
                 (drow ? drow + kDRot : a.rot_g + 4 * (size_t)f)[i] = inv_qn * w;
             }
         }
-        // SH coefficients (compute_sh_coeffs_grad!, backward_core.jl:936-964), staged
+        // SH coefficients (compute_sh_coeffs_grad!, backward_core.jl:936-964), staged; or
+        // their factors: the colour gradients and which channels are live
+        if (a.colour) {
+            const float fl = 1.0f + (col[0] >= 0.0f ? 2.0f : 0.0f) + (col[1] >= 0.0f ? 4.0f : 0.0f) +
+                             (col[2] >= 0.0f ? 8.0f : 0.0f);
+            a.colour[gi - a.g_begin] = make_float4(cgr[0], cgr[1], cgr[2], fl);
+        } else if (!a.skip_sh) {
 #pragma unroll
-        for (int l = 0; l < 3; ++l) {
+          for (int l = 0; l < 3; ++l) {
             const bool live = col[l] >= 0.0f;
 #pragma unroll
             for (int k = 1; k <= MAXO; ++k)
                 mys[(k - 1) + l * MAXO] = live ? cgr[l] * sh_basis(k, nd0, nd1, nd2) : 0.0f;
+          }
         }
       }
       __syncwarp();
       const int nrows = (int)min((int64_t)32, (int64_t)F - fb);
       float* const warp_stage = &stage[threadIdx.x >> 5][0][0];
-      if (a.dense) {  // row `row` of the warp goes to dense row gidx - g_begin (if in range)
+      if (a.colour || a.skip_sh) {
+          // factored rows: written per Gaussian above; or no SH gradients
+      } else if (a.dense) {  // row `row` of the warp goes to dense row gidx - g_begin (if in range)
           const int rel = gi >= 0 ? gi - a.g_begin : -1;
           for (int e = lane; e < 32 * NSH; e += 32) {
               const int row = e / NSH, rem = e - row * NSH;
@@ -670,13 +666,15 @@ constexpr unsigned kPhaseRaster = 1u, kPhaseProject = 2u;
 
 // backward! in phases: kPhaseRaster = B1 + B2 (the 2D gradients), kPhaseProject = B3 + B4 for
 // the filtered Gaussians with index in [g_begin, g_end), with the 3D gradients into the
-// F-compact arrays of fg (dense == NULL) or into dense rows (row gidx - g_begin; zeroed here
-// first when zero_rows > 0: rows [0, zero_rows) of dense).
+// F-compact arrays of fg (dense == NULL, geom == NULL), into dense rows (row gidx - g_begin;
+// zeroed here first when zero_rows > 0: rows [0, zero_rows) of dense), or into factored
+// geometry and colour rows (row gidx - g_begin of each).
 int backward_impl(const gs3d_fgradients* fg, const float* rgb_grad,
                   const gs3d_render_outputs* out, const gs3d_gaussians* g, const gs3d_camera* cam,
                   const gs3d_tiling* til, const gs3d_render_options* opt,
                   const gs3d_render_buffers* buf, uint32_t flags, unsigned phases, float* dense,
-                  int32_t zero_rows, int32_t g_begin, int32_t g_end, cudaStream_t stream) {
+                  int32_t zero_rows, int32_t g_begin, int32_t g_end, cudaStream_t stream,
+                  float* geom = nullptr, float* colour = nullptr) {
     GS3D_RETURN_IF(check_render_common(g, cam, til, opt));
     if (!fg || !buf) return invalid("NULL argument");
     if ((phases & kPhaseRaster) &&
@@ -684,10 +682,10 @@ int backward_impl(const gs3d_fgradients* fg, const float* rgb_grad,
         return invalid("backward needs the gradient image, transmittance and last-contributor images");
     if (!fg->mean2d_grads || !fg->opacity_grads || !fg->licov2d_grads || !fg->color_grads)
         return invalid("NULL 2D gradient array");
-    const bool compact_out = (phases & kPhaseProject) && !dense;
+    const bool compact_out = (phases & kPhaseProject) && !dense && !geom;
     if (compact_out && (!fg->mean3d_grads || !fg->opacity_feature_grads ||
                         !fg->scaling_features_grads || !fg->rotation_features_grads ||
-                        !fg->sh_coeffs_grads))
+                        (!fg->sh_coeffs_grads && !(flags & GS3D_BACKWARD_SKIP_SH_GRADS))))
         return invalid("NULL gradient array");
     if (g_begin < 0 || g_end < g_begin) return invalid("Gaussian range [%d, %d)", g_begin, g_end);
     if (compact_out && (fg->sh_degree < opt->sh_degree || fg->sh_degree > 3))
@@ -760,7 +758,10 @@ int backward_impl(const gs3d_fgradients* fg, const float* rgb_grad,
     p.sh_g = fg->sh_coeffs_grads;
     p.sh_grad_stride = (fg->sh_degree + 1) * (fg->sh_degree + 1);
     p.fix_sh16 = (flags & GS3D_BACKWARD_FIX_SH16) ? 1 : 0;
+    p.skip_sh = (compact_out && (flags & GS3D_BACKWARD_SKIP_SH_GRADS)) ? 1 : 0;
     p.dense = dense;
+    p.geom = geom;
+    p.colour = reinterpret_cast<float4*>(colour);
     p.g_begin = g_begin;
     p.g_end = g_end;
     const int grid = grid_for(cap_n, 128, 16);
@@ -824,4 +825,22 @@ extern "C" GS3D_API int gs3d_backward_project_dense(const gs3d_fgradients* fg,
     if (!g || g_end > g->n) return invalid("Gaussian range end %d > n", g_end);
     return backward_impl(fg, nullptr, nullptr, g, cam, til, opt, buf, flags, kPhaseProject,
                          dense_rows, 0, g_begin, g_end, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" GS3D_API int gs3d_backward_project_factored(const gs3d_fgradients* fg,
+                                                       const gs3d_gaussians* g,
+                                                       const gs3d_camera* cam,
+                                                       const gs3d_tiling* til,
+                                                       const gs3d_render_options* opt,
+                                                       const gs3d_render_buffers* buf,
+                                                       uint32_t flags, float* geom_rows,
+                                                       float* colour_rows, int32_t g_begin,
+                                                       int32_t g_end, gs3d_stream_t stream) {
+    if (!geom_rows || !colour_rows) return invalid("NULL factored rows");
+    if ((reinterpret_cast<uintptr_t>(colour_rows) & 15) != 0)
+        return invalid("colour rows not 16-byte aligned");
+    if (!g || g_end > g->n) return invalid("Gaussian range end %d > n", g_end);
+    return backward_impl(fg, nullptr, nullptr, g, cam, til, opt, buf, flags, kPhaseProject,
+                         nullptr, 0, g_begin, g_end, reinterpret_cast<cudaStream_t>(stream),
+                         geom_rows, colour_rows);
 }

@@ -104,29 +104,6 @@ __global__ void __launch_bounds__(kChunkThreads) k_keep_downsweep(const uint8_t*
     }
 }
 
-// evaluate_sh_basis_function (sh.jl:123-149), i 1-based (constant after unrolling)
-__device__ __forceinline__ float sh_basis(int i, float x, float y, float z) {
-    switch (i) {
-        case 1: return sh_c(1);
-        case 2: return -y * sh_c(2);
-        case 3: return z * sh_c(3);
-        case 4: return -x * sh_c(4);
-        case 5: return x * y * sh_c(5);
-        case 6: return y * z * sh_c(6);
-        case 7: return (2.0f * (z * z) - x * x - y * y) * sh_c(7);
-        case 8: return x * z * sh_c(8);
-        case 9: return (x * x - y * y) * sh_c(9);
-        case 10: return y * (3.0f * (x * x) - y * y) * sh_c(10);
-        case 11: return x * y * z * sh_c(11);
-        case 12: return y * (4.0f * (z * z) - x * x - y * y) * sh_c(12);
-        case 13: return z * (2.0f * (z * z) - 3.0f * (x * x + y * y)) * sh_c(13);
-        case 14: return x * (4.0f * (z * z) - x * x - y * y) * sh_c(14);
-        case 15: return z * (x * x - y * y) * sh_c(15);
-        case 16: return x * (x * x - 3.0f * (y * y)) * sh_c(16);
-        default: return 0.0f;
-    }
-}
-
 // sh_coeffs_to_color (sh.jl:38-112) for one channel; hc = coefficient 1 of that channel
 template <int DEG>
 __device__ __forceinline__ float sh_channel(const float* hc, float x, float y, float z) {

@@ -20,6 +20,11 @@ GS3D_STATUS_DUP_OVERFLOW = 1
 GS3D_RENDER_NO_HOST_SYNC = 1
 GS3D_RENDER_REFERENCE_ORDER = 2
 GS3D_BACKWARD_FIX_SH16 = 1
+GS3D_BACKWARD_SKIP_SH_GRADS = 2
+GS3D_DENSE_ROW = 60
+GS3D_GEOM_ROW = 12
+GS3D_COLOUR_ROW = 4
+GS3D_MAX_FACTORED_VIEWS = 64
 
 f32p = C.POINTER(C.c_float)
 i32p = C.POINTER(C.c_int32)
@@ -146,6 +151,17 @@ SIGNATURES = {
     "gs3d_backward_project_dense": (C.c_int, [P(FGradientsC), P(GaussiansC), P(Camera), P(TilingC),
                                               P(RenderOptionsC), P(RenderBuffersC), C.c_uint32,
                                               C.c_void_p, C.c_int32, C.c_int32, C.c_void_p]),
+    "gs3d_backward_project_factored": (C.c_int, [P(FGradientsC), P(GaussiansC), P(Camera),
+                                                 P(TilingC), P(RenderOptionsC), P(RenderBuffersC),
+                                                 C.c_uint32, C.c_void_p, C.c_void_p, C.c_int32,
+                                                 C.c_int32, C.c_void_p]),
+    "gs3d_adam_step_factored_range": (C.c_int, [P(GaussiansC), P(AdamMomentsC), C.c_void_p,
+                                                C.c_void_p, C.c_int32, C.c_int64,
+                                                P(C.c_float), C.c_int32, C.c_int32,
+                                                P(AdamParamsC), C.c_void_p]),
+    "gs3d_adam_step_rebuild_sh": (C.c_int, [P(GaussiansC), P(AdamMomentsC), P(FGradientsC),
+                                            C.c_void_p, C.c_void_p, C.c_void_p, P(C.c_float),
+                                            P(AdamParamsC), C.c_void_p]),
     "gs3d_loss_workspace_size": (C.c_int, [C.c_int32, C.c_int32, P(C.c_size_t)]),
     "gs3d_loss_l1_dssim": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_float,
                                      C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),

@@ -75,18 +75,21 @@ class FilteredGaussiansGradients:
 def backward(fgradients: FilteredGaussiansGradients, rgb_image_grad: torch.Tensor,
              outputs: RenderOutputs, gaussians: GaussiansVector, camera: PinholeCamera,
              tiling: Tiling, options: RenderOptions, buffers: RenderBuffers,
-             fix_sh16: bool = False, stream: torch.cuda.Stream | None = None):
+             fix_sh16: bool = False, stream: torch.cuda.Stream | None = None,
+             skip_sh_grads: bool = False):
     """Gradients of the loss w.r.t. the filtered Gaussians' parameters, from the gradient
     image `rgb_image_grad` ((w, h, 3), i.e. 3 x h x w). The forward render must have run with
     the same arguments. `fix_sh16` uses SH coefficient 16 in the last degree-3 term of the
-    colour/direction Jacobian; the default reproduces the reference (coefficient 15)."""
+    colour/direction Jacobian; the default reproduces the reference (coefficient 15).
+    `skip_sh_grads` leaves the SH gradients unwritten (for AdamOptimizer.update_rebuild_sh)."""
     assert rgb_image_grad.is_contiguous() and rgb_image_grad.dtype == torch.float32
     if fgradients.capacity < buffers.capacity_n:
         raise ValueError("gradient buffers smaller than the render buffers")
     lib = _abi.lib()
     args = [fgradients.to_c(), outputs.to_c(), gaussians.to_c(), camera.to_c(), tiling.to_c(),
             options.to_c(), buffers.to_c()]
-    flags = _abi.GS3D_BACKWARD_FIX_SH16 if fix_sh16 else 0
+    flags = (_abi.GS3D_BACKWARD_FIX_SH16 if fix_sh16 else 0) | \
+        (_abi.GS3D_BACKWARD_SKIP_SH_GRADS if skip_sh_grads else 0)
     _abi.check(lib.gs3d_backward(C.byref(args[0]), C.c_void_p(rgb_image_grad.data_ptr()),
                                  C.byref(args[1]), C.byref(args[2]), C.byref(args[3]),
                                  C.byref(args[4]), C.byref(args[5]), C.byref(args[6]), flags,
@@ -151,3 +154,24 @@ def backward_dense(fgradients: FilteredGaussiansGradients, rgb_image_grad: torch
                                        C.c_void_p(dense.data_ptr()), dense.shape[0],
                                        C.c_void_p(_stream_handle(stream))))
     return dense
+
+
+def backward_project_factored(fgradients: FilteredGaussiansGradients, gaussians: GaussiansVector,
+                              camera: PinholeCamera, tiling: Tiling, options: RenderOptions,
+                              buffers: RenderBuffers, geom_rows: torch.Tensor,
+                              colour_rows: torch.Tensor, g_begin: int, g_end: int,
+                              fix_sh16: bool = False,
+                              stream: torch.cuda.Stream | None = None) -> None:
+    """backward_project_dense() into factored rows: geometry row (12 floats) and colour row
+    (3 colour gradients + live flags) gidx - g_begin of views starting at row g_begin."""
+    for t in (geom_rows, colour_rows):
+        assert t.is_contiguous() and t.dtype == torch.float32
+    lib = _abi.lib()
+    args = [fgradients.to_c(), gaussians.to_c(), camera.to_c(), tiling.to_c(), options.to_c(),
+            buffers.to_c()]
+    flags = _abi.GS3D_BACKWARD_FIX_SH16 if fix_sh16 else 0
+    _abi.check(lib.gs3d_backward_project_factored(
+        C.byref(args[0]), C.byref(args[1]), C.byref(args[2]), C.byref(args[3]), C.byref(args[4]),
+        C.byref(args[5]), flags, C.c_void_p(geom_rows.data_ptr()),
+        C.c_void_p(colour_rows.data_ptr()), int(g_begin), int(g_end),
+        C.c_void_p(_stream_handle(stream))))

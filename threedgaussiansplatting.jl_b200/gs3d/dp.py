@@ -29,11 +29,13 @@ from torch.distributed.distributed_c10d import _coalescing_manager
 
 from . import _abi
 from . import adc as adc_mod
-from .backward import backward_dense, backward_project_dense, backward_raster
+from .backward import backward_project_dense, backward_project_factored, backward_raster
 from .render import _stream_handle, render
 from .training import Trainer
 
-DENSE_ROW = 60
+DENSE_ROW = _abi.GS3D_DENSE_ROW
+GEOM_ROW = _abi.GS3D_GEOM_ROW
+COLOUR_ROW = _abi.GS3D_COLOUR_ROW
 CHUNKS = 4
 
 
@@ -56,17 +58,39 @@ def chunk_layout(n: int, world: int, chunks: int) -> tuple[int, int]:
     return S, S * world
 
 
+def exchange_factored_chunk(geom: torch.Tensor, colour: torch.Tensor, colour_recv: torch.Tensor,
+                            c: int, S: int, C_: int, rank: int, group=None, in_place: bool = True):
+    """Chunk c of the factored rows: reduce-scatter of its geometry rows into the owners'
+    sub-ranges (in place) and all-to-all of its colour rows: rank p receives, in slot q of
+    `colour_recv` ((world, S, COLOUR_ROW)), rank q's colour rows of p's sub-range. Returns the
+    two async works. `in_place=False` reduces from a copy (for backends without in-place
+    reduce-scatter)."""
+    gflat = geom[c * C_:(c + 1) * C_].reshape(-1)
+    per = S * GEOM_ROW
+    w1 = dist.reduce_scatter_tensor(gflat[rank * per:(rank + 1) * per],
+                                    gflat if in_place else gflat.clone(),
+                                    op=dist.ReduceOp.SUM, group=group, async_op=True)
+    w2 = dist.all_to_all_single(colour_recv.reshape(-1), colour[c * C_:(c + 1) * C_].reshape(-1),
+                                group=group, async_op=True)
+    return (w1, w2)
+
+
 class DataParallelTrainer(Trainer):
     """`optimizer_step`: "sharded" (reduce-scatter rows, Adam on the rank's sub-ranges,
     all-gather parameters) or "replicated" (all-reduce rows chunk by chunk, the full Adam update
-    on every rank, no parameter exchange)."""
+    on every rank, no parameter exchange). `factored` (sharded step, SH storage degree 3, outside
+    densify steps): exchange factored rows instead of dense rows, i.e. reduce-scatter the 12
+    geometry floats per Gaussian and send each owner the 3 colour gradients of every view
+    (all-to-all), from which it rebuilds the 48 SH gradients (gs3d_adam_step_factored_range):
+    16 floats per Gaussian cross the links instead of 60."""
 
     def __init__(self, *args, group=None, optimizer_step: str = "sharded", chunks: int | None = None,
-                 **kw):
+                 factored: bool = True, **kw):
         super().__init__(*args, **kw)
         if optimizer_step not in ("sharded", "replicated"):
             raise ValueError(f"optimizer_step {optimizer_step!r}")
         self.optimizer_step = optimizer_step
+        self.factored = bool(factored)
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         # pipeline depth (measured at 3M Gaussians: 4 chunks best up to 4 ranks; with 8 ranks
@@ -77,6 +101,9 @@ class DataParallelTrainer(Trainer):
         self.perm = self.rng.permutation(len(self.cameras))
         self._bases = {}
         self.dense = None
+        self.geom = None
+        self.colour = None
+        self.colour_recv = None
         self._side = None
         self._ensure_padded()
 
@@ -110,6 +137,31 @@ class DataParallelTrainer(Trainer):
         m.sh_coeffs_moments = self._pad("shm", m.sh_coeffs_moments, rows)
         if self.dense is None or self.dense.shape[0] != rows:
             self.dense = torch.zeros((rows, DENSE_ROW), dtype=torch.float32, device=self.device)
+        if self.factored and self.optimizer_step == "sharded":
+            S, _ = chunk_layout(self.gaussians.n, self.world, self.chunks)
+            f = dict(dtype=torch.float32, device=self.device)
+            if self.geom is None or self.geom.shape[0] != rows:
+                self.geom = torch.zeros((rows, GEOM_ROW), **f)
+                self.colour = torch.zeros((rows, COLOUR_ROW), **f)
+            if self.world > 1 and (self.colour_recv is None or self.colour_recv.shape[2] != S):
+                self.colour_recv = torch.empty((self.chunks, self.world, S, COLOUR_ROW), **f)
+
+    def _use_factored(self, in_adc: bool) -> bool:
+        return (self.factored and self.optimizer_step == "sharded" and not in_adc and
+                self.gaussians.sh_degree == 3 and self.world <= _abi.GS3D_MAX_FACTORED_VIEWS)
+
+    def _view_positions(self):
+        """Camera positions (float32, rank order) of this step's views: the colour rows of
+        rank p's view arrive in slot p of the all-to-all."""
+        import numpy as np
+        pos = np.stack([self.cameras[view_index(self.step_index, p, self.world, self.perm,
+                                                len(self.cameras))].position
+                        for p in range(self.world)]).astype(np.float32)
+        return np.ascontiguousarray(pos)
+
+    def _exchange_factored(self, c: int, S: int, C_: int):
+        return exchange_factored_chunk(self.geom, self.colour, self.colour_recv[c], c, S, C_,
+                                       self.rank, self.group)
 
     def _gather_chunk(self, keys, c: int, async_op: bool):
         """In-place all-gather of chunk c of each padded array (rank r's sub-range to all), as
@@ -144,15 +196,18 @@ class DataParallelTrainer(Trainer):
         self._ensure_padded()
         compute = torch.cuda.current_stream(self.device)
         o = self.options
-        in_adc = (self.iteration_nb <= o.adc_final_iteration_nb and
-                  self.iteration_nb >= o.adc_start_iteration_nb and
-                  self.iteration_nb % o.adc_interval == 0)
+        in_adc = self.densifies_this_iteration()
+        factored = self._use_factored(in_adc)
         # zero the rows on a side stream while the forward runs
         if self._side is None:
             self._side = torch.cuda.Stream(self.device)
         self._side.wait_stream(compute)
         with torch.cuda.stream(self._side):
-            self.dense.zero_()
+            if factored:
+                self.geom.zero_()
+                self.colour.zero_()
+            else:
+                self.dense.zero_()
         zeroed = torch.cuda.Event()
         zeroed.record(self._side)
 
@@ -188,7 +243,7 @@ class DataParallelTrainer(Trainer):
             g, m = self.gaussians.to_c(), self.optimizer.moments.to_c()
             _abi.check(lib.gs3d_adam_step_dense(C.byref(g), C.byref(m), C.c_void_p(self.dense.data_ptr()),
                                                 C.byref(params), stream))
-        elif self.optimizer_step == "replicated" or self.world == 1:
+        elif self.optimizer_step == "replicated" or (self.world == 1 and not factored):
             # chunk c: its rows, then their all-reduce while chunk c + 1 is computed; then the
             # full update of chunk c on every rank while the later chunks are still exchanged
             ar = []
@@ -219,6 +274,14 @@ class DataParallelTrainer(Trainer):
             rs = []
             for c in range(self.chunks):
                 lo, hi = c * C_, min((c + 1) * C_, n)
+                if factored:
+                    if lo < hi:
+                        backward_project_factored(self.fgradients, self.gaussians, cam, self.tiling,
+                                                  self.render_options, rb, self.geom[lo:],
+                                                  self.colour[lo:], lo, hi)
+                    if self.world > 1:
+                        rs.append(self._exchange_factored(c, S, C_))
+                    continue
                 if lo < hi:
                     backward_project_dense(self.fgradients, self.gaussians, cam, self.tiling,
                                            self.render_options, rb, self.dense[lo:], lo, hi)
@@ -235,12 +298,23 @@ class DataParallelTrainer(Trainer):
             params = self.optimizer.params_c(self.render_options.sh_degree)
             g, m = self.gaussians.to_c(), self.optimizer.moments.to_c()
             ag = []
+            if factored:
+                pos = self._view_positions()
+                pos_p = pos.ctypes.data_as(C.POINTER(C.c_float))
             for c in range(self.chunks):
                 if rs:
-                    rs[c].wait()
+                    for w in (rs[c] if factored else (rs[c],)):
+                        w.wait()
                 lo = c * C_ + self.rank * S
                 hi = min(lo + S, n)
-                if lo < hi:
+                if factored:
+                    if lo < hi:
+                        views = self.colour_recv[c] if self.world > 1 else self.colour[lo:]
+                        _abi.check(lib.gs3d_adam_step_factored_range(
+                            C.byref(g), C.byref(m), C.c_void_p(self.geom[lo:].data_ptr()),
+                            C.c_void_p(views.data_ptr()), self.world, S, pos_p, lo, hi,
+                            C.byref(params), stream))
+                elif lo < hi:
                     rows = self.dense[lo:]
                     _abi.check(lib.gs3d_adam_step_dense_range(C.byref(g), C.byref(m),
                                                               C.c_void_p(rows.data_ptr()), lo, hi,

@@ -111,6 +111,25 @@ class AdamOptimizer:
         self.update_count += 1
         return self.gaussians
 
+    def update_rebuild_sh(self, fgradients: FilteredGaussiansGradients, fgidx_to_gidx: torch.Tensor,
+                          device_counts: torch.Tensor, projected: torch.Tensor, camera_position,
+                          sh_degree: int, stream: torch.cuda.Stream | None = None) -> GaussiansVector:
+        """update() with the SH gradients recomputed from the colour gradients, the projected
+        colours (`projected`: the render buffers' (n, 9) projection rows) and the camera
+        position the backward ran for (gs3d_adam_step_rebuild_sh): the same step, bit for bit,
+        when the Gaussians did not change since the backward; needs SH storage degree 3."""
+        import numpy as np
+        pos = np.ascontiguousarray(np.asarray(camera_position, dtype=np.float32).reshape(3))
+        args = [self.gaussians.to_c(), self.moments.to_c(), fgradients.to_c(),
+                self.params_c(sh_degree)]
+        _abi.check(_abi.lib().gs3d_adam_step_rebuild_sh(
+            C.byref(args[0]), C.byref(args[1]), C.byref(args[2]),
+            C.c_void_p(fgidx_to_gidx.data_ptr()), C.c_void_p(device_counts.data_ptr()),
+            C.c_void_p(projected.data_ptr()), pos.ctypes.data_as(C.POINTER(C.c_float)),
+            C.byref(args[3]), C.c_void_p(_stream_handle(stream))))
+        self.update_count += 1
+        return self.gaussians
+
 
 def bias_corrections(beta1: float, beta2: float, update_count: int) -> tuple[float, float]:
     """1 - beta^t rounded to float32 (t = update_count + 1), as libgs3d computes them."""

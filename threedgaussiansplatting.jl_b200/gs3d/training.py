@@ -89,7 +89,12 @@ class Trainer:
 
     def __init__(self, gaussians: GaussiansVector, cameras: list[PinholeCamera], targets,
                  render_options: RenderOptions, tiling: Tiling, options: TrainingOptions,
-                 seed: int = 0, capacity_dup: int | None = None, adc_seed: int = 1234):
+                 seed: int = 0, capacity_dup: int | None = None, adc_seed: int = 1234,
+                 rebuild_sh_grads: bool = True):
+        # outside densify steps the Adam kernel recomputes the SH gradients from the colour
+        # gradients instead of reading them back (the same update, without the 192 bytes per
+        # filtered Gaussian written by the backward and read by the update)
+        self.rebuild_sh_grads = rebuild_sh_grads
         self.gaussians = gaussians
         self.cameras = cameras
         self.targets = targets
@@ -154,6 +159,13 @@ class Trainer:
         x = F32(min(max(x, F32(0)), F32(1)))
         lr = math.exp((1 - x) * math.log(o.initial_means_lr) + x * math.log(o.final_means_lr))
         self.optimizer.lrs.means = float(F32(lr))
+
+    def densifies_this_iteration(self) -> bool:
+        """Whether maybe_densify_and_prune densifies at the current iteration_nb."""
+        o = self.options
+        return (self.iteration_nb <= o.adc_final_iteration_nb and
+                self.iteration_nb >= o.adc_start_iteration_nb and
+                self.iteration_nb % o.adc_interval == 0)
 
     def maybe_densify_and_prune(self) -> bool:
         o = self.options
@@ -258,12 +270,18 @@ class Trainer:
         if gt is self._gt_buffers[self._gt_slot]:
             self._gt_free[self._gt_slot].record(torch.cuda.current_stream(self.device))
         self.prefetch_target()
+        rebuild = (self.rebuild_sh_grads and not self.densifies_this_iteration() and
+                   self.gaussians.sh_degree == 3)
         backward(self.fgradients, self.rgb_image_grad, self.render_outputs, self.gaussians, cam,
-                 self.tiling, self.render_options, rb)
+                 self.tiling, self.render_options, rb, skip_sh_grads=rebuild)
         in_adc = self.maybe_densify_and_prune()
         self.update_learning_rates()
-        self.optimizer.update(self.fgradients, rb.fgidx_to_gidx, rb.device_counts,
-                              self.render_options.sh_degree)
+        if rebuild:
+            self.optimizer.update_rebuild_sh(self.fgradients, rb.fgidx_to_gidx, rb.device_counts,
+                                             rb.f2d, cam.position, self.render_options.sh_degree)
+        else:
+            self.optimizer.update(self.fgradients, rb.fgidx_to_gidx, rb.device_counts,
+                                  self.render_options.sh_degree)
         if in_adc:
             self.complete_adc_step()
         self.maybe_opacity_reset()
