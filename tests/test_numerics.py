@@ -11,38 +11,56 @@ REPO = Path(__file__).resolve().parent.parent
 DIV_CHECK = r"""
 #include <cmath>
 #include <cstdio>
-#include <cstdint>
+#include <cstring>
 #include <random>
-#define GS_HD inline
-static inline float fabsf_(float x) { return std::fabs(x); }
-// the division helper of csrc/common.cuh, restated verbatim for the host
-GS_HD float div_by_const(float x, float b, float rb) {
-    const float ax = fabsf_(x);
-    if (!(ax >= 1e-25f && ax <= 1e25f)) return x / b;
-    const float q0 = x * rb;
-    const float r = std::fmaf(-b, q0, x);
-    return std::fmaf(r, rb, q0);
+#include "common.cuh"
+using namespace gs3d;
+static bool same(float a, float b) {
+    if (a != a && b != b) return true;
+    return std::memcmp(&a, &b, 4) == 0;
 }
 int main() {
     std::mt19937_64 rng(12345);
-    std::uniform_real_distribution<double> e(-25.0, 25.0), m(1.0, 2.0);
+    std::uniform_real_distribution<double> e(-45.0, 39.0), m(1.0, 2.0);
+    std::uniform_int_distribution<uint32_t> bits(0u, 0xffffffffu);
     long bad = 0, total = 0;
+    auto draw = [&](int k) -> float {
+        if (k % 11 == 0) { uint32_t u = bits(rng); float x; std::memcpy(&x, &u, 4); return x; }  // any pattern
+        float x = (float)(m(rng) * std::pow(10.0, e(rng)));
+        if (k % 13 == 0) x = std::ldexp(1.0f, -149 + (int)(bits(rng) % 60)) * (float)m(rng);  // subnormal..tiny
+        if (k & 1) x = -x;
+        if (k % 7 == 0) x = std::nextafter(x, 2 * x);
+        return x;
+    };
+    const float specials[] = {0.0f, -0.0f, INFINITY, -INFINITY, NAN, 1e-45f, -1e-45f, 0x1p-100f,
+                              0x1p-101f, 0x1p80f, 0x1p81f, 0x1p-60f, 0x1p-61f, 3.4e38f};
+    // div_by_const: the bias corrections 1 - beta^t (and divisors outside the fast range)
     const float betas[4] = {0.9f, 0.999f, 0.5f, 0.99f};
-    for (float beta : betas) {
+    std::vector<float> bs;
+    for (float beta : betas)
         for (int t = 1; t <= 40000; ++t) {
             const float b = 1.0f - (float)std::pow((double)beta, (double)t);
-            if (!(b > 0.0f)) continue;
-            const float rb = 1.0f / b;
-            const int n = t <= 200 ? 20000 : 200;
-            for (int k = 0; k < n; ++k) {
-                float x = (float)(m(rng) * std::pow(10.0, e(rng)));
-                if (k & 1) x = -x;
-                if (k % 7 == 0) x = std::nextafter(x, 2 * x);
-                const float want = x / b, got = div_by_const(x, b, rb);
-                ++total;
-                if (std::memcmp(&want, &got, 4) != 0) ++bad;
-            }
+            if (t <= 200 || t % 97 == 0) bs.push_back(b);
         }
+    for (float b : {0x1p-41f, 0x1p-40f, 1.5f, 0.0f, -0.25f}) bs.push_back(b);
+    for (float b : bs) {
+        const float rb = 1.0f / b;
+        for (int k = 0; k < 3000; ++k) {
+            const float x = draw(k);
+            ++total; if (!same(div_by_const(x, b, rb), x / b)) ++bad;
+        }
+        for (float x : specials) { ++total; if (!same(div_by_const(x, b, rb), x / b)) ++bad; }
+    }
+    // div_small_num: numerators of every size over denominators sqrt(h) + eps and extremes
+    for (int j = 0; j < 4000; ++j) {
+        float d = (float)(m(rng) * std::pow(10.0, -15.0 + 20.0 * (j % 100) / 100.0));
+        if (j % 50 == 0) d = specials[(j / 50) % 14];
+        if (j % 77 == 0) d = -d;
+        for (int k = 0; k < 2000; ++k) {
+            const float x = draw(k);
+            ++total; if (!same(div_small_num(x, d), x / d)) ++bad;
+        }
+        for (float x : specials) { ++total; if (!same(div_small_num(x, d), x / d)) ++bad; }
     }
     std::printf("%ld %ld\n", bad, total);
     return 0;
@@ -50,15 +68,29 @@ int main() {
 """
 
 
-def test_division_by_launch_constant_is_correctly_rounded(tmp_path):
-    src = tmp_path / "div.cpp"
-    src.write_text("#include <cstring>\n" + DIV_CHECK)
-    exe = tmp_path / "div"
-    subprocess.run(["g++", "-O2", "-std=c++17", "-ffp-contract=off", "-mfma", str(src), "-o", str(exe)],
-                   check=True)
+def _build_and_run(tmp_path, name: str, source: str) -> tuple[int, int]:
+    """Compile `source` (including csrc/common.cuh) as host code with nvcc and the library's
+    floating-point flags; returns the program's (bad, total)."""
+    import shutil
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    src = tmp_path / f"{name}.cu"
+    src.write_text(source)
+    exe = tmp_path / name
+    csrc = REPO / "threedgaussiansplatting.jl_b200" / "csrc"
+    subprocess.run([nvcc, "-std=c++17", "-O2", "-fmad=false", "-Xcompiler", "-ffp-contract=off",
+                    f"-I{csrc}", str(src), "-o", str(exe)], check=True, capture_output=True)
     bad, total = map(int, subprocess.run([str(exe)], capture_output=True, text=True,
                                          check=True).stdout.split())
-    assert total > 10_000_000
+    return bad, total
+
+
+def test_division_helpers_are_correctly_rounded(tmp_path):
+    """div_by_const (Markstein quotient with the launch-constant reciprocal, exact detours for
+    zero and tiny dividends) and div_small_num (zero and small numerators scaled) of
+    csrc/common.cuh give the IEEE quotient bit for bit: normal, tiny, subnormal, zero, huge and
+    non-finite operands, the Adam bias corrections and divisors outside the fast range."""
+    bad, total = _build_and_run(tmp_path, "div", DIV_CHECK)
+    assert total > 15_000_000
     assert bad == 0, f"{bad} of {total} quotients differ"
 
 
@@ -103,23 +135,8 @@ int main() {
 def test_blend_exp_fast_path_is_bit_identical(tmp_path):
     """The rasterisers' gs_expf_blend / min_hi (csrc/common.cuh, compiled here as host code by
     nvcc with the library's flags) against gs_expf / fmin_jl, bit for bit."""
-    import shutil
-    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
-    src = tmp_path / "blend.cu"
-    src.write_text(BLEND_CHECK)
-    exe = tmp_path / "blend"
-    csrc = REPO / "threedgaussiansplatting.jl_b200" / "csrc"
-    subprocess.run([nvcc, "-std=c++17", "-O2", "-fmad=false", "-Xcompiler", "-ffp-contract=off",
-                    f"-I{csrc}", str(src), "-o", str(exe)], check=True, capture_output=True)
-    bad, total = map(int, subprocess.run([str(exe)], capture_output=True, text=True,
-                                         check=True).stdout.split())
+    bad, total = _build_and_run(tmp_path, "blend", BLEND_CHECK)
     assert total > 250_000_000
     assert bad == 0, f"{bad} of {total} results differ"
 
 
-def test_division_helper_matches_library_source():
-    """The restated helper above must stay identical to csrc/common.cuh's."""
-    src = (REPO / "threedgaussiansplatting.jl_b200" / "csrc" / "common.cuh").read_text()
-    for line in ("const float q0 = x * rb;", "const float r = fmaf(-b, q0, x);",
-                 "return fmaf(r, rb, q0);", "if (!(ax >= 1e-25f && ax <= 1e25f)) return x / b;"):
-        assert line in src

@@ -48,25 +48,33 @@ struct AdamArgs {
     int64_t ncap;          // capacity of fgidx_to_gidx (the Gaussians' n): F is clamped to it
 };
 
+// One scalar update: p - (lr (m1 / bc1)) / (sqrt(m2 / bc2) + eps) with every operation
+// correctly rounded. Zero gradients and moments are common (clamped colour channels, unused SH
+// bands) and the second moments tiny (squared gradients of 1e-10 and below), so the divisions
+// go through div_by_const / div_small_num, which give the same bits without the division's
+// slow path.
+__device__ __forceinline__ float adam_param(float p, float nm1, float nm2, float lr,
+                                            const AdamArgs& a) {
+    const float h1 = div_by_const(nm1, a.bc1, a.rbc1);
+    const float h2 = div_by_const(nm2, a.bc2, a.rbc2);
+    return p - div_small_num(lr * h1, sqrtf(h2) + a.eps);
+}
+
 __device__ __forceinline__ void adam_scalar(float* p, float g, float* m, float lr, const AdamArgs& a) {
     const float nm1 = a.b1 * m[0] + (1.0f - a.b1) * g;
     const float nm2 = a.b2 * m[1] + (1.0f - a.b2) * (g * g);
-    const float h1 = div_by_const(nm1, a.bc1, a.rbc1);
-    const float h2 = div_by_const(nm2, a.bc2, a.rbc2);
     m[0] = nm1;
     m[1] = nm2;
-    *p = *p - lr * h1 / (sqrtf(h2) + a.eps);
+    *p = adam_param(*p, nm1, nm2, lr, a);
 }
 
 __device__ __forceinline__ void adam_reg(float& p, float g, float& m1, float& m2, float lr,
                                          const AdamArgs& a) {
     const float nm1 = a.b1 * m1 + (1.0f - a.b1) * g;
     const float nm2 = a.b2 * m2 + (1.0f - a.b2) * (g * g);
-    const float h1 = div_by_const(nm1, a.bc1, a.rbc1);
-    const float h2 = div_by_const(nm2, a.bc2, a.rbc2);
     m1 = nm1;
     m2 = nm2;
-    p = p - lr * h1 / (sqrtf(h2) + a.eps);
+    p = adam_param(p, nm1, nm2, lr, a);
 }
 
 // Scalar slot s of filtered Gaussian f / Gaussian gi: parameter, first moment (m2 follows),

@@ -124,17 +124,44 @@ GS_HD float gs_logf(float x) {
     return fmaf(ef, 0.693147182464599609375f, fmaf(ef, -1.904654323148236e-09f, logm));
 }
 
-// x / b, correctly rounded, for a divisor b fixed for a whole launch with rb = RN(1/b) from
-// the host: q0 = RN(x rb), r = x - b q0 (exact with one FMA), q = RN(q0 + r rb) equals RN(x/b)
-// for normal operands (P. Markstein, "Computation of elementary functions on the IBM RISC
-// System/6000 processor", IBM J. Res. Dev. 34(1), 1990); tiny, huge or non-finite x take the
-// ordinary division.
-GS_HD float div_by_const(float x, float b, float rb) {
-    const float ax = fabsf(x);
-    if (!(ax >= 1e-25f && ax <= 1e25f)) return x / b;
+// x / b, correctly rounded, for a divisor b > 0 fixed for a whole launch with rb = RN(1/b)
+// from the host: q0 = RN(x rb), r = x - b q0 (exact with one FMA), q = RN(q0 + r rb) equals
+// RN(x/b) while x, the remainder and the quotient stay clear of underflow and overflow
+// (P. Markstein, "Computation of elementary functions on the IBM RISC System/6000 processor",
+// IBM J. Res. Dev. 34(1), 1990), i.e. for 2^-100 <= |x| <= 2^80 and b in [2^-40, 1] (the
+// bias corrections 1 - beta^t). The other x take exact detours instead of the division's slow
+// path: +-0 / b = +-0; a tiny x is divided as x 2^64 and the quotient scaled back by 2^-64,
+// exact while that quotient is normal; what is left (subnormal quotients, huge or non-finite
+// x, b outside that range) is the ordinary division.
+GS_HD float markstein_quotient(float x, float b, float rb) {
     const float q0 = x * rb;
     const float r = fmaf(-b, q0, x);
     return fmaf(r, rb, q0);
+}
+
+GS_HD float div_by_const(float x, float b, float rb) {
+    const float ax = fabsf(x);
+    const bool b_ok = b >= 0x1p-40f && b <= 1.0f;
+    if (b_ok && ax >= 0x1p-100f && ax <= 0x1p80f) return markstein_quotient(x, b, rb);
+    if (ax == 0.0f && b > 0.0f) return x;
+    if (b_ok && ax < 0x1p-100f) {
+        const float qs = markstein_quotient(x * 0x1p64f, b, rb);
+        if (fabsf(qs) >= 0x1p-62f) return qs * 0x1p-64f;
+    }
+    return x / b;
+}
+
+// num / d (IEEE, correctly rounded) with zero and small numerators kept off the division's
+// slow path: +-0 / d = +-0 for d > 0; for |num| < 2^-60 the quotient of num 2^64 is scaled back
+// by 2^-64, exact while it is normal and finite; NaN, infinite and the remaining cases divide
+// directly.
+GS_HD float div_small_num(float num, float d) {
+    const float an = fabsf(num);
+    if (!(an < 0x1p-60f)) return num / d;
+    if (an == 0.0f && d > 0.0f) return num;
+    const float qs = (num * 0x1p64f) / d;
+    const float aq = fabsf(qs);
+    return (aq >= 0x1p-62f && aq <= 0x1p127f) ? qs * 0x1p-64f : num / d;
 }
 
 GS_HD float gs_sigmoid(float x) { return 1.0f / (1.0f + gs_expf(-x)); }
