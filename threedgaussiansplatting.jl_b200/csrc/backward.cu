@@ -91,6 +91,10 @@ __device__ __forceinline__ int reduce9_index(int lane) {
     return idx < 9 && (lane & 1) == 0 ? idx : -1;
 }
 
+#ifndef GS3D_BWD_DIRECT_MAX
+#define GS3D_BWD_DIRECT_MAX 8
+#endif
+
 __global__ void __launch_bounds__(512) k_bwd_raster(const BwdArgs a) {
     extern __shared__ __align__(16) float4 sm4[];
     const int nthr = blockDim.x;
@@ -235,7 +239,7 @@ __global__ void __launch_bounds__(512) k_bwd_raster(const BwdArgs a) {
                 const unsigned cmask = __ballot_sync(0xffffffffu, contrib);
                 if (cmask == 0) continue;
                 const int fg = sF[jj];
-                if (__popc(cmask) == 1) {
+                if (__popc(cmask) <= GS3D_BWD_DIRECT_MAX) {
                     if (contrib) {
                         atomicAdd(a.mean2d_g + 2 * fg, v[0]);
                         atomicAdd(a.mean2d_g + 2 * fg + 1, v[1]);
