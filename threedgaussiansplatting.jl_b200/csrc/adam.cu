@@ -169,6 +169,13 @@ __device__ __forceinline__ void adam4(float4& p, const float4& g, float4& m01, f
     if (nup > 3) adam_reg(p.w, g.w, m23.z, m23.w, lr, a);
 }
 
+#ifndef GS3D_ADAM_GEOM_MINB
+#define GS3D_ADAM_GEOM_MINB 5
+#endif
+#ifndef GS3D_ADAM_SH_MINB
+#define GS3D_ADAM_SH_MINB 8
+#endif
+
 template <int Q>
 __device__ __forceinline__ float4 sh_basis4(float x, float y, float z) {
     return make_float4(sh_basis(4 * Q + 1, x, y, z), sh_basis(4 * Q + 2, x, y, z),
@@ -198,7 +205,7 @@ __device__ __forceinline__ float4 sh_grad_unit(int q, float cg, bool live, const
 // gradient (fgradients' color_grads), its projected colour (row f of the render buffers'
 // projected array, floats 6..8: live where >= 0) and the camera position; runs before
 // k_adam_geom, which updates the means it reads.
-__global__ void __launch_bounds__(256) k_adam_sh16_rebuild(const AdamArgs a,
+__global__ void __launch_bounds__(256, GS3D_ADAM_SH_MINB) k_adam_sh16_rebuild(const AdamArgs a,
                                                            const float* __restrict__ color_g,
                                                            const float* __restrict__ projected,
                                                            float px, float py, float pz) {
@@ -248,7 +255,8 @@ __global__ void __launch_bounds__(256) k_adam_sh16(const AdamArgs a) {
     mp[1] = m23;
 }
 
-__global__ void __launch_bounds__(256) k_adam_geom(const AdamArgs a) {
+
+__global__ void __launch_bounds__(256, GS3D_ADAM_GEOM_MINB) k_adam_geom(const AdamArgs a) {
     const int64_t F = max((int64_t)0, min((int64_t)a.counts[0], a.ncap));
     const int64_t f = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (f >= F) return;

@@ -95,7 +95,11 @@ __device__ __forceinline__ int reduce9_index(int lane) {
 #define GS3D_BWD_DIRECT_MAX 8
 #endif
 
-__global__ void __launch_bounds__(512) k_bwd_raster(const BwdArgs a) {
+#ifndef GS3D_BWDRASTER_MINB
+#define GS3D_BWDRASTER_MINB 2
+#endif
+
+__global__ void __launch_bounds__(512, GS3D_BWDRASTER_MINB) k_bwd_raster(const BwdArgs a) {
     extern __shared__ __align__(16) float4 sm4[];
     const int nthr = blockDim.x;
     float4* sA = sm4;                                          // x y opacity ic11
@@ -307,8 +311,12 @@ constexpr int kDenseRow = GS3D_DENSE_ROW;
 constexpr int kDGeom = 48, kGeomRow = GS3D_GEOM_ROW;
 constexpr int kDMean = 0, kDOpacity = 3, kDScale = 4, kDRot = 7, kDTouched = 11;
 
+#ifndef GS3D_BWDPROJ_MINB
+#define GS3D_BWDPROJ_MINB 4
+#endif
+
 template <int DEG>
-__global__ void __launch_bounds__(128, 6) k_bwd_project(const BProjArgs a, const gs3d_camera cam,
+__global__ void __launch_bounds__(128, GS3D_BWDPROJ_MINB) k_bwd_project(const BProjArgs a, const gs3d_camera cam,
                                                      const gs3d_render_options opt) {
     const int F = a.counts[0];
     float Ps[3][3];

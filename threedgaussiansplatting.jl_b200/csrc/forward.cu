@@ -142,8 +142,12 @@ struct ProjectArgs {
     int32_t* ntiles;
 };
 
+#ifndef GS3D_PROJECT_MINB
+#define GS3D_PROJECT_MINB 4
+#endif
+
 template <int DEG>
-__global__ void __launch_bounds__(256) k_project(const ProjectArgs a, const gs3d_camera cam,
+__global__ void __launch_bounds__(256, GS3D_PROJECT_MINB) k_project(const ProjectArgs a, const gs3d_camera cam,
                                                  const gs3d_tiling til,
                                                  const gs3d_render_options opt) {
     const int F = a.counts[0];

@@ -42,8 +42,12 @@ struct RasterArgs {
     float min_alpha, max_alpha, min_T, q_skip, log_min_alpha;
 };
 
+#ifndef GS3D_RASTER_MINB
+#define GS3D_RASTER_MINB 3
+#endif
+
 template <int GS>
-__global__ void __launch_bounds__(512) k_raster(const RasterArgs a) {
+__global__ void __launch_bounds__(512, GS3D_RASTER_MINB) k_raster(const RasterArgs a) {
     extern __shared__ __align__(16) float4 sm4[];
     const int nthr = blockDim.x;
     float4* sA = sm4;                 // p1 p2 p3 p4
