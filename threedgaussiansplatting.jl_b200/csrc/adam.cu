@@ -172,6 +172,9 @@ __device__ __forceinline__ void adam4(float4& p, const float4& g, float4& m01, f
 #ifndef GS3D_ADAM_GEOM_MINB
 #define GS3D_ADAM_GEOM_MINB 5
 #endif
+#ifndef GS3D_ADAM_DGEOM_MINB
+#define GS3D_ADAM_DGEOM_MINB 4
+#endif
 #ifndef GS3D_ADAM_SH_MINB
 #define GS3D_ADAM_SH_MINB 8
 #endif
@@ -232,7 +235,7 @@ __global__ void __launch_bounds__(256, GS3D_ADAM_SH_MINB) k_adam_sh16_rebuild(co
     mp[1] = m23;
 }
 
-__global__ void __launch_bounds__(256) k_adam_sh16(const AdamArgs a) {
+__global__ void __launch_bounds__(256, GS3D_ADAM_SH_MINB) k_adam_sh16(const AdamArgs a) {
     // 32-bit indices: the host only takes this path when 12 n < 2^31
     const uint32_t F = (uint32_t)max(0, min(a.counts[0], (int32_t)a.ncap));
     const uint32_t it = blockIdx.x * blockDim.x + threadIdx.x;
@@ -396,7 +399,7 @@ __global__ void __launch_bounds__(256) k_adam_dense(const AdamArgs a, const floa
 
 // Storage degree 3 (the k_adam_sh16 / k_adam_geom forms over dense rows): thread
 // 12 (g - g_begin) + c updates SH unit c of Gaussian g from the row's 16-byte unit c.
-__global__ void __launch_bounds__(256) k_adam_dense_sh16(const AdamArgs a,
+__global__ void __launch_bounds__(256, GS3D_ADAM_SH_MINB) k_adam_dense_sh16(const AdamArgs a,
                                                          const float* __restrict__ dense,
                                                          int64_t g_begin, int64_t g_end) {
     const int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -420,7 +423,7 @@ __global__ void __launch_bounds__(256) k_adam_dense_sh16(const AdamArgs a,
 
 // Geometry part of a row: 12 floats at `geom` + (g - g_begin) * stride (the dense row's last 12,
 // stride kDenseRow, or a factored geometry row, stride kGeomRow).
-__global__ void __launch_bounds__(256) k_adam_dense_geom(const AdamArgs a,
+__global__ void __launch_bounds__(256, GS3D_ADAM_DGEOM_MINB) k_adam_dense_geom(const AdamArgs a,
                                                          const float* __restrict__ geom, int stride,
                                                          int64_t g_begin, int64_t g_end) {
     const int64_t lr_ = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -473,7 +476,7 @@ struct ViewPositions {
     float p[GS3D_MAX_FACTORED_VIEWS][3];
 };
 
-__global__ void __launch_bounds__(256) k_adam_factored_sh16(const AdamArgs a,
+__global__ void __launch_bounds__(256, GS3D_ADAM_SH_MINB) k_adam_factored_sh16(const AdamArgs a,
                                                             const float* __restrict__ geom,
                                                             const float4* __restrict__ colour,
                                                             int nv, int64_t view_stride,

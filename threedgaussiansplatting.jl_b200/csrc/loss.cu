@@ -81,7 +81,11 @@ __device__ __forceinline__ void stage_rgb2(const float* __restrict__ K, const fl
     }
 }
 
-__global__ void __launch_bounds__(LT, 4) k_ssim_forward(const LossArgs a) {
+#ifndef GS3D_SSIM_MINB
+#define GS3D_SSIM_MINB 4
+#endif
+
+__global__ void __launch_bounds__(LT, GS3D_SSIM_MINB) k_ssim_forward(const LossArgs a) {
     __shared__ float sx[3][RU][RVP];
     __shared__ float sy[3][RU][RVP];
     __shared__ float tmp[5][RU][TVP];
@@ -178,7 +182,7 @@ __global__ void __launch_bounds__(LT, 4) k_ssim_forward(const LossArgs a) {
     }
 }
 
-__global__ void __launch_bounds__(LT, 4) k_ssim_backward(const LossArgs a) {
+__global__ void __launch_bounds__(LT, GS3D_SSIM_MINB) k_ssim_backward(const LossArgs a) {
     __shared__ float sd[3][RU][RVP];
     __shared__ float tmp[3][RU][TVP];
     __shared__ float red[LT / 32];

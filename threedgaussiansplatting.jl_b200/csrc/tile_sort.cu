@@ -262,7 +262,13 @@ __device__ void radix_depth_sort(uint64_t* kA, uint64_t* kB, int* wc, int* scan_
     }
 }
 
-__global__ void __launch_bounds__(kSegThreads) k_tile_segsort(
+#ifndef GS3D_SEGSORT_MINB
+#define GS3D_SEGSORT_LB __launch_bounds__(kSegThreads)
+#else
+#define GS3D_SEGSORT_LB __launch_bounds__(kSegThreads, GS3D_SEGSORT_MINB)
+#endif
+
+__global__ void GS3D_SEGSORT_LB k_tile_segsort(
     const int32_t* __restrict__ counts, int64_t capacity, const int32_t* __restrict__ tiles_end,
     const uint64_t* __restrict__ keys, uint64_t* __restrict__ scratch, int64_t* __restrict__ codes,
     int32_t* __restrict__ vals) {
