@@ -179,10 +179,10 @@ def stage_bytes(stage: str, F: int, D: int, n: int, w: int, h: int, passes: int,
 # launch's algorithmic bytes; the full-size traffic is that fraction of the full-size bytes
 # (traffic grows with the same units).
 NCU_TRAFFIC_FRACTION = {
-    # 114.26 MB read + 6.23 MB write at F = 992,004, D = 943,223, 1920x1080
-    "bwd_raster": 120.49e6 / (40.0 * 943_223 + 24.0 * 2_073_600 + 36.0 * 992_004),
-    # 39.40 MB read + 9.17 MB write
-    "raster": 48.57e6 / (40.0 * 943_223 + 20.0 * 2_073_600),
+    # 114.17 MB read + 5.78 MB write at F = 992,004, D = 943,223, 1920x1080
+    "bwd_raster": 119.95e6 / (40.0 * 943_223 + 24.0 * 2_073_600 + 36.0 * 992_004),
+    # 39.35 MB read + 8.02 MB write
+    "raster": 47.36e6 / (40.0 * 943_223 + 20.0 * 2_073_600),
 }
 
 

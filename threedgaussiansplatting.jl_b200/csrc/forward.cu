@@ -73,34 +73,41 @@ __global__ void __launch_bounds__(kChunkThreads) k_keep_upsweep(const float4* __
     if (threadIdx.x == 0) sums[blockIdx.x] = total;
 }
 
+// Second pass: each warp owns 16 rows of 32 consecutive Gaussians of the block's chunk; a
+// ballot per row gives the row's keep mask, the lanes' prefixes are popcounts of the mask below
+// them, and keep_cs / fgidx_to_gidx are written a row (32 consecutive entries) at a time.
 __global__ void __launch_bounds__(kChunkThreads) k_keep_downsweep(const uint8_t* __restrict__ keep,
                                                                   int n,
                                                                   const int32_t* __restrict__ sums,
                                                                   int32_t* __restrict__ keep_cs,
                                                                   int32_t* __restrict__ f2g) {
     __shared__ int sm[33];
-    const int64_t base = (int64_t)blockIdx.x * kChunk;
-    const int64_t mine = base + (int64_t)threadIdx.x * kChunkItems;
-    uint32_t flags = 0;
-    int s = 0;
+    constexpr int kRows = kChunk / kChunkThreads;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t wbase = (int64_t)blockIdx.x * kChunk + (int64_t)warp * (32 * kRows);
+    uint32_t masks[kRows];
+    int cnt = 0;
 #pragma unroll
-    for (int k = 0; k < kChunkItems; ++k) {
-        const int64_t i = mine + k;
-        const uint32_t f = (i < n && keep[i]) ? 1u : 0u;
-        flags |= f << k;
-        s += (int)f;
+    for (int r = 0; r < kRows; ++r) {
+        const int64_t i = wbase + r * 32 + lane;
+        masks[r] = __ballot_sync(0xffffffffu, i < n && keep[i] != 0);
+        cnt += __popc(masks[r]);
     }
     int total;
-    int run = block_exclusive_scan(s, sm, &total) + sums[blockIdx.x];
+    const int wex = block_exclusive_scan(lane == 0 ? cnt : 0, sm, &total);  // lane 0: the warp's offset
+    int run = __shfl_sync(0xffffffffu, wex, 0) + sums[blockIdx.x];
+    const uint32_t below = (1u << lane) - 1u;
 #pragma unroll
-    for (int k = 0; k < kChunkItems; ++k) {
-        const int64_t i = mine + k;
+    for (int r = 0; r < kRows; ++r) {
+        const int64_t i = wbase + r * 32 + lane;
+        const uint32_t m = masks[r];
+        const uint32_t mine = (m >> lane) & 1u;
+        const int incl = run + __popc(m & below) + (int)mine;
         if (i < n) {
-            const int f = (flags >> k) & 1u;
-            run += f;
-            if (keep_cs) keep_cs[i] = run;
-            if (f) f2g[run - 1] = (int32_t)(i + 1);
+            if (keep_cs) keep_cs[i] = incl;
+            if (mine) f2g[incl - 1] = (int32_t)(i + 1);
         }
+        run += __popc(m);
     }
 }
 
