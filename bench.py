@@ -437,8 +437,9 @@ def main() -> None:
                 "peak_source": peak_kind, "unit": "GB/s",
                 "frac": round(achieved / peak, 4) if achieved else None,
                 "traffic": traffic, "traffic_unit": "GB per launch",
-                "limiter": ("FP32 issue (ncu: ~83% issue-active, <2% DRAM)"
-                            if dominant in ("raster", "bwd_raster") else "HBM")}
+                "limiter": {"bwd_raster": "instruction issue (ncu at 1M: 82% issue active, 2% DRAM)",
+                            "raster": "instruction issue (ncu at 1M: 92% issue active, 2% DRAM)"}
+                           .get(dominant, "HBM")}
     gpu_launches = 0
     for name, (cnt, _) in prof.items():
         k = KERNELS_PER_STAGE.get(name, 1)
