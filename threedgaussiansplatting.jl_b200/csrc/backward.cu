@@ -432,7 +432,13 @@ __global__ void __launch_bounds__(128, GS3D_BWDPROJ_MINB) k_bwd_project(const BP
                 V[k] = RS[i][0] * RS[j][0] + RS[i][1] * RS[j][1] + RS[i][2] * RS[j][2];
             }
         }
-        // mean3d gradient from cov2d (Transposed_dsigma_dm, backward_core.jl:789-922)
+        // mean3d gradient from cov2d (Transposed_dsigma_dm, backward_core.jl:789-922). The
+        // reference contracts dSigma/dm_k = dJ_k V J^T + J V dJ_k^T (dJ_k: 2x3, 18 entries per k)
+        // with the lower-triangle cov2d gradient G. V is symmetric, so with W_i = V J_i^T the
+        // contraction is sum_al dJ[0][al][k] U0[al] + dJ[1][al][k] U1[al], U0 = 2 G00 W0 + G10 W1,
+        // U1 = 2 G11 W1 + G10 W0; each dJ[i][al][k] is e_i[al] Ps[i][k] + r_i[al] Ps[2][k], so the
+        // sum is Ps[0][k] a0 + Ps[1][k] a1 + Ps[2][k] (b0 + b1): ~50 operations instead of ~470
+        // (same value up to rounding).
         {
             const float c2x = cmx + cmx, c2y = cmy + cmy;
             float dlx = 1.0f, dly = 1.0f;
@@ -440,36 +446,25 @@ __global__ void __launch_bounds__(128, GS3D_BWDPROJ_MINB) k_bwd_project(const BP
                 dlx = (opt.clip_x_min < cmx && cmx <= opt.clip_x_max) ? 1.0f : 0.0f;
                 dly = (opt.clip_y_min < cmy && cmy <= opt.clip_y_max) ? 1.0f : 0.0f;
             }
-            float dJ[2][3][3];
+            float a0 = 0.0f, b0 = 0.0f, a1 = 0.0f, b1 = 0.0f;
 #pragma unroll
             for (int al = 0; al < 3; ++al) {
+                const float w0 = V[low3(al, 0)] * J[0][0] + V[low3(al, 1)] * J[0][1] + V[low3(al, 2)] * J[0][2];
+                const float w1 = V[low3(al, 0)] * J[1][0] + V[low3(al, 1)] * J[1][1] + V[low3(al, 2)] * J[1][2];
+                const float u0 = 2.0f * cg[0] * w0 + cg[1] * w1;
+                const float u1 = 2.0f * cg[2] * w1 + cg[1] * w0;
                 const float r0 = Ps[0][al] - c2x * Ps[2][al];
                 const float r1 = Ps[1][al] - c2y * Ps[2][al];
-                const float e0 = dlx * Ps[2][al];
-                const float e1 = dly * Ps[2][al];
-#pragma unroll
-                for (int k = 0; k < 3; ++k) {
-                    dJ[0][al][k] = e0 * Ps[0][k] + r0 * Ps[2][k];
-                    dJ[1][al][k] = e1 * Ps[1][k] + r1 * Ps[2][k];
-                }
+                a0 = a0 + (dlx * Ps[2][al]) * u0;
+                b0 = b0 + r0 * u0;
+                a1 = a1 + (dly * Ps[2][al]) * u1;
+                b1 = b1 + r1 * u1;
             }
             const float sc = -(1.0f / (depth * depth));
+            const float b01 = b0 + b1;
 #pragma unroll
-            for (int k = 0; k < 3; ++k) {
-                float acc3 = 0.0f;
-#pragma unroll
-                for (int p = 0; p < 3; ++p) {
-                    const int i = L2I[p], j = L2J[p];
-                    float tt = 0.0f;
-#pragma unroll
-                    for (int al = 0; al < 3; ++al)
-#pragma unroll
-                        for (int be = 0; be < 3; ++be)
-                            tt = tt + V[low3(al, be)] * (dJ[i][al][k] * J[j][be] + J[i][al] * dJ[j][be][k]);
-                    acc3 = acc3 + tt * cg[p];
-                }
-                m3[k] = m3[k] + sc * acc3;
-            }
+            for (int k = 0; k < 3; ++k)
+                m3[k] = m3[k] + sc * (Ps[0][k] * a0 + Ps[1][k] * a1 + Ps[2][k] * b01);
         }
         // mean3d gradient from the view-dependent colour
         const float vx = mo.x - cam.position[0], vy = mo.y - cam.position[1], vz = mo.z - cam.position[2];
