@@ -30,16 +30,17 @@ def test_shard_ranges_partition_the_gaussians():
 
 def test_chunk_ownership_partitions_the_gaussians():
     """Rank r owns [c C + r S, c C + (r + 1) S) of every chunk c; together they cover [0, n)."""
-    for n in (1, 5, 8, 9, 1000, 313_001):
-        for world in (1, 2, 3, 8):
-            S, C_ = chunk_layout(n, world, CHUNKS)
-            assert C_ == S * world and CHUNKS * C_ >= n
-            covered = []
-            for c in range(CHUNKS):
-                for r in range(world):
-                    lo = c * C_ + r * S
-                    covered.extend(range(min(lo, n), min(lo + S, n)))
-            assert sorted(covered) == list(range(n)), (n, world)
+    for chunks in sorted({1, 2, 3, 4, CHUNKS}):
+        for n in (1, 5, 8, 9, 1000, 313_001):
+            for world in (1, 2, 3, 8):
+                S, C_ = chunk_layout(n, world, chunks)
+                assert C_ == S * world and chunks * C_ >= n
+                covered = []
+                for c in range(chunks):
+                    for r in range(world):
+                        lo = c * C_ + r * S
+                        covered.extend(range(min(lo, n), min(lo + S, n)))
+                assert sorted(covered) == list(range(n)), (n, world, chunks)
 
 
 def test_views_of_a_step_are_distinct():
