@@ -44,6 +44,8 @@ METRIC = "train iters/s and render frames/s, 3M Gaussians @1920x1080, 1/2/4/8 B2
 UNIT = "train views/s"
 CONFIG_ID = 4
 START_ITERATION = 3000
+WORKLOAD = ("3M Gaussians (BASELINE config 4 scene), 1920x1080, 1 view per GPU per step: "
+            "render + L1/DSSIM + backward + ADC stats + Adam")
 POOL = 8  # distinct target images (one per camera index modulo POOL)
 FALLBACK_HBM_GBS = 6650.0
 
@@ -208,10 +210,11 @@ def run_reference(args, rank: int, world: int) -> None:
     opts = TrainingOptions(scene_radius=radius)
     rng = np.random.default_rng(0)
     perm = rng.permutation(len(cams))
-    steps = 0
-    t0 = time.perf_counter()
-    while True:
-        cam_i = int(perm[steps % len(cams)])
+    done = 0
+
+    def one_step():
+        nonlocal done
+        cam_i = int(perm[done % len(cams)])
         cam = cams[cam_i]
         target = pool_host[cam_i % POOL].numpy()
         f = O.render(g, cam, til, ro)
@@ -221,25 +224,38 @@ def run_reference(args, rank: int, world: int) -> None:
         lrs = opts.learning_rates()
         p.lr_means, p.lr_opacity_features, p.lr_scaling_features = lrs.means, lrs.opacity_features, lrs.scaling_features
         p.lr_rotation_features, p.lr_sh_dc, p.lr_sh_rest = lrs.rotation_features, lrs.sh_coeffs_dc, lrs.sh_coeffs_rest
-        p.beta1, p.beta2, p.epsilon, p.update_count, p.sh_degree = 0.9, 0.999, 1e-15, steps, 3
-        bc1, bc2 = bias_corrections(0.9, 0.999, steps)
+        p.beta1, p.beta2, p.epsilon, p.update_count, p.sh_degree = 0.9, 0.999, 1e-15, done, 3
+        bc1, bc2 = bias_corrections(0.9, 0.999, done)
         O.adam(g, m, b, f["fgidx_to_gidx"], p, bc1, bc2)
+        done += 1
+
+    # warm-up steps as asked, each a full step; capped at half the time budget in all
+    warm = 0
+    tw = time.perf_counter()
+    while warm < args.warmup and (warm == 0 or time.perf_counter() - tw < args.ref_budget_s / 2):
+        one_step()
+        warm += 1
+    steps = 0
+    t0 = time.perf_counter()
+    while True:
+        one_step()
         steps += 1
         el = time.perf_counter() - t0
         if steps >= args.steps or el >= args.ref_budget_s:
             break
     value = steps / el
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps,
-            "warmup": 0, "ms_per_step": 1000 * el / steps, "higher_is_better": True,
+            "warmup": warm, "ms_per_step": 1000 * el / steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "impl": "reference",
-            "config": {"workload": "3M Gaussians (config 4 scene), 1920x1080, 1 view per step, "
-                                   "render+L1/DSSIM+backward+Adam", "global_batch": 1,
-                       "parallelism": "cpu"},
+            "config": {"workload": WORKLOAD, "global_batch": 1, "views_per_gpu": 1,
+                       "resolution": [cams[0].width, cams[0].height], "n_gaussians": n,
+                       "parallelism": "cpu",
+                       "note": "the oracle step computes no ADC statistics (under 1% of the GPU step)"},
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                             "sample": f"{steps} full training step(s) of the workload (time-bounded "
-                                       f"{args.ref_budget_s:.0f} s), CPU restatement of the reference's "
-                                       f"GPU-path arithmetic, {threads} threads"},
+                             "sample": f"{steps} full training step(s) of the workload after {warm} "
+                                       f"warm-up step(s) (time-bounded {args.ref_budget_s:.0f} s), CPU "
+                                       f"restatement of the reference's GPU-path arithmetic, {threads} threads"},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -452,8 +468,7 @@ def main() -> None:
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "3M Gaussians (BASELINE config 4 scene), 1920x1080, 1 view per GPU "
-                                   "per step: render + L1/DSSIM + backward + ADC stats + Adam",
+            "config": {"workload": WORKLOAD,
                        "global_batch": world, "views_per_gpu": 1, "resolution": [w, h],
                        "n_gaussians": gv.n, "filtered_F": F, "duplicates_D": D,
                        "tiles": [til.tile_width, til.tile_height],
