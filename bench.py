@@ -154,20 +154,25 @@ def build_workload(device, seed_offset=0, n_override=None):
 
 
 def stage_bytes(stage: str, F: int, D: int, n: int, w: int, h: int, passes: int,
-                world: int = 1, factored: bool = True) -> float | None:
-    """Algorithmic bytes of one step of a stage on one rank (the per-unit figures of the
-    hot-path analysis). Adam: 1416 B of parameters and moments read and written per Gaussian
-    plus its gradients: 44 B of geometry gradients, the colour gradients and projected colours
-    (24 B) from which the SH gradients are rebuilt, the fgidx_to_gidx entry; data parallel: the
-    rank's n / world Gaussians with a 48 B geometry row and a 16 B colour row per view
-    (factored) or a 240 B dense row."""
+                world: int = 1, factored: bool = True, tiles: int = 0) -> float | None:
+    """Algorithmic bytes of one step of a stage on one rank: the hot-path analysis' minimum
+    traffic per unit in the reference's data layouts (a stage that moves less than the
+    reference layout needs is still credited with these bytes): keep + scan + compact 31 B per
+    Gaussian; projection 300 B per filtered Gaussian; duplication 28 B read per filtered
+    Gaussian (the tile counts here) and 12 B written per duplicate, the sort at the reference's
+    key width (`passes` = ceil(key bits / 8) passes x 24 B per duplicate: 6 at 1080p) and the
+    tile ranges 8 B per duplicate + 4 B per
+    tile (the scatter + segment sort here); backward projection 548 B and Adam 1656 B per
+    filtered Gaussian (data parallel: per Gaussian of the rank's n / world); blends as
+    documented per rasteriser."""
+    sort_bytes_per_dup = 24.0 * passes
     return {
         "project": 300.0 * F,
-        "sort": 20.0 * F + 28.0 * D,          # scatter (rect, depth; key) + segment sort (key; code, value)
-        "tile_count": 16.0 * F,              # tile rectangles
-        "adam": 1488.0 * F,
-        "adam_dense": (1416.0 + (48.0 + 16.0 * world if factored else 240.0)) * n / world,
-        "bwd_project": 356.0 * F,
+        "tile_count": 28.0 * F + 4.0 * tiles,
+        "sort": (12.0 + sort_bytes_per_dup + 8.0) * D,
+        "adam": 1656.0 * F,
+        "adam_dense": 1656.0 * n / world,
+        "bwd_project": 548.0 * F,
         "keep_compact": 31.0 * n,
         "dup_keys": 28.0 * F + 12.0 * D,
         "raster": 40.0 * D + 20.0 * w * h,
@@ -437,7 +442,7 @@ def main() -> None:
     factored = world > 1 and args.dp_exchange == "factored"
     for name, (cnt, tot) in prof.items():
         avg = tot / max(cnt, 1)
-        b = stage_bytes(name, F, D, gv.n, w, h, passes, world, factored)
+        b = stage_bytes(name, F, D, gv.n, w, h, passes, world, factored, til.nb_tiles)
         b = b * args.steps / cnt if b and cnt else b  # per launch (chunked stages: a share)
         stages[name] = {"launches": cnt, "avg_ms": round(avg, 4),
                         "share": round(tot / max(sum(t for _, t in prof.values()), 1e-9), 4),
@@ -445,7 +450,7 @@ def main() -> None:
     dominant = max(prof.items(), key=lambda kv: kv[1][1])[0]
     dom = stages[dominant]
     achieved = dom["alg_GBps"]
-    dom_bytes = stage_bytes(dominant, F, D, gv.n, w, h, passes, world, factored)
+    dom_bytes = stage_bytes(dominant, F, D, gv.n, w, h, passes, world, factored, til.nb_tiles)
     dom_bytes = dom_bytes * args.steps / prof[dominant][0] if dom_bytes else dom_bytes
     traffic = (round(NCU_TRAFFIC_FRACTION[dominant] * dom_bytes / 1e9, 4)
                if dominant in NCU_TRAFFIC_FRACTION and dom_bytes else None)
