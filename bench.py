@@ -64,7 +64,7 @@ def parse():
     ap.add_argument("--impl", choices=["gs3d", "reference"], default="gs3d")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--ref-budget-s", type=float, default=120.0)
+    ap.add_argument("--ref-seconds", type=float, default=120.0)
     ap.add_argument("--n-gaussians", type=int, default=None,
                     help="override the Gaussian count (same distributions); for small profiling cases")
     ap.add_argument("--dp-exchange", choices=["factored", "dense"], default="factored",
@@ -234,10 +234,10 @@ def run_reference(args, rank: int, world: int) -> None:
         O.adam(g, m, b, f["fgidx_to_gidx"], p, bc1, bc2)
         done += 1
 
-    # warm-up steps as asked, each a full step; capped at half the time budget in all
+    # warm-up steps as asked, each a full step; capped at half the time cap in all
     warm = 0
     tw = time.perf_counter()
-    while warm < args.warmup and (warm == 0 or time.perf_counter() - tw < args.ref_budget_s / 2):
+    while warm < args.warmup and (warm == 0 or time.perf_counter() - tw < args.ref_seconds / 2):
         one_step()
         warm += 1
     steps = 0
@@ -246,7 +246,7 @@ def run_reference(args, rank: int, world: int) -> None:
         one_step()
         steps += 1
         el = time.perf_counter() - t0
-        if steps >= args.steps or el >= args.ref_budget_s:
+        if steps >= args.steps or el >= args.ref_seconds:
             break
     value = steps / el
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps,
@@ -259,7 +259,7 @@ def run_reference(args, rank: int, world: int) -> None:
                        "note": "the oracle step computes no ADC statistics (under 1% of the GPU step)"},
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                              "sample": f"{steps} full training step(s) of the workload after {warm} "
-                                       f"warm-up step(s) (time-bounded {args.ref_budget_s:.0f} s), CPU "
+                                       f"warm-up step(s) (time-bounded {args.ref_seconds:.0f} s), CPU "
                                        f"restatement of the reference's GPU-path arithmetic, {threads} threads"},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)

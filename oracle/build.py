@@ -23,7 +23,8 @@ LIB_DIR = ORACLE_DIR / "_lib"
 REF_DIR = ORACLE_DIR / "_ref"
 ORACLE_LIB = LIB_DIR / "libgs3d_oracle.so"
 REF_LIB = REF_DIR / "cub_sort_pairs_wrapper.so"
-REFERENCE_ROOT = Path(os.environ.get("GS3D_REFERENCE_ROOT", "/root/reference"))
+# the reference checkout: $GS3D_REFERENCE_ROOT, else the directory `reference` beside the repository
+REFERENCE_ROOT = Path(os.environ.get("GS3D_REFERENCE_ROOT", ORACLE_DIR.parent.parent / "reference"))
 REF_SRC_REL = Path("deps/cub_sort_pairs/cub_sort_pairs_wrapper.cu")
 
 

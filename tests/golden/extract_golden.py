@@ -4,7 +4,7 @@ reference_golden.json (committed beside this script).
 The reference is Julia and cannot run in this image, so its tests are read as text: every
 number below comes from the literal arrays in the reference's test files, located by the
 statements that hold them. Run from the repository root with the reference checkout at
-$GS3D_REFERENCE_ROOT (default /root/reference):
+$GS3D_REFERENCE_ROOT (default: the directory `reference` beside the repository):
 
     python tests/golden/extract_golden.py
 """
@@ -15,7 +15,8 @@ import os
 import re
 from pathlib import Path
 
-ROOT = Path(os.environ.get("GS3D_REFERENCE_ROOT", "/root/reference"))
+ROOT = Path(os.environ.get("GS3D_REFERENCE_ROOT",
+                           Path(__file__).resolve().parents[3] / "reference"))
 OUT = Path(__file__).resolve().parent / "reference_golden.json"
 NUM = re.compile(r"[-+]?(?:\d+\.\d*|\.\d+|\d+)(?:[eE][-+]?\d+)?")
 

@@ -2,7 +2,7 @@
 // scratch in this library's own static device memory instead of caller-provided temp storage.
 //
 // Who needs it: a caller that cannot hand the library a temporary device buffer. A plain C or
-// Julia render loop that keeps a fixed device-memory budget per frame, or that must not call
+// Julia render loop that keeps its device memory fixed across frames, or that must not call
 // into its allocator while a frame is in flight (CUDA.jl's pool may run the garbage collector
 // to satisfy an allocation, which stalls the frame), has nowhere to get the temp storage that
 // sort_pairs wants; the reference itself reallocates that buffer inside render!
