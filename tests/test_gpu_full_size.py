@@ -1,7 +1,8 @@
 """Full-size checks on the bench workload (3M Gaussians, 1920x1080, 256
-hemisphere cameras), where the CPU oracle would take minutes per frame. The exact comparisons
-with the oracle run at smaller sizes (test_gpu_forward.py, test_gpu_backward_adam.py); here the
-CUDA path is held to the properties that hold at any size:
+hemisphere cameras) and the 4K render-only config 3 (6M Gaussians, 3840x2160), where the CPU
+oracle would take minutes per frame. The exact comparisons with the oracle run at smaller sizes
+(test_gpu_forward.py, test_gpu_backward_adam.py); here the CUDA path is held to the properties
+that hold at any size:
 
 * compaction: keep_gaussians_cs is the inclusive prefix of keep_gaussians, fgidx_to_gidx lists
   the kept Gaussians in order;
@@ -29,11 +30,16 @@ from gs3d.scene import CONFIGS, synthetic_gaussians
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(scope="module")
-def scene(cuda):
-    cfg = CONFIGS[4]
-    gv = synthetic_gaussians(cfg["spec"], cfg["seed"]).to(cuda)
-    return gv, cfg["cameras"]()
+_SCENES = {}
+
+
+def config_scene(cfg_id, device):
+    """Gaussians (on the device) and cameras of a BASELINE config, built once per module."""
+    if cfg_id not in _SCENES:
+        _SCENES.clear()  # one full-size scene resident at a time
+        cfg = CONFIGS[cfg_id]
+        _SCENES[cfg_id] = (synthetic_gaussians(cfg["spec"], cfg["seed"]).to(device), cfg["cameras"]())
+    return _SCENES[cfg_id]
 
 
 def render_full(gv, cam, device, reference_order=False):
@@ -46,9 +52,12 @@ def render_full(gv, cam, device, reference_order=False):
     return out, buf, opt, til
 
 
-@pytest.mark.parametrize("cam_index", [0, 131])
-def test_full_size_forward_properties(cuda, scene, cam_index):
-    gv, cams = scene
+@pytest.mark.parametrize("cfg_id, cam_index", [(4, 0), (4, 131), (3, 0)],
+                         ids=["cfg4_cam0", "cfg4_cam131", "cfg3_4k_cam0"])
+def test_full_size_forward_properties(cuda, cfg_id, cam_index):
+    """Config 4 (3M, 1080p, the bench scene) and config 3 (6M, 3840x2160, 16,320 tiles, 46 key
+    bits: the render-only case)."""
+    gv, cams = config_scene(cfg_id, cuda)
     cam = cams[cam_index]
     out, buf, opt, til = render_full(gv, cam, cuda)
     n = gv.n
@@ -112,8 +121,8 @@ def test_full_size_forward_properties(cuda, scene, cam_index):
         assert torch.equal(a, b)
 
 
-def test_full_size_backward_and_update_paths_agree(cuda, scene):
-    gv, cams = scene
+def test_full_size_backward_and_update_paths_agree(cuda):
+    gv, cams = config_scene(4, cuda)
     cam = cams[7]
     g = gv.clone()
     out, buf, opt, til = render_full(g, cam, cuda)
