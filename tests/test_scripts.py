@@ -1,0 +1,62 @@
+"""Host logic of the headless entry points (gs3d/scripts.py) on the CPU: image files, the
+validation-camera choice and the model choice of scripts/train.jl and scripts/render.jl."""
+import numpy as np
+import pytest
+import torch
+
+from gs3d import scripts
+
+
+def test_image_files_round_trip(tmp_path):
+    rng = np.random.default_rng(0)
+    img = torch.from_numpy(rng.uniform(0, 1, size=(7, 5, 3)).astype(np.float32))  # (w, h, 3)
+    scripts.write_image(tmp_path / "a.npy", img)
+    assert torch.equal(scripts.read_image(tmp_path / "a.npy"), img)
+    assert np.load(tmp_path / "a.npy").shape == (5, 7, 3)  # stored as (h, w, 3)
+    scripts.write_image(tmp_path / "a.ppm", img)
+    back = scripts.read_image(tmp_path / "a.ppm")
+    assert back.shape == (7, 5, 3)
+    assert torch.equal(back, torch.from_numpy(np.rint(img.numpy() * 255).astype(np.float32) / 255))
+
+
+def test_ppm_pgm_headers_and_uint8_npy(tmp_path):
+    w, h = 3, 2
+    px = bytes(range(w * h * 3))
+    (tmp_path / "c.ppm").write_bytes(b"P6\n# comment\n3 2\n255\n" + px)
+    a = scripts.read_image(tmp_path / "c.ppm")
+    want = np.frombuffer(px, np.uint8).reshape(h, w, 3).astype(np.float32) / 255
+    assert torch.equal(a, torch.from_numpy(want.transpose(1, 0, 2).copy()))
+    (tmp_path / "g.pgm").write_bytes(b"P5 3 2 255\n" + bytes(range(6)))
+    g = scripts.read_image(tmp_path / "g.pgm")
+    assert g.shape == (3, 2, 3) and torch.equal(g[..., 0], g[..., 2])
+    np.save(tmp_path / "u.npy", np.full((h, w, 3), 51, np.uint8))
+    assert torch.allclose(scripts.read_image(tmp_path / "u.npy"), torch.full((w, h, 3), 0.2))
+    (tmp_path / "x.png").write_bytes(b"")
+    with pytest.raises(ValueError):
+        scripts.read_image(tmp_path / "x.png")
+
+
+def test_validation_cameras_as_the_script_picks_them():
+    rng = np.random.default_rng(0)
+    assert scripts.validation_camera_ids(10, 0.0, False, rng) == []
+    assert scripts.validation_camera_ids(10, 0.2, False, rng) == [4, 9]      # 1-based 5:5:10
+    assert scripts.validation_camera_ids(11, 0.2, False, rng) == [5]         # k = 2, step 6: 6:6:11
+    ids = scripts.validation_camera_ids(20, 0.25, True, rng)
+    assert len(ids) == 5 and len(set(ids)) == 5 and all(0 <= i < 20 for i in ids)
+
+
+def test_evaluation_and_save_schedules():
+    assert scripts._due(0, 1000) and scripts._due(2000, 1000) and not scripts._due(999, 1000)
+    assert scripts._due(7000, (7000, 30_000)) and not scripts._due(7001, (7000, 30_000))
+
+
+def test_model_choice(tmp_path):
+    for n in (10, 300, 30):
+        d = tmp_path / "out" / "point_cloud" / f"iteration_{n}"
+        d.mkdir(parents=True)
+        (d / "point_cloud.ply").write_bytes(b"")
+    assert scripts.model_path(tmp_path / "out").parent.name == "iteration_300"
+    assert scripts.model_path(tmp_path / "out", 30).parent.name == "iteration_30"
+    assert scripts.model_path(tmp_path / "m.ply") == tmp_path / "m.ply"
+    cam = scripts.default_camera()
+    assert (cam.width, cam.height) == (1280, 720) and cam.fx == pytest.approx(640.0)
