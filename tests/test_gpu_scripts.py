@@ -16,7 +16,22 @@ from gs3d.training import TrainingOptions
 pytestmark = pytest.mark.gpu
 
 
-def test_headless_train_then_render(cuda, tmp_path):
+def _write_point_cloud(path, n, seed):
+    rng = np.random.default_rng(seed)
+    rec = np.zeros(n, dtype=[("x", "<f4"), ("y", "<f4"), ("z", "<f4"),
+                             ("red", "u1"), ("green", "u1"), ("blue", "u1")])
+    for k in ("x", "y", "z"):
+        rec[k] = rng.uniform(-1, 1, n)
+    for k in ("red", "green", "blue"):
+        rec[k] = rng.integers(0, 256, n)
+    head = (f"ply\nformat binary_little_endian 1.0\nelement vertex {n}\nproperty float x\n"
+            "property float y\nproperty float z\nproperty uchar red\nproperty uchar green\n"
+            "property uchar blue\nend_header\n").encode()
+    path.write_bytes(head + rec.tobytes())
+
+
+@pytest.mark.parametrize("start", ["model", "point_cloud"])
+def test_headless_train_then_render(cuda, tmp_path, start):
     w, h = 96, 64
     cams = [look_at_camera(w, h, 60.0, (np.cos(a) * 3, 0.8, np.sin(a) * 3))
             for a in np.linspace(0, 2 * np.pi, 5, endpoint=False)]
@@ -34,7 +49,10 @@ def test_headless_train_then_render(cuda, tmp_path):
         scripts.write_image(inp / name, out.rgb)
         entries.append(name)
     io.save_cameras_json(inp / "cameras.json", cams, image_paths=entries)
-    io.save_ply(inp / "point_cloud.ply", synthetic_gaussians(SceneSpec(2_000, "uniform:1", -4.0, 0.5), 5))
+    if start == "model":
+        io.save_ply(inp / "point_cloud.ply", synthetic_gaussians(SceneSpec(2_000, "uniform:1", -4.0, 0.5), 5))
+    else:  # a coloured point cloud starts as the reference's first model (SH degree 0)
+        _write_point_cloud(inp / "point_cloud.ply", 2_000, 5)
 
     logs = []
     outd = tmp_path / "output"

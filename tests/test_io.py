@@ -171,3 +171,40 @@ def test_cameras_json_3dgs_entries_and_rescaling(tmp_path):
     f, _ = io.load_cameras_json(p, forced_width=800, forced_height=600)
     assert (f.width, f.height) == (800, 600)
     assert f.fy == float(np.float32(np.float32(900.0) * (np.float32(600) / np.float32(750))))
+
+
+def test_gaussians_from_point_cloud_as_the_reference_initialises(tmp_path):
+    """gaussians.jl:597-639: means at the points, logit(0.1) opacity features, degree-0 SH from
+    the colours, identity rotations, log-scales = log(sum of the 4 nearest distances incl. the
+    point itself / 3); a coloured point-cloud PLY (uchar colours) goes through it."""
+    from gs3d.scene import gaussians_from_point_cloud
+    rng = np.random.default_rng(2)
+    pts = rng.uniform(-1, 1, size=(50, 3)).astype(np.float32)
+    cols = rng.uniform(0, 1, size=(50, 3)).astype(np.float32)
+    g = gaussians_from_point_cloud(pts, cols)
+    assert g.n == 50 and g.sh_degree == 0
+    mo = g.means_opacity_features.numpy()
+    assert np.array_equal(mo[:, :3], pts)
+    assert np.allclose(1 / (1 + np.exp(-mo[:, 3].astype(np.float64))), 0.1, rtol=1e-6)
+    assert np.allclose(g.sh_coeffs.numpy()[:, :, 0] * 0.28209479177387814 + 0.5, cols, atol=1e-6)
+    assert np.array_equal(g.rotation_features.numpy(), np.tile([1, 0, 0, 0], (50, 1)).astype(np.float32))
+    d = np.sqrt(((pts[:, None, :].astype(np.float64) - pts[None, :, :]) ** 2).sum(-1))
+    want = np.log(np.sort(d, axis=1)[:, :4].sum(1) / 3)
+    sf = g.scaling_features.numpy()
+    assert np.allclose(sf[:, 0], want, rtol=1e-5) and np.array_equal(sf[:, 0], sf[:, 2])
+
+    header = ("ply\nformat binary_little_endian 1.0\nelement vertex 50\nproperty float x\n"
+              "property float y\nproperty float z\nproperty uchar red\nproperty uchar green\n"
+              "property uchar blue\nend_header\n").encode()
+    u8 = (cols * 255).astype(np.uint8)
+    rec = np.zeros(50, dtype=[("x", "<f4"), ("y", "<f4"), ("z", "<f4"), ("r", "u1"), ("g", "u1"), ("b", "u1")])
+    rec["x"], rec["y"], rec["z"] = pts[:, 0], pts[:, 1], pts[:, 2]
+    rec["r"], rec["g"], rec["b"] = u8[:, 0], u8[:, 1], u8[:, 2]
+    p = tmp_path / "points.ply"
+    p.write_bytes(header + rec.tobytes())
+    pc = io.load_model_or_point_cloud(p)
+    assert pc.sh_degree == 0 and np.array_equal(pc.means_opacity_features.numpy()[:, :3], pts)
+    assert np.allclose(pc.sh_coeffs.numpy()[:, :, 0] * 0.28209479177387814 + 0.5, u8 / 255.0, atol=1e-6)
+    m = tmp_path / "model.ply"
+    io.save_ply(m, g)
+    assert torch.equal(io.load_model_or_point_cloud(m).sh_coeffs, g.sh_coeffs)

@@ -148,6 +148,28 @@ def load_ply(path, device="cpu") -> GaussiansVector:
     return GaussiansVector(t(mo), t(sf), t(rf), t(sh))
 
 
+def read_point_cloud(path) -> tuple[np.ndarray, np.ndarray]:
+    """A coloured point cloud PLY (x y z and red green blue, as COLMAP exports its points):
+    ((n, 3) float32 points, (n, 3) float32 colours in [0, 1]; 8-bit colours are divided by 255)."""
+    v = _read_ply(path)
+    pts = np.stack([v["x"], v["y"], v["z"]], axis=1).astype(F32)
+    cols = np.stack([v["red"], v["green"], v["blue"]], axis=1)
+    if cols.dtype == np.uint8:
+        cols = cols.astype(F32) / F32(255)
+    return pts, cols.astype(F32)
+
+
+def load_model_or_point_cloud(path, device="cpu") -> GaussiansVector:
+    """A 3DGS model PLY as is, or a coloured point cloud PLY through
+    `gaussians_from_point_cloud` (the script's first model)."""
+    from .scene import gaussians_from_point_cloud
+    props = _read_ply(path)
+    if "f_dc_0" in props:
+        return load_ply(path, device=device)
+    pts, cols = read_point_cloud(path)
+    return gaussians_from_point_cloud(pts, cols, device=device)
+
+
 # -- cameras.json -----------------------------------------------------------------------------
 def _f32(x) -> float:
     return float(F32(x))

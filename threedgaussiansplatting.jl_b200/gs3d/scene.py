@@ -64,6 +64,34 @@ def create_test_scene(sh_degree: int = 0, two_cameras: bool = False, device="cpu
     return gv, cams
 
 
+def gaussians_from_point_cloud(points, rgb_colors, device="cpu") -> GaussiansVector:
+    """The trainable Gaussians a coloured point cloud starts as (gaussians.jl:597-639): means
+    at the points, opacity features logit(0.1), SH degree 0 with DC = (colour - 0.5) / C0 (the
+    inverse of the degree-0 colour), identity rotations (1, 0, 0, 0), and all three log-scales
+    = log of the mean Euclidean distance to the 3 nearest other points (the 4 nearest
+    neighbours including the point itself, summed and divided by 3, as the reference does)."""
+    from scipy.spatial import cKDTree
+    pts = np.asarray(points, dtype=F32).reshape(-1, 3)
+    cols = np.asarray(rgb_colors, dtype=F32).reshape(-1, 3)
+    n = pts.shape[0]
+    k = min(4, n)
+    d, _ = cKDTree(pts.astype(np.float64)).query(pts.astype(np.float64), k=k)
+    d = np.asarray(d, dtype=np.float64).reshape(n, k).astype(F32)
+    mean_d = d.sum(axis=1, dtype=F32) / F32(3)
+    with np.errstate(divide="ignore"):
+        log_s = np.log(mean_d).astype(F32)
+    mo = np.empty((n, 4), F32)
+    mo[:, :3] = pts
+    mo[:, 3] = logit_np(np.full(n, 0.1, F32))
+    sf = np.repeat(log_s[:, None], 3, axis=1)
+    rf = np.zeros((n, 4), F32)
+    rf[:, 0] = 1
+    c0 = F32(0.28209479177387814)
+    sh = ((cols - F32(0.5)) / c0).astype(F32).reshape(n, 3, 1)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(device)
+    return GaussiansVector(t(mo), t(sf), t(rf), t(sh))
+
+
 def scene_radius(cameras, enlargement_factor: float = 1.1) -> float:
     """_compute_scene_radius (scene.jl:49-73): 1.1 x max distance to the camera centroid."""
     pos = np.stack([c.position.astype(np.float64) for c in cameras])

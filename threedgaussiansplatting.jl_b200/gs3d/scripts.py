@@ -6,7 +6,9 @@ train(input_dir, output_dir) differs from the reference only where the reference
 the training path: instead of running COLMAP on a directory of images and building the first
 model from its points (`process_colmap`, `processed_colmap_to_cameras_with_images_and_gaussians_model`),
 `input_dir` holds `cameras.json` (entries with a `path` to each training image, relative to
-`input_dir` or absolute) and the initial model `point_cloud.ply`. Everything else follows the
+`input_dir` or absolute) and `point_cloud.ply`: a 3DGS model, or a coloured point cloud (x y z red
+green blue, e.g. exported from an SfM run) that starts as the reference's first model
+(`gaussians_from_point_cloud`). Everything else follows the
 script: validation cameras (`validation_ratio`, equidistant or random), `TrainingOptions` from the
 training scene, the loop `while iteration_nb <= nb_iterations: maybe_eval_losses; training_step;
 maybe_save` (so the last step brings iteration_nb to nb_iterations + 1, as there), the MSE / MAE /
@@ -146,7 +148,7 @@ def train(input_dir, output_dir, *, render_options_from_camera=None, training_op
     for cam, img in zip(cameras, images):
         if img.shape != (cam.width, cam.height, 3):
             raise ValueError(f"image of size {tuple(img.shape[:2])} for a {cam.width}x{cam.height} camera")
-    gaussians = io.load_ply(input_dir / "point_cloud.ply", device=device)
+    gaussians = io.load_model_or_point_cloud(input_dir / "point_cloud.ply", device=device)
     output_dir.mkdir(parents=True, exist_ok=True)
     io.save_cameras_json(output_dir / "cameras.json", cameras, image_paths=[str(p) for p in paths])
 
