@@ -95,6 +95,16 @@ typedef struct gs3d_gaussians {
     float* sh_coeffs;               /* (d+1)^2 x 3 x n                                 */
 } gs3d_gaussians;
 
+/* RenderOnlyGaussiansVector (gaussians.jl:342-392): precomputed 3D covariances and opacities
+ * after the sigmoid, for rendering only (no gradients). */
+typedef struct gs3d_render_only_gaussians {
+    int32_t n;
+    int32_t sh_degree;              /* storage degree: sh_coeffs holds (d+1)^2 x 3 x n     */
+    float* means_opacities;         /* 4 x n : x, y, z, opacity (16-byte aligned)          */
+    float* covariances;             /* 6 x n : lower 3D covariance 11, 21, 31, 22, 32, 33  */
+    float* sh_coeffs;               /* (d+1)^2 x 3 x n                                     */
+} gs3d_render_only_gaussians;
+
 /* RenderBuffers (forward_structs.jl:1541-1600) + Filtered2DGaussiansVector
  * (forward_structs.jl:762-786). All arrays are caller-owned. */
 typedef struct gs3d_render_buffers {
@@ -246,6 +256,15 @@ GS3D_API int gs3d_render_forward_workspace_size(
  * GS3D_ERR_CAPACITY (host_counts filled, outputs undefined) when D > capacity_dup. */
 GS3D_API int gs3d_render_forward(
     const gs3d_render_outputs* outputs, const gs3d_gaussians* gaussians,
+    const gs3d_camera* camera, const gs3d_tiling* tiling,
+    const gs3d_render_options* options, gs3d_render_buffers* buffers,
+    int32_t* host_counts, uint32_t flags, gs3d_stream_t stream);
+
+/* render! for a RenderOnlyGaussiansVector: gs3d_render_forward with the stored opacities and
+ * the 2D covariances J V J^T of the stored 3D covariances V (gaussians.jl:1324-1327; T = J V,
+ * then the lower entries of T J^T, each sum in index order); every other stage is shared. */
+GS3D_API int gs3d_render_forward_render_only(
+    const gs3d_render_outputs* outputs, const gs3d_render_only_gaussians* gaussians,
     const gs3d_camera* camera, const gs3d_tiling* tiling,
     const gs3d_render_options* options, gs3d_render_buffers* buffers,
     int32_t* host_counts, uint32_t flags, gs3d_stream_t stream);

@@ -123,6 +123,22 @@ static inline void project_covariance(const Mat23& J, const float R[3][3], const
     c22 = A[1][0] * A[1][0] + A[1][1] * A[1][1] + A[1][2] * A[1][2];
 }
 
+// Render-only input (RenderOnlyGaussiansVector, gaussians.jl:342-392): the 2D covariance is the
+// congruence transform J V J^T of the stored 3D covariance (gaussians.jl:1324-1327,
+// special_sarrays.jl:1801-1810): T = J V, then the lower entries of T J^T, each sum in index
+// order (the order the kernel uses; StaticArrays' unrolling is not recoverable).
+static void project_covariance_given(const Mat23& J, const float* cv, float& c11, float& c21,
+                                     float& c22) {
+    const float V[3][3] = {{cv[0], cv[1], cv[2]}, {cv[1], cv[3], cv[4]}, {cv[2], cv[4], cv[5]}};
+    float T[2][3];
+    for (int i = 0; i < 2; ++i)
+        for (int k = 0; k < 3; ++k)
+            T[i][k] = J.a[i][0] * V[0][k] + J.a[i][1] * V[1][k] + J.a[i][2] * V[2][k];
+    c11 = T[0][0] * J.a[0][0] + T[0][1] * J.a[0][1] + T[0][2] * J.a[0][2];
+    c21 = T[1][0] * J.a[0][0] + T[1][1] * J.a[0][1] + T[1][2] * J.a[0][2];
+    c22 = T[1][0] * J.a[1][0] + T[1][1] * J.a[1][1] + T[1][2] * J.a[1][2];
+}
+
 struct Projected {
     float mx, my, depth, opacity, ic11, ic21, ic22, col[3];
     int32_t rect[4];  // tile xmin, ymin, xmax, ymax
@@ -130,12 +146,14 @@ struct Projected {
 };
 
 // project_fgaussians_kernel! body (forward_core.jl:425-515) for one filtered Gaussian.
-static Projected project_one(const gs3d_gaussians& g, int gidx0, const gs3d_camera& cam,
-                             const gs3d_tiling& til, const gs3d_render_options& opt) {
+// cov != NULL: render-only input (opacity stored as is, covariances 6 x n lower).
+static Projected project_one(const gs3d_gaussians& g, const float* cov, int gidx0,
+                             const gs3d_camera& cam, const gs3d_tiling& til,
+                             const gs3d_render_options& opt) {
     Projected p;
     const float* mo = g.means_opacity_features + 4 * (size_t)gidx0;
     const float m[3] = {mo[0], mo[1], mo[2]};
-    float opacity = o_sigmoid(mo[3]);
+    float opacity = cov ? mo[3] : o_sigmoid(mo[3]);
     float mx, my, depth;
     project_point(cam, m, mx, my, depth);
     float cu = mx, cv = my;
@@ -144,12 +162,16 @@ static Projected project_one(const gs3d_gaussians& g, int gidx0, const gs3d_came
         cv = o_clamp(my, opt.clip_y_min, opt.clip_y_max);
     }
     const Mat23 J = linearized_projection(cam, cu, cv, depth);
-    const float* sf = g.scaling_features + 3 * (size_t)gidx0;
-    const float s[3] = {o_expf(sf[0]), o_expf(sf[1]), o_expf(sf[2])};
-    float R[3][3];
-    quat_to_rot(g.rotation_features + 4 * (size_t)gidx0, R);
     float c11, c21, c22;
-    project_covariance(J, R, s, c11, c21, c22);
+    if (cov) {
+        project_covariance_given(J, cov + 6 * (size_t)gidx0, c11, c21, c22);
+    } else {
+        const float* sf = g.scaling_features + 3 * (size_t)gidx0;
+        const float s[3] = {o_expf(sf[0]), o_expf(sf[1]), o_expf(sf[2])};
+        float R[3][3];
+        quat_to_rot(g.rotation_features + 4 * (size_t)gidx0, R);
+        project_covariance(J, R, s, c11, c21, c22);
+    }
     float undilated_det = 0.0f;
     if (opt.use_antialiasing) undilated_det = std::max(c11 * c22 - c21 * c21, 0.0f);
     c11 += opt.dilation_x;
@@ -194,11 +216,11 @@ static Projected project_one(const gs3d_gaussians& g, int gidx0, const gs3d_came
 }
 
 // fill_keep_gaussians_kernel! body (forward_core.jl:337-352)
-static bool keep_one(const gs3d_gaussians& g, int gidx0, const gs3d_camera& cam,
+static bool keep_one(const gs3d_gaussians& g, const float* cov, int gidx0, const gs3d_camera& cam,
                      const gs3d_render_options& opt) {
     const float* mo = g.means_opacity_features + 4 * (size_t)gidx0;
     const float m[3] = {mo[0], mo[1], mo[2]};
-    const float opacity = o_sigmoid(mo[3]);
+    const float opacity = cov ? mo[3] : o_sigmoid(mo[3]);
     bool keep = opacity >= opt.min_alpha;
     if (keep) {
         if (opt.clipping_mode == 1) {
@@ -287,12 +309,34 @@ void oracle_tiles_end(const int64_t* scodes, int64_t D, int32_t nb_tiles, int32_
 // Full GPU-path render. Arrays use the reference layouts (see gs3d.h). Returns 0, or
 // GS3D_ERR_CAPACITY when D > dup_capacity (counts still written: counts[0] = F,
 // counts[1] = D). Any output image pointer may be NULL.
+// Render-only input: gp's means_opacity_features hold x y z opacity, cov the 6 x n lower
+// covariances (scaling / rotation features unused). Otherwise as oracle_render.
+int oracle_render_ro(const gs3d_gaussians* gp, const float* cov, const gs3d_camera* camp,
+                     const gs3d_tiling* tp, const gs3d_render_options* op, uint8_t* keep,
+                     int32_t* keep_cs, int32_t* fgidx_to_gidx, float* depths, float* f2d,
+                     int32_t* ranges, int32_t* ntiles, int32_t* ntiles_cs, int64_t dup_capacity,
+                     int64_t* codes, int32_t* dfgidx, int64_t* scodes, int32_t* sfgidx,
+                     int32_t* tiles_end, float* rgb, float* trans, float* depth_img, int32_t* last,
+                     int64_t* counts);
+
 int oracle_render(const gs3d_gaussians* gp, const gs3d_camera* camp, const gs3d_tiling* tp,
                   const gs3d_render_options* op, uint8_t* keep, int32_t* keep_cs,
                   int32_t* fgidx_to_gidx, float* depths, float* f2d, int32_t* ranges,
                   int32_t* ntiles, int32_t* ntiles_cs, int64_t dup_capacity, int64_t* codes,
                   int32_t* dfgidx, int64_t* scodes, int32_t* sfgidx, int32_t* tiles_end,
                   float* rgb, float* trans, float* depth_img, int32_t* last, int64_t* counts) {
+    return oracle_render_ro(gp, nullptr, camp, tp, op, keep, keep_cs, fgidx_to_gidx, depths, f2d,
+                            ranges, ntiles, ntiles_cs, dup_capacity, codes, dfgidx, scodes, sfgidx,
+                            tiles_end, rgb, trans, depth_img, last, counts);
+}
+
+int oracle_render_ro(const gs3d_gaussians* gp, const float* cov, const gs3d_camera* camp,
+                     const gs3d_tiling* tp, const gs3d_render_options* op, uint8_t* keep,
+                     int32_t* keep_cs, int32_t* fgidx_to_gidx, float* depths, float* f2d,
+                     int32_t* ranges, int32_t* ntiles, int32_t* ntiles_cs, int64_t dup_capacity,
+                     int64_t* codes, int32_t* dfgidx, int64_t* scodes, int32_t* sfgidx,
+                     int32_t* tiles_end, float* rgb, float* trans, float* depth_img, int32_t* last,
+                     int64_t* counts) {
     const gs3d_gaussians& g = *gp;
     const gs3d_camera& cam = *camp;
     const gs3d_tiling& til = *tp;
@@ -302,7 +346,7 @@ int oracle_render(const gs3d_gaussians* gp, const gs3d_camera* camp, const gs3d_
     const int nb_tiles = til.nb_tiles_x * til.nb_tiles_y;
 
     // F1 + F2
-    parallel_for(0, n, [&](int64_t i) { keep[i] = keep_one(g, (int)i, cam, opt) ? 1 : 0; });
+    parallel_for(0, n, [&](int64_t i) { keep[i] = keep_one(g, cov, (int)i, cam, opt) ? 1 : 0; });
     int32_t cs = 0;
     for (int i = 0; i < n; ++i) {
         cs += keep[i];
@@ -327,7 +371,7 @@ int oracle_render(const gs3d_gaussians* gp, const gs3d_camera* camp, const gs3d_
 
     // F3 + F4
     parallel_for(0, F, [&](int64_t f) {
-        const Projected p = project_one(g, fgidx_to_gidx[f] - 1, cam, til, opt);
+        const Projected p = project_one(g, cov, fgidx_to_gidx[f] - 1, cam, til, opt);
         depths[f] = p.depth;
         float* r = f2d + 9 * (size_t)f;
         r[0] = p.mx; r[1] = p.my; r[2] = p.opacity; r[3] = p.ic11; r[4] = p.ic21; r[5] = p.ic22;

@@ -38,6 +38,9 @@ def lib():
         _LIB.oracle_render.restype = C.c_int
         _LIB.oracle_render.argtypes = [P(_abi.GaussiansC), P(_abi.Camera), P(_abi.TilingC),
                                        P(_abi.RenderOptionsC)] + [vp] * 8 + [C.c_int64] + [vp] * 10
+        _LIB.oracle_render_ro.restype = C.c_int
+        _LIB.oracle_render_ro.argtypes = [P(_abi.GaussiansC), vp, P(_abi.Camera), P(_abi.TilingC),
+                                          P(_abi.RenderOptionsC)] + [vp] * 8 + [C.c_int64] + [vp] * 10
         _LIB.oracle_backward.restype = C.c_int
         _LIB.oracle_backward.argtypes = [P(_abi.GaussiansC), P(_abi.Camera), P(_abi.TilingC),
                                          P(_abi.RenderOptionsC), C.c_int32] + [vp] * 7 + \
@@ -142,8 +145,33 @@ class NpGaussians:
         return NpGaussians(self.mo.copy(), self.sf.copy(), self.rf.copy(), self.sh.copy())
 
 
-def render(g: NpGaussians, camera, tiling, options, dup_capacity: int | None = None) -> dict:
-    """GPU-path render restatement; returns every intermediate in reference layouts."""
+class NpRenderOnlyGaussians:
+    """RenderOnlyGaussiansVector (gaussians.jl:342-392) as numpy arrays: (n, 4) x y z opacity,
+    (n, 6) lower covariances (11 21 31 22 32 33), (n, 3, (d+1)^2) SH coefficients."""
+
+    def __init__(self, means_opacities, covariances, sh_coeffs):
+        f = lambda a: np.ascontiguousarray(np.asarray(a, dtype=np.float32))
+        self.mo, self.cov, self.sh = map(f, (means_opacities, covariances, sh_coeffs))
+
+    @property
+    def n(self):
+        return self.mo.shape[0]
+
+    @property
+    def sh_degree(self):
+        return int(round(np.sqrt(self.sh.shape[2]))) - 1
+
+    def to_c(self):
+        g = _abi.GaussiansC()
+        g.n, g.sh_degree = self.n, self.sh_degree
+        g.means_opacity_features = _p(self.mo)
+        g.sh_coeffs = _p(self.sh)
+        return g
+
+
+def render(g, camera, tiling, options, dup_capacity: int | None = None) -> dict:
+    """GPU-path render restatement; returns every intermediate in reference layouts. `g` is an
+    NpGaussians or an NpRenderOnlyGaussians."""
     n, W, H = g.n, camera.width, camera.height
     cap = max(n, 1)
     out = dict(
@@ -160,7 +188,10 @@ def render(g: NpGaussians, camera, tiling, options, dup_capacity: int | None = N
     while True:
         dup = dict(codes=np.zeros(dc, np.int64), dfg=np.zeros(dc, np.int32),
                    scodes=np.zeros(dc, np.int64), sfg=np.zeros(dc, np.int32))
-        st = lib().oracle_render(C.byref(gc), C.byref(cc), C.byref(tc), C.byref(oc),
+        ro = isinstance(g, NpRenderOnlyGaussians)
+        head = ((lib().oracle_render_ro, C.byref(gc), _p(g.cov)) if ro
+                else (lib().oracle_render, C.byref(gc)))
+        st = head[0](*head[1:], C.byref(cc), C.byref(tc), C.byref(oc),
                                  _p(out["keep"]), _p(out["keep_cs"]), _p(out["fgidx_to_gidx"]),
                                  _p(out["depths"]), _p(out["f2d"]), _p(out["ranges"]),
                                  _p(out["ntiles"]), _p(out["ntiles_cs"]), dc, _p(dup["codes"]),

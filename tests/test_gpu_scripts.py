@@ -75,9 +75,11 @@ def test_headless_train_then_render(cuda, tmp_path, start):
     # render: the directory's latest model for its cameras, written as images
     imgs = scripts.render(outd, tmp_path / "renders", image_format="npy", device=cuda)
     assert len(imgs) == 5 and len(list((tmp_path / "renders").glob("render_*.npy"))) == 5
+    # the script renders the model as a RenderOnlyGaussiansVector, as the reference's does
     out = RenderOutputs.create(w, h, cuda)
     til = Tiling.for_camera(cams[2])
-    gs3d.render(out, final, cams[2], til, RenderOptions.for_camera(cams[2], final.sh_degree),
+    gs3d.render(out, gs3d.RenderOnlyGaussiansVector.from_trainable(final), cams[2], til,
+                RenderOptions.for_camera(cams[2], final.sh_degree),
                 RenderBuffers.create(final.n, til.nb_tiles, cuda))
     assert torch.equal(imgs[2], out.rgb)
     assert torch.equal(scripts.read_image(tmp_path / "renders" / "render_00002.npy").to(cuda), out.rgb)

@@ -31,9 +31,10 @@ __device__ __forceinline__ void project_point(const gs3d_camera& c, float m0, fl
     py = h1 / h2;
 }
 
+// ro: render-only input, mo.w is the opacity itself
 __device__ __forceinline__ bool keep_gaussian(const float4 mo, const gs3d_camera& cam,
-                                              const gs3d_render_options& opt) {
-    const float opacity = gs_sigmoid(mo.w);
+                                              const gs3d_render_options& opt, bool ro = false) {
+    const float opacity = ro ? mo.w : gs_sigmoid(mo.w);
     bool keep = opacity >= opt.min_alpha;
     if (keep) {
         if (opt.clipping_mode == 1) {  // BoundaryFilter
@@ -55,7 +56,8 @@ __global__ void __launch_bounds__(kChunkThreads) k_keep_upsweep(const float4* __
                                                                 int n, gs3d_camera cam,
                                                                 gs3d_render_options opt,
                                                                 uint8_t* __restrict__ keep,
-                                                                int32_t* __restrict__ sums) {
+                                                                int32_t* __restrict__ sums,
+                                                                int ro) {
     __shared__ int sm[33];
     const int64_t base = (int64_t)blockIdx.x * kChunk;
     int cnt = 0;
@@ -63,7 +65,7 @@ __global__ void __launch_bounds__(kChunkThreads) k_keep_upsweep(const float4* __
     for (int k = 0; k < kChunkItems; ++k) {
         const int64_t i = base + k * kChunkThreads + threadIdx.x;
         if (i < n) {
-            const bool kp = keep_gaussian(mo4[i], cam, opt);
+            const bool kp = keep_gaussian(mo4[i], cam, opt, ro != 0);
             keep[i] = kp ? 1 : 0;
             cnt += kp ? 1 : 0;
         }
@@ -147,13 +149,15 @@ struct ProjectArgs {
     float* f2d;
     int32_t* ranges;
     int32_t* ntiles;
+    const float* cov;  // render-only input: 6 x n lower 3D covariances (else NULL)
 };
 
 #ifndef GS3D_PROJECT_MINB
 #define GS3D_PROJECT_MINB 4
 #endif
 
-template <int DEG>
+// RO: render-only input (stored opacity and 3D covariance).
+template <int DEG, bool RO>
 __global__ void __launch_bounds__(256, GS3D_PROJECT_MINB) k_project(const ProjectArgs a, const gs3d_camera cam,
                                                  const gs3d_tiling til,
                                                  const gs3d_render_options opt) {
@@ -161,7 +165,7 @@ __global__ void __launch_bounds__(256, GS3D_PROJECT_MINB) k_project(const Projec
     for (int f = blockIdx.x * blockDim.x + threadIdx.x; f < F; f += gridDim.x * blockDim.x) {
         const int gi = a.f2g[f] - 1;
         const float4 mo = a.mo4[gi];
-        float opacity = gs_sigmoid(mo.w);
+        float opacity = RO ? mo.w : gs_sigmoid(mo.w);
         float mx, my, depth;
         project_point(cam, mo.x, mo.y, mo.z, mx, my, depth);
         float cu = mx, cv = my;
@@ -178,32 +182,49 @@ __global__ void __launch_bounds__(256, GS3D_PROJECT_MINB) k_project(const Projec
             J[0][j] = idepth * (P[0 + 3 * j] + (-cu) * P[2 + 3 * j]);
             J[1][j] = idepth * (P[1 + 3 * j] + (-cv) * P[2 + 3 * j]);
         }
-        // scale and rotation (gaussians.jl:1280-1331, misc.jl:133-141)
-        const float s0 = gs_expf(a.scal[3 * (size_t)gi]);
-        const float s1 = gs_expf(a.scal[3 * (size_t)gi + 1]);
-        const float s2 = gs_expf(a.scal[3 * (size_t)gi + 2]);
-        const float4 q = a.rot4[gi];
-        const float qss = q.x * q.x + q.y * q.y + q.z * q.z + q.w * q.w;
-        const float qs = sqrtf(2.0f * (1.0f / qss));
-        const float r = q.x * qs, x = q.y * qs, y = q.z * qs, z = q.w * qs;
-        const float R[3][3] = {{1.0f - (y * y + z * z), x * y - r * z, x * z + r * y},
-                               {x * y + r * z, 1.0f - (x * x + z * z), y * z - r * x},
-                               {x * z - r * y, y * z + r * x, 1.0f - (x * x + y * y)}};
-        const float s[3] = {s0, s1, s2};
-        float RS[3][3];
+        float c11, c21, c22;
+        if (RO) {
+            // congruence transform J V J^T of the stored covariance (gaussians.jl:1324-1327):
+            // T = J V, then the lower entries of T J^T, each sum in index order
+            const float* cv = a.cov + 6 * (size_t)gi;
+            const float V[3][3] = {{cv[0], cv[1], cv[2]}, {cv[1], cv[3], cv[4]}, {cv[2], cv[4], cv[5]}};
+            float T[2][3];
 #pragma unroll
-        for (int i = 0; i < 3; ++i)
+            for (int i = 0; i < 2; ++i)
 #pragma unroll
-            for (int j = 0; j < 3; ++j) RS[i][j] = R[i][j] * s[j];
-        float A[2][3];
+                for (int k = 0; k < 3; ++k)
+                    T[i][k] = J[i][0] * V[0][k] + J[i][1] * V[1][k] + J[i][2] * V[2][k];
+            c11 = T[0][0] * J[0][0] + T[0][1] * J[0][1] + T[0][2] * J[0][2];
+            c21 = T[1][0] * J[0][0] + T[1][1] * J[0][1] + T[1][2] * J[0][2];
+            c22 = T[1][0] * J[1][0] + T[1][1] * J[1][1] + T[1][2] * J[1][2];
+        } else {
+            // scale and rotation (gaussians.jl:1280-1331, misc.jl:133-141)
+            const float s0 = gs_expf(a.scal[3 * (size_t)gi]);
+            const float s1 = gs_expf(a.scal[3 * (size_t)gi + 1]);
+            const float s2 = gs_expf(a.scal[3 * (size_t)gi + 2]);
+            const float4 q = a.rot4[gi];
+            const float qss = q.x * q.x + q.y * q.y + q.z * q.z + q.w * q.w;
+            const float qs = sqrtf(2.0f * (1.0f / qss));
+            const float r = q.x * qs, x = q.y * qs, y = q.z * qs, z = q.w * qs;
+            const float R[3][3] = {{1.0f - (y * y + z * z), x * y - r * z, x * z + r * y},
+                                   {x * y + r * z, 1.0f - (x * x + z * z), y * z - r * x},
+                                   {x * z - r * y, y * z + r * x, 1.0f - (x * x + y * y)}};
+            const float s[3] = {s0, s1, s2};
+            float RS[3][3];
 #pragma unroll
-        for (int i = 0; i < 2; ++i)
+            for (int i = 0; i < 3; ++i)
 #pragma unroll
-            for (int k = 0; k < 3; ++k)
-                A[i][k] = J[i][0] * RS[0][k] + J[i][1] * RS[1][k] + J[i][2] * RS[2][k];
-        float c11 = A[0][0] * A[0][0] + A[0][1] * A[0][1] + A[0][2] * A[0][2];
-        const float c21 = A[1][0] * A[0][0] + A[1][1] * A[0][1] + A[1][2] * A[0][2];
-        float c22 = A[1][0] * A[1][0] + A[1][1] * A[1][1] + A[1][2] * A[1][2];
+                for (int j = 0; j < 3; ++j) RS[i][j] = R[i][j] * s[j];
+            float A[2][3];
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+#pragma unroll
+                for (int k = 0; k < 3; ++k)
+                    A[i][k] = J[i][0] * RS[0][k] + J[i][1] * RS[1][k] + J[i][2] * RS[2][k];
+            c11 = A[0][0] * A[0][0] + A[0][1] * A[0][1] + A[0][2] * A[0][2];
+            c21 = A[1][0] * A[0][0] + A[1][1] * A[0][1] + A[1][2] * A[0][2];
+            c22 = A[1][0] * A[1][0] + A[1][1] * A[1][1] + A[1][2] * A[1][2];
+        }
         float undilated_det = 0.0f;
         if (opt.use_antialiasing) undilated_det = fmaxf(c11 * c22 - c21 * c21, 0.0f);
         c11 += opt.dilation_x;
@@ -400,10 +421,11 @@ GS3D_API int gs3d_render_forward_workspace_size(int64_t capacity_n, int64_t capa
     return GS3D_OK;
 }
 
-GS3D_API int gs3d_render_forward(const gs3d_render_outputs* outputs, const gs3d_gaussians* g,
-                                 const gs3d_camera* cam, const gs3d_tiling* til,
-                                 const gs3d_render_options* opt, gs3d_render_buffers* buf,
-                                 int32_t* host_counts, uint32_t flags, gs3d_stream_t stream_) {
+// cov != NULL: render-only input (g's means_opacity_features hold the opacities themselves).
+static int render_forward_impl(const gs3d_render_outputs* outputs, const gs3d_gaussians* g,
+                               const float* cov, const gs3d_camera* cam, const gs3d_tiling* til,
+                               const gs3d_render_options* opt, gs3d_render_buffers* buf,
+                               int32_t* host_counts, uint32_t flags, gs3d_stream_t stream_) {
     cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
     GS3D_RETURN_IF(check_common(g, cam, til, opt));
     if (!outputs || !buf) return invalid("NULL outputs or buffers");
@@ -415,7 +437,7 @@ GS3D_API int gs3d_render_forward(const gs3d_render_outputs* outputs, const gs3d_
         !buf->tiles_end_sdfgidx || !buf->device_counts)
         return invalid("NULL render buffer array");
     if (((uintptr_t)buf->intersected_tile_ranges & 15) || ((uintptr_t)g->means_opacity_features & 15) ||
-        ((uintptr_t)g->rotation_features & 15))
+        (!cov && ((uintptr_t)g->rotation_features & 15)))
         return invalid("tile ranges, means/opacity and rotation arrays must be 16-byte aligned");
     const FwdLayout L = fwd_layout(buf->capacity_n, buf->capacity_dup,
                                    til->nb_tiles_x * til->nb_tiles_y);
@@ -436,7 +458,7 @@ GS3D_API int gs3d_render_forward(const gs3d_render_outputs* outputs, const gs3d_
         const unsigned nch = (unsigned)ceil_div(n, kChunk);
         k_keep_upsweep<<<nch, kChunkThreads, 0, stream>>>(
             reinterpret_cast<const float4*>(g->means_opacity_features), n, *cam, *opt,
-            buf->keep_gaussians, sums);
+            buf->keep_gaussians, sums, cov ? 1 : 0);
         GS3D_LAUNCHED("k_keep_upsweep");
         GS3D_RETURN_IF(scan_spine(sums, cap_n, nullptr, n, counts + 0, stream));
         k_keep_downsweep<<<nch, kChunkThreads, 0, stream>>>(buf->keep_gaussians, n, sums,
@@ -457,14 +479,24 @@ GS3D_API int gs3d_render_forward(const gs3d_render_outputs* outputs, const gs3d_
     pa.f2d = buf->means2d_opacities_inverse_covariances_colors;
     pa.ranges = buf->intersected_tile_ranges;
     pa.ntiles = buf->nb_overlapped_tiles;
+    pa.cov = cov;
     const int pgrid = grid_for(n, 256, 8);
     {
         ProfScope prof("project", stream);
-        switch (opt->sh_degree) {
-            case 0: k_project<0><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
-            case 1: k_project<1><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
-            case 2: k_project<2><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
-            default: k_project<3><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
+        if (cov) {
+            switch (opt->sh_degree) {
+                case 0: k_project<0, true><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
+                case 1: k_project<1, true><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
+                case 2: k_project<2, true><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
+                default: k_project<3, true><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
+            }
+        } else {
+            switch (opt->sh_degree) {
+                case 0: k_project<0, false><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
+                case 1: k_project<1, false><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
+                case 2: k_project<2, false><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
+                default: k_project<3, false><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
+            }
         }
         GS3D_LAUNCHED("k_project");
     }
@@ -559,6 +591,32 @@ GS3D_API int gs3d_render_forward(const gs3d_render_outputs* outputs, const gs3d_
                                   stream),
                   "copy counts");
     return GS3D_OK;
+}
+
+GS3D_API int gs3d_render_forward(const gs3d_render_outputs* outputs, const gs3d_gaussians* g,
+                                 const gs3d_camera* cam, const gs3d_tiling* til,
+                                 const gs3d_render_options* opt, gs3d_render_buffers* buf,
+                                 int32_t* host_counts, uint32_t flags, gs3d_stream_t stream) {
+    return render_forward_impl(outputs, g, nullptr, cam, til, opt, buf, host_counts, flags, stream);
+}
+
+GS3D_API int gs3d_render_forward_render_only(const gs3d_render_outputs* outputs,
+                                             const gs3d_render_only_gaussians* ro,
+                                             const gs3d_camera* cam, const gs3d_tiling* til,
+                                             const gs3d_render_options* opt,
+                                             gs3d_render_buffers* buf, int32_t* host_counts,
+                                             uint32_t flags, gs3d_stream_t stream) {
+    if (!ro) return invalid("NULL Gaussians");
+    if (ro->n > 0 && !ro->covariances) return invalid("NULL covariances");
+    gs3d_gaussians g{};
+    g.n = ro->n;
+    g.sh_degree = ro->sh_degree;
+    g.means_opacity_features = ro->means_opacities;
+    g.scaling_features = ro->covariances;   // not read: satisfies the shared argument checks
+    g.rotation_features = ro->covariances;
+    g.sh_coeffs = ro->sh_coeffs;
+    return render_forward_impl(outputs, &g, ro->n > 0 ? ro->covariances : nullptr, cam, til, opt,
+                               buf, host_counts, flags, stream);
 }
 
 }  // extern "C"

@@ -58,6 +58,11 @@ class GaussiansC(C.Structure):
                 ("sh_coeffs", C.c_void_p)]
 
 
+class RenderOnlyGaussiansC(C.Structure):
+    _fields_ = [("n", C.c_int32), ("sh_degree", C.c_int32), ("means_opacities", C.c_void_p),
+                ("covariances", C.c_void_p), ("sh_coeffs", C.c_void_p)]
+
+
 class RenderBuffersC(C.Structure):
     _fields_ = [("capacity_n", C.c_int64), ("capacity_dup", C.c_int64),
                 ("keep_gaussians", C.c_void_p), ("keep_gaussians_cs", C.c_void_p),
@@ -131,6 +136,10 @@ SIGNATURES = {
     "gs3d_render_forward": (C.c_int, [P(RenderOutputsC), P(GaussiansC), P(Camera), P(TilingC),
                                       P(RenderOptionsC), P(RenderBuffersC), C.c_void_p,
                                       C.c_uint32, C.c_void_p]),
+    "gs3d_render_forward_render_only": (C.c_int, [P(RenderOutputsC), P(RenderOnlyGaussiansC),
+                                                  P(Camera), P(TilingC), P(RenderOptionsC),
+                                                  P(RenderBuffersC), C.c_void_p, C.c_uint32,
+                                                  C.c_void_p]),
     "gs3d_backward": (C.c_int, [P(FGradientsC), C.c_void_p, P(RenderOutputsC), P(GaussiansC),
                                 P(Camera), P(TilingC), P(RenderOptionsC), P(RenderBuffersC),
                                 C.c_uint32, C.c_void_p]),

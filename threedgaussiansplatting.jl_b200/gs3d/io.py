@@ -148,6 +148,13 @@ def load_ply(path, device="cpu") -> GaussiansVector:
     return GaussiansVector(t(mo), t(sf), t(rf), t(sh))
 
 
+def load_ply_render_only(path, device="cpu"):
+    """RenderOnlyGaussiansVector(ply_path) (gaussians.jl:741-762): a 3DGS PLY model with the
+    opacities after the sigmoid and the 3D covariances precomputed."""
+    from .structs import RenderOnlyGaussiansVector
+    return RenderOnlyGaussiansVector.from_trainable(load_ply(path, device=device))
+
+
 def read_point_cloud(path) -> tuple[np.ndarray, np.ndarray]:
     """A coloured point cloud PLY (x y z and red green blue, as COLMAP exports its points):
     ((n, 3) float32 points, (n, 3) float32 colours in [0, 1]; 8-bit colours are divided by 255)."""

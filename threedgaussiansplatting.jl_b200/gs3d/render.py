@@ -6,7 +6,8 @@ import ctypes as C
 import torch
 
 from . import _abi
-from .structs import (GaussiansVector, PinholeCamera, RenderBuffers, RenderOptions,
+from .structs import (GaussiansVector, PinholeCamera, RenderBuffers, RenderOnlyGaussiansVector,
+                      RenderOptions,
                       RenderOutputs, Tiling)
 
 
@@ -25,7 +26,8 @@ def render(outputs: RenderOutputs, gaussians: GaussiansVector, camera: PinholeCa
     without it nothing blocks and an overflow shows up in buffers.device_counts[2].
     `reference_order` also fills the unsorted duplicate arrays and the duplicate-count scan
     as the reference does (GS3D_RENDER_REFERENCE_ORDER); the sorted arrays, tile ends and
-    images are the same either way."""
+    images are the same either way. `gaussians` may also be a RenderOnlyGaussiansVector
+    (stored opacities and 3D covariances; gs3d_render_forward_render_only)."""
     if gaussians.n > buffers.capacity_n:
         raise ValueError(f"{gaussians.n} Gaussians exceed the buffers' capacity {buffers.capacity_n}")
     lib = _abi.lib()
@@ -35,9 +37,11 @@ def render(outputs: RenderOutputs, gaussians: GaussiansVector, camera: PinholeCa
     host = buffers.host_counts
     hptr = C.c_void_p(host.data_ptr()) if host is not None else None
     args = (outputs.to_c(), gaussians.to_c(), camera.to_c(), tiling.to_c(), options.to_c())
+    entry = (lib.gs3d_render_forward_render_only if isinstance(gaussians, RenderOnlyGaussiansVector)
+             else lib.gs3d_render_forward)
     for _ in range(4):
         b = buffers.to_c()
-        st = lib.gs3d_render_forward(C.byref(args[0]), C.byref(args[1]), C.byref(args[2]),
+        st = entry(C.byref(args[0]), C.byref(args[1]), C.byref(args[2]),
                                      C.byref(args[3]), C.byref(args[4]), C.byref(b), hptr,
                                      flags, C.c_void_p(_stream_handle(stream)))
         if st == _abi.GS3D_ERR_CAPACITY:

@@ -212,13 +212,14 @@ def model_path(path, iterations=None) -> Path:
 
 def render(path, out_dir=None, *, iterations=None, cameras=None, sh_degree=None,
            image_format: str = "ppm", device="cuda") -> list[torch.Tensor]:
-    """Render the model at `path` (a .ply, or a training output directory) for each camera (by
+    """Render the model at `path` (a .ply, or a training output directory), loaded as a
+    RenderOnlyGaussiansVector like the script does, for each camera (by
     default the output directory's cameras.json, else `default_camera()`); write
     `out_dir/render_<i>.<image_format>` when `out_dir` is given. Returns the (width, height, 3)
     images on the device."""
     device = torch.device(device)
     p = Path(path)
-    g = io.load_ply(model_path(p, iterations), device=device)
+    g = io.load_ply_render_only(model_path(p, iterations), device=device)  # as the script loads it
     if cameras is None:
         cameras = (io.load_cameras_json(p / "cameras.json")
                    if p.is_dir() and (p / "cameras.json").exists() else [default_camera()])

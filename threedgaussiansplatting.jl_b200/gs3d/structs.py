@@ -296,6 +296,76 @@ class GaussiansVector:
 
 
 @dataclass
+class RenderOnlyGaussiansVector:
+    """RenderOnlyGaussiansVector (gaussians.jl:342-392): (n, 4) means + opacities (after the
+    sigmoid), (n, 6) lower 3D covariances (11, 21, 31, 22, 32, 33), (n, 3, (d+1)^2) SH
+    coefficients. Rendered by gs3d_render_forward_render_only; not trainable."""
+
+    means_opacities: torch.Tensor
+    covariances: torch.Tensor
+    sh_coeffs: torch.Tensor
+
+    def __post_init__(self):
+        n = self.means_opacities.shape[0]
+        assert self.means_opacities.shape == (n, 4) and self.covariances.shape == (n, 6)
+        assert self.sh_coeffs.shape[:2] == (n, 3)
+        for t in (self.means_opacities, self.covariances, self.sh_coeffs):
+            assert t.dtype == torch.float32 and t.is_contiguous()
+
+    @property
+    def n(self) -> int:
+        return self.means_opacities.shape[0]
+
+    @property
+    def sh_degree(self) -> int:
+        return int(round(math.sqrt(self.sh_coeffs.shape[2]))) - 1
+
+    @property
+    def device(self):
+        return self.means_opacities.device
+
+    def tensors(self):
+        return (self.means_opacities, self.covariances, self.sh_coeffs)
+
+    def to(self, device) -> "RenderOnlyGaussiansVector":
+        return RenderOnlyGaussiansVector(*(t.to(device).contiguous() for t in self.tensors()))
+
+    @classmethod
+    def from_trainable(cls, g: "GaussiansVector") -> "RenderOnlyGaussiansVector":
+        """The conversion of RenderOnlyGaussiansVector(ply_path) (gaussians.jl:741-762):
+        opacities = sigmoid(opacity features), covariances = lower((R S)(R S)^T) with R the
+        rotation of the normalised quaternion and S = diag(exp(scaling features))
+        (`_scaling_rotation_features_to_covariances`, gaussians.jl:467-482), in float32."""
+        mo = g.means_opacity_features.detach().cpu().numpy().astype(F32)
+        s = np.exp(g.scaling_features.detach().cpu().numpy().astype(F32)).astype(F32)
+        q = g.rotation_features.detach().cpu().numpy().astype(F32)
+        qss = (q * q).sum(axis=1, dtype=F32)
+        qs = np.sqrt(F32(2) * (F32(1) / qss)).astype(F32)
+        r, x, y, z = (q[:, i] * qs for i in range(4))
+        R = np.empty((q.shape[0], 3, 3), F32)
+        R[:, 0, 0] = 1 - (y * y + z * z); R[:, 0, 1] = x * y - r * z; R[:, 0, 2] = x * z + r * y
+        R[:, 1, 0] = x * y + r * z; R[:, 1, 1] = 1 - (x * x + z * z); R[:, 1, 2] = y * z - r * x
+        R[:, 2, 0] = x * z - r * y; R[:, 2, 1] = y * z + r * x; R[:, 2, 2] = 1 - (x * x + y * y)
+        RS = (R * s[:, None, :]).astype(F32)
+        cov = np.einsum("nik,njk->nij", RS, RS).astype(F32)
+        lower = np.stack([cov[:, 0, 0], cov[:, 1, 0], cov[:, 2, 0], cov[:, 1, 1], cov[:, 2, 1],
+                          cov[:, 2, 2]], axis=1).astype(F32)
+        mo_ro = mo.copy()
+        mo_ro[:, 3] = (F32(1) / (F32(1) + np.exp(-mo[:, 3]))).astype(F32)
+        dev = g.means_opacity_features.device
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+        return cls(t(mo_ro), t(lower), g.sh_coeffs.detach().clone())
+
+    def to_c(self) -> _abi.RenderOnlyGaussiansC:
+        g = _abi.RenderOnlyGaussiansC()
+        g.n, g.sh_degree = self.n, self.sh_degree
+        g.means_opacities = _ptr(self.means_opacities)
+        g.covariances = _ptr(self.covariances)
+        g.sh_coeffs = _ptr(self.sh_coeffs)
+        return g
+
+
+@dataclass
 class RenderOutputs:
     """RenderOutputs: rgb (w, h, 3), transmittance / depth / last index (w, h)."""
 
