@@ -46,7 +46,7 @@ STRUCTS = {
     "gs3d_render_buffers": _abi.RenderBuffersC, "gs3d_render_outputs": _abi.RenderOutputsC,
     "gs3d_fgradients": _abi.FGradientsC, "gs3d_adam_moments": _abi.AdamMomentsC,
     "gs3d_adam_params": _abi.AdamParamsC, "gs3d_adc_buffers": _abi.AdcBuffersC,
-    "gs3d_adc_params": _abi.AdcParamsC,
+    "gs3d_adc_params": _abi.AdcParamsC, "gs3d_render_only_gaussians": _abi.RenderOnlyGaussiansC,
 }
 
 
@@ -81,3 +81,16 @@ def test_invalid_arguments_are_reported_not_crashed():
     assert b"invalid argument" in lib.gs3d_last_error_string()
     with pytest.raises(_abi.Gs3dError):
         _abi.check(st)
+
+
+def test_render_only_entry_rejects_bad_arguments_without_a_gpu():
+    """gs3d_render_forward_render_only validates its arguments before touching the device."""
+    lib = _abi.lib()
+    null = C.POINTER(_abi.RenderOnlyGaussiansC)()
+    st = lib.gs3d_render_forward_render_only(None, null, None, None, None, None, None, 0, None)
+    assert st == _abi.GS3D_ERR_INVALID_ARGUMENT
+    ro = _abi.RenderOnlyGaussiansC()
+    ro.n, ro.sh_degree = 10, 0
+    st = lib.gs3d_render_forward_render_only(None, C.byref(ro), None, None, None, None, None, 0, None)
+    assert st == _abi.GS3D_ERR_INVALID_ARGUMENT
+    assert b"covariances" in lib.gs3d_last_error_string()
