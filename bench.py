@@ -198,7 +198,7 @@ def run_reference(args, rank: int, world: int) -> None:
     if rank != 0:
         return
     import numpy as np
-    from gs3d.optimizer import bias_corrections, LearningRates, AdamOptimizer  # noqa: F401
+    from gs3d.optimizer import bias_corrections
     from gs3d import _abi
     from gs3d.scene import CONFIGS, synthetic_gaussians
     from gs3d.training import TrainingOptions

@@ -12,7 +12,7 @@ import torch
 
 import gs3d
 from gs3d import RenderBuffers, RenderOptions, RenderOutputs, Tiling
-from gs3d.scene import CONFIGS, SceneSpec, create_test_scene, look_at_camera, synthetic_gaussians
+from gs3d.scene import SceneSpec, create_test_scene, look_at_camera, synthetic_gaussians
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu

@@ -10,7 +10,6 @@ import torch
 
 from gs3d import io
 from gs3d.scene import SceneSpec, look_at_camera, synthetic_gaussians
-from gs3d.structs import GaussiansVector
 
 
 def random_gaussians(n, degree, seed=0):

@@ -1,10 +1,8 @@
 """Numerics of libgs3d's own arithmetic helpers, checked on the CPU (no GPU): the same float
 operations (IEEE binary32 with explicit fused multiply-adds) give the same bits on both."""
 import subprocess
-import textwrap
 from pathlib import Path
 
-import pytest
 
 REPO = Path(__file__).resolve().parent.parent
 

@@ -28,8 +28,8 @@ import torch
 from . import io
 from .render import render as gs_render
 from .scene import scene_radius
-from .structs import (GaussiansVector, PinholeCamera, RenderBuffers, RenderOptions, RenderOutputs,
-                      Tiling, fov_deg_to_focal_length)
+from .structs import (PinholeCamera, RenderBuffers, RenderOptions, RenderOutputs, Tiling,
+                      fov_deg_to_focal_length)
 
 # -- images -----------------------------------------------------------------------------------
 def read_image(path) -> torch.Tensor:

@@ -6,7 +6,7 @@ only orders the calls (and, like the reference, reads n' back at a densify step)
 from __future__ import annotations
 
 import math
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
 import numpy as np
 import torch
