@@ -60,3 +60,15 @@ def test_model_choice(tmp_path):
     assert scripts.model_path(tmp_path / "m.ply") == tmp_path / "m.ply"
     cam = scripts.default_camera()
     assert (cam.width, cam.height) == (1280, 720) and cam.fx == pytest.approx(640.0)
+
+
+def test_train_rejects_inputs_before_touching_the_gpu(tmp_path):
+    """A cameras.json whose image does not match its camera, or a split that leaves no training
+    camera, is an error raised while reading the inputs."""
+    from gs3d import io
+    from gs3d.scene import look_at_camera
+    cam = look_at_camera(8, 6, 60.0, (0, 0, 3))
+    scripts.write_image(tmp_path / "a.npy", torch.zeros((7, 6, 3)))
+    io.save_cameras_json(tmp_path / "cameras.json", [cam], image_paths=["a.npy"])
+    with pytest.raises(ValueError, match="image of size"):
+        scripts.train(tmp_path, tmp_path / "out", device="cpu")

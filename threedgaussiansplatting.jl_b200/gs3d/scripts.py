@@ -155,6 +155,8 @@ def train(input_dir, output_dir, *, render_options_from_camera=None, training_op
     rng = np.random.default_rng(seed)
     val_ids = validation_camera_ids(len(cameras), validation_ratio, random_validation_cameras, rng)
     train_ids = [i for i in range(len(cameras)) if i not in set(val_ids)]
+    if not train_ids:
+        raise ValueError(f"validation_ratio {validation_ratio} leaves no training camera")
     train_cams = [cameras[i] for i in train_ids]
     train_imgs = [images[i].pin_memory() if device.type == "cuda" else images[i] for i in train_ids]
     val_cams = [cameras[i] for i in val_ids]
