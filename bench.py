@@ -301,6 +301,24 @@ def cpu_baseline_leg(gv_cpu, cams, pool_host, ro, til, opts) -> dict:
                       f"{threads} threads, {el:.1f} s"}
 
 
+def cpu_render_leg(gv_cpu, cams, ro) -> dict:
+    """The reference's own CPU renderer (forward_core.jl:25-177, restated in
+    oracle/cpu_render.cpp): one frame of the render workload on all host threads and one on a
+    single thread, as the reference runs it."""
+    from oracle import oracle as O
+    g = O.NpGaussians.from_vector(gv_cpu)
+    threads = os.cpu_count() or 1
+    out = {}
+    for th in (threads, 1):
+        t0 = time.perf_counter()
+        O.cpu_render(g, cams[0], ro, th)
+        out[th] = 1.0 / (time.perf_counter() - t0)
+    return {"value": out[threads], "unit": "frames/s", "cores": threads, "kind": "port",
+            "single_thread_value": out[1],
+            "sample": f"one frame (camera 0) through the restated reference CPU renderer on "
+                      f"{threads} threads, and one on 1 thread"}
+
+
 def main() -> None:
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -468,6 +486,7 @@ def main() -> None:
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_leg(gv_cpu, cams, pool_host, ro, til, opts)
+        render_fps["cpu_baseline"] = cpu_render_leg(gv_cpu, cams, ro)
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
