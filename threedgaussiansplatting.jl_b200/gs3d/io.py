@@ -232,7 +232,8 @@ def save_cameras_json(path, cameras, image_paths=None) -> None:
 def save_checkpoint(path, trainer) -> None:
     """Everything a Trainer needs to continue: parameters, Adam moments and update count, ADC
     accumulators, iteration number, render SH degree, camera-order state."""
-    torch.cuda.synchronize(trainer.device) if trainer.device.type == "cuda" else None
+    if trainer.device.type == "cuda":
+        torch.cuda.synchronize(trainer.device)
     g, m, a = trainer.gaussians, trainer.optimizer.moments, trainer.adc_buffers
     state = {
         "format": "gs3d-checkpoint-1",
