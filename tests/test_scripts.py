@@ -1,5 +1,7 @@
 """Host logic of the headless entry points (gs3d/scripts.py) on the CPU: image files, the
 validation-camera choice and the model choice of scripts/train.jl and scripts/render.jl."""
+import math
+
 import numpy as np
 import pytest
 import torch
@@ -72,3 +74,41 @@ def test_train_rejects_inputs_before_touching_the_gpu(tmp_path):
     io.save_cameras_json(tmp_path / "cameras.json", [cam], image_paths=["a.npy"])
     with pytest.raises(ValueError, match="image of size"):
         scripts.train(tmp_path, tmp_path / "out", device="cpu")
+
+
+# ---- learning-rate annealing (training.jl:287-302) -------------------------------------
+def test_annealed_means_lr_schedule():
+    from gs3d.training import TrainingOptions, annealed_means_lr
+
+    o = TrainingOptions(scene_radius=2.5, nb_iterations=30_000)
+    a, b = o.initial_means_lr, o.final_means_lr
+    lrs = [annealed_means_lr(it, o) for it in (1, 2, 100, 15_000, 29_999, 30_000, 40_000)]
+    # iteration 1 uses the initial rate, the last annealing iteration and later the final one
+    # (each through one Float32 log and exp, as the reference evaluates them: log(lr) ~ -9
+    # rounded to Float32 moves exp by up to ~2^-21 relative)
+    assert lrs[0] == pytest.approx(a, rel=1e-6)
+    assert lrs[-2] == lrs[-1] and lrs[-1] == pytest.approx(b, rel=1e-6)
+    assert all(x > y for x, y in zip(lrs, lrs[1:-1]))
+    # log-linear in between: the midpoint is the geometric mean
+    mid = annealed_means_lr(1 + (30_000 - 1) // 2, o)
+    assert mid == pytest.approx(math.sqrt(a * b), rel=1e-4)
+    for it in (1, 7, 1234, 29_000):
+        x = (it - 1) / (30_000 - 1)
+        want = math.exp((1 - x) * math.log(a) + x * math.log(b))
+        assert annealed_means_lr(it, o) == pytest.approx(want, rel=2e-6)
+        assert isinstance(annealed_means_lr(it, o), float)
+        assert annealed_means_lr(it, o) == float(np.float32(annealed_means_lr(it, o)))
+
+
+def test_annealed_means_lr_degenerate_step_counts():
+    from gs3d.training import TrainingOptions, annealed_means_lr
+
+    two = TrainingOptions(scene_radius=1.0, nb_lr_annealing_steps=2)
+    assert annealed_means_lr(1, two) == pytest.approx(two.initial_means_lr, rel=1e-6)
+    assert annealed_means_lr(2, two) == pytest.approx(two.final_means_lr, rel=1e-6)
+    one = TrainingOptions(scene_radius=1.0, nb_lr_annealing_steps=1)
+    with pytest.raises(ValueError):
+        annealed_means_lr(1, one)
+    assert annealed_means_lr(5, one) == pytest.approx(one.final_means_lr, rel=1e-6)
+    zero = TrainingOptions(scene_radius=1.0, nb_lr_annealing_steps=0)   # x clamps to 0
+    assert annealed_means_lr(9, zero) == pytest.approx(zero.initial_means_lr, rel=1e-6)

@@ -82,6 +82,28 @@ class TrainingOptions:
                              self.rotation_features_lr, self.sh_coeffs_dc_lr, self.sh_coeffs_rest_lr)
 
 
+def annealed_means_lr(iteration_nb: int, o: TrainingOptions) -> float:
+    """Means learning rate of update_learning_rates! (training.jl:287-302) in Float32
+    arithmetic: x = clamp((it - 1) / Float32(steps - 1), 0, 1) and
+    exp((1 - x) log(initial) + x log(final)), each log and exp rounded once to Float32 (Julia's
+    Float32 log and exp evaluate in Float64 and round), products and sum rounded as Float32."""
+    den = F32(o.nb_lr_annealing_steps - 1)
+    if den == 0:
+        # one annealing step: the reference divides by zero, Inf clamps to 1 and 0 / 0 = NaN
+        # fails its positivity check on the learning rate
+        if iteration_nb == 1:
+            raise ValueError("nb_lr_annealing_steps == 1 gives a NaN means learning rate at "
+                             "iteration 1")
+        x = F32(1)
+    else:
+        x = F32(iteration_nb - 1) / den
+    x = F32(min(max(x, F32(0)), F32(1)))
+    la = F32(math.log(o.initial_means_lr))
+    lb = F32(math.log(o.final_means_lr))
+    t = F32(F32(F32(1) - x) * la) + F32(x * lb)
+    return float(F32(math.exp(float(t))))
+
+
 class Trainer:
     """Trainer (training.jl:40-151). `targets[i]` is the ground-truth image of camera i as a
     (w, h, 3) float32 tensor, on the device or in (pinned) host memory; host images are
@@ -154,11 +176,7 @@ class Trainer:
             adc_mod.opacity_reset(self.gaussians, self.optimizer.moments, o.opacity_reset_max_value)
 
     def update_learning_rates(self) -> None:
-        o = self.options
-        x = F32((self.iteration_nb - 1) / F32(o.nb_lr_annealing_steps - 1)) if o.nb_lr_annealing_steps > 1 else F32(1)
-        x = F32(min(max(x, F32(0)), F32(1)))
-        lr = math.exp((1 - x) * math.log(o.initial_means_lr) + x * math.log(o.final_means_lr))
-        self.optimizer.lrs.means = float(F32(lr))
+        self.optimizer.lrs.means = annealed_means_lr(self.iteration_nb, self.options)
 
     def densifies_this_iteration(self) -> bool:
         """Whether maybe_densify_and_prune densifies at the current iteration_nb."""
