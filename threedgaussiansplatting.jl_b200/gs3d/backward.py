@@ -10,7 +10,7 @@ import torch
 from . import _abi
 from .render import _stream_handle
 from .structs import (GaussiansVector, PinholeCamera, RenderBuffers, RenderOptions,
-                      RenderOutputs, Tiling, _ptr)
+                      RenderOutputs, Tiling, _ptr, check_sh_degree)
 
 
 @dataclass
@@ -44,7 +44,9 @@ class FilteredGaussiansGradients:
         return int(round(self.sh_coeffs_grads.shape[2] ** 0.5)) - 1
 
     def set_sh_degree(self, d: int) -> None:
-        """set_sh_degree! for gradients: grow the SH axis (new entries zero)."""
+        """set_sh_degree! for gradients (backward_structs.jl:342-354): grow the SH axis (new
+        entries zero; the reference leaves them unset)."""
+        check_sh_degree(d)
         old = self.sh_coeffs_grads
         new = torch.zeros((old.shape[0], 3, (d + 1) ** 2), dtype=old.dtype, device=old.device)
         k = min(old.shape[2], new.shape[2])

@@ -11,7 +11,7 @@ import torch
 from . import _abi
 from .backward import FilteredGaussiansGradients
 from .render import _stream_handle
-from .structs import GaussiansVector, _ptr
+from .structs import GaussiansVector, _ptr, check_sh_degree
 
 DEFAULT_BETA1 = 0.9
 DEFAULT_BETA2 = 0.999
@@ -45,7 +45,8 @@ class AdamMoments:
                 self.rotation_features_moments, self.sh_coeffs_moments)
 
     def set_sh_degree(self, d: int) -> None:
-        """set_sh_degree! (optimizer.jl:733-745): grow the SH axis keeping old values."""
+        """set_sh_degree! (optimizer.jl:737-746): grow the SH axis keeping old values."""
+        check_sh_degree(d)
         old = self.sh_coeffs_moments
         new = torch.zeros((old.shape[0], 3, (d + 1) ** 2, 2), dtype=old.dtype, device=old.device)
         k = min(old.shape[2], new.shape[2])

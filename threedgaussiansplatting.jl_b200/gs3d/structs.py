@@ -44,6 +44,12 @@ def fov_deg_to_focal_length(fov_deg: float, axis_size: float) -> float:
     return fov_to_focal_length(math.radians(fov_deg), axis_size)
 
 
+def check_sh_degree(d: int) -> None:
+    """_check_sh_degree (gaussians.jl:243-252): SH degrees are 0, 1, 2 or 3."""
+    if not 0 <= int(d) <= 3:
+        raise ValueError(f"spherical harmonics degree {d} is not in 0..3")
+
+
 @dataclass
 class PinholeCamera:
     """PinholeCamera (cameras.jl:50-106). R_c2w / t_c2w are camera-to-world."""
@@ -273,7 +279,9 @@ class GaussiansVector:
                 self.sh_coeffs)
 
     def set_sh_degree(self, d: int) -> None:
-        """set_sh_degree! (gaussians.jl): grow or shrink the SH axis; new coefficients are 0."""
+        """set_sh_degree! (gaussians.jl:1070-1080): grow or shrink the SH axis; new coefficients
+        are 0."""
+        check_sh_degree(d)
         old = self.sh_coeffs
         new = torch.zeros((old.shape[0], 3, (d + 1) ** 2), dtype=old.dtype, device=old.device)
         k = min(old.shape[2], new.shape[2])
