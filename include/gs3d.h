@@ -409,6 +409,7 @@ GS3D_API int gs3d_adc_stats(
     const int32_t* fgidx_to_gidx, const int32_t* device_counts,
     int32_t width, int32_t height, gs3d_stream_t stream);
 
+/* Bytes of adc_buffers.workspace (the scan of the new-Gaussian counts) for n Gaussians. */
 GS3D_API int gs3d_adc_workspace_size(int32_t n, size_t* bytes);
 
 /* Masks, counts and their scan (training.jl:325-389) and ngidx_to_gidx
