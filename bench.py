@@ -64,6 +64,8 @@ def parse():
     ap.add_argument("--impl", choices=["gs3d", "reference"], default="gs3d")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the config-3 render-only and densify-step legs")
     ap.add_argument("--ref-seconds", type=float, default=120.0)
     ap.add_argument("--n-gaussians", type=int, default=None,
                     help="override the Gaussian count (same distributions); for small profiling cases")
@@ -82,6 +84,29 @@ def measured_peaks() -> tuple[float, str]:
         except Exception:
             pass
     return FALLBACK_HBM_GBS, "fallback"
+
+
+def fp32_peak() -> tuple[float, float, str]:
+    """(FP32 lane-op peak per second, MUFU peak per second, source): 148 SMs x 128 FP32 lanes
+    (16 MUFU lanes) x the maximum SM clock of MEASURED_PEAKS.json (sm_max_mhz; else the B200's
+    nominal 1965 MHz). Derived, not measured: the measured peaks hold no FP32 figure."""
+    mhz, src = 1965.0, "derived from the nominal 1965 MHz"
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            mhz = float(json.loads(p.read_text())["sm_max_mhz"])
+            src = "derived: 148 SMs x 128 lanes x MEASURED_PEAKS.json sm_max_mhz"
+        except Exception:
+            pass
+    return 148 * 128 * mhz * 1e6, 148 * 16 * mhz * 1e6, src
+
+
+# FP32 operations per unit of the rasterisers' work (the hot-path analysis' per-unit costs):
+# a forward blend (one (pixel, Gaussian) evaluation of the reference's loop) is ~13 FP32
+# operations + 1 MUFU exponential; a contributing (pixel, Gaussian) pair of the backward blend
+# is ~45 FP32 operations (+ its atomics).
+FWD_OPS_PER_BLEND = 13.0
+BWD_OPS_PER_PAIR = 45.0
 
 
 class ClockSampler:
@@ -213,6 +238,8 @@ def run_reference(args, rank: int, world: int) -> None:
     m = O.NpMoments(np.zeros((n, 3, 2)), np.zeros((n, 2)), np.zeros((n, 3, 2)), np.zeros((n, 4, 2)),
                     np.zeros((n, 3, 16, 2)))
     opts = TrainingOptions(scene_radius=radius)
+    acc = np.zeros(n, np.float32)
+    cnt = np.zeros(n, np.int32)
     rng = np.random.default_rng(0)
     perm = rng.permutation(len(cams))
     done = 0
@@ -225,6 +252,7 @@ def run_reference(args, rank: int, world: int) -> None:
         f = O.render(g, cam, til, ro)
         (_, _, _), grad = O.loss(f["rgb"], target, opts.loss_dssim_vs_L1_weight)
         b = O.backward(g, cam, til, ro, f, grad)
+        O.adc_stats(acc, cnt, b["mean2d"], f["fgidx_to_gidx"], cam.width, cam.height)
         p = _abi.AdamParamsC()
         lrs = opts.learning_rates()
         p.lr_means, p.lr_opacity_features, p.lr_scaling_features = lrs.means, lrs.opacity_features, lrs.scaling_features
@@ -253,14 +281,12 @@ def run_reference(args, rank: int, world: int) -> None:
             "warmup": warm, "ms_per_step": 1000 * el / steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "impl": "reference",
-            "config": {"workload": WORKLOAD, "global_batch": 1, "views_per_gpu": 1,
-                       "resolution": [cams[0].width, cams[0].height], "n_gaussians": n,
-                       "parallelism": "cpu",
-                       "note": "the oracle step computes no ADC statistics (under 1% of the GPU step)"},
+            "config": workload_config(world, cams[0].width, cams[0].height, n),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                              "sample": f"{steps} full training step(s) of the workload after {warm} "
                                        f"warm-up step(s) (time-bounded {args.ref_seconds:.0f} s), CPU "
-                                       f"restatement of the reference's GPU-path arithmetic, {threads} threads"},
+                                       f"restatement of the reference's GPU-path arithmetic (render, loss, "
+                                       f"backward, ADC statistics, Adam), {threads} threads"},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -319,6 +345,211 @@ def cpu_render_leg(gv_cpu, cams, ro) -> dict:
                       f"{threads} threads, and one on 1 thread"}
 
 
+def count_work(gaussians, cams, cam_indices, til, ro, buf, outputs) -> tuple[int, int]:
+    """Sum over renders of the given cameras of (blends, contributions): the rasterisers'
+    algorithmic work as the reference's blend loop performs it (gs3d_render_work_counts)."""
+    from gs3d import _abi
+    from gs3d import render as gs_render
+    from gs3d.render import work_counts
+    tb = tc = 0
+    for i in cam_indices:
+        gs_render(outputs, gaussians, cams[i], til, ro, buf, host_sync=False)
+        b, c = work_counts(cams[i], til, ro, buf)
+        if int(buf.device_counts[2].item()) & _abi.GS3D_STATUS_DUP_OVERFLOW:
+            raise RuntimeError("duplicate-key capacity overflow while counting work")
+        tb += b
+        tc += c
+    return tb, tc
+
+
+def raster_rates(blends: float, contrib: float, fwd_ms: float | None, bwd_ms: float | None) -> dict:
+    """FP32 / MUFU rates of the rasterisers from per-launch work counts and kernel times."""
+    fp32, mufu, src = fp32_peak()
+    out = {"fp32_peak_Tops": round(fp32 / 1e12, 2), "mufu_peak_Tops": round(mufu / 1e12, 3),
+           "peak_source": src, "blends_per_launch": int(blends), "contributing_pairs_per_launch": int(contrib)}
+    if fwd_ms:
+        bps = blends / (fwd_ms / 1e3)
+        out["forward"] = {"kernel": "k_raster", "avg_ms": round(fwd_ms, 4), "blends_per_s": bps,
+                          "fp32_Tops": round(FWD_OPS_PER_BLEND * bps / 1e12, 3),
+                          "fp32_frac": round(FWD_OPS_PER_BLEND * bps / fp32, 4),
+                          "mufu_frac": round(bps / mufu, 4)}
+    if bwd_ms:
+        pps = contrib / (bwd_ms / 1e3)
+        out["backward"] = {"kernel": "k_bwd_raster", "avg_ms": round(bwd_ms, 4), "pairs_per_s": pps,
+                           "fp32_Tops": round(BWD_OPS_PER_PAIR * pps / 1e12, 3),
+                           "fp32_frac": round(BWD_OPS_PER_PAIR * pps / fp32, 4)}
+    return out
+
+
+def flush_l2(device) -> None:
+    import torch
+    global _FLUSH
+    try:
+        _FLUSH
+    except NameError:
+        _FLUSH = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    _FLUSH.fill_(1)
+
+
+def sort_baseline_leg(buf, device, bits: int, reps: int = 20) -> dict:
+    """The duplicated keys of the last reference-order render (in filtered order: the input the
+    reference's render! passes to its CUB sort) sorted by (a) the reference's own CUB wrapper,
+    compiled from its source (oracle/_ref/cub_sort_pairs_wrapper.so), and (b) libgs3d.so's
+    drop-in sort_pairs with the same signature, each timed per call with CUDA events on the
+    legacy default stream (both run there), L2 flushed before every call; outputs compared."""
+    import ctypes as C
+    import torch
+    from gs3d import _abi
+    from oracle import build as obuild
+    D = int(buf.device_counts[1].item())
+    keys = buf.df2dgs_codes[:D].clone()
+    vals = buf.dfgidx_to_fgidx[:D].clone()
+    out = {"D": D, "key_bits": bits, "reps": reps, "l2": "flushed before every call"}
+    libs = {"gs3d_sort_pairs": _abi.lib()}
+    ref = obuild.REF_LIB
+    if ref.exists():
+        libs["reference_cub_sort_pairs"] = C.CDLL(str(ref))
+    else:
+        out["reference_cub_sort_pairs"] = "unavailable: oracle/_ref/cub_sort_pairs_wrapper.so not built"
+    results = {}
+    stream0 = torch.cuda.default_stream(device)
+    for name, lib in libs.items():
+        lib.determine_sort_pairs_temp_storage.restype = C.c_size_t
+        lib.determine_sort_pairs_temp_storage.argtypes = [C.c_void_p] * 4 + [C.c_int, C.c_int]
+        lib.sort_pairs.restype = None
+        lib.sort_pairs.argtypes = [C.c_void_p, C.c_size_t] + [C.c_void_p] * 4 + [C.c_int, C.c_int]
+        nbytes = int(lib.determine_sort_pairs_temp_storage(None, None, None, None, D, bits))
+        tmp = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=device)
+        ko, vo = torch.empty_like(keys), torch.empty_like(vals)
+        args = (C.c_void_p(tmp.data_ptr()), nbytes, C.c_void_p(keys.data_ptr()), C.c_void_p(ko.data_ptr()),
+                C.c_void_p(vals.data_ptr()), C.c_void_p(vo.data_ptr()), D, bits)
+        times = []
+        with torch.cuda.stream(stream0):
+            for r in range(reps + 3):
+                flush_l2(device)
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream0)
+                lib.sort_pairs(*args)
+                b.record(stream0)
+                torch.cuda.synchronize()
+                if r >= 3:
+                    times.append(a.elapsed_time(b))
+        results[name] = (ko, vo)
+        ms = statistics.median(times)
+        out[name] = {"median_ms": round(ms, 4), "min_ms": round(min(times), 4), "temp_bytes": nbytes,
+                     "keys_per_s": D / (ms / 1e3),
+                     "hbm_GBps_at_reference_passes": round(24.0 * math.ceil(bits / 8) * D / (ms / 1e3) / 1e9, 1)}
+    if len(results) == 2:
+        (k1, v1), (k2, v2) = results.values()
+        out["outputs_equal"] = bool(torch.equal(k1, k2) and torch.equal(v1, v2))
+    return out
+
+
+def render_only_leg(cfg_id: int, frames: int, world: int, rank: int, device, with_sort: bool) -> dict:
+    """Render-only throughput of a BASELINE config (config 3: 6M Gaussians, 3840x2160, 64-frame
+    orbit): device-timed frames/s, max over ranks, each rank rendering frames k * world + rank of
+    the orbit; blends/s of the forward blend from its stage time and the blends the reference's
+    loop performs on those frames."""
+    import torch
+    import torch.distributed as dist
+    from gs3d import RenderBuffers, RenderOptions, RenderOutputs, Tiling, _abi
+    from gs3d import render as gs_render
+    from gs3d.scene import CONFIGS, synthetic_gaussians
+    cfg = CONFIGS[cfg_id]
+    g = synthetic_gaussians(cfg["spec"], cfg["seed"]).to(device)
+    cams = cfg["cameras"]()
+    ro = RenderOptions.for_camera(cams[0], 3)
+    til = Tiling.for_camera(cams[0])
+    outs = RenderOutputs.create(cams[0].width, cams[0].height, device)
+    buf = RenderBuffers.create(g.n, til.nb_tiles, device, capacity_dup=8 * g.n)
+    order = [(k * world + rank) % len(cams) for k in range(frames)]
+    for k in range(3):
+        gs_render(outs, g, cams[order[k % len(order)]], til, ro, buf, host_sync=False)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _abi.profile_enable(True)
+    e0.record(stream)
+    for i in order:
+        gs_render(outs, g, cams[i], til, ro, buf, host_sync=False)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    prof = _abi.profile_report()
+    _abi.profile_enable(False)
+    if int(buf.device_counts[2].item()) & _abi.GS3D_STATUS_DUP_OVERFLOW:
+        raise RuntimeError("duplicate-key capacity overflow during the render-only timing")
+    ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    blends, contrib = count_work(g, cams, order, til, ro, buf, outs)
+    fwd_ms = prof["raster"][1] / max(prof["raster"][0], 1)
+    rates = raster_rates(blends / frames, contrib / frames, fwd_ms, None)
+    res = {"config": cfg_id, "n_gaussians": g.n, "resolution": [cams[0].width, cams[0].height],
+           "tiles": [til.tile_width, til.tile_height], "frames_per_rank": frames,
+           "value": world * frames / (ms / 1e3), "unit": "frames/s", "ms_per_frame": ms / frames,
+           "blends_per_frame": blends / frames, "blends_per_s_whole_frame": world * blends / (ms / 1e3),
+           "forward_blend": rates.get("forward"),
+           "stages_ms_per_frame": {k: round(t / frames, 4) for k, (c, t) in prof.items()}}
+    if with_sort and rank == 0:
+        gs_render(outs, g, cams[0], til, ro, buf, reference_order=True)
+        res["sort_vs_reference_cub"] = sort_baseline_leg(buf, device, til.highest_key_bit)
+    del g, buf, outs
+    torch.cuda.empty_cache()
+    return res
+
+
+def densify_leg(trainer, world: int, steady_ms: float, device) -> dict:
+    """Cost of one densify/prune step (the reference's maybe_densify_and_prune! every 100
+    iterations, training.jl:313-444) at the bench's model size: the whole training step at a
+    densify iteration, device-timed (max over ranks), against the steady-state step; the ADC
+    statistics are the ones accumulated over the bench's earlier steps."""
+    import torch
+    import torch.distributed as dist
+    o = trainer.options
+    o.adc_interval = 100
+    nxt = (trainer.iteration_nb // 100 + 1) * 100
+    while nxt % o.opacity_reset_interval == 0 or not (o.adc_start_iteration_nb <= nxt <= o.adc_final_iteration_nb):
+        nxt += 100
+    trainer.iteration_nb = nxt - 1
+    n0 = trainer.gaussians.n
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    trainer.training_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    n1 = trainer.gaussians.n
+    # steady state after the densify step, with the changed model
+    for _ in range(3):
+        trainer.training_step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(10):
+        trainer.training_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    after = torch.tensor([e0.elapsed_time(e1) / 10], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(after, op=dist.ReduceOp.MAX)
+    return {"iteration": nxt, "densify_step_ms": round(ms, 3), "steady_step_ms": round(steady_ms, 3),
+            "densify_extra_ms": round(ms - steady_ms, 3), "n_before": n0, "n_after": n1,
+            "step_ms_after": round(float(after.item()), 3),
+            "amortised_extra_ms_per_step": round((ms - steady_ms) / 100, 4),
+            "note": "one densify step every 100 iterations within the densify window"}
+
+
 def main() -> None:
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -370,6 +601,9 @@ def main() -> None:
     torch.cuda.synchronize()
     trainer.render_host_sync = False
     F, D = (int(x) for x in trainer.render_buffers.device_counts[:2].cpu())
+    # cameras of the timed steps (for the rasterisers' work counts afterwards)
+    first = 0 if world > 1 else 1
+    timed_cams = [trainer.peek_camera_index(first + k) for k in range(args.steps)]
 
     # ---- device-timed throughput, inputs resident in HBM ------------------------------
     # nvidia-smi numbers GPUs physically: map this rank's device through CUDA_VISIBLE_DEVICES
@@ -431,18 +665,22 @@ def main() -> None:
     # each rank renders its own frames, device-timed, max over ranks --------------------------
     from gs3d import render as gs_render
     rb = trainer.render_buffers
+    render_cams = [(k * world + rank) % len(cams) for k in range(args.steps)]
     for k in range(3):
         gs_render(trainer.render_outputs, trainer.gaussians, cams[k % len(cams)], trainer.tiling,
                   trainer.render_options, rb, host_sync=False)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    _abi.profile_enable(True)
     e0.record(stream)
-    for k in range(args.steps):
-        gs_render(trainer.render_outputs, trainer.gaussians, cams[(k * world + rank) % len(cams)],
-                  trainer.tiling, trainer.render_options, rb, host_sync=False)
+    for k in render_cams:
+        gs_render(trainer.render_outputs, trainer.gaussians, cams[k], trainer.tiling,
+                  trainer.render_options, rb, host_sync=False)
     e1.record(stream)
     torch.cuda.synchronize()
+    rprof = _abi.profile_report()
+    _abi.profile_enable(False)
     if int(rb.device_counts[2].item()) & _abi.GS3D_STATUS_DUP_OVERFLOW:
         raise RuntimeError("duplicate-key capacity overflow during the render timing")
     ms3 = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
@@ -452,6 +690,20 @@ def main() -> None:
                   "ms_per_frame": float(ms3.item()) / args.steps,
                   "workload": "forward render only, same scene, 1920x1080, one frame per GPU per step"}
 
+    # ---- the rasterisers' algorithmic work (outside every timed region) ------------------
+    # the reference's blend loop on the cameras of the timed training steps and of the render
+    # timing, with the parameters as they are now (a few hundred small Adam steps later)
+    tb, tc = count_work(trainer.gaussians, cams, timed_cams, trainer.tiling, trainer.render_options,
+                        rb, trainer.render_outputs)
+    rbl, rco = count_work(trainer.gaussians, cams, render_cams, trainer.tiling, trainer.render_options,
+                          rb, trainer.render_outputs)
+    avg = lambda pr, k: pr[k][1] / max(pr[k][0], 1) if k in pr else None
+    train_rates = raster_rates(tb / args.steps, tc / args.steps, avg(prof, "raster"), avg(prof, "bwd_raster"))
+    render_rates = raster_rates(rbl / args.steps, rco / args.steps, avg(rprof, "raster"), None)
+    render_fps["forward_blend"] = render_rates.get("forward")
+    render_fps["blends_per_frame"] = rbl / args.steps
+    render_fps["blends_per_s_whole_frame"] = world * rbl / (float(ms3.item()) / 1000.0)
+
     # ---- roofline of the dominant kernel ---------------------------------------------
     peak, peak_kind = measured_peaks()
     w, h = cams[0].width, cams[0].height
@@ -459,54 +711,89 @@ def main() -> None:
     stages = {}
     factored = world > 1 and args.dp_exchange == "factored"
     for name, (cnt, tot) in prof.items():
-        avg = tot / max(cnt, 1)
+        av = tot / max(cnt, 1)
         b = stage_bytes(name, F, D, gv.n, w, h, passes, world, factored, til.nb_tiles)
         b = b * args.steps / cnt if b and cnt else b  # per launch (chunked stages: a share)
-        stages[name] = {"launches": cnt, "avg_ms": round(avg, 4),
+        stages[name] = {"launches": cnt, "avg_ms": round(av, 4),
                         "share": round(tot / max(sum(t for _, t in prof.values()), 1e-9), 4),
-                        "alg_GBps": round(b / (avg / 1000) / 1e9, 1) if b else None}
+                        "alg_GBps": round(b / (av / 1000) / 1e9, 1) if b else None}
     dominant = max(prof.items(), key=lambda kv: kv[1][1])[0]
     dom = stages[dominant]
-    achieved = dom["alg_GBps"]
     dom_bytes = stage_bytes(dominant, F, D, gv.n, w, h, passes, world, factored, til.nb_tiles)
     dom_bytes = dom_bytes * args.steps / prof[dominant][0] if dom_bytes else dom_bytes
     traffic = (round(NCU_TRAFFIC_FRACTION[dominant] * dom_bytes / 1e9, 4)
                if dominant in NCU_TRAFFIC_FRACTION and dom_bytes else None)
-    roofline = {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peak,
-                "peak_source": peak_kind, "unit": "GB/s",
-                "frac": round(achieved / peak, 4) if achieved else None,
-                "traffic": traffic, "traffic_unit": "GB per launch",
-                "limiter": {"bwd_raster": "instruction issue (ncu at 1M: 82% issue active, 2% DRAM)",
-                            "raster": "instruction issue (ncu at 1M: 92% issue active, 2% DRAM)"}
-                           .get(dominant, "HBM")}
+    if dominant in ("bwd_raster", "raster"):
+        part = train_rates["backward" if dominant == "bwd_raster" else "forward"]
+        fp32, _, fp32_src = fp32_peak()
+        roofline = {"bound": "fp32-issue", "kernel": part["kernel"], "achieved": part["fp32_Tops"],
+                    "peak": round(fp32 / 1e12, 2), "peak_source": fp32_src, "unit": "TFLOP/s",
+                    "frac": part["fp32_frac"],
+                    "work": (f"{BWD_OPS_PER_PAIR:.0f} FP32 ops x {tc / args.steps:.0f} contributing "
+                             f"(pixel, Gaussian) pairs per launch" if dominant == "bwd_raster" else
+                             f"{FWD_OPS_PER_BLEND:.0f} FP32 ops x {tb / args.steps:.0f} blends per launch"),
+                    "avg_ms": dom["avg_ms"], "traffic": traffic, "traffic_unit": "GB per launch",
+                    "hbm_frac": round(dom["alg_GBps"] / peak, 4) if dom["alg_GBps"] else None,
+                    "hbm_peak": peak, "hbm_peak_source": peak_kind}
+    else:
+        roofline = {"bound": "hbm", "kernel": dominant, "achieved": dom["alg_GBps"], "peak": peak,
+                    "peak_source": peak_kind, "unit": "GB/s",
+                    "frac": round(dom["alg_GBps"] / peak, 4) if dom["alg_GBps"] else None,
+                    "traffic": traffic, "traffic_unit": "GB per launch"}
     gpu_launches = 0
     for name, (cnt, _) in prof.items():
         k = KERNELS_PER_STAGE.get(name, 1)
         gpu_launches += cnt * k
+
+    # ---- config 3: render-only 6M Gaussians at 3840x2160 ----------------------------------
+    render_4k = None
+    if not args.no_extra:
+        render_4k = render_only_leg(3, 64, world, rank, device,
+                                    with_sort=(world == 1 and not args.no_cpu_baseline))
+
+    # ---- reference baselines (rank 0, one GPU): CPU oracle step, CPU renderer, CUB sort ----
     cpu = None
+    sort_1080 = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        gs_render(trainer.render_outputs, trainer.gaussians, cams[timed_cams[-1]], trainer.tiling,
+                  trainer.render_options, rb, reference_order=True)
+        sort_1080 = sort_baseline_leg(rb, device, til.highest_key_bit)
+        sort_1080["gs3d_tile_bucket_pipeline"] = {
+            "avg_ms": round((avg(prof, "tile_count") or 0) + (avg(prof, "sort") or 0), 4),
+            "stages": "tile_count + sort (counts, scan, scatter, per-tile sort: the render's default "
+                      "F4-F7, which also yields tile ends)", "D_of_training_step": D}
         cpu = cpu_baseline_leg(gv_cpu, cams, pool_host, ro, til, opts)
         render_fps["cpu_baseline"] = cpu_render_leg(gv_cpu, cams, ro)
+
+    # ---- one densify step at the bench's size (all ranks: it is collective) ---------------
+    densify = None
+    if not args.no_extra:
+        densify = densify_leg(trainer, world, ms_max / args.steps, device)
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": WORKLOAD,
-                       "global_batch": world, "views_per_gpu": 1, "resolution": [w, h],
-                       "n_gaussians": gv.n, "filtered_F": F, "duplicates_D": D,
-                       "tiles": [til.tile_width, til.tile_height],
-                       "parallelism": f"dp{world}" if world > 1 else "single",
-                       **({"dp_exchange": args.dp_exchange, "dp_chunks": trainer.chunks}
-                          if world > 1 else {}),
-                       "l2": "inputs larger than L2 (2.1 GB params+moments), no flush"},
-            "e2e": e2e, "render": render_fps, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk,
-            "gpu_launches": gpu_launches, "stages": stages,
+            "config": workload_config(world, w, h, gv.n),
+            "workload_stats": {"filtered_F": F, "duplicates_D": D, "tiles": [til.tile_width, til.tile_height],
+                               **({"dp_exchange": args.dp_exchange, "dp_chunks": trainer.chunks}
+                                  if world > 1 else {})},
+            "e2e": e2e, "render": render_fps, "roofline": roofline, "rasterisers": train_rates,
+            "cpu_baseline": cpu, "clocks": clk, "gpu_launches": gpu_launches, "stages": stages,
+            "render_config3_4k": render_4k, "densify": densify, "sort_vs_reference_cub": sort_1080,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def workload_config(world: int, w: int, h: int, n: int) -> dict:
+    """The workload's config, identical in both arms (the reference arm times the same one)."""
+    return {"workload": WORKLOAD, "global_batch": world, "views_per_gpu": 1, "resolution": [w, h],
+            "n_gaussians": n, "parallelism": f"dp{world}" if world > 1 else "single",
+            "l2": "inputs larger than L2 (2.1 GB params+moments), no flush"}
 
 
 if __name__ == "__main__":

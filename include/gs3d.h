@@ -220,15 +220,15 @@ GS3D_API int gs3d_sort_pairs_async(
     const int32_t* values_in, int32_t* values_out,
     int nb_items, int highest_key_bit, gs3d_stream_t stream);
 
-/* No counterpart in the reference (its sort always takes caller temp storage,
- * forward_core.jl:629-659). gs3d_sort_pairs_async without temp storage: the scratch is a
+/* No counterpart in the reference. gs3d_sort_pairs_async without temp storage: the scratch is a
  * static device array inside libgs3d.so (13 MiB per device), so the call allocates nothing,
  * for callers that cannot provide or allocate a temporary buffer. At most
  * GS3D_SORT_NO_ALLOC_MAX_ITEMS pairs (larger calls return GS3D_ERR_INVALID_ARGUMENT and
  * launch nothing). The scratch is shared by all calls on a device: calls whose work overlaps
- * on the device race; calls on one stream do not. The first call with nb_items > 0 on a
- * device does host-side setup (scratch address lookup, kernel attribute) and must come
- * before any stream capture on that device. */
+ * on the device race; calls on one stream do not. Every call with nb_items > 0 looks the
+ * scratch address up on the current device (nothing is cached, so a device reset between calls
+ * is harmless); the first call on a device also loads the array there and must come before any
+ * stream capture on that device. */
 #define GS3D_SORT_NO_ALLOC_MAX_ITEMS (1 << 20)
 GS3D_API int gs3d_sort_pairs_no_alloc(
     const int64_t* keys_in, int64_t* keys_out,
@@ -268,6 +268,18 @@ GS3D_API int gs3d_render_forward_render_only(
     const gs3d_camera* camera, const gs3d_tiling* tiling,
     const gs3d_render_options* options, gs3d_render_buffers* buffers,
     int32_t* host_counts, uint32_t flags, gs3d_stream_t stream);
+
+/* Work counts of the last gs3d_render_forward with these buffers (sorted arrays, tile ends,
+ * 2D records and device counts as it left them), as the reference's blend loop performs the
+ * work (render_tiles_kernel!, forward_core.jl:928-968: every pixel examines its tile's entries
+ * in sorted order until it stops): counts_device[0] = (pixel, Gaussian) evaluations, the
+ * terminating one included; counts_device[1] = evaluations blended into the pixel, which are
+ * also the (pixel, Gaussian) pairs the backward blend (backward_core.jl:96-293) differentiates.
+ * counts_device is 2 uint64 in device memory, overwritten. For rooflines and tests; not on the
+ * training path (it evaluates every pair without the rasteriser's culling). */
+GS3D_API int gs3d_render_work_counts(
+    const gs3d_camera* camera, const gs3d_tiling* tiling, const gs3d_render_options* options,
+    const gs3d_render_buffers* buffers, uint64_t* counts_device, gs3d_stream_t stream);
 
 /* ---- backward: backward! (backward_core.jl:37-72) ----------------------------------- */
 

@@ -446,6 +446,59 @@ int oracle_render_ro(const gs3d_gaussians* gp, const float* cov, const gs3d_came
     return 0;
 }
 
+// Work counts of the blend loop (render_tiles_kernel!, forward_core.jl:928-968) over the
+// arrays a render left: out[0] = (pixel, Gaussian) evaluations until each pixel stops (the
+// terminating evaluation included), out[1] = evaluations blended into the pixel.
+void oracle_work_counts(const float* f2d, const int32_t* sfgidx, const int32_t* tiles_end,
+                        const gs3d_camera* camp, const gs3d_tiling* tp,
+                        const gs3d_render_options* op, int64_t* out) {
+    const gs3d_camera& cam = *camp;
+    const gs3d_tiling& til = *tp;
+    const gs3d_render_options& opt = *op;
+    const int W = cam.width, H = cam.height;
+    const int TW = til.tile_width, TH = til.tile_height;
+    const int64_t T = (int64_t)til.nb_tiles_x * til.nb_tiles_y;
+    std::vector<int64_t> nb(T, 0), nc(T, 0);
+    parallel_for(0, T, [&](int64_t tl) {
+        const int txi = (int)(tl % til.nb_tiles_x) + 1, tyi = (int)(tl / til.nb_tiles_x) + 1;
+        const int tile = txi + (tyi - 1) * til.nb_tiles_x;
+        const int start = tile == 1 ? 0 : tiles_end[tile - 2];
+        const int end = tiles_end[tile - 1];
+        const int u0 = (txi - 1) * TW, v0 = (tyi - 1) * TH;
+        for (int pv = 1; pv <= TH; ++pv)
+            for (int pu = 1; pu <= TW; ++pu) {
+                if (!(pu + u0 <= W && pv + v0 <= H)) continue;
+                const float cu = (float)pu - 0.5f, cv = (float)pv - 0.5f;
+                const float uu = cu * cu, uv = cu * cv, vv = cv * cv;
+                float Tr = 1.0f;
+                for (int s = start + 1; s <= end; ++s) {
+                    const float* r = f2d + 9 * (size_t)(sfgidx[s - 1] - 1);
+                    const float du = r[0] - (float)u0, dv = r[1] - (float)v0;
+                    const float ic11 = r[3], ic21 = r[4], ic22 = r[5];
+                    const float ic11_du = ic11 * du, ic21_du = ic21 * du, ic22_dv = ic22 * dv;
+                    const float p1 = -0.5f * ic11, p2 = -0.5f * ic22, p3 = -ic21;
+                    const float p4 = ic11_du + ic21 * dv;
+                    const float p5 = ic21_du + ic22_dv;
+                    const float p6 = -0.5f * (ic11_du * du + ic22_dv * dv) - ic21_du * dv +
+                                     o_logf(r[2]);
+                    const float q = p1 * uu + p2 * vv + p3 * uv + p4 * cu + p5 * cv + p6;
+                    ++nb[tl];
+                    const float alpha = o_min(opt.max_alpha, o_expf(q));
+                    if (alpha < opt.min_alpha) continue;
+                    const float nextT = Tr * (1.0f - alpha);
+                    if (nextT < opt.min_transmittance) break;
+                    Tr = nextT;
+                    ++nc[tl];
+                }
+            }
+    });
+    out[0] = out[1] = 0;
+    for (int64_t t = 0; t < T; ++t) {
+        out[0] += nb[t];
+        out[1] += nc[t];
+    }
+}
+
 void oracle_set_threads(int32_t n) { thread_count() = n < 1 ? 1 : n; }
 
 // Exposed for the oracle self-tests.

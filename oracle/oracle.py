@@ -71,6 +71,9 @@ def lib():
         _LIB.oracle_logf.argtypes = [C.c_float]
         _LIB.oracle_split_normals.restype = None
         _LIB.oracle_split_normals.argtypes = [C.c_uint64, C.c_uint64, vp]
+        _LIB.oracle_work_counts.restype = None
+        _LIB.oracle_work_counts.argtypes = [vp, vp, vp, P(_abi.Camera), P(_abi.TilingC),
+                                            P(_abi.RenderOptionsC), vp]
         _LIB.oracle_set_threads.restype = None
         _LIB.oracle_set_threads.argtypes = [C.c_int32]
         _LIB.oracle_compact.restype = C.c_int32
@@ -213,6 +216,18 @@ def render(g, camera, tiling, options, dup_capacity: int | None = None) -> dict:
     for k in ("codes", "dfg", "scodes", "sfg"):
         out[k] = out[k][:D]
     return out
+
+
+def work_counts(fwd: dict, camera, tiling, options) -> tuple[int, int]:
+    """(blends, contributions) of the blend loop over a render() result: (pixel, Gaussian)
+    evaluations until each pixel stops, and the evaluations blended into a pixel."""
+    out = np.zeros(2, np.int64)
+    if fwd["D"] == 0:
+        return 0, 0
+    cc, tc, oc = camera.to_c(), tiling.to_c(), options.to_c()
+    lib().oracle_work_counts(_p(np.ascontiguousarray(fwd["f2d"])), _p(np.ascontiguousarray(fwd["sfg"])),
+                             _p(fwd["tiles_end"]), C.byref(cc), C.byref(tc), C.byref(oc), _p(out))
+    return int(out[0]), int(out[1])
 
 
 def backward(g: NpGaussians, camera, tiling, options, fwd: dict, rgb_grad: np.ndarray,

@@ -268,3 +268,23 @@ def test_render_only_input_matches_oracle(cuda, case):
     tr, _ = gpu_render(gv, cam, til, opt, cuda)
     d = np.abs(gpu["rgb"].astype(np.float64) - tr["rgb"])
     assert np.mean(d <= 1e-4) >= 0.999 and d.mean() <= 1e-5, (d.max(), d.mean())
+
+
+@pytest.mark.parametrize("case", [c for c in CASES if c[0] in ("cfg0", "cfg0_aa_bg", "ragged_720p",
+                                                                "big_tiles_1080", "odd_size")],
+                         ids=lambda c: c[0])
+def test_work_counts_vs_oracle(cuda, case):
+    """gs3d_render_work_counts (blends and contributions of the reference's blend loop) equal
+    the oracle's counts over the same render."""
+    from gs3d.render import work_counts
+    _, spec, seed, (w, h, fov, pos), tile, kw, deg = case
+    gv = synthetic_gaussians(spec, seed)
+    cam = look_at_camera(w, h, fov, pos)
+    opt = RenderOptions.for_camera(cam, deg, **kw)
+    til = Tiling.for_camera(cam, *(tile or (None, None)))
+    _, buf = gpu_render(gv, cam, til, opt, cuda)
+    blends, contrib = work_counts(cam, til, opt, buf)
+    ref = O.render(O.NpGaussians.from_vector(gv), cam, til, opt)
+    want = O.work_counts(ref, cam, til, opt)
+    assert (blends, contrib) == want
+    assert 0 < contrib <= blends

@@ -127,3 +127,48 @@ def test_sort_pairs_stable_and_masked():
     masked = keys & ((1 << 36) - 1)
     order = np.argsort(masked, kind="stable")
     assert np.array_equal(vo, vals[order]) and np.array_equal(ko, keys[order])
+
+
+def test_oracle_work_counts_match_a_direct_loop():
+    """oracle_work_counts (the bench's roofline numerators) against a plain Python walk of the
+    reference's blend loop (forward_core.jl:928-968) over the same render, on a small scene."""
+    from gs3d.scene import SceneSpec, look_at_camera, synthetic_gaussians
+    gv = synthetic_gaussians(SceneSpec(300, "uniform:1", -3.0, 0.5), 3)
+    cam = look_at_camera(48, 40, 60.0, (0, 0, 3))
+    opt = RenderOptions.for_camera(cam, 3)
+    til = Tiling.for_camera(cam, 16, 8)
+    f = O.render(O.NpGaussians.from_vector(gv), cam, til, opt)
+    f32 = np.float32
+    blends = contrib = 0
+    for ty in range(til.nb_tiles_y):
+        for tx in range(til.nb_tiles_x):
+            tile = tx + ty * til.nb_tiles_x + 1
+            start = 0 if tile == 1 else int(f["tiles_end"][tile - 2])
+            end = int(f["tiles_end"][tile - 1])
+            u0, v0 = tx * til.tile_width, ty * til.tile_height
+            for pv in range(1, til.tile_height + 1):
+                for pu in range(1, til.tile_width + 1):
+                    if pu + u0 > cam.width or pv + v0 > cam.height:
+                        continue
+                    cu, cv = f32(pu) - f32(0.5), f32(pv) - f32(0.5)
+                    T = f32(1)
+                    for s in range(start, end):
+                        r = f["f2d"][f["sfg"][s] - 1]
+                        du, dv = r[0] - f32(u0), r[1] - f32(v0)
+                        p4 = r[3] * du + r[4] * dv
+                        p5 = r[4] * du + r[5] * dv
+                        p6 = (f32(-0.5) * (r[3] * du * du + r[5] * dv * dv) - r[4] * du * dv
+                              + f32(O.logf(float(r[2]))))
+                        q = (f32(-0.5) * r[3] * (cu * cu) + f32(-0.5) * r[5] * (cv * cv)
+                             - r[4] * (cu * cv) + p4 * cu + p5 * cv + p6)
+                        blends += 1
+                        alpha = min(f32(opt.max_alpha), f32(O.expf(float(q))))
+                        if alpha < f32(opt.min_alpha):
+                            continue
+                        nT = T * (f32(1) - alpha)
+                        if nT < f32(opt.min_transmittance):
+                            break
+                        T = nT
+                        contrib += 1
+    assert O.work_counts(f, cam, til, opt) == (blends, contrib)
+    assert contrib > 0 and blends > contrib

@@ -66,7 +66,8 @@ def test_two_calls_in_a_row_match_the_existing_entry_point(cuda):
 
 def test_small_and_boundary_sizes(cuda):
     lib = gs3d.lib()
-    for n, bits in [(1, 35), (4095, 64), (4096, 33), (4097, 8)]:
+    # (1000, 0): no key bits, the sort only copies; (MAX_ITEMS, 64): the widest keys at the limit
+    for n, bits in [(1, 35), (4095, 64), (4096, 33), (4097, 8), (1000, 0), (MAX_ITEMS, 64)]:
         keys, vals = _inputs(n, n + bits)
         k_in, v_in = torch.from_numpy(keys).to(cuda), torch.from_numpy(vals).to(cuda)
         ko, vo = _sort_no_alloc(lib, k_in, v_in, n, bits)

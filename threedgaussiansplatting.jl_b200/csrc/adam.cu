@@ -1,13 +1,14 @@
-// adam.cu — update!(opt, fgradients, Val(sh)) (optimizer.jl:964-1009) as ONE kernel.
+// adam.cu — update!(opt, fgradients, Val(sh)) (optimizer.jl:964-1009).
 //
 // The reference launches five kernels (four component groups, then the SH coefficients:
-// optimizer.jl:1084-1127, :1165-1248), each walking the F filtered Gaussians. Here one kernel
-// does all 59 parameters: k_adam_sh16 + k_adam_geom when every SH array has storage degree 3 (48 words per
-// Gaussian, moved as 16-byte units; the training configuration), else k_adam_warp4, which gives
-// each warp four filtered Gaussians at a time; lane s updates scalar slot s of each (SH
-// coefficients first, then mean, opacity feature, scales, rotation), so all lanes run the same
-// update with no divergence, the SH rows move as consecutive words, and every load of the four
-// Gaussians is in flight before the first update.
+// optimizer.jl:1084-1127, :1165-1248), each walking the F filtered Gaussians. Here two launches
+// cover all 59 parameters when every SH array has storage degree 3 (the training configuration):
+// k_adam_sh16 (48 words per Gaussian, moved as 16-byte units) and k_adam_geom (the 11 geometry
+// scalars). Other storage degrees use one launch, k_adam_warp4, which gives each warp four
+// filtered Gaussians at a time; lane s updates scalar slot s of each (SH coefficients first,
+// then mean, opacity feature, scales, rotation), so all lanes run the same update with no
+// divergence, the SH rows move as consecutive words, and every load of the four Gaussians is in
+// flight before the first update.
 // Per scalar the reference's update (scalar_adam_update, optimizer.jl:941-953):
 //   m1 <- b1 m1 + (1 - b1) g ; m2 <- b2 m2 + (1 - b2) g^2
 //   p  <- p - lr (m1 / (1 - b1^t)) / (sqrt(m2 / (1 - b2^t)) + eps),  t = update_count + 1

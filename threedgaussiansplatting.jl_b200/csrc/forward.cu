@@ -16,6 +16,9 @@ namespace gs3d {
 int launch_raster(const gs3d_render_outputs& out, const gs3d_camera& cam, const gs3d_tiling& til,
                   const gs3d_render_options& opt, const gs3d_render_buffers& buf,
                   cudaStream_t stream);
+int launch_raster_counts(const gs3d_camera& cam, const gs3d_tiling& til,
+                         const gs3d_render_options& opt, const gs3d_render_buffers& buf,
+                         unsigned long long* counts_out, cudaStream_t stream);
 
 namespace {
 
@@ -617,6 +620,23 @@ GS3D_API int gs3d_render_forward_render_only(const gs3d_render_outputs* outputs,
     g.sh_coeffs = ro->sh_coeffs;
     return render_forward_impl(outputs, &g, ro->n > 0 ? ro->covariances : nullptr, cam, til, opt,
                                buf, host_counts, flags, stream);
+}
+
+GS3D_API int gs3d_render_work_counts(const gs3d_camera* cam, const gs3d_tiling* til,
+                                     const gs3d_render_options* opt,
+                                     const gs3d_render_buffers* buf, uint64_t* counts_device,
+                                     gs3d_stream_t stream) {
+    if (!cam || !til || !opt || !buf || !counts_device) return invalid("NULL argument");
+    if (til->tile_width <= 0 || til->tile_height <= 0 || til->tile_width * til->tile_height > 512 ||
+        til->nb_tiles_x <= 0 || til->nb_tiles_y <= 0)
+        return invalid("tiling %dx%d tiles of %dx%d", til->nb_tiles_x, til->nb_tiles_y,
+                       til->tile_width, til->tile_height);
+    if (!buf->sdfgidx_to_fgidx || !buf->tiles_end_sdfgidx || !buf->device_counts ||
+        !buf->means2d_opacities_inverse_covariances_colors)
+        return invalid("NULL render buffer array");
+    return launch_raster_counts(*cam, *til, *opt, *buf,
+                                reinterpret_cast<unsigned long long*>(counts_device),
+                                reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

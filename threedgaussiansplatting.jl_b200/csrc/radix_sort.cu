@@ -257,15 +257,12 @@ int radix_sort_pairs(void* ws, size_t ws_bytes, const int64_t* keys_in, int64_t*
     k_rs_global_hist<<<gh_blocks, RS_THREADS, 0, stream>>>(keys_in, capacity, count_dev, count_host,
                                                            passes, highest_key_bit, ghist);
     GS3D_LAUNCHED("k_rs_global_hist");
-    static bool attr_set[64] = {};
-    int dev = 0;
-    GS3D_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
-    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        GS3D_CUDA(cudaFuncSetAttribute(k_rs_downsweep, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)sizeof(DownSmem)),
-                  "downsweep smem attribute");
-        if (dev >= 0 && dev < 64) attr_set[dev] = true;
-    }
+    // set on every call: the attribute belongs to the current context (lost on a device reset),
+    // the call is a cheap host-side update, and it needs no per-device state shared between
+    // host threads
+    GS3D_CUDA(cudaFuncSetAttribute(k_rs_downsweep, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)sizeof(DownSmem)),
+              "downsweep smem attribute");
     const int64_t* src_k = keys_in;
     const int32_t* src_v = values_in;
     for (int p = 0; p < passes; ++p) {

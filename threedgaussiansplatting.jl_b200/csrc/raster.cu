@@ -162,11 +162,81 @@ __global__ void __launch_bounds__(512, GS3D_RASTER_MINB) k_raster(const RasterAr
     }
 }
 
+// Work counts of the blend as the reference performs it (render_tiles_kernel!,
+// forward_core.jl:928-968): every pixel examines its tile's entries in sorted order until it
+// stops. blends = (pixel, entry) evaluations, the terminating one included; contributions =
+// evaluations blended into the pixel (alpha >= min_alpha and T (1 - alpha) >= min_T). Same
+// staging and arithmetic as k_raster, without its culling, so the counts are the ones the
+// reference's loop would reach. For rooflines and tests only; not on the render path.
+__global__ void __launch_bounds__(512) k_raster_counts(const RasterArgs a,
+                                                       unsigned long long* __restrict__ out) {
+    extern __shared__ __align__(16) float4 sm4[];
+    __shared__ unsigned long long blk[2];
+    const int nthr = blockDim.x;
+    float4* sA = sm4;
+    float4* sB = sm4 + nthr;
+    const int t = threadIdx.x;
+    if (t < 2) blk[t] = 0ull;
+    int lu, lv;
+    tile_pixel(a.compact, a.tile_w, a.tile_h, t, lu, lv);
+    const int txi = blockIdx.x, tyi = blockIdx.y;
+    const int u0 = txi * a.tile_w, v0 = tyi * a.tile_h;
+    const bool inside = u0 + lu + 1 <= a.width && v0 + lv + 1 <= a.height;
+    const int F = a.counts[0];
+    const int64_t Draw = a.counts[1];
+    __syncthreads();
+    if (F == 0 || Draw == 0 || Draw > a.capacity_dup) return;
+    const int tile = txi + tyi * a.tiles_x + 1;
+    const int start = tile == 1 ? 0 : a.tiles_end[tile - 2];
+    const int end = a.tiles_end[tile - 1];
+    const float cu = (float)(lu + 1) - 0.5f, cv = (float)(lv + 1) - 0.5f;
+    const float uu = cu * cu, uv = cu * cv, vv = cv * cv;
+    float T = 1.0f;
+    bool done = !inside;
+    unsigned long long nb = 0, nc = 0;
+    for (int base = start; base < end; base += nthr) {
+        if (__syncthreads_count(!done) == 0) break;
+        const int idx = base + t;
+        if (idx < end) {
+            const int fg = a.sfgidx[idx] - 1;
+            const float* r = a.f2d + 9 * (size_t)fg;
+            const float du = r[0] - (float)u0, dv = r[1] - (float)v0;
+            const float ic11 = r[3], ic21 = r[4], ic22 = r[5];
+            const float ic11_du = ic11 * du, ic21_du = ic21 * du, ic22_dv = ic22 * dv;
+            const float p6 = -0.5f * (ic11_du * du + ic22_dv * dv) - ic21_du * dv + gs_logf(r[2]);
+            sA[t] = make_float4(-0.5f * ic11, -0.5f * ic22, -ic21, ic11_du + ic21 * dv);
+            sB[t] = make_float4(ic21_du + ic22_dv, p6, 0.0f, 0.0f);
+        }
+        __syncthreads();
+        const int n = min(nthr, end - base);
+        for (int j = 0; j < n && !done; ++j) {
+            const float4 A = sA[j], B = sB[j];
+            const float q = A.x * uu + A.y * vv + A.z * uv + A.w * cu + B.x * cv + B.y;
+            ++nb;
+            if (q < a.q_skip) continue;
+            const float alpha = min_hi(a.max_alpha, gs_expf_blend(q));
+            if (alpha < a.min_alpha) continue;
+            const float nT = T * (1.0f - alpha);
+            if (nT < a.min_T) { done = true; break; }
+            T = nT;
+            ++nc;
+        }
+    }
+    atomicAdd(&blk[0], nb);
+    atomicAdd(&blk[1], nc);
+    __syncthreads();
+    if (t == 0) {
+        atomicAdd(out, blk[0]);
+        atomicAdd(out + 1, blk[1]);
+    }
+}
+
 }  // namespace
 
-int launch_raster(const gs3d_render_outputs& out, const gs3d_camera& cam, const gs3d_tiling& til,
-                  const gs3d_render_options& opt, const gs3d_render_buffers& buf,
-                  cudaStream_t stream) {
+namespace {
+RasterArgs raster_args(const gs3d_render_outputs& out, const gs3d_camera& cam,
+                       const gs3d_tiling& til, const gs3d_render_options& opt,
+                       const gs3d_render_buffers& buf) {
     RasterArgs a;
     a.sfgidx = buf.sdfgidx_to_fgidx;
     a.tiles_end = buf.tiles_end_sdfgidx;
@@ -193,6 +263,28 @@ int launch_raster(const gs3d_render_outputs& out, const gs3d_camera& cam, const 
     // exp(q) < min_alpha for every q < log(min_alpha) - 0.01 (margin >> 2 ulp)
     a.log_min_alpha = opt.min_alpha > 0.0f ? gs_logf(opt.min_alpha) : -INFINITY;
     a.q_skip = opt.min_alpha > 0.0f ? a.log_min_alpha - 0.01f : -INFINITY;
+    return a;
+}
+}  // namespace
+
+int launch_raster_counts(const gs3d_camera& cam, const gs3d_tiling& til,
+                         const gs3d_render_options& opt, const gs3d_render_buffers& buf,
+                         unsigned long long* counts_out, cudaStream_t stream) {
+    const gs3d_render_outputs none = {};
+    const RasterArgs a = raster_args(none, cam, til, opt, buf);
+    const int nthr = til.tile_width * til.tile_height;
+    GS3D_CUDA(cudaMemsetAsync(counts_out, 0, 2 * sizeof(unsigned long long), stream),
+              "zero work counts");
+    k_raster_counts<<<dim3(til.nb_tiles_x, til.nb_tiles_y), nthr, (size_t)nthr * 2 * sizeof(float4),
+                      stream>>>(a, counts_out);
+    GS3D_LAUNCHED("k_raster_counts");
+    return GS3D_OK;
+}
+
+int launch_raster(const gs3d_render_outputs& out, const gs3d_camera& cam, const gs3d_tiling& til,
+                  const gs3d_render_options& opt, const gs3d_render_buffers& buf,
+                  cudaStream_t stream) {
+    const RasterArgs a = raster_args(out, cam, til, opt, buf);
     const int nthr = til.tile_width * til.tile_height;
     const size_t smem = (size_t)nthr * (3 * sizeof(float4) + sizeof(float2));
     dim3 grid(til.nb_tiles_x, til.nb_tiles_y);

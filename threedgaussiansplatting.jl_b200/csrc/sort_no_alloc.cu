@@ -14,17 +14,16 @@
 //  * the scratch is one array per device, shared by every call on that device: two calls
 //    whose work overlaps on the device (different streams without an event between them, or
 //    different host threads) race on it and produce garbage. Calls on one stream are safe;
-//  * the scratch occupies kScratchBytes of device memory on each device where this library's
-//    device code is loaded, whether or not this entry point is ever called;
+//  * the scratch occupies kScratchBytes of device memory on each device where this module is
+//    loaded: under CUDA's default lazy module loading (CUDA_MODULE_LOADING=LAZY) that is the
+//    first call of this entry point on the device, otherwise the library's load;
 //  * no part of the scratch has to start at zero: the one region the sort accumulates into
 //    (the per-digit histograms) is cleared by every call on its own stream before use, and the
 //    other regions are fully written before they are read;
-//  * the first call with nb_items > 0 on a device does per-device setup on the host: it looks
-//    the scratch address up (cudaGetSymbolAddress, which also loads this library's device code
-//    on that device if it is not yet loaded) and sets the sort kernel's shared-memory limit.
-//    Make that first call before capturing any stream on the device.
-#include <mutex>
-
+//  * every call with nb_items > 0 looks the scratch address of the current device up
+//    (cudaGetSymbolAddress, which on the first call also loads this module's device code on that
+//    device). Nothing is cached across calls, so a device reset or a new primary context between
+//    calls is harmless. Make the first call on a device before capturing any stream on it.
 #include "common.cuh"
 #include "internal.h"
 
@@ -38,34 +37,23 @@ constexpr size_t kScratchBytes = (size_t)13 << 20;
 
 static __device__ __align__(256) unsigned char g_sort_scratch[kScratchBytes];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_mutex;
-void* g_scratch_ptr[kMaxDevices] = {};
-
-// Address of this device's scratch, looked up once per device (the device must be current).
+// Address of the current device's scratch. Looked up on every call (a cheap host-side query)
+// rather than cached, because a cached address goes stale when the device's context is torn
+// down and re-created (cudaDeviceReset), after which it would point at memory this module no
+// longer owns.
 int scratch_for_current_device(void** out) {
-    int dev = -1;
-    GS3D_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
-    if (dev < 0 || dev >= kMaxDevices)
-        return set_error("gs3d_sort_pairs_no_alloc: device ordinal %d outside [0, %d)", dev,
-                         kMaxDevices),
+    const size_t need = radix_sort_workspace_bytes(GS3D_SORT_NO_ALLOC_MAX_ITEMS);
+    if (need > kScratchBytes)
+        return set_error("gs3d_sort_pairs_no_alloc: static scratch of %zu bytes is smaller "
+                         "than the %zu bytes %d pairs need",
+                         kScratchBytes, need, GS3D_SORT_NO_ALLOC_MAX_ITEMS),
                GS3D_ERR_UNSUPPORTED;
-    std::lock_guard<std::mutex> lock(g_mutex);
-    if (!g_scratch_ptr[dev]) {
-        const size_t need = radix_sort_workspace_bytes(GS3D_SORT_NO_ALLOC_MAX_ITEMS);
-        if (need > kScratchBytes)
-            return set_error("gs3d_sort_pairs_no_alloc: static scratch of %zu bytes is smaller "
-                             "than the %zu bytes %d pairs need",
-                             kScratchBytes, need, GS3D_SORT_NO_ALLOC_MAX_ITEMS),
-                   GS3D_ERR_UNSUPPORTED;
-        void* p = nullptr;
-        GS3D_CUDA(cudaGetSymbolAddress(&p, g_sort_scratch), "cudaGetSymbolAddress(sort scratch)");
-        if (!p || (reinterpret_cast<uintptr_t>(p) & 255u) != 0)
-            return set_error("gs3d_sort_pairs_no_alloc: scratch address %p is not 256-aligned", p),
-                   GS3D_ERR_CUDA;
-        g_scratch_ptr[dev] = p;
-    }
-    *out = g_scratch_ptr[dev];
+    void* p = nullptr;
+    GS3D_CUDA(cudaGetSymbolAddress(&p, g_sort_scratch), "cudaGetSymbolAddress(sort scratch)");
+    if (!p || (reinterpret_cast<uintptr_t>(p) & 255u) != 0)
+        return set_error("gs3d_sort_pairs_no_alloc: scratch address %p is not 256-aligned", p),
+               GS3D_ERR_CUDA;
+    *out = p;
     return GS3D_OK;
 }
 

@@ -409,18 +409,14 @@ TsLayout ts_layout(void* ws, int nb_tiles) {
     return L;
 }
 
-int set_hist_smem(int nb_tiles) {
-    static int done[64] = {};
-    int dev = 0;
-    GS3D_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
-    const int bytes = nb_tiles * (int)sizeof(int32_t);
-    if (dev >= 0 && dev < 64 && done[dev] >= bytes) return GS3D_OK;
+// Set on every call: the attribute belongs to the current context (lost on a device reset), the
+// call is a cheap host-side update, and it needs no per-device state shared between host threads.
+int set_hist_smem() {
     const int want = tile_sort_max_tiles() * (int)sizeof(int32_t);
     GS3D_CUDA(cudaFuncSetAttribute(k_tile_hist, cudaFuncAttributeMaxDynamicSharedMemorySize, want),
               "tile histogram shared memory");
     GS3D_CUDA(cudaFuncSetAttribute(k_tile_scatter, cudaFuncAttributeMaxDynamicSharedMemorySize, want),
               "tile scatter shared memory");
-    if (dev >= 0 && dev < 64) done[dev] = want;
     return GS3D_OK;
 }
 }  // namespace
@@ -434,7 +430,7 @@ int tile_sort_count(void* ws, size_t ws_bytes, int32_t* counts, const int4* rang
     if (nb_tiles > tile_sort_max_tiles())
         return set_error("%d tiles exceed the tile sort's %d", nb_tiles, tile_sort_max_tiles()),
                GS3D_ERR_UNSUPPORTED;
-    GS3D_RETURN_IF(set_hist_smem(nb_tiles));
+    GS3D_RETURN_IF(set_hist_smem());
     const TsLayout L = ts_layout(ws, nb_tiles);
     const size_t smem = (size_t)nb_tiles * sizeof(int32_t);
     k_tile_hist<<<kHistBlocks, kHistThreads, smem, stream>>>(counts, ranges, tiles_x, nb_tiles, L.bcount);

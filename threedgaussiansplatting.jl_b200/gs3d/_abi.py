@@ -136,6 +136,8 @@ SIGNATURES = {
     "gs3d_render_forward": (C.c_int, [P(RenderOutputsC), P(GaussiansC), P(Camera), P(TilingC),
                                       P(RenderOptionsC), P(RenderBuffersC), C.c_void_p,
                                       C.c_uint32, C.c_void_p]),
+    "gs3d_render_work_counts": (C.c_int, [P(Camera), P(TilingC), P(RenderOptionsC),
+                                          P(RenderBuffersC), C.c_void_p, C.c_void_p]),
     "gs3d_render_forward_render_only": (C.c_int, [P(RenderOutputsC), P(RenderOnlyGaussiansC),
                                                   P(Camera), P(TilingC), P(RenderOptionsC),
                                                   P(RenderBuffersC), C.c_void_p, C.c_uint32,

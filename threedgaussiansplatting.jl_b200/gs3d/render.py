@@ -56,3 +56,17 @@ def counts(buffers: RenderBuffers) -> tuple[int, int]:
     """(F, D) of the last render (reads device memory; synchronises)."""
     c = buffers.device_counts.cpu()
     return int(c[0]), int(c[1])
+
+
+def work_counts(camera: PinholeCamera, tiling: Tiling, options: RenderOptions,
+                buffers: RenderBuffers, stream: torch.cuda.Stream | None = None) -> tuple[int, int]:
+    """(blends, contributions) of the last render with `buffers`, as the reference's blend loop
+    performs the work (gs3d_render_work_counts): (pixel, Gaussian) evaluations until each pixel
+    stops, and the evaluations blended into a pixel (the pairs the backward blend
+    differentiates). Synchronises; for rooflines and tests."""
+    out = torch.zeros(2, dtype=torch.int64, device=buffers.device_counts.device)
+    _abi.check(_abi.lib().gs3d_render_work_counts(
+        C.byref(camera.to_c()), C.byref(tiling.to_c()), C.byref(options.to_c()),
+        C.byref(buffers.to_c()), C.c_void_p(out.data_ptr()), C.c_void_p(_stream_handle(stream))))
+    c = out.cpu()
+    return int(c[0]), int(c[1])
