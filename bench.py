@@ -461,10 +461,11 @@ def render_only_leg(cfg_id: int, frames: int, world: int, rank: int, device, wit
     ro = RenderOptions.for_camera(cams[0], 3)
     til = Tiling.for_camera(cams[0])
     outs = RenderOutputs.create(cams[0].width, cams[0].height, device)
-    buf = RenderBuffers.create(g.n, til.nb_tiles, device, capacity_dup=8 * g.n)
+    buf = RenderBuffers.create(g.n, til.nb_tiles, device, capacity_dup=8 * g.n, mask_dup=None)
     order = [(k * world + rank) % len(cams) for k in range(frames)]
     for k in range(3):
-        gs_render(outs, g, cams[order[k % len(order)]], til, ro, buf, host_sync=False)
+        gs_render(outs, g, cams[order[k % len(order)]], til, ro, buf, host_sync=False,
+                  contrib_masks=False)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -473,7 +474,7 @@ def render_only_leg(cfg_id: int, frames: int, world: int, rank: int, device, wit
     _abi.profile_enable(True)
     e0.record(stream)
     for i in order:
-        gs_render(outs, g, cams[i], til, ro, buf, host_sync=False)
+        gs_render(outs, g, cams[i], til, ro, buf, host_sync=False, contrib_masks=False)
     e1.record(stream)
     torch.cuda.synchronize()
     prof = _abi.profile_report()
@@ -668,7 +669,7 @@ def main() -> None:
     render_cams = [(k * world + rank) % len(cams) for k in range(args.steps)]
     for k in range(3):
         gs_render(trainer.render_outputs, trainer.gaussians, cams[k % len(cams)], trainer.tiling,
-                  trainer.render_options, rb, host_sync=False)
+                  trainer.render_options, rb, host_sync=False, contrib_masks=False)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -676,7 +677,7 @@ def main() -> None:
     e0.record(stream)
     for k in render_cams:
         gs_render(trainer.render_outputs, trainer.gaussians, cams[k], trainer.tiling,
-                  trainer.render_options, rb, host_sync=False)
+                  trainer.render_options, rb, host_sync=False, contrib_masks=False)
     e1.record(stream)
     torch.cuda.synchronize()
     rprof = _abi.profile_report()

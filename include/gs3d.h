@@ -47,6 +47,8 @@ typedef struct CUstream_st* gs3d_stream_t; /* ABI-compatible with cudaStream_t *
 /* render flags */
 #define GS3D_RENDER_NO_HOST_SYNC 1u /* never block: D is checked on the device only      */
 #define GS3D_RENDER_REFERENCE_ORDER 2u /* F4-F7 as the reference stages them (see below)   */
+#define GS3D_RENDER_NO_CONTRIB_MASKS 4u /* leave render_buffers.contrib_masks unwritten (a
+                                       render that no backward follows)                   */
 
 /* backward flags */
 #define GS3D_BACKWARD_FIX_SH16 1u /* use coefficient 16 in the degree-3 direction Jacobian
@@ -123,9 +125,19 @@ typedef struct gs3d_render_buffers {
     int64_t* sdf2dgs_codes;        /* capacity_dup  sorted                              */
     int32_t* sdfgidx_to_fgidx;     /* capacity_dup  sorted                              */
     int32_t* tiles_end_sdfgidx;    /* nb_tiles                                          */
-    int32_t* device_counts;        /* >= 4 int32: [0] F, [1] D, [2] status bits         */
+    int32_t* device_counts;        /* >= 4 int32: [0] F, [1] D, [2] status bits,
+                                      [3] 1 when the render wrote contrib_masks          */
     void* workspace;               /* scan / sort scratch                               */
     size_t workspace_bytes;
+    /* Optional (NULL: not used). Per-pixel contribution masks the forward blend writes for
+     * the backward blend: one bit per (pixel, duplicated entry) the pixel evaluated with
+     * alpha >= 0.999 min_alpha before it stopped, 32 entries of a tile per 32-bit word. The
+     * backward then visits only those pairs. The forward writes them (and sets
+     * device_counts[3]) when contrib_mask_words >= (D / 32 + #tiles + 1) * tile pixels and
+     * the tile has a multiple of 32 pixels; otherwise the backward tests every entry itself,
+     * with the same results. */
+    uint32_t* contrib_masks;
+    int64_t contrib_mask_words;
 } gs3d_render_buffers;
 
 /* RenderOutputs (forward_structs.jl:1-65). Any pointer may be NULL except that backward

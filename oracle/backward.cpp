@@ -112,6 +112,20 @@ extern "C" {
 // Reverse blend (B2) + projection backward (B3). Inputs are the forward's outputs in the
 // reference layouts; F is the number of filtered Gaussians. All gradient outputs are
 // F-indexed (fgradients layout) and fully written (2D ones are zeroed first, B1).
+// oracle_backward with two test-only options: `project_only` != 0 skips B1 + B2 and takes
+// mean2d_g, opacity_g, licov_g and color_g as inputs (to check the projection backward on given
+// 2D gradients); `mag` (NULL or 9 x F floats) receives, per filtered Gaussian and per 2D
+// gradient component (mean2d 2, opacity 1, licov 3, colour 3), the sum of the absolute values
+// of the per-pixel terms, the scale of the rounding error of any summation order.
+int oracle_backward_ex(const gs3d_gaussians* gp, const gs3d_camera* camp, const gs3d_tiling* tp,
+                       const gs3d_render_options* op, int32_t F, const int32_t* fgidx_to_gidx,
+                       const float* f2d, const int32_t* sfgidx, const int32_t* tiles_end,
+                       const float* trans, const int32_t* last, const float* rgb_grad,
+                       uint32_t flags, float* mean2d_g, float* opacity_g, float* licov_g,
+                       float* color_g, float* mean3d_g, float* opf_g, float* scale_g,
+                       float* rot_g, float* sh_g, int32_t sh_grad_degree, int32_t project_only,
+                       float* mag);
+
 int oracle_backward(const gs3d_gaussians* gp, const gs3d_camera* camp, const gs3d_tiling* tp,
                     const gs3d_render_options* op, int32_t F, const int32_t* fgidx_to_gidx,
                     const float* f2d, const int32_t* sfgidx, const int32_t* tiles_end,
@@ -119,6 +133,19 @@ int oracle_backward(const gs3d_gaussians* gp, const gs3d_camera* camp, const gs3
                     uint32_t flags, float* mean2d_g, float* opacity_g, float* licov_g,
                     float* color_g, float* mean3d_g, float* opf_g, float* scale_g,
                     float* rot_g, float* sh_g, int32_t sh_grad_degree) {
+    return oracle_backward_ex(gp, camp, tp, op, F, fgidx_to_gidx, f2d, sfgidx, tiles_end, trans,
+                              last, rgb_grad, flags, mean2d_g, opacity_g, licov_g, color_g,
+                              mean3d_g, opf_g, scale_g, rot_g, sh_g, sh_grad_degree, 0, nullptr);
+}
+
+int oracle_backward_ex(const gs3d_gaussians* gp, const gs3d_camera* camp, const gs3d_tiling* tp,
+                       const gs3d_render_options* op, int32_t F, const int32_t* fgidx_to_gidx,
+                       const float* f2d, const int32_t* sfgidx, const int32_t* tiles_end,
+                       const float* trans, const int32_t* last, const float* rgb_grad,
+                       uint32_t flags, float* mean2d_g, float* opacity_g, float* licov_g,
+                       float* color_g, float* mean3d_g, float* opf_g, float* scale_g,
+                       float* rot_g, float* sh_g, int32_t sh_grad_degree, int32_t project_only,
+                       float* mag) {
     const gs3d_gaussians& g = *gp;
     const gs3d_camera& cam = *camp;
     const gs3d_tiling& til = *tp;
@@ -127,9 +154,10 @@ int oracle_backward(const gs3d_gaussians* gp, const gs3d_camera* camp, const gs3
     const bool fix16 = (flags & GS3D_BACKWARD_FIX_SH16) != 0;
 
     // B1 + B2 with double accumulators
-    std::vector<double> acc((size_t)F * 9, 0.0);  // mean2d(2) opacity(1) licov(3) color(3)
+    std::vector<double> acc(project_only ? 0 : (size_t)F * 9, 0.0);  // mean2d(2) opacity(1) licov(3) color(3)
+    std::vector<double> macc(mag && !project_only ? (size_t)F * 9 : 0, 0.0);
     const int TW = til.tile_width, TH = til.tile_height;
-    parallel_for(0, (int64_t)til.nb_tiles_x * til.nb_tiles_y, [&](int64_t tl) {
+    parallel_for(0, project_only ? 0 : (int64_t)til.nb_tiles_x * til.nb_tiles_y, [&](int64_t tl) {
             const int txi = (int)(tl % til.nb_tiles_x) + 1, tyi = (int)(tl / til.nb_tiles_x) + 1;
             const int tile = txi + (tyi - 1) * til.nb_tiles_x;
             const int first = tile == 1 ? 1 : tiles_end[tile - 2] + 1;
@@ -175,10 +203,18 @@ int oracle_backward(const gs3d_gaussians* gp, const gs3d_camera* camp, const gs3
                         atomic_add(&a[3], g11); atomic_add(&a[4], g21 + g21); atomic_add(&a[5], g22);
                         atomic_add(&a[6], ta * gr[0]); atomic_add(&a[7], ta * gr[1]);
                         atomic_add(&a[8], ta * gr[2]);
+                        if (!macc.empty()) {
+                            double* b = &macc[9 * (size_t)fg];
+                            const float t9[9] = {m0, m1, opg, g11, g21 + g21, g22, ta * gr[0],
+                                                 ta * gr[1], ta * gr[2]};
+                            for (int k = 0; k < 9; ++k) atomic_add(&b[k], std::fabs((double)t9[k]));
+                        }
                     }
                 }
         });
-    for (int f = 0; f < F; ++f) {
+    if (!macc.empty())
+        for (size_t k = 0; k < (size_t)F * 9; ++k) mag[k] = (float)macc[k];
+    for (int f = 0; f < (project_only ? 0 : F); ++f) {
         const double* a = &acc[9 * (size_t)f];
         mean2d_g[2 * f] = (float)a[0]; mean2d_g[2 * f + 1] = (float)a[1];
         opacity_g[f] = (float)a[2];

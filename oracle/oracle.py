@@ -45,6 +45,8 @@ def lib():
         _LIB.oracle_backward.argtypes = [P(_abi.GaussiansC), P(_abi.Camera), P(_abi.TilingC),
                                          P(_abi.RenderOptionsC), C.c_int32] + [vp] * 7 + \
             [C.c_uint32] + [vp] * 9 + [C.c_int32]
+        _LIB.oracle_backward_ex.restype = C.c_int
+        _LIB.oracle_backward_ex.argtypes = _LIB.oracle_backward.argtypes + [C.c_int32, vp]
         _LIB.oracle_sort_pairs.restype = C.c_int
         _LIB.oracle_sort_pairs.argtypes = [vp, vp, vp, vp, C.c_int64, C.c_int]
         _LIB.oracle_cpu_render.restype = C.c_int32
@@ -231,7 +233,12 @@ def work_counts(fwd: dict, camera, tiling, options) -> tuple[int, int]:
 
 
 def backward(g: NpGaussians, camera, tiling, options, fwd: dict, rgb_grad: np.ndarray,
-             flags: int = 0, sh_grad_degree: int | None = None) -> dict:
+             flags: int = 0, sh_grad_degree: int | None = None, grads_2d: dict | None = None,
+             with_magnitudes: bool = False) -> dict:
+    """backward! restated. `grads_2d` (mean2d, opacity, licov, color arrays of F rows): run only
+    the projection backward on these 2D gradients. `with_magnitudes`: also return "mag", per
+    filtered Gaussian the sums of the absolute per-pixel terms of the 9 2D gradient components
+    (mean2d 2, opacity 1, licov 3, colour 3)."""
     F = fwd["F"]
     d = g.sh_degree if sh_grad_degree is None else sh_grad_degree
     S = (d + 1) ** 2
@@ -241,18 +248,25 @@ def backward(g: NpGaussians, camera, tiling, options, fwd: dict, rgb_grad: np.nd
              mean3d=np.zeros((cap, 3), np.float32), opacity_feature=np.zeros(cap, np.float32),
              scaling=np.zeros((cap, 3), np.float32), rotation=np.zeros((cap, 4), np.float32),
              sh=np.zeros((cap, 3, S), np.float32))
+    if grads_2d is not None:
+        for k, shape in (("mean2d", (F, 2)), ("opacity", (F,)), ("licov", (F, 3)), ("color", (F, 3))):
+            o[k][:F] = np.asarray(grads_2d[k], np.float32).reshape(shape)
+    mag = np.zeros((cap, 9), np.float32) if with_magnitudes else None
     rg = np.ascontiguousarray(rgb_grad, dtype=np.float32)
     sfg = fwd["sfg"] if fwd["D"] > 0 else np.zeros(1, np.int32)
     gc, cc, tc, oc = g.to_c(), camera.to_c(), tiling.to_c(), options.to_c()
-    st = lib().oracle_backward(C.byref(gc), C.byref(cc), C.byref(tc), C.byref(oc), F,
+    st = lib().oracle_backward_ex(C.byref(gc), C.byref(cc), C.byref(tc), C.byref(oc), F,
                                _p(np.ascontiguousarray(fwd["fgidx_to_gidx"])), _p(np.ascontiguousarray(fwd["f2d"])),
                                _p(np.ascontiguousarray(sfg)), _p(fwd["tiles_end"]), _p(fwd["trans"]),
                                _p(fwd["last"]), _p(rg), flags, _p(o["mean2d"]), _p(o["opacity"]),
                                _p(o["licov"]), _p(o["color"]), _p(o["mean3d"]),
                                _p(o["opacity_feature"]), _p(o["scaling"]), _p(o["rotation"]),
-                               _p(o["sh"]), d)
+                               _p(o["sh"]), d, 1 if grads_2d is not None else 0, _p(mag))
     assert st == 0
-    return {k: v[:F] for k, v in o.items()}
+    out = {k: v[:F] for k, v in o.items()}
+    if mag is not None:
+        out["mag"] = mag[:F]
+    return out
 
 
 class NpMoments:

@@ -5,12 +5,17 @@
 * config 1 (500K Gaussians, 1280x720, ring camera 0): one training step;
 * config 3 (6M Gaussians, 3840x2160, 16,320 tiles, 46 key bits): the forward render.
 
-Bars (the same as the small-scene tests): compaction, depths, 2D records, tile rectangles,
-duplicate counts, sorted keys and values, tile ends, images and last contributors bit-exact
-(images also asserted within 1e-4); the loss within the loss test's tolerance; the nine
-gradient arrays within 1e-3 relative L2 (test_gpu_backward_adam.check_grads); one Adam step
-bit-exact given the same gradients, through both the written-SH-gradient update and the
-trainer's rebuilt-SH update. The oracle runs on all host threads (a few seconds per frame here).
+Bars: compaction, depths, 2D records, tile rectangles, duplicate counts, sorted keys and
+values, tile ends, images and last contributors bit-exact (images also asserted within 1e-4);
+the rasterisers' work counts exact; the loss within the loss test's tolerance; the nine gradient
+arrays within 1e-3 relative L2 with >= 99.9% of the Gaussians within 1e-3
+(test_gpu_backward_adam.check_grads). Per Gaussian, with millions of them some sums cancel to far
+below their terms, where float atomics (the reference's summation too) lose digits that the
+oracle's double sums keep: each Gaussian's 2D gradients are held to 1e-3 of their value plus 1e-4
+of the sum of their terms' magnitudes, and the projection backward to 1e-3 per Gaussian on the
+GPU's own 2D gradients. One Adam step is bit-exact given the same gradients, through both the
+written-SH-gradient update and the trainer's rebuilt-SH update. The oracle runs on all host
+threads (a few seconds per frame here).
 
 Also `update_adc_stats_kernel!` (training.jl:472-497): the ADC accumulators after three views,
 bit-exact against the oracle's accumulation of the same 2D gradients.
@@ -30,7 +35,7 @@ from gs3d.optimizer import AdamOptimizer, LearningRates, bias_corrections
 from gs3d.scene import CONFIGS, scene_radius, synthetic_gaussians, target_image
 from oracle import oracle as O
 
-from test_gpu_backward_adam import check_grads
+from test_gpu_backward_adam import check_grads, check_grads_2d_terms, rel_l2
 from test_gpu_forward import compare
 
 pytestmark = pytest.mark.gpu
@@ -126,8 +131,20 @@ def test_full_size_training_step_vs_oracle(cuda, cfg_id, cam_index):
                  mean3d=cpu(fg.mean3d_grads), opacity_feature=cpu(fg.opacity_feature_grads),
                  scaling=cpu(fg.scaling_features_grads), rotation=cpu(fg.rotation_features_grads),
                  sh=cpu(fg.sh_coeffs_grads))
-    ref_g = O.backward(npg, cam, til, opt, ref_f, grad_np)
-    check_grads(gpu_g, ref_g)
+    ref_g = O.backward(npg, cam, til, opt, ref_f, grad_np, with_magnitudes=True)
+    # arrays within 1e-3 relative L2, >= 99.9% of the Gaussians within 1e-3; every Gaussian's 2D
+    # gradients within 1e-3 of its value plus 1e-4 of the size of its per-pixel terms
+    check_grads(gpu_g, ref_g, every_gaussian=False)
+    check_grads_2d_terms(gpu_g, ref_g, ref_g["mag"])
+    # the projection backward on the GPU's own 2D gradients (no summation-order effects):
+    # every Gaussian with a gradient above 1e-3 of the largest within 1e-3 relative L2
+    ref_p = O.backward(npg, cam, til, opt, ref_f, grad_np, grads_2d=gpu_g)
+    for k in ("mean3d", "opacity_feature", "scaling", "rotation", "sh"):
+        total, per = rel_l2(gpu_g[k], ref_p[k])
+        norms = np.linalg.norm(np.asarray(ref_p[k], np.float64).reshape(len(per), -1), axis=1)
+        big = norms > 1e-3 * norms.max()
+        assert total <= 1e-5, (k, total)
+        assert np.all(per[big] <= 1e-3), (k, per[big].max(), np.count_nonzero(per[big] > 1e-3))
 
     # update!: the GPU step from written SH gradients and the trainer's rebuilt-SH step both
     # equal the oracle's step on the GPU's gradients, bit for bit

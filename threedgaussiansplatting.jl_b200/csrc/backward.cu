@@ -51,6 +51,7 @@ struct BwdArgs {
     float* color_g;
     int32_t width, height, tile_w, tile_h, tiles_x, compact;
     float bg0, bg1, bg2, min_alpha, max_alpha, log_min_alpha;
+    int32_t use_masks;  // the masks kernel is launched too (it takes renders with masks)
 };
 
 // Sum 9 per-lane values over the warp by recursive halving: at each of the five xor levels a
@@ -112,6 +113,7 @@ __global__ void __launch_bounds__(512, GS3D_BWDRASTER_MINB) k_bwd_raster(const B
     const int F = a.counts[0];
     const int64_t Draw = a.counts[1];
     if (F == 0 || Draw == 0 || Draw > a.capacity_dup) return;  // nothing drawn (or overflow)
+    if (a.use_masks && a.counts[3] == 1) return;  // k_bwd_raster_masks does this render
 
     const int t = threadIdx.x;
     const int lane = t & 31, warp = t >> 5;
@@ -260,6 +262,179 @@ __global__ void __launch_bounds__(512, GS3D_BWDRASTER_MINB) k_bwd_raster(const B
                     if (vi >= 0) atomicAdd(vptr + (size_t)vstride * fg, s);
                 }
             }
+        }
+    }
+}
+
+// ---- backward blend over the forward's contribution masks -------------------------------------
+// The pairs the reference's backward differentiates are a subset of the pairs the forward marked
+// in render_buffers.contrib_masks (every pair it blended, plus those within 0.1% below
+// min_alpha: the backward recomputes alpha as opacity x exp(conic form) while the forward folds
+// log(opacity) into the exponent, and the two roundings differ by a few ulps). So each thread
+// walks, back to front from its pixel's last contributor, only the entries its own mask bits
+// name, and applies the reference's test and formulas to each (the same as k_bwd_raster: the
+// same pairs in the same order per pixel). The lanes of a warp then work on different entries
+// at once, so the 9 gradients of a pair are added to per-entry accumulators in shared memory,
+// which are flushed to the per-Gaussian arrays with one global atomic per entry and value
+// after each batch of staged entries. Mask rows are those k_raster writes: row
+// (start / 32 + tile - 1 + c) holds chunk c (32 consecutive entries of the tile), one word per
+// thread, for the thread -> pixel map of the forward (fwd_pixel).
+__device__ __forceinline__ void fwd_pixel(int compact, int tw, int th, int t, int& lu, int& lv) {
+    if (compact) {
+        const PixelGroups<16> pg(compact, tw, th, t, lu, lv);
+        (void)pg;
+    } else {
+        tile_pixel(compact, tw, th, t, lu, lv);
+    }
+}
+
+#ifndef GS3D_BWDPP_MINB
+#define GS3D_BWDPP_MINB 2
+#endif
+
+__global__ void __launch_bounds__(512, GS3D_BWDPP_MINB) k_bwd_raster_masks(const BwdArgs a,
+                                                                          const uint32_t* cmask) {
+    extern __shared__ __align__(16) float4 sm4[];
+    const int nthr = blockDim.x;                        // tile pixels, a multiple of 32, <= 512
+    float4* E0 = sm4;                                   // x y ic11 ic21
+    float4* E1 = sm4 + nthr;                            // ic22 opacity r g
+    float* E2 = reinterpret_cast<float*>(sm4 + 2 * nthr);   // b
+    int* EF = reinterpret_cast<int*>(E2 + nthr);            // fgidx (0-based)
+    float* ACC = reinterpret_cast<float*>(EF + nthr);       // 9 planes of nthr accumulators
+    uint32_t* MW = reinterpret_cast<uint32_t*>(ACC + 9 * nthr);  // nthr / 32 rows of nthr words
+    __shared__ int red[32];
+
+    const int F = a.counts[0];
+    const int64_t Draw = a.counts[1];
+    if (F == 0 || Draw == 0 || Draw > a.capacity_dup || a.counts[3] != 1) return;
+
+    const int t = threadIdx.x;
+    const int lane = t & 31, warp = t >> 5;
+    int lu, lv;
+    fwd_pixel(a.compact, a.tile_w, a.tile_h, t, lu, lv);
+    const int txi = blockIdx.x, tyi = blockIdx.y;
+    const int U = txi * a.tile_w + lu + 1, V = tyi * a.tile_h + lv + 1;
+    const bool inside = U <= a.width && V <= a.height;
+    const size_t px = (size_t)(V - 1) + (size_t)a.height * (size_t)(U - 1);
+    const int tile = txi + tyi * a.tiles_x + 1;
+    const int start = tile == 1 ? 0 : a.tiles_end[tile - 2];
+    const int end = a.tiles_end[tile - 1];
+
+    float T = 0.0f, g0 = 0.0f, g1 = 0.0f, g2 = 0.0f;
+    int lastc = 0;
+    if (inside) {
+        lastc = a.last[px];
+        T = a.trans[px];
+        g0 = a.rgb_grad[3 * px];
+        g1 = a.rgb_grad[3 * px + 1];
+        g2 = a.rgb_grad[3 * px + 2];
+    }
+    float p0 = T * a.bg0, p1 = T * a.bg1, p2 = T * a.bg2;
+    const float cpu = (float)U - 0.5f, cpv = (float)V - 0.5f;
+
+    const int wl = (int)__reduce_max_sync(0xffffffffu, (unsigned)lastc);
+    if (lane == 0) red[warp] = wl;
+    __syncthreads();
+    int blast = 0;
+    for (int w = 0; w < (nthr >> 5); ++w) blast = max(blast, red[w]);
+    if (blast <= start) return;  // no pixel of the tile has a contributor (block-uniform)
+    // entries are indexed relative to the tile start; this pixel may take entries [0, rl)
+    int rl = lastc > start ? lastc - start : 0;
+    const int words = nthr >> 5;  // mask rows per batch
+    const uint32_t* mbase = cmask + ((int64_t)(start >> 5) + (tile - 1)) * nthr + t;
+
+    for (int b0 = ((blast - 1 - start) / nthr) * nthr; b0 >= 0; b0 -= nthr) {
+        __syncthreads();  // the previous batch's flush is done with the staging arrays
+        const int e = start + b0 + t;
+        if (e < end) {
+            const int fg = a.sfgidx[e] - 1;
+            const float* r = a.f2d + 9 * (size_t)fg;
+            E0[t] = make_float4(r[0], r[1], r[3], r[4]);
+            E1[t] = make_float4(r[5], r[2], r[6], r[7]);
+            E2[t] = r[8];
+            EF[t] = fg;
+        }
+#pragma unroll
+        for (int k = 0; k < 9; ++k) ACC[k * nthr + t] = 0.0f;
+        const int rows = min(words, (blast - 1 - start - b0) / 32 + 1);  // rows holding entries <= blast
+        for (int w = 0; w < rows; ++w) MW[w * nthr + t] = mbase[(int64_t)((b0 >> 5) + w) * nthr];
+        __syncthreads();
+
+        // this pixel's marked entries of the batch, back to front from min(rl, batch end)
+        const int hi = min(rl - b0, nthr);  // exclusive bound inside the batch
+        int w = hi > 0 ? (hi - 1) >> 5 : 0;
+        uint32_t m = 0;
+        if (hi > 0) {
+            const int nb = hi - (w << 5);  // 1..32 valid bits in row w
+            m = MW[w * nthr + t] & (nb == 32 ? 0xffffffffu : ((1u << nb) - 1u));
+        }
+        for (;;) {
+            while (m == 0 && w > 0) {
+                --w;
+                m = MW[w * nthr + t];
+            }
+            const bool has = m != 0;
+            if (!__any_sync(0xffffffffu, has)) break;
+            if (has) {
+                const int j = 31 - __clz(m);
+                m &= ~(1u << j);
+                const int en = (w << 5) + j;
+                const float4 A = E0[en];
+                const float4 B = E1[en];
+                const float du = cpu - A.x, dv = cpv - A.y;
+                const float ic11 = A.z, ic21 = A.w, ic22 = B.x;
+                const float du2 = du * du, dv2 = dv * dv, duv = du * dv;
+                const float q = fmaf(-0.5f, fmaf(ic11, du2, ic22 * dv2), -ic21 * duv);
+                // as k_bwd_raster: __expf, with the exact exponential deciding within 4e-6
+                // (relative) of min_alpha
+                float ge = __expf(q);
+                float alpha = min_hi(a.max_alpha, B.y * ge);
+                if (fabsf(alpha - a.min_alpha) <= 4e-6f * a.min_alpha) {
+                    ge = gs_expf_blend(q);
+                    alpha = min_hi(a.max_alpha, B.y * ge);
+                }
+                if (alpha >= a.min_alpha) {
+                    const float inv1m = __fdividef(1.0f, 1.0f - alpha);
+                    T *= inv1m;
+                    const float tc0 = T * B.z, tc1 = T * B.w, tc2 = T * E2[en];
+                    p0 = fmaf(alpha, tc0, p0);
+                    p1 = fmaf(alpha, tc1, p1);
+                    p2 = fmaf(alpha, tc2, p2);
+                    const float ag = inv1m * fmaf(g0, tc0 - p0, fmaf(g1, tc1 - p1, g2 * (tc2 - p2)));
+                    const float aga = alpha * ag;
+                    const float sc = -0.5f * aga;
+                    const float g21 = sc * duv;
+                    const float ta = T * alpha;
+                    float* acc = ACC + en;
+                    atomicAdd(acc, aga * fmaf(du, ic11, dv * ic21));
+                    atomicAdd(acc + nthr, aga * fmaf(du, ic21, dv * ic22));
+                    atomicAdd(acc + 2 * nthr, ge * ag);
+                    atomicAdd(acc + 3 * nthr, sc * du2);
+                    atomicAdd(acc + 4 * nthr, g21 + g21);
+                    atomicAdd(acc + 5 * nthr, sc * dv2);
+                    atomicAdd(acc + 6 * nthr, ta * g0);
+                    atomicAdd(acc + 7 * nthr, ta * g1);
+                    atomicAdd(acc + 8 * nthr, ta * g2);
+                }
+            }
+        }
+        rl = min(rl, b0);
+        __syncthreads();
+        // flush this batch's sums (one atomic per entry and nonzero value)
+        if (e < end) {
+            const int fg = EF[t];
+            float v[9];
+#pragma unroll
+            for (int k = 0; k < 9; ++k) v[k] = ACC[k * nthr + t];
+            if (v[0] != 0.0f) atomicAdd(a.mean2d_g + 2 * fg, v[0]);
+            if (v[1] != 0.0f) atomicAdd(a.mean2d_g + 2 * fg + 1, v[1]);
+            if (v[2] != 0.0f) atomicAdd(a.opacity_g + fg, v[2]);
+            if (v[3] != 0.0f) atomicAdd(a.licov_g + 3 * fg, v[3]);
+            if (v[4] != 0.0f) atomicAdd(a.licov_g + 3 * fg + 1, v[4]);
+            if (v[5] != 0.0f) atomicAdd(a.licov_g + 3 * fg + 2, v[5]);
+            if (v[6] != 0.0f) atomicAdd(a.color_g + 3 * fg, v[6]);
+            if (v[7] != 0.0f) atomicAdd(a.color_g + 3 * fg + 1, v[7]);
+            if (v[8] != 0.0f) atomicAdd(a.color_g + 3 * fg + 2, v[8]);
         }
     }
 }
@@ -738,8 +913,20 @@ int backward_impl(const gs3d_fgradients* fg, const float* rgb_grad,
         a.log_min_alpha = opt->min_alpha > 0.0f ? gs_logf(opt->min_alpha) : -INFINITY;
         const int nthr = til->tile_width * til->tile_height;
         const size_t smem = (size_t)nthr * (3 * sizeof(float4) + sizeof(float2) + sizeof(int));
+        // with contribution masks: k_bwd_raster_masks takes renders that wrote them
+        // (device_counts[3]), k_bwd_raster the others; each returns at once on the other's
+        a.use_masks = (buf->contrib_masks != nullptr && (nthr & 31) == 0) ? 1 : 0;
+        const size_t smem_m = (size_t)nthr * (2 * sizeof(float4) + 2 * sizeof(float) + 9 * sizeof(float)) +
+                              (size_t)(nthr / 32) * nthr * sizeof(uint32_t);
         ProfScope prof("bwd_raster", stream);
         const dim3 grid(til->nb_tiles_x, til->nb_tiles_y);
+        if (a.use_masks) {
+            GS3D_CUDA(cudaFuncSetAttribute(k_bwd_raster_masks,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_m),
+                      "backward blend shared memory");
+            k_bwd_raster_masks<<<grid, nthr, smem_m, stream>>>(a, buf->contrib_masks);
+            GS3D_LAUNCHED("k_bwd_raster_masks");
+        }
         k_bwd_raster<<<grid, nthr, smem, stream>>>(a);
         GS3D_LAUNCHED("k_bwd_raster");
     }

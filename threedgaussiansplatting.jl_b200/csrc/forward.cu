@@ -14,7 +14,7 @@
 namespace gs3d {
 
 int launch_raster(const gs3d_render_outputs& out, const gs3d_camera& cam, const gs3d_tiling& til,
-                  const gs3d_render_options& opt, const gs3d_render_buffers& buf,
+                  const gs3d_render_options& opt, const gs3d_render_buffers& buf, bool masks,
                   cudaStream_t stream);
 int launch_raster_counts(const gs3d_camera& cam, const gs3d_tiling& til,
                          const gs3d_render_options& opt, const gs3d_render_buffers& buf,
@@ -533,7 +533,8 @@ static int render_forward_impl(const gs3d_render_outputs* outputs, const gs3d_ga
         }
         {
             ProfScope prof("raster", stream);
-            GS3D_RETURN_IF(launch_raster(*outputs, *cam, *til, *opt, *buf, stream));
+            GS3D_RETURN_IF(launch_raster(*outputs, *cam, *til, *opt, *buf,
+                                         !(flags & GS3D_RENDER_NO_CONTRIB_MASKS), stream));
         }
         if ((flags & GS3D_RENDER_NO_HOST_SYNC) && host_counts)
             GS3D_CUDA(cudaMemcpyAsync(host_counts, counts, 4 * sizeof(int32_t),
@@ -587,7 +588,8 @@ static int render_forward_impl(const gs3d_render_outputs* outputs, const gs3d_ga
     // F8 / F9
     {
         ProfScope prof("raster", stream);
-        GS3D_RETURN_IF(launch_raster(*outputs, *cam, *til, *opt, *buf, stream));
+        GS3D_RETURN_IF(launch_raster(*outputs, *cam, *til, *opt, *buf,
+                                         !(flags & GS3D_RENDER_NO_CONTRIB_MASKS), stream));
     }
     if ((flags & GS3D_RENDER_NO_HOST_SYNC) && host_counts)
         GS3D_CUDA(cudaMemcpyAsync(host_counts, counts, 4 * sizeof(int32_t), cudaMemcpyDeviceToHost,

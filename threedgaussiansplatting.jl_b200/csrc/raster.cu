@@ -40,6 +40,11 @@ struct RasterArgs {
     int32_t compact;            // 4 x 8 warp blocks
     float bg0, bg1, bg2;
     float min_alpha, max_alpha, min_T, q_skip, log_min_alpha;
+    // contribution masks for the backward blend (NULL: none); see k_raster
+    uint32_t* cmask;
+    int64_t cmask_words;
+    float min_alpha_mark;
+    int32_t* mask_flag;         // device_counts[3]
 };
 
 #ifndef GS3D_RASTER_MINB
@@ -81,6 +86,15 @@ __global__ void __launch_bounds__(512, GS3D_RASTER_MINB) k_raster(const RasterAr
     const int tile = txi + tyi * a.tiles_x + 1;  // 1-based linear, x-contiguous
     const int start = tile == 1 ? 0 : a.tiles_end[tile - 2];
     const int end = a.tiles_end[tile - 1];
+    // contribution masks: row (start / 32 + tile - 1 + c) holds, for chunk c of 32 consecutive
+    // entries of this tile, one 32-bit word per thread; bit j of thread t's word is set when
+    // thread t's pixel evaluated entry 32 c + j with alpha >= min_alpha_mark before it stopped
+    // (every entry it blended, plus those within 0.1% below min_alpha). Rows of distinct tiles
+    // never overlap, and D / 32 + #tiles + 1 rows cover every tile.
+    const bool wmask = a.cmask != nullptr && (nthr & 31) == 0 &&
+                       (Draw / 32 + (int64_t)a.tiles_x * gridDim.y + 1) * nthr <= a.cmask_words;
+    if (wmask && t == 0 && blockIdx.x == 0 && blockIdx.y == 0) *a.mask_flag = 1;
+    uint32_t* const mrow = wmask ? a.cmask + ((int64_t)(start >> 5) + (tile - 1)) * nthr + t : nullptr;
 
     const float cu = (float)(lu + 1) - 0.5f, cv = (float)(lv + 1) - 0.5f;
     const float uu = cu * cu, uv = cu * cv, vv = cv * cv;
@@ -124,6 +138,7 @@ __global__ void __launch_bounds__(512, GS3D_RASTER_MINB) k_raster(const RasterAr
                 }
                 unsigned mask = pg.relevant(valid, eu0, eu1, ev0, ev1);
                 const int iters = PixelGroups<GS>::iterations(mask);
+                uint32_t mw = 0;
                 for (int it = 0; it < iters; ++it) {
                     if (!mask) continue;
                     const int jj = ch + __ffs(mask) - 1;
@@ -134,6 +149,7 @@ __global__ void __launch_bounds__(512, GS3D_RASTER_MINB) k_raster(const RasterAr
                     const float q = A.x * uu + A.y * vv + A.z * uv + A.w * cu + B.x * cv + B.y;
                     if (q < a.q_skip) continue;
                     const float alpha = min_hi(a.max_alpha, gs_expf_blend(q));
+                    if (alpha >= a.min_alpha_mark) mw |= 1u << (jj - ch);
                     if (alpha < a.min_alpha) continue;
                     const float nT = T * (1.0f - alpha);
                     if (nT < a.min_T) { done = true; continue; }
@@ -146,6 +162,7 @@ __global__ void __launch_bounds__(512, GS3D_RASTER_MINB) k_raster(const RasterAr
                     dep += w * C.y;
                     lastc = base + jj + 1;
                 }
+                if (mrow) mrow[(int64_t)((base - start + ch) >> 5) * nthr] = mw;
                 if (__all_sync(0xffffffffu, done)) break;
             }
         }
@@ -263,6 +280,10 @@ RasterArgs raster_args(const gs3d_render_outputs& out, const gs3d_camera& cam,
     // exp(q) < min_alpha for every q < log(min_alpha) - 0.01 (margin >> 2 ulp)
     a.log_min_alpha = opt.min_alpha > 0.0f ? gs_logf(opt.min_alpha) : -INFINITY;
     a.q_skip = opt.min_alpha > 0.0f ? a.log_min_alpha - 0.01f : -INFINITY;
+    a.cmask = buf.contrib_masks;
+    a.cmask_words = buf.contrib_mask_words;
+    a.min_alpha_mark = opt.min_alpha * 0.999f;
+    a.mask_flag = buf.device_counts + 3;
     return a;
 }
 }  // namespace
@@ -271,7 +292,8 @@ int launch_raster_counts(const gs3d_camera& cam, const gs3d_tiling& til,
                          const gs3d_render_options& opt, const gs3d_render_buffers& buf,
                          unsigned long long* counts_out, cudaStream_t stream) {
     const gs3d_render_outputs none = {};
-    const RasterArgs a = raster_args(none, cam, til, opt, buf);
+    RasterArgs a = raster_args(none, cam, til, opt, buf);
+    a.cmask = nullptr;
     const int nthr = til.tile_width * til.tile_height;
     GS3D_CUDA(cudaMemsetAsync(counts_out, 0, 2 * sizeof(unsigned long long), stream),
               "zero work counts");
@@ -282,9 +304,10 @@ int launch_raster_counts(const gs3d_camera& cam, const gs3d_tiling& til,
 }
 
 int launch_raster(const gs3d_render_outputs& out, const gs3d_camera& cam, const gs3d_tiling& til,
-                  const gs3d_render_options& opt, const gs3d_render_buffers& buf,
+                  const gs3d_render_options& opt, const gs3d_render_buffers& buf, bool masks,
                   cudaStream_t stream) {
-    const RasterArgs a = raster_args(out, cam, til, opt, buf);
+    RasterArgs a = raster_args(out, cam, til, opt, buf);
+    if (!masks) a.cmask = nullptr;
     const int nthr = til.tile_width * til.tile_height;
     const size_t smem = (size_t)nthr * (3 * sizeof(float4) + sizeof(float2));
     dim3 grid(til.nb_tiles_x, til.nb_tiles_y);

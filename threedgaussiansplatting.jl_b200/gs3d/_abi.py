@@ -19,6 +19,7 @@ GS3D_ERR_UNSUPPORTED = -5
 GS3D_STATUS_DUP_OVERFLOW = 1
 GS3D_RENDER_NO_HOST_SYNC = 1
 GS3D_RENDER_REFERENCE_ORDER = 2
+GS3D_RENDER_NO_CONTRIB_MASKS = 4
 GS3D_BACKWARD_FIX_SH16 = 1
 GS3D_BACKWARD_SKIP_SH_GRADS = 2
 GS3D_DENSE_ROW = 60
@@ -73,7 +74,8 @@ class RenderBuffersC(C.Structure):
                 ("dfgidx_to_fgidx", C.c_void_p), ("sdf2dgs_codes", C.c_void_p),
                 ("sdfgidx_to_fgidx", C.c_void_p), ("tiles_end_sdfgidx", C.c_void_p),
                 ("device_counts", C.c_void_p), ("workspace", C.c_void_p),
-                ("workspace_bytes", C.c_size_t)]
+                ("workspace_bytes", C.c_size_t), ("contrib_masks", C.c_void_p),
+                ("contrib_mask_words", C.c_int64)]
 
 
 class RenderOutputsC(C.Structure):

@@ -19,7 +19,7 @@ def _stream_handle(stream: torch.cuda.Stream | None) -> int:
 def render(outputs: RenderOutputs, gaussians: GaussiansVector, camera: PinholeCamera,
            tiling: Tiling, options: RenderOptions, buffers: RenderBuffers,
            stream: torch.cuda.Stream | None = None, host_sync: bool = True,
-           reference_order: bool = False) -> RenderOutputs:
+           reference_order: bool = False, contrib_masks: bool = True) -> RenderOutputs:
     """Render `gaussians` for `camera` into `outputs` (in place), like the reference's
     GPU `render!`. With `host_sync` the call waits once for the duplicate count and grows the
     duplicate buffers when they are too small (the reference's set_nb_dfgaussians!);
@@ -27,13 +27,17 @@ def render(outputs: RenderOutputs, gaussians: GaussiansVector, camera: PinholeCa
     `reference_order` also fills the unsorted duplicate arrays and the duplicate-count scan
     as the reference does (GS3D_RENDER_REFERENCE_ORDER); the sorted arrays, tile ends and
     images are the same either way. `gaussians` may also be a RenderOnlyGaussiansVector
-    (stored opacities and 3D covariances; gs3d_render_forward_render_only)."""
+    (stored opacities and 3D covariances; gs3d_render_forward_render_only).
+    `contrib_masks=False` leaves the buffers' contribution masks unwritten (for renders that no
+    backward follows; GS3D_RENDER_NO_CONTRIB_MASKS)."""
     if gaussians.n > buffers.capacity_n:
         raise ValueError(f"{gaussians.n} Gaussians exceed the buffers' capacity {buffers.capacity_n}")
     lib = _abi.lib()
     flags = 0 if host_sync else _abi.GS3D_RENDER_NO_HOST_SYNC
     if reference_order:
         flags |= _abi.GS3D_RENDER_REFERENCE_ORDER
+    if not contrib_masks:
+        flags |= _abi.GS3D_RENDER_NO_CONTRIB_MASKS
     host = buffers.host_counts
     hptr = C.c_void_p(host.data_ptr()) if host is not None else None
     args = (outputs.to_c(), gaussians.to_c(), camera.to_c(), tiling.to_c(), options.to_c())

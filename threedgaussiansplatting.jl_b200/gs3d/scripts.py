@@ -118,7 +118,7 @@ def evaluate(trainer, cameras, images, device) -> dict[str, float] | None:
     for cam, img in zip(cameras, images):
         gt = img.to(device)
         gs_render(trainer.render_outputs, trainer.gaussians, cam, trainer.tiling,
-                  trainer.render_options, trainer.render_buffers)
+                  trainer.render_options, trainer.render_buffers, contrib_masks=False)
         rgb = trainer.render_outputs.rgb
         v = lc(rgb, gt, scratch).clone()
         mse += float(((rgb - gt) ** 2).mean())
@@ -233,9 +233,9 @@ def render(path, out_dir=None, *, iterations=None, cameras=None, sh_degree=None,
         til = Tiling.for_camera(cam)
         if key != (cam.width, cam.height, til.nb_tiles):
             out = RenderOutputs.create(cam.width, cam.height, device)
-            buf = RenderBuffers.create(g.n, til.nb_tiles, device)
+            buf = RenderBuffers.create(g.n, til.nb_tiles, device, mask_dup=None)
             key = (cam.width, cam.height, til.nb_tiles)
-        gs_render(out, g, cam, til, RenderOptions.for_camera(cam, deg), buf)
+        gs_render(out, g, cam, til, RenderOptions.for_camera(cam, deg), buf, contrib_masks=False)
         img = out.rgb.clone()
         images.append(img)
         if out_dir is not None:

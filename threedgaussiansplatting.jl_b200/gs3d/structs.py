@@ -406,6 +406,9 @@ class RenderOutputs:
         return o
 
 
+MAX_TILE_PIXELS = 512  # the rasterisers' CTA size bound (one thread per pixel of a tile)
+
+
 @dataclass
 class RenderBuffers:
     """RenderBuffers + Filtered2DGaussiansVector, capacity-allocated on `device`."""
@@ -429,10 +432,16 @@ class RenderBuffers:
     device_counts: torch.Tensor
     workspace: torch.Tensor
     host_counts: torch.Tensor = field(default=None)
+    # per-pixel contribution masks written by the forward blend for the backward blend
+    # (gs3d_render_buffers.contrib_masks); None: not used
+    contrib_masks: torch.Tensor = field(default=None)
 
     @classmethod
     def create(cls, capacity_n: int, nb_tiles: int, device, capacity_dup: int | None = None,
-               keep_cs: bool = True) -> "RenderBuffers":
+               keep_cs: bool = True, mask_dup: int | None = -1) -> "RenderBuffers":
+        """`mask_dup`: duplicated entries the contribution masks can describe (-1: the smaller
+        of capacity_dup and 2 capacity_n + 65536; None or 0: no masks). Renders with more
+        duplicates than that run the backward blend without masks."""
         if capacity_dup is None:
             capacity_dup = max(4 * capacity_n, 1 << 16)
         dev = torch.device(device)
@@ -452,6 +461,11 @@ class RenderBuffers:
                 torch.zeros(4, **i32), torch.empty(ws, dtype=torch.uint8, device=dev))
         if dev.type == "cuda":
             b.host_counts = torch.zeros(4, dtype=torch.int32, pin_memory=True)
+        if mask_dup == -1:
+            mask_dup = min(capacity_dup, 2 * max(capacity_n, 1) + 65536)
+        if mask_dup:
+            words = (mask_dup // 32 + max(nb_tiles, 1) + 1) * MAX_TILE_PIXELS
+            b.contrib_masks = torch.empty(words, dtype=torch.int32, device=dev)
         return b
 
     def grow_dup(self, needed: int) -> None:
@@ -485,6 +499,9 @@ class RenderBuffers:
         b.device_counts = _ptr(self.device_counts)
         b.workspace = _ptr(self.workspace)
         b.workspace_bytes = self.workspace.numel()
+        if self.contrib_masks is not None:
+            b.contrib_masks = _ptr(self.contrib_masks)
+            b.contrib_mask_words = self.contrib_masks.numel()
         return b
 
 
