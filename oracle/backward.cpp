@@ -115,8 +115,10 @@ extern "C" {
 // oracle_backward with two test-only options: `project_only` != 0 skips B1 + B2 and takes
 // mean2d_g, opacity_g, licov_g and color_g as inputs (to check the projection backward on given
 // 2D gradients); `mag` (NULL or 9 x F floats) receives, per filtered Gaussian and per 2D
-// gradient component (mean2d 2, opacity 1, licov 3, colour 3), the sum of the absolute values
-// of the per-pixel terms, the scale of the rounding error of any summation order.
+// gradient component (mean2d 2, opacity 1, licov 3, colour 3), the sum over its per-pixel terms
+// of each term evaluated on absolute values (with its colour differences T c - (colour behind)
+// taken as |T c| + |behind|): the scale of the rounding errors of any float evaluation and
+// summation order, also where the terms or the sum cancel.
 int oracle_backward_ex(const gs3d_gaussians* gp, const gs3d_camera* camp, const gs3d_tiling* tp,
                        const gs3d_render_options* op, int32_t F, const int32_t* fgidx_to_gidx,
                        const float* f2d, const int32_t* sfgidx, const int32_t* tiles_end,
@@ -204,10 +206,23 @@ int oracle_backward_ex(const gs3d_gaussians* gp, const gs3d_camera* camp, const 
                         atomic_add(&a[6], ta * gr[0]); atomic_add(&a[7], ta * gr[1]);
                         atomic_add(&a[8], ta * gr[2]);
                         if (!macc.empty()) {
+                            // each term evaluated on absolute values, with the colour
+                            // differences T c - (colour behind) replaced by |T c| + |behind|:
+                            // the size that rounding errors scale with, even where the term
+                            // itself cancels
                             double* b = &macc[9 * (size_t)fg];
-                            const float t9[9] = {m0, m1, opg, g11, g21 + g21, g22, ta * gr[0],
-                                                 ta * gr[1], ta * gr[2]};
-                            for (int k = 0; k < 9; ++k) atomic_add(&b[k], std::fabs((double)t9[k]));
+                            const double agm = (double)inv1m *
+                                (std::fabs(gr[0]) * ((double)std::fabs(tc[0]) + std::fabs(part[0])) +
+                                 std::fabs(gr[1]) * ((double)std::fabs(tc[1]) + std::fabs(part[1])) +
+                                 std::fabs(gr[2]) * ((double)std::fabs(tc[2]) + std::fabs(part[2])));
+                            const double agam = alpha * agm, scm = 0.5 * agam;
+                            const double adu = std::fabs(du), adv = std::fabs(dv);
+                            const double t9[9] = {agam * (adu * std::fabs(ic11) + adv * std::fabs(ic21)),
+                                                  agam * (adu * std::fabs(ic21) + adv * std::fabs(ic22)),
+                                                  geval * agm, scm * adu * adu, 2.0 * scm * adu * adv,
+                                                  scm * adv * adv, std::fabs(ta * gr[0]),
+                                                  std::fabs(ta * gr[1]), std::fabs(ta * gr[2])};
+                            for (int k = 0; k < 9; ++k) atomic_add(&b[k], t9[k]);
                         }
                     }
                 }

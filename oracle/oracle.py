@@ -238,7 +238,8 @@ def backward(g: NpGaussians, camera, tiling, options, fwd: dict, rgb_grad: np.nd
     """backward! restated. `grads_2d` (mean2d, opacity, licov, color arrays of F rows): run only
     the projection backward on these 2D gradients. `with_magnitudes`: also return "mag", per
     filtered Gaussian the sums of the absolute per-pixel terms of the 9 2D gradient components
-    (mean2d 2, opacity 1, licov 3, colour 3)."""
+    (mean2d 2, opacity 1, licov 3, colour 3), each term evaluated on absolute values (its
+    colour differences taken as sums of magnitudes): the scale of float rounding errors."""
     F = fwd["F"]
     d = g.sh_degree if sh_grad_degree is None else sh_grad_degree
     S = (d + 1) ** 2

@@ -1,7 +1,8 @@
 """Build libgs3d.so (all CUDA sources under ../csrc) for sm_100a, in-tree.
 
-Every translation unit is compiled with ``-fmad=false``: floating-point contraction is
-written explicitly (``fmaf``) where wanted, so results are reproducible by the CPU oracle.
+Every translation unit except bwd_raster.cu (FILE_FLAGS) is compiled with ``-fmad=false``:
+floating-point contraction is written explicitly (``fmaf``) where wanted, so results are
+reproducible by the CPU oracle.
 Objects are rebuilt only when their source or a header is newer. Usage:
 
     python -m gs3d.build            (from threedgaussiansplatting.jl_b200/)
@@ -40,8 +41,19 @@ def _headers() -> list[Path]:
     return sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + sorted(INCLUDE.glob("*.h"))
 
 
+# Per-file exceptions to the numerics flags. bwd_raster.cu (the backward blend: float-atomic
+# gradient sums, compared within a tolerance) allows floating-point contraction; its decision
+# of which (pixel, Gaussian) pairs to take does not depend on it (see the file).
+FILE_FLAGS = {"bwd_raster.cu": {"-fmad=false": "-fmad=true"}}
+
+
+def _flags(src: Path) -> list[str]:
+    sub = FILE_FLAGS.get(src.name, {})
+    return [sub.get(f, f) for f in NVCC_FLAGS]
+
+
 def _compile(src: Path, obj: Path, verbose_ptxas: bool) -> str:
-    cmd = [nvcc(), *ARCH_FLAGS, *NVCC_FLAGS, "-c", str(src), "-o", str(obj)]
+    cmd = [nvcc(), *ARCH_FLAGS, *_flags(src), "-c", str(src), "-o", str(obj)]
     if verbose_ptxas:
         cmd += ["-Xptxas", "-v"]
     res = subprocess.run(cmd, capture_output=True, text=True)
