@@ -73,6 +73,12 @@ def parse():
                     help="N > 1: gradient rows exchanged as factored rows (16 floats per Gaussian) "
                          "or dense rows (60)")
     ap.add_argument("--dp-chunks", type=int, default=None, help="N > 1: pipeline depth")
+    ap.add_argument("--views-per-gpu", type=int, default=None,
+                    help="views rendered and back-propagated per GPU per step (default 1: the "
+                         "reference's one view per iteration on one GPU)")
+    ap.add_argument("--global-batch", type=int, default=None,
+                    help="views per step over all GPUs (BASELINE config 4: 8, 16 or 32); sets "
+                         "--views-per-gpu to global-batch / N")
     return ap.parse_args()
 
 
@@ -579,6 +585,11 @@ def main() -> None:
     from gs3d.training import Trainer, TrainingOptions
     gs3d.lib()
 
+    V = args.views_per_gpu or 1
+    if args.global_batch:
+        if args.global_batch % world:
+            raise SystemExit(f"--global-batch {args.global_batch} is not a multiple of {world} GPUs")
+        V = args.global_batch // world
     gv_cpu, cams, pool_host, ro, til, radius = build_workload(device, n_override=args.n_gaussians)
     opts = TrainingOptions(scene_radius=radius)
     if START_ITERATION + args.warmup + 2 * args.steps + 8 >= START_ITERATION + 100:
@@ -588,10 +599,10 @@ def main() -> None:
     targets_dev = [pool_dev[i % POOL] for i in range(len(cams))]
     pool_pinned = [t.pin_memory() for t in pool_host]
     targets_host = [pool_pinned[i % POOL] for i in range(len(cams))]
-    if world > 1:
+    if world > 1 or V > 1:
         trainer = DataParallelTrainer(gv, cams, targets_dev, ro, til, opts, seed=0,
                                       capacity_dup=8 * gv.n, chunks=args.dp_chunks,
-                                      factored=args.dp_exchange == "factored")
+                                      factored=args.dp_exchange == "factored", views_per_rank=V)
     else:
         trainer = Trainer(gv, cams, targets_dev, ro, til, opts, seed=0, capacity_dup=8 * gv.n)
     trainer.iteration_nb = START_ITERATION
@@ -603,8 +614,8 @@ def main() -> None:
     trainer.render_host_sync = False
     F, D = (int(x) for x in trainer.render_buffers.device_counts[:2].cpu())
     # cameras of the timed steps (for the rasterisers' work counts afterwards)
-    first = 0 if world > 1 else 1
-    timed_cams = [trainer.peek_camera_index(first + k) for k in range(args.steps)]
+    first = 0 if isinstance(trainer, DataParallelTrainer) else 1
+    timed_cams = [trainer.peek_camera_index(first + k) for k in range(args.steps * V)]
 
     # ---- device-timed throughput, inputs resident in HBM ------------------------------
     # nvidia-smi numbers GPUs physically: map this rank's device through CUDA_VISIBLE_DEVICES
@@ -635,7 +646,7 @@ def main() -> None:
     if world > 1:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms_max = float(ms_t.item())
-    value = world * args.steps / (ms_max / 1000.0)
+    value = world * V * args.steps / (ms_max / 1000.0)
 
     # ---- end to end through the public API: pinned host targets in, loss out ----------
     e2e = None
@@ -659,8 +670,8 @@ def main() -> None:
         if world > 1:
             dist.all_reduce(ms2, op=dist.ReduceOp.MAX)
         w, h = cams[0].width, cams[0].height
-        e2e = {"value": world * args.steps / (float(ms2.item()) / 1000.0), "unit": UNIT,
-               "h2d_bytes_per_step": 3 * w * h * 4 * world, "d2h_bytes_per_step": 16 * world}
+        e2e = {"value": world * V * args.steps / (float(ms2.item()) / 1000.0), "unit": UNIT,
+               "h2d_bytes_per_step": 3 * w * h * 4 * world * V, "d2h_bytes_per_step": 16 * world}
 
     # ---- render-only throughput (the metric's "render frames/s"): same scene and cameras,
     # each rank renders its own frames, device-timed, max over ranks --------------------------
@@ -699,7 +710,8 @@ def main() -> None:
     rbl, rco = count_work(trainer.gaussians, cams, render_cams, trainer.tiling, trainer.render_options,
                           rb, trainer.render_outputs)
     avg = lambda pr, k: pr[k][1] / max(pr[k][0], 1) if k in pr else None
-    train_rates = raster_rates(tb / args.steps, tc / args.steps, avg(prof, "raster"), avg(prof, "bwd_raster"))
+    train_rates = raster_rates(tb / (args.steps * V), tc / (args.steps * V), avg(prof, "raster"),
+                               avg(prof, "bwd_raster"))
     render_rates = raster_rates(rbl / args.steps, rco / args.steps, avg(rprof, "raster"), None)
     render_fps["forward_blend"] = render_rates.get("forward")
     render_fps["blends_per_frame"] = rbl / args.steps
@@ -714,6 +726,8 @@ def main() -> None:
     for name, (cnt, tot) in prof.items():
         av = tot / max(cnt, 1)
         b = stage_bytes(name, F, D, gv.n, w, h, passes, world, factored, til.nb_tiles)
+        if b and name not in ("adam", "adam_dense"):
+            b *= V  # every view of a step runs the render and backward stages
         b = b * args.steps / cnt if b and cnt else b  # per launch (chunked stages: a share)
         stages[name] = {"launches": cnt, "avg_ms": round(av, 4),
                         "share": round(tot / max(sum(t for _, t in prof.values()), 1e-9), 4),
@@ -721,6 +735,8 @@ def main() -> None:
     dominant = max(prof.items(), key=lambda kv: kv[1][1])[0]
     dom = stages[dominant]
     dom_bytes = stage_bytes(dominant, F, D, gv.n, w, h, passes, world, factored, til.nb_tiles)
+    if dom_bytes and dominant not in ("adam", "adam_dense"):
+        dom_bytes *= V
     dom_bytes = dom_bytes * args.steps / prof[dominant][0] if dom_bytes else dom_bytes
     traffic = (round(NCU_TRAFFIC_FRACTION[dominant] * dom_bytes / 1e9, 4)
                if dominant in NCU_TRAFFIC_FRACTION and dom_bytes else None)
@@ -730,9 +746,9 @@ def main() -> None:
         roofline = {"bound": "fp32-issue", "kernel": part["kernel"], "achieved": part["fp32_Tops"],
                     "peak": round(fp32 / 1e12, 2), "peak_source": fp32_src, "unit": "TFLOP/s",
                     "frac": part["fp32_frac"],
-                    "work": (f"{BWD_OPS_PER_PAIR:.0f} FP32 ops x {tc / args.steps:.0f} contributing "
+                    "work": (f"{BWD_OPS_PER_PAIR:.0f} FP32 ops x {tc / (args.steps * V):.0f} contributing "
                              f"(pixel, Gaussian) pairs per launch" if dominant == "bwd_raster" else
-                             f"{FWD_OPS_PER_BLEND:.0f} FP32 ops x {tb / args.steps:.0f} blends per launch"),
+                             f"{FWD_OPS_PER_BLEND:.0f} FP32 ops x {tb / (args.steps * V):.0f} blends per launch"),
                     "avg_ms": dom["avg_ms"], "traffic": traffic, "traffic_unit": "GB per launch",
                     "hbm_frac": round(dom["alg_GBps"] / peak, 4) if dom["alg_GBps"] else None,
                     "hbm_peak": peak, "hbm_peak_source": peak_kind}
@@ -775,8 +791,8 @@ def main() -> None:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": workload_config(world, w, h, gv.n),
+            "scaling": "strong" if args.global_batch else "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": workload_config(world, w, h, gv.n, V),
             "workload_stats": {"filtered_F": F, "duplicates_D": D, "tiles": [til.tile_width, til.tile_height],
                                **({"dp_exchange": args.dp_exchange, "dp_chunks": trainer.chunks}
                                   if world > 1 else {})},
@@ -790,9 +806,10 @@ def main() -> None:
         dist.destroy_process_group()
 
 
-def workload_config(world: int, w: int, h: int, n: int) -> dict:
+def workload_config(world: int, w: int, h: int, n: int, views: int = 1) -> dict:
     """The workload's config, identical in both arms (the reference arm times the same one)."""
-    return {"workload": WORKLOAD, "global_batch": world, "views_per_gpu": 1, "resolution": [w, h],
+    return {"workload": WORKLOAD if views == 1 else WORKLOAD.replace("1 view per GPU", f"{views} views per GPU"),
+            "global_batch": world * views, "views_per_gpu": views, "resolution": [w, h],
             "n_gaussians": n, "parallelism": f"dp{world}" if world > 1 else "single",
             "l2": "inputs larger than L2 (2.1 GB params+moments), no flush"}
 

@@ -55,6 +55,10 @@ typedef struct CUstream_st* gs3d_stream_t; /* ABI-compatible with cudaStream_t *
                                      (the reference reads coefficient 15: sh.jl:249)     */
 #define GS3D_BACKWARD_SKIP_SH_GRADS 2u /* leave sh_coeffs_grads unwritten: for an update by
                                      gs3d_adam_step_rebuild_sh, which recomputes them      */
+#define GS3D_BACKWARD_ACCUMULATE_ROWS 4u /* the projection-backward entry points that write
+                                     dense or geometry rows add to the rows (several views
+                                     per step) instead of overwriting them; colour rows are
+                                     per view and always written                          */
 
 /* ---- POD parameter structs ---------------------------------------------------------- */
 

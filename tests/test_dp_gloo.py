@@ -44,11 +44,19 @@ def test_chunk_ownership_partitions_the_gaussians():
 
 
 def test_views_of_a_step_are_distinct():
+    """The world x V views of a step are distinct cameras (batches up to #cameras), and
+    consecutive steps walk the shared permutation without gaps."""
     perm = np.random.default_rng(0).permutation(256)
-    for world in (2, 4, 8):
-        for step in range(100):
-            views = {view_index(step, r, world, perm, 256) for r in range(world)}
-            assert len(views) == world
+    for world in (1, 2, 4, 8):
+        for V in (1, 4, 8, 16, 32):
+            if world * V > 256:
+                continue
+            seen = []
+            for step in range(300):
+                views = [view_index(step, r, world, perm, 256, V, v) for r in range(world) for v in range(V)]
+                assert len(set(views)) == world * V
+                seen.extend(views)
+            assert seen[:256] == [int(x) for x in perm] or world * V * 300 < 256
 
 
 def _free_port() -> int:
@@ -107,7 +115,7 @@ def test_sharded_collectives_on_padded_storage(world):
         assert ok_rs is True and ok_ag is True, (rank, ok_rs, ok_ag)
 
 
-def _factored_worker(rank, world, port, q):
+def _factored_worker(rank, world, port, q, views=1):
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
         dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -117,38 +125,43 @@ def _factored_worker(rank, world, port, q):
         ar = torch.arange(n, dtype=torch.float32)
         geom = torch.zeros((rows, GEOM_ROW))
         geom[:n] = (ar[:, None] * GEOM_ROW + torch.arange(GEOM_ROW)) * (rank + 1)
-        colour = torch.zeros((rows, COLOUR_ROW))
-        colour[:n] = ar[:, None] * 10 + torch.arange(COLOUR_ROW) + 1000 * rank
+        # one colour row per view (views == 1: the (rows, COLOUR_ROW) single-view layout)
+        colour = torch.zeros((views, rows, COLOUR_ROW))
+        for v in range(views):
+            colour[v, :n] = ar[:, None] * 10 + torch.arange(COLOUR_ROW) + 1000 * rank + 100000 * v
         total = sum(r + 1 for r in range(world))
         want_geom = (ar[:, None] * GEOM_ROW + torch.arange(GEOM_ROW)) * total
         ok = True
         for c in range(CHUNKS):
-            recv = torch.full((world, S, COLOUR_ROW), -7.0)
-            for w in exchange_factored_chunk(geom, colour, recv, c, S, C_, rank, in_place=False):
+            recv = torch.full((views, world, S, COLOUR_ROW), -7.0)
+            for w in exchange_factored_chunk(geom, colour[0] if views == 1 else colour,
+                                             recv[0] if views == 1 else recv, c, S, C_, rank,
+                                             in_place=False):
                 w.wait()
             lo = c * C_ + rank * S
             hi = min(lo + S, n)
             if lo < hi:
                 ok = ok and torch.equal(geom[lo:hi], want_geom[lo:hi])
-                for src in range(world):  # slot src: rank src's colour rows of this sub-range
-                    want = ar[lo:hi, None] * 10 + torch.arange(COLOUR_ROW) + 1000 * src
-                    ok = ok and torch.equal(recv[src, : hi - lo], want)
-                    ok = ok and bool(torch.all(recv[src, hi - lo:] == 0))
+                for v in range(views):
+                    for src in range(world):  # slot (v, src): rank src's view-v rows of this range
+                        want = ar[lo:hi, None] * 10 + torch.arange(COLOUR_ROW) + 1000 * src + 100000 * v
+                        ok = ok and torch.equal(recv[v, src, : hi - lo], want)
+                        ok = ok and bool(torch.all(recv[v, src, hi - lo:] == 0))
         q.put((rank, ok))
         dist.destroy_process_group()
     except Exception as e:  # report instead of hanging the parent
         q.put((rank, repr(e)))
 
 
-@pytest.mark.parametrize("world", [2, 3])
-def test_factored_exchange_on_padded_storage(world):
+@pytest.mark.parametrize("world, views", [(2, 1), (3, 1), (2, 3)])
+def test_factored_exchange_on_padded_storage(world, views):
     """Geometry rows summed into each owner's sub-range; every view's colour rows of that
-    sub-range delivered to the owner in rank order (the order the owner rebuilds the SH
-    gradients in); padding rows arrive as zeros."""
+    sub-range delivered to the owner in (view, rank) order (the order the owner rebuilds the
+    SH gradients in); padding rows arrive as zeros. views > 1: several views per rank."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_factored_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_factored_worker, args=(r, world, port, q, views)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=120) for _ in range(world)]

@@ -4,7 +4,7 @@ import pytest
 import torch
 
 import gs3d
-from gs3d import RenderOptions, Tiling, _abi
+from gs3d import RenderBuffers, RenderOptions, RenderOutputs, Tiling, _abi
 from gs3d import adc as adc_mod
 from gs3d.loss import LossComputer
 from gs3d.optimizer import AdamMoments, bias_corrections
@@ -276,3 +276,58 @@ def test_checkpoint_resume_follows_the_uninterrupted_run(cuda, tmp_path):
     # Gaussian may go either way between two runs
     assert abs(t1.gaussians.n - t2.gaussians.n) <= max(2, t1.gaussians.n // 1000)
     assert torch.allclose(torch.stack(run1), torch.stack(run2), rtol=1e-4, atol=0)
+
+
+@pytest.mark.parametrize("factored", [False, True])
+def test_multi_view_step_equals_summed_views(cuda, factored):
+    """views_per_rank = 3 on one rank (a batch of three views per step): the update equals the
+    dense update of the three views' dense rows summed in view order, bit for bit, and the step
+    returns the mean of the three views' losses. Dense rows: the projection backward adds the
+    later views into the first view's rows (GS3D_BACKWARD_ACCUMULATE_ROWS); factored rows: the
+    geometry rows add up the same way and the update rebuilds the SH gradients from the three
+    colour rows."""
+    import ctypes as C
+
+    from gs3d.backward import FilteredGaussiansGradients, backward_dense
+    from gs3d.dp import DataParallelTrainer, view_index
+    from gs3d.optimizer import AdamOptimizer
+    from gs3d.training import annealed_means_lr
+    gv = synthetic_gaussians(SceneSpec(16_384, "uniform:1", -4.0, 0.5), 9)
+    cams = [look_at_camera(256, 256, 60.0, p)
+            for p in ((0, 0, 3), (0.5, 0.2, 2.8), (-0.4, 0.3, 2.9), (0.2, -0.5, 3.1))]
+    targets = [target_image(256, 256, 300 + i, cuda) for i in range(len(cams))]
+    ro = RenderOptions.for_camera(cams[0], 3)
+    til = Tiling.for_camera(cams[0])
+    opts = TrainingOptions(scene_radius=3.3)
+    t = DataParallelTrainer(gv.to(cuda), cams, targets, ro, til, opts, seed=7, factored=factored,
+                            views_per_rank=3)
+    t.iteration_nb = 3000
+    views = [view_index(0, 0, 1, t.perm, len(cams), 3, v) for v in range(3)]
+    assert len(set(views)) == 3
+    loss = t.training_step().clone()
+
+    g = gv.to(cuda)
+    n = g.n
+    out = RenderOutputs.create(256, 256, cuda)
+    buf = RenderBuffers.create(n, til.nb_tiles, cuda)
+    lc = LossComputer(256, 256, cuda, opts.loss_dssim_vs_L1_weight)
+    grad = torch.empty((256, 256, 3), dtype=torch.float32, device=cuda)
+    fg = FilteredGaussiansGradients.create(n, 3, cuda)
+    total, losses = None, []
+    for i in views:
+        gs3d.render(out, g, cams[i], til, ro, buf)
+        losses.append(lc(out.rgb, targets[i], grad).clone())
+        d = backward_dense(fg, grad, out, g, cams[i], til, ro, buf,
+                           torch.empty((n, 60), dtype=torch.float32, device=cuda))
+        total = d.clone() if total is None else total + d
+    adam = AdamOptimizer(g, opts.learning_rates())
+    adam.lrs.means = annealed_means_lr(3001, opts)
+    gc, mc, pc = g.to_c(), adam.moments.to_c(), adam.params_c(3)
+    _abi.check(_abi.lib().gs3d_adam_step_dense(C.byref(gc), C.byref(mc), C.c_void_p(total.data_ptr()),
+                                               C.byref(pc), None))
+    torch.cuda.synchronize()
+    for x, y in zip(t.gaussians.tensors(), g.tensors()):
+        assert torch.equal(x[:n], y)
+    want = (losses[0] + losses[1] + losses[2]) / 3
+    assert torch.equal(loss[:3], want[:3])
+    assert t.optimizer.update_count == 1

@@ -60,6 +60,7 @@ struct BProjArgs {
     int sh_grad_stride;
     int fix_sh16;
     int skip_sh;  // GS3D_BACKWARD_SKIP_SH_GRADS: no SH gradients (F-compact output only)
+    int accumulate;  // GS3D_BACKWARD_ACCUMULATE_ROWS: add into dense / geometry rows
     // NULL, or dense gradient rows indexed by Gaussian (kDenseRow floats, layout in gs3d.h):
     // the 3D gradients then go to row gidx - g_begin instead of the F-compact arrays above
     float* dense;
@@ -119,7 +120,7 @@ __global__ void __launch_bounds__(128, GS3D_BWDPROJ_MINB) k_bwd_project(const BP
         const float og = a.opacity_g[f];
         const float opf = opt.use_antialiasing ? og * opac * (1.0f - orig_op) : og * opac * (1.0f - opac);
         if (drow) {
-            drow[kDOpacity] = opf;
+            drow[kDOpacity] = a.accumulate ? drow[kDOpacity] + opf : opf;
             drow[kDTouched] = 1.0f;
         } else {
             a.opf_g[f] = opf;
@@ -310,9 +311,10 @@ __global__ void __launch_bounds__(128, GS3D_BWDPROJ_MINB) k_bwd_project(const BP
             m3[i] = m3[i] + inv_vn * w;
         }
         float* const m3out = drow ? drow + kDMean : a.mean3d_g + 3 * (size_t)f;
-        m3out[0] = m3[0];
-        m3out[1] = m3[1];
-        m3out[2] = m3[2];
+        const bool acc = drow && a.accumulate;
+        m3out[0] = acc ? m3out[0] + m3[0] : m3[0];
+        m3out[1] = acc ? m3out[1] + m3[1] : m3[1];
+        m3out[2] = acc ? m3out[2] + m3[2] : m3[2];
 
         // scaling features: v gradient = Transposed_dsigma_dv(J) * cg
         float vg[6];
@@ -334,7 +336,8 @@ __global__ void __launch_bounds__(128, GS3D_BWDPROJ_MINB) k_bwd_project(const BP
             float tt = 0.0f;
 #pragma unroll
             for (int i = 0; i < 6; ++i) tt = tt + (s[j] * R[L3I[i]][j] * R[L3J[i]][j]) * vg[i];
-            (drow ? drow + kDScale : a.scale_g + 3 * (size_t)f)[j] = (2.0f * tt) * s[j];
+            float* const so = (drow ? drow + kDScale : a.scale_g + 3 * (size_t)f) + j;
+            *so = acc ? *so + (2.0f * tt) * s[j] : (2.0f * tt) * s[j];
         }
         // rotation features
         {
@@ -377,7 +380,8 @@ __global__ void __launch_bounds__(128, GS3D_BWDPROJ_MINB) k_bwd_project(const BP
                     const float Nij = i == j ? 1.0f - nq[i] * nq[i] : -nq[i < j ? i : j] * nq[i < j ? j : i];
                     w = w + Nij * nqg[j];
                 }
-                (drow ? drow + kDRot : a.rot_g + 4 * (size_t)f)[i] = inv_qn * w;
+                float* const ro = (drow ? drow + kDRot : a.rot_g + 4 * (size_t)f) + i;
+                *ro = acc ? *ro + inv_qn * w : inv_qn * w;
             }
         }
         // SH coefficients (compute_sh_coeffs_grad!, backward_core.jl:936-964), staged; or
@@ -408,7 +412,9 @@ __global__ void __launch_bounds__(128, GS3D_BWDPROJ_MINB) k_bwd_project(const BP
               const int grow = __shfl_sync(0xffffffffu, rel, row);
               if (row >= nrows || grow < 0) continue;
               const int c = rem / MAXO, k = rem - c * MAXO;
-              a.dense[(size_t)grow * kDenseRow + (size_t)(c * 16 + k)] = warp_stage[row * (NSH + 1) + rem];
+              float* const d = a.dense + (size_t)grow * kDenseRow + (size_t)(c * 16 + k);
+              const float val = warp_stage[row * (NSH + 1) + rem];
+              *d = a.accumulate ? *d + val : val;
           }
       } else {
           for (int e = lane; e < nrows * NSH; e += 32) {
@@ -504,6 +510,7 @@ int backward_impl(const gs3d_fgradients* fg, const float* rgb_grad,
     p.sh_grad_stride = (fg->sh_degree + 1) * (fg->sh_degree + 1);
     p.fix_sh16 = (flags & GS3D_BACKWARD_FIX_SH16) ? 1 : 0;
     p.skip_sh = (compact_out && (flags & GS3D_BACKWARD_SKIP_SH_GRADS)) ? 1 : 0;
+    p.accumulate = (!compact_out && (flags & GS3D_BACKWARD_ACCUMULATE_ROWS)) ? 1 : 0;
     p.dense = dense;
     p.geom = geom;
     p.colour = reinterpret_cast<float4*>(colour);

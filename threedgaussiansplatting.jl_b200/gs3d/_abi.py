@@ -22,6 +22,7 @@ GS3D_RENDER_REFERENCE_ORDER = 2
 GS3D_RENDER_NO_CONTRIB_MASKS = 4
 GS3D_BACKWARD_FIX_SH16 = 1
 GS3D_BACKWARD_SKIP_SH_GRADS = 2
+GS3D_BACKWARD_ACCUMULATE_ROWS = 4
 GS3D_DENSE_ROW = 60
 GS3D_GEOM_ROW = 12
 GS3D_COLOUR_ROW = 4

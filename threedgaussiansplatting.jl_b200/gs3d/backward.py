@@ -120,14 +120,16 @@ def backward_project_dense(fgradients: FilteredGaussiansGradients, gaussians: Ga
                            camera: PinholeCamera, tiling: Tiling, options: RenderOptions,
                            buffers: RenderBuffers, dense_rows: torch.Tensor, g_begin: int,
                            g_end: int, fix_sh16: bool = False,
-                           stream: torch.cuda.Stream | None = None) -> None:
+                           stream: torch.cuda.Stream | None = None, accumulate: bool = False) -> None:
     """Second phase: 3D gradients of the filtered Gaussians with index in [g_begin, g_end)
-    into row gidx - g_begin of `dense_rows` (a view starting at row g_begin; not zeroed here)."""
+    into row gidx - g_begin of `dense_rows` (a view starting at row g_begin; not zeroed here).
+    `accumulate`: add to the rows (another view of the same step) instead of overwriting."""
     assert dense_rows.is_contiguous() and dense_rows.dtype == torch.float32
     lib = _abi.lib()
     args = [fgradients.to_c(), gaussians.to_c(), camera.to_c(), tiling.to_c(), options.to_c(),
             buffers.to_c()]
-    flags = _abi.GS3D_BACKWARD_FIX_SH16 if fix_sh16 else 0
+    flags = (_abi.GS3D_BACKWARD_FIX_SH16 if fix_sh16 else 0) | \
+        (_abi.GS3D_BACKWARD_ACCUMULATE_ROWS if accumulate else 0)
     _abi.check(lib.gs3d_backward_project_dense(
         C.byref(args[0]), C.byref(args[1]), C.byref(args[2]), C.byref(args[3]), C.byref(args[4]),
         C.byref(args[5]), flags, C.c_void_p(dense_rows.data_ptr()), int(g_begin), int(g_end),
@@ -163,15 +165,19 @@ def backward_project_factored(fgradients: FilteredGaussiansGradients, gaussians:
                               buffers: RenderBuffers, geom_rows: torch.Tensor,
                               colour_rows: torch.Tensor, g_begin: int, g_end: int,
                               fix_sh16: bool = False,
-                              stream: torch.cuda.Stream | None = None) -> None:
+                              stream: torch.cuda.Stream | None = None,
+                              accumulate: bool = False) -> None:
     """backward_project_dense() into factored rows: geometry row (12 floats) and colour row
-    (3 colour gradients + live flags) gidx - g_begin of views starting at row g_begin."""
+    (3 colour gradients + live flags) gidx - g_begin of views starting at row g_begin.
+    `accumulate`: add to the geometry rows (another view of the same step); the colour rows are
+    this view's own."""
     for t in (geom_rows, colour_rows):
         assert t.is_contiguous() and t.dtype == torch.float32
     lib = _abi.lib()
     args = [fgradients.to_c(), gaussians.to_c(), camera.to_c(), tiling.to_c(), options.to_c(),
             buffers.to_c()]
-    flags = _abi.GS3D_BACKWARD_FIX_SH16 if fix_sh16 else 0
+    flags = (_abi.GS3D_BACKWARD_FIX_SH16 if fix_sh16 else 0) | \
+        (_abi.GS3D_BACKWARD_ACCUMULATE_ROWS if accumulate else 0)
     _abi.check(lib.gs3d_backward_project_factored(
         C.byref(args[0]), C.byref(args[1]), C.byref(args[2]), C.byref(args[3]), C.byref(args[4]),
         C.byref(args[5]), flags, C.c_void_p(geom_rows.data_ptr()),

@@ -17,7 +17,12 @@ decisions and the full update, as the reference retargets fgidx_to_gidx. With on
 is the reference's sparse update. `optimizer_step="replicated"` instead all-reduces each chunk's
 rows and lets every rank apply the full update (no parameter exchange; measured slower).
 Views: a permutation of the cameras drawn from a seed shared by all ranks; at step k rank r
-takes entry (k * world + r) mod #cameras.
+takes entries ((k * world + r) * V + v) mod #cameras, v < V, for V views per rank
+(`views_per_rank`; a global batch of world * V views). Every view is rendered and
+back-propagated in turn; the rows of a step carry the sum over its views (the first view
+writes them, later views add: GS3D_BACKWARD_ACCUMULATE_ROWS; factored rows keep one colour row
+per view), the last view's projection backward is the one pipelined with the exchange, and the
+update is applied once per step.
 """
 from __future__ import annotations
 
@@ -39,10 +44,10 @@ COLOUR_ROW = _abi.GS3D_COLOUR_ROW
 CHUNKS = 2
 
 
-def view_index(step: int, rank: int, world: int, perm, ncams: int) -> int:
-    """Camera of rank `rank` at (0-based) step `step`: entry (step * world + rank) of the
-    shared permutation, re-drawn every #cameras views."""
-    k = step * world + rank
+def view_index(step: int, rank: int, world: int, perm, ncams: int, views: int = 1, v: int = 0) -> int:
+    """Camera of view v of rank `rank` at (0-based) step `step`: entry
+    ((step * world + rank) * views + v) of the shared permutation, taken modulo #cameras."""
+    k = (step * world + rank) * views + v
     return int(perm[k % ncams])
 
 
@@ -61,18 +66,23 @@ def chunk_layout(n: int, world: int, chunks: int) -> tuple[int, int]:
 def exchange_factored_chunk(geom: torch.Tensor, colour: torch.Tensor, colour_recv: torch.Tensor,
                             c: int, S: int, C_: int, rank: int, group=None, in_place: bool = True):
     """Chunk c of the factored rows: reduce-scatter of its geometry rows into the owners'
-    sub-ranges (in place) and all-to-all of its colour rows: rank p receives, in slot q of
-    `colour_recv` ((world, S, COLOUR_ROW)), rank q's colour rows of p's sub-range. Returns the
-    two async works. `in_place=False` reduces from a copy (for backends without in-place
-    reduce-scatter)."""
+    sub-ranges (in place) and, per view v, all-to-all of its colour rows: rank p receives, in
+    slot (v, q) of `colour_recv` ((V, world, S, COLOUR_ROW)), rank q's colour rows of view v for
+    p's sub-range. `colour` is (V, rows, COLOUR_ROW) (or (rows, COLOUR_ROW) for one view).
+    Returns the async works. `in_place=False` reduces from a copy (for backends without
+    in-place reduce-scatter)."""
     gflat = geom[c * C_:(c + 1) * C_].reshape(-1)
     per = S * GEOM_ROW
-    w1 = dist.reduce_scatter_tensor(gflat[rank * per:(rank + 1) * per],
-                                    gflat if in_place else gflat.clone(),
-                                    op=dist.ReduceOp.SUM, group=group, async_op=True)
-    w2 = dist.all_to_all_single(colour_recv.reshape(-1), colour[c * C_:(c + 1) * C_].reshape(-1),
-                                group=group, async_op=True)
-    return (w1, w2)
+    works = [dist.reduce_scatter_tensor(gflat[rank * per:(rank + 1) * per],
+                                        gflat if in_place else gflat.clone(),
+                                        op=dist.ReduceOp.SUM, group=group, async_op=True)]
+    col = colour if colour.dim() == 3 else colour.unsqueeze(0)
+    recv = colour_recv if colour_recv.dim() == 4 else colour_recv.unsqueeze(0)
+    for v in range(col.shape[0]):
+        works.append(dist.all_to_all_single(recv[v].reshape(-1),
+                                            col[v, c * C_:(c + 1) * C_].reshape(-1),
+                                            group=group, async_op=True))
+    return tuple(works)
 
 
 class DataParallelTrainer(Trainer):
@@ -85,8 +95,12 @@ class DataParallelTrainer(Trainer):
     16 floats per Gaussian cross the links instead of 60."""
 
     def __init__(self, *args, group=None, optimizer_step: str = "sharded", chunks: int | None = None,
-                 factored: bool = True, **kw):
+                 factored: bool = True, views_per_rank: int = 1, **kw):
         super().__init__(*args, **kw)
+        if views_per_rank < 1:
+            raise ValueError(f"views_per_rank {views_per_rank} < 1")
+        self.views = int(views_per_rank)
+        self._vi = 0  # view of the current step being processed
         if optimizer_step not in ("sharded", "replicated"):
             raise ValueError(f"optimizer_step {optimizer_step!r}")
         self.optimizer_step = optimizer_step
@@ -143,21 +157,22 @@ class DataParallelTrainer(Trainer):
             f = dict(dtype=torch.float32, device=self.device)
             if self.geom is None or self.geom.shape[0] != rows:
                 self.geom = torch.zeros((rows, GEOM_ROW), **f)
-                self.colour = torch.zeros((rows, COLOUR_ROW), **f)
-            if self.world > 1 and (self.colour_recv is None or self.colour_recv.shape[2] != S):
-                self.colour_recv = torch.empty((self.chunks, self.world, S, COLOUR_ROW), **f)
+                self.colour = torch.zeros((self.views, rows, COLOUR_ROW), **f)
+            if self.world > 1 and (self.colour_recv is None or self.colour_recv.shape[3] != S):
+                self.colour_recv = torch.empty((self.chunks, self.views, self.world, S, COLOUR_ROW), **f)
 
     def _use_factored(self, in_adc: bool) -> bool:
         return (self.factored and self.optimizer_step == "sharded" and not in_adc and
-                self.gaussians.sh_degree == 3 and self.world <= _abi.GS3D_MAX_FACTORED_VIEWS)
+                self.gaussians.sh_degree == 3 and
+                self.world * self.views <= _abi.GS3D_MAX_FACTORED_VIEWS)
 
     def _view_positions(self):
-        """Camera positions (float32, rank order) of this step's views: the colour rows of
-        rank p's view arrive in slot p of the all-to-all."""
+        """Camera positions (float32) of this step's views in the order of the colour-row slots
+        the update reads: view v of rank p at slot v * world + p."""
         import numpy as np
         pos = np.stack([self.cameras[view_index(self.step_index, p, self.world, self.perm,
-                                                len(self.cameras))].position
-                        for p in range(self.world)]).astype(np.float32)
+                                                len(self.cameras), self.views, v)].position
+                        for v in range(self.views) for p in range(self.world)]).astype(np.float32)
         return np.ascontiguousarray(pos)
 
     def _exchange_factored(self, c: int, S: int, C_: int):
@@ -184,34 +199,19 @@ class DataParallelTrainer(Trainer):
             dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
 
     def current_camera_index(self) -> int:
-        return view_index(self.step_index, self.rank, self.world, self.perm, len(self.cameras))
+        return view_index(self.step_index, self.rank, self.world, self.perm, len(self.cameras),
+                          self.views, self._vi)
 
     def peek_camera_index(self, ahead: int) -> int:
-        return view_index(self.step_index + ahead, self.rank, self.world, self.perm, len(self.cameras))
+        """Camera of the view `ahead` views after the current one (of this rank)."""
+        k = self._vi + ahead
+        return view_index(self.step_index + k // self.views, self.rank, self.world, self.perm,
+                          len(self.cameras), self.views, k % self.views)
 
     # -- one step ---------------------------------------------------------------------------
-    def training_step(self) -> torch.Tensor:
-        lib = _abi.lib()
-        self.iteration_nb += 1
-        self.maybe_increase_sh_degree()
-        self._ensure_padded()
-        compute = torch.cuda.current_stream(self.device)
-        o = self.options
-        in_adc = self.densifies_this_iteration()
-        factored = self._use_factored(in_adc)
-        # zero the rows on a side stream while the forward runs
-        if self._side is None:
-            self._side = torch.cuda.Stream(self.device)
-        self._side.wait_stream(compute)
-        with torch.cuda.stream(self._side):
-            if factored:
-                self.geom.zero_()
-                self.colour.zero_()
-            else:
-                self.dense.zero_()
-        zeroed = torch.cuda.Event()
-        zeroed.record(self._side)
-
+    def _render_view(self, compute):
+        """Render the current view, its loss and its 2D gradients (backward_raster); returns
+        (camera, loss tensor)."""
         idx = self.current_camera_index()
         cam = self.cameras[idx]
         rb = self.render_buffers
@@ -224,13 +224,64 @@ class DataParallelTrainer(Trainer):
         self.prefetch_target()
         backward_raster(self.fgradients, self.rgb_image_grad, self.render_outputs, self.gaussians,
                         cam, self.tiling, self.render_options, rb)
-        compute.wait_event(zeroed)
+        return cam, loss
+
+    def training_step(self) -> torch.Tensor:
+        lib = _abi.lib()
+        self.iteration_nb += 1
+        self.maybe_increase_sh_degree()
+        self._ensure_padded()
+        compute = torch.cuda.current_stream(self.device)
+        o = self.options
+        in_adc = self.densifies_this_iteration()
+        factored = self._use_factored(in_adc)
+        V = self.views
+        # zero the rows on a side stream while the first forward runs
+        if self._side is None:
+            self._side = torch.cuda.Stream(self.device)
+        self._side.wait_stream(compute)
+        with torch.cuda.stream(self._side):
+            if factored:
+                self.geom.zero_()
+                self.colour.zero_()
+            else:
+                self.dense.zero_()
+        zeroed = torch.cuda.Event()
+        zeroed.record(self._side)
+
         stream = C.c_void_p(_stream_handle(None))
         n = self.gaussians.n
         S, C_ = chunk_layout(n, self.world, self.chunks)
+        rb = self.render_buffers
+        track_adc = self.iteration_nb <= o.adc_final_iteration_nb
+        loss_sum = None
+        # views 0 .. V-2: rows of every Gaussian at once, added up (no exchange yet)
+        for v in range(V - 1):
+            self._vi = v
+            cam, loss = self._render_view(compute)
+            loss_sum = loss.clone() if loss_sum is None else loss_sum.add_(loss)
+            if v == 0:
+                compute.wait_event(zeroed)
+            if factored:
+                backward_project_factored(self.fgradients, self.gaussians, cam, self.tiling,
+                                          self.render_options, rb, self.geom, self.colour[v], 0, n,
+                                          accumulate=v > 0)
+            else:
+                backward_project_dense(self.fgradients, self.gaussians, cam, self.tiling,
+                                       self.render_options, rb, self.dense, 0, n, accumulate=v > 0)
+            if track_adc or in_adc:
+                adc_mod.adc_stats(self.adc_buffers, self.fgradients, rb.fgidx_to_gidx, rb.device_counts,
+                                  self.width, self.height)
+        # the last view: its projection backward pipelined with the exchange, chunk by chunk
+        self._vi = V - 1
+        acc = V > 1
+        cam, loss = self._render_view(compute)
+        loss_sum = loss if loss_sum is None else loss_sum.add_(loss)
+        if V == 1:
+            compute.wait_event(zeroed)
         if in_adc:
             backward_project_dense(self.fgradients, self.gaussians, cam, self.tiling,
-                                   self.render_options, rb, self.dense, 0, n)
+                                   self.render_options, rb, self.dense, 0, n, accumulate=acc)
             adc_mod.adc_stats(self.adc_buffers, self.fgradients, rb.fgidx_to_gidx, rb.device_counts,
                               self.width, self.height)
             self.update_learning_rates()
@@ -252,11 +303,12 @@ class DataParallelTrainer(Trainer):
                 lo, hi = c * C_, min((c + 1) * C_, n)
                 if lo < hi:
                     backward_project_dense(self.fgradients, self.gaussians, cam, self.tiling,
-                                           self.render_options, rb, self.dense[lo:], lo, hi)
+                                           self.render_options, rb, self.dense[lo:], lo, hi,
+                                           accumulate=acc)
                 if self.world > 1:
                     ar.append(dist.all_reduce(self.dense[c * C_:(c + 1) * C_], op=dist.ReduceOp.SUM,
                                               group=self.group, async_op=True))
-            if self.iteration_nb <= o.adc_final_iteration_nb:
+            if track_adc:
                 adc_mod.adc_stats(self.adc_buffers, self.fgradients, rb.fgidx_to_gidx, rb.device_counts,
                                   self.width, self.height)
             self.update_learning_rates()
@@ -279,20 +331,21 @@ class DataParallelTrainer(Trainer):
                     if lo < hi:
                         backward_project_factored(self.fgradients, self.gaussians, cam, self.tiling,
                                                   self.render_options, rb, self.geom[lo:],
-                                                  self.colour[lo:], lo, hi)
+                                                  self.colour[V - 1, lo:], lo, hi, accumulate=acc)
                     if self.world > 1:
                         rs.append(self._exchange_factored(c, S, C_))
                     continue
                 if lo < hi:
                     backward_project_dense(self.fgradients, self.gaussians, cam, self.tiling,
-                                           self.render_options, rb, self.dense[lo:], lo, hi)
+                                           self.render_options, rb, self.dense[lo:], lo, hi,
+                                           accumulate=acc)
                 if self.world > 1:
                     flat = self.dense[c * C_:(c + 1) * C_].reshape(-1)
                     per = S * DENSE_ROW
                     rs.append(dist.reduce_scatter_tensor(flat[self.rank * per:(self.rank + 1) * per], flat,
                                                          op=dist.ReduceOp.SUM, group=self.group,
                                                          async_op=True))
-            if self.iteration_nb <= o.adc_final_iteration_nb:
+            if track_adc:
                 adc_mod.adc_stats(self.adc_buffers, self.fgradients, rb.fgidx_to_gidx, rb.device_counts,
                                   self.width, self.height)
             self.update_learning_rates()
@@ -310,10 +363,13 @@ class DataParallelTrainer(Trainer):
                 hi = min(lo + S, n)
                 if factored:
                     if lo < hi:
-                        views = self.colour_recv[c] if self.world > 1 else self.colour[lo:]
+                        if self.world > 1:
+                            views, stride = self.colour_recv[c], S
+                        else:
+                            views, stride = self.colour[0, lo:], self.colour.shape[1]
                         _abi.check(lib.gs3d_adam_step_factored_range(
                             C.byref(g), C.byref(m), C.c_void_p(self.geom[lo:].data_ptr()),
-                            C.c_void_p(views.data_ptr()), self.world, S, pos_p, lo, hi,
+                            C.c_void_p(views.data_ptr()), self.world * V, stride, pos_p, lo, hi,
                             C.byref(params), stream))
                 elif lo < hi:
                     rows = self.dense[lo:]
@@ -329,8 +385,11 @@ class DataParallelTrainer(Trainer):
             self._ensure_padded()
         self.maybe_opacity_reset()
         self.step_index += 1
-        self.last_loss = loss
-        return loss
+        self._vi = 0
+        if V > 1:
+            loss_sum.div_(V)
+        self.last_loss = loss_sum
+        return loss_sum
 
     def _densify(self) -> None:
         o = self.options
