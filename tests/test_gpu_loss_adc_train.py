@@ -280,12 +280,15 @@ def test_checkpoint_resume_follows_the_uninterrupted_run(cuda, tmp_path):
 
 @pytest.mark.parametrize("factored", [False, True])
 def test_multi_view_step_equals_summed_views(cuda, factored):
-    """views_per_rank = 3 on one rank (a batch of three views per step): the update equals the
-    dense update of the three views' dense rows summed in view order, bit for bit, and the step
-    returns the mean of the three views' losses. Dense rows: the projection backward adds the
-    later views into the first view's rows (GS3D_BACKWARD_ACCUMULATE_ROWS); factored rows: the
-    geometry rows add up the same way and the update rebuilds the SH gradients from the three
-    colour rows."""
+    """views_per_rank = 3 on one rank (a batch of three views per step): the step's gradient rows
+    are the three views' dense rows summed, the update follows them, and the step returns the
+    mean of the three views' losses. Dense rows: the projection backward adds the later views
+    into the first view's rows (GS3D_BACKWARD_ACCUMULATE_ROWS); factored rows: the geometry rows
+    add up the same way and each view keeps its colour row. The 2D gradients are float-atomic
+    sums whose order differs between runs, so rows are compared within 1e-5 of their scale and
+    the parameters after the update mostly bit for bit (Adam's first step moves a parameter by
+    about its learning rate times the sign of its gradient, so a gradient that is zero up to
+    rounding may move either way)."""
     import ctypes as C
 
     from gs3d.backward import FilteredGaussiansGradients, backward_dense
@@ -313,13 +316,29 @@ def test_multi_view_step_equals_summed_views(cuda, factored):
     lc = LossComputer(256, 256, cuda, opts.loss_dssim_vs_L1_weight)
     grad = torch.empty((256, 256, 3), dtype=torch.float32, device=cuda)
     fg = FilteredGaussiansGradients.create(n, 3, cuda)
-    total, losses = None, []
+    total, losses, live = None, [], []
     for i in views:
         gs3d.render(out, g, cams[i], til, ro, buf)
         losses.append(lc(out.rgb, targets[i], grad).clone())
         d = backward_dense(fg, grad, out, g, cams[i], til, ro, buf,
                            torch.empty((n, 60), dtype=torch.float32, device=cuda))
+        live.append(d[:, 59] > 0)
         total = d.clone() if total is None else total + d
+    want = (losses[0] + losses[1] + losses[2]) / 3
+    assert torch.equal(loss[:3], want[:3])  # forward and loss are deterministic
+
+    def close(a, b):
+        scale = b.abs().amax(dim=0, keepdim=True).clamp_min(1e-30)
+        return bool(((a - b).abs() <= 1e-5 * scale).all())
+
+    if factored:
+        assert close(t.geom[:n, :11], total[:, 48:59])
+        assert torch.equal(t.geom[:n, 11] > 0, total[:, 59] > 0)
+        for v in range(3):
+            assert torch.equal(t.colour[v, :n, 3] > 0, live[v])
+    else:
+        assert close(t.dense[:n, :59], total[:, :59])
+        assert torch.equal(t.dense[:n, 59] > 0, total[:, 59] > 0)
     adam = AdamOptimizer(g, opts.learning_rates())
     adam.lrs.means = annealed_means_lr(3001, opts)
     gc, mc, pc = g.to_c(), adam.moments.to_c(), adam.params_c(3)
@@ -327,7 +346,6 @@ def test_multi_view_step_equals_summed_views(cuda, factored):
                                                C.byref(pc), None))
     torch.cuda.synchronize()
     for x, y in zip(t.gaussians.tensors(), g.tensors()):
-        assert torch.equal(x[:n], y)
-    want = (losses[0] + losses[1] + losses[2]) / 3
-    assert torch.equal(loss[:3], want[:3])
+        same = (x[:n] == y).float().mean().item()
+        assert same >= 0.999, same
     assert t.optimizer.update_count == 1
