@@ -191,6 +191,32 @@ def test_sort_pairs_dropin(cuda, n, bits):
     assert np.array_equal(ko, rk) and np.array_equal(vo, rv)
 
 
+@pytest.mark.parametrize("dist,n,bits", [("tiles", 2_000_000, 44), ("tiles", 700_001, 46),
+                                          ("one_bucket", 300_000, 40), ("low_ties", 500_000, 36),
+                                          ("random", 123_457, 33), ("random", 1_000_000, 46)])
+def test_sort_pairs_bucket_path(cuda, dist, n, bits):
+    """Key widths 33..46 take the bucket path (bits above 32 pick a bucket, each bucket sorted in
+    shared memory): render-like keys tile << 32 | depth bits, every key in one bucket (the
+    global-memory network), many equal low words (stability), random keys with bits above
+    highest_key_bit set (ignored by the order, kept in the output)."""
+    rng = np.random.default_rng(n + bits)
+    nb = 1 << (bits - 32)
+    if dist == "tiles":
+        tiles = rng.integers(1, nb, n)
+        depth = rng.uniform(0.2, 50.0, n).astype(np.float32).view(np.int32).astype(np.int64)
+        keys = (tiles.astype(np.int64) << 32) | depth
+    elif dist == "one_bucket":
+        keys = (np.int64(5) << 32) | rng.integers(0, 1 << 32, n, dtype=np.int64)
+    elif dist == "low_ties":
+        keys = (rng.integers(0, nb, n).astype(np.int64) << 32) | rng.integers(0, 50, n)
+    else:
+        keys = rng.integers(0, 1 << 62, n, dtype=np.int64)
+    vals = rng.permutation(n).astype(np.int32)
+    ko, vo = _sort_gpu(keys, vals, bits, cuda)
+    rk, rv = O.sort_pairs(keys, vals, bits)
+    assert np.array_equal(ko, rk) and np.array_equal(vo, rv)
+
+
 def _reference_sort_lib():
     """The reference's own CUB wrapper (deps/cub_sort_pairs/cub_sort_pairs_wrapper.cu),
     compiled from the reference checkout by oracle/build.py into oracle/_ref/."""

@@ -129,8 +129,12 @@ GS3D_API int gs3d_profile_report(char* buf, size_t len) {
 GS3D_API size_t determine_sort_pairs_temp_storage(const int64_t* keys_in, int64_t* keys_out,
                                                   const int32_t* values_in, int32_t* values_out,
                                                   int nb_items, int highest_key_bit) {
-    (void)keys_in; (void)keys_out; (void)values_in; (void)values_out; (void)highest_key_bit;
-    return radix_sort_workspace_bytes(nb_items > 0 ? nb_items : 1);
+    (void)keys_in; (void)keys_out; (void)values_in; (void)values_out;
+    const int64_t n = nb_items > 0 ? nb_items : 1;
+    size_t bytes = radix_sort_workspace_bytes(n);
+    if (bucket_sort_applies(n, highest_key_bit))
+        bytes = std::max(bytes, bucket_sort_workspace_bytes(n, highest_key_bit));
+    return bytes;
 }
 
 GS3D_API int gs3d_sort_pairs_async(void* temp_storage, size_t temp_storage_bytes,
@@ -141,6 +145,13 @@ GS3D_API int gs3d_sort_pairs_async(void* temp_storage, size_t temp_storage_bytes
     if (nb_items == 0) return GS3D_OK;
     if (!temp_storage || !keys_in || !keys_out || !values_in || !values_out)
         return invalid("NULL pointer");
+    // 33 .. 46 key bits (the reference's keys: 33 + floor(log2 #tiles)): bucket by the bits
+    // above 32, sort each bucket in shared memory; other widths: LSD radix sort
+    if (bucket_sort_applies(nb_items, highest_key_bit) &&
+        temp_storage_bytes >= bucket_sort_workspace_bytes(nb_items, highest_key_bit))
+        return bucket_sort_pairs(temp_storage, temp_storage_bytes, keys_in, keys_out, values_in,
+                                 values_out, nb_items, highest_key_bit,
+                                 reinterpret_cast<cudaStream_t>(stream));
     return radix_sort_pairs(temp_storage, temp_storage_bytes, keys_in, keys_out, values_in,
                             values_out, nb_items, nullptr, nb_items, highest_key_bit,
                             reinterpret_cast<cudaStream_t>(stream));

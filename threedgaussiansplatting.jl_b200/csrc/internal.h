@@ -31,6 +31,15 @@ int tile_sort_order(void* ws, const int32_t* counts, const int4* ranges, const f
                     const int32_t* tiles_end, int64_t* keys_scratch, int64_t* sorted_codes,
                     int32_t* sorted_vals, cudaStream_t stream);
 
+// Stable pair sort of n (int64 key, int32 value) pairs on bits [0, highest_key_bit) for
+// 32 < highest_key_bit <= 46 (bucket_sort_applies): the tile pipeline's histogram, scatter
+// and per-segment sort with bits [32, highest_key_bit) as the bucket (tile_sort.cu).
+bool bucket_sort_applies(int64_t n, int highest_key_bit);
+size_t bucket_sort_workspace_bytes(int64_t n, int highest_key_bit);
+int bucket_sort_pairs(void* ws, size_t ws_bytes, const int64_t* keys_in, int64_t* keys_out,
+                      const int32_t* vals_in, int32_t* vals_out, int64_t n, int highest_key_bit,
+                      cudaStream_t stream);
+
 // Device-wide scans over int32 with the length on the device (len_dev[0]) or on the host.
 size_t scan_workspace_bytes(int64_t capacity);
 // inclusive scan of in[0, len) into out; the total is written to total_dev[0].

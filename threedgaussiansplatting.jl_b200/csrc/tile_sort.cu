@@ -154,6 +154,59 @@ __global__ void __launch_bounds__(kHistThreads) k_tile_scatter(
     }
 }
 
+// ---- the generic stable pair sort (sort_pairs) on the same machinery -----------------------
+// Keys of highest_key_bit = 32 + B bits (1 <= B <= kMaxBucketBits): bits [32, 32 + B) pick one
+// of 2^B buckets, which play the tiles' part; inside a bucket the entries are sorted by
+// (bits [0, 32) of the key, input index), i.e. stably. Block b of kHistBlocks takes the items
+// [b chunk, (b + 1) chunk), chunk = ceil(n / kHistBlocks).
+constexpr int kMaxBucketBits = 14;
+
+__device__ __forceinline__ void item_chunk(int64_t n, int64_t& i0, int64_t& i1) {
+    const int64_t chunk = (n + kHistBlocks - 1) / kHistBlocks;
+    i0 = min(n, (int64_t)blockIdx.x * chunk);
+    i1 = min(n, i0 + chunk);
+}
+
+__global__ void __launch_bounds__(kHistThreads) k_key_hist(const int64_t* __restrict__ keys, int64_t n,
+                                                          int nb_buckets, int32_t* __restrict__ bcount,
+                                                          int32_t* __restrict__ counts) {
+    extern __shared__ int32_t hist[];
+    for (int i = threadIdx.x; i < nb_buckets; i += blockDim.x) hist[i] = 0;
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        counts[0] = 1;  // non-zero: the segment sort's "something to sort" test
+        counts[2] = 0;
+    }
+    __syncthreads();
+    int64_t i0, i1;
+    item_chunk(n, i0, i1);
+    const uint32_t bmask = (uint32_t)nb_buckets - 1u;
+    for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x)
+        atomicAdd(&hist[(uint32_t)((uint64_t)keys[i] >> 32) & bmask], 1);
+    __syncthreads();
+    int32_t* out = bcount + (size_t)blockIdx.x * nb_buckets;
+    for (int i = threadIdx.x; i < nb_buckets; i += blockDim.x) out[i] = hist[i];
+}
+
+// Item i goes to its bucket's sub-range of block b as (low 32 key bits) << 32 | i; the order
+// inside a sub-range does not matter (the entries are unique and sorted afterwards).
+__global__ void __launch_bounds__(kHistThreads) k_key_scatter(
+    const int64_t* __restrict__ keys, int64_t n, int nb_buckets,
+    const int32_t* __restrict__ bucket_start, const int32_t* __restrict__ bcount,
+    uint64_t* __restrict__ out) {
+    extern __shared__ int32_t cur[];
+    const int32_t* base = bcount + (size_t)blockIdx.x * nb_buckets;
+    for (int i = threadIdx.x; i < nb_buckets; i += blockDim.x) cur[i] = bucket_start[i] + base[i];
+    __syncthreads();
+    int64_t i0, i1;
+    item_chunk(n, i0, i1);
+    const uint32_t bmask = (uint32_t)nb_buckets - 1u;
+    for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+        const uint64_t k = (uint64_t)keys[i];
+        const int pos = atomicAdd(&cur[(uint32_t)(k >> 32) & bmask], 1);
+        out[pos] = (k << 32) | (uint64_t)(uint32_t)i;
+    }
+}
+
 // Compare-exchange of the bitonic network: pair p of stage (k, j) is (i, i + j), ascending
 // when bit k of the (global) index i is clear.
 __device__ __forceinline__ void bitonic_pair(int p, int j, int& i, int& l) {
@@ -268,10 +321,29 @@ __device__ void radix_depth_sort(uint64_t* kA, uint64_t* kB, int* wc, int* scan_
 #define GS3D_SEGSORT_LB __launch_bounds__(kSegThreads, GS3D_SEGSORT_MINB)
 #endif
 
+// Output of one sorted entry. The render's tile pipeline: the reference's code and value
+// (emit). The generic pair sort (Pairs non-NULL): the entry's low 32 bits are its input index,
+// whose key and value are copied.
+struct Pairs {
+    const int64_t* keys_in;
+    const int32_t* vals_in;
+};
+
+__device__ __forceinline__ void emit_any(const Pairs& pr, int64_t pos, uint64_t key, uint64_t tile_hi,
+                                         int64_t* __restrict__ codes, int32_t* __restrict__ vals) {
+    if (pr.keys_in) {
+        const uint32_t idx = (uint32_t)key;
+        codes[pos] = pr.keys_in[idx];
+        vals[pos] = pr.vals_in[idx];
+    } else {
+        emit(pos, key, tile_hi, codes, vals);
+    }
+}
+
 __global__ void GS3D_SEGSORT_LB k_tile_segsort(
     const int32_t* __restrict__ counts, int64_t capacity, const int32_t* __restrict__ tiles_end,
     const uint64_t* __restrict__ keys, uint64_t* __restrict__ scratch, int64_t* __restrict__ codes,
-    int32_t* __restrict__ vals) {
+    int32_t* __restrict__ vals, const Pairs pr) {
     __shared__ __align__(16) unsigned char raw[kSegSmemBytes];
     __shared__ int scan_sm[33];
     const int64_t D = counts[1];
@@ -330,14 +402,14 @@ __global__ void GS3D_SEGSORT_LB k_tile_segsort(
             }
             __syncthreads();
         }
-        for (int i = threadIdx.x; i < m; i += blockDim.x) emit(start + i, kA[i], tile_hi, codes, vals);
+        for (int i = threadIdx.x; i < m; i += blockDim.x) emit_any(pr, start + i, kA[i], tile_hi, codes, vals);
         return;
     }
     if (P <= kSegCap) {
         for (int i = threadIdx.x; i < P; i += blockDim.x) s[i] = i < m ? keys[start + i] : ~0ull;
         __syncthreads();
         bitonic_local(s, P, 0, 2, P, P);
-        for (int i = threadIdx.x; i < m; i += blockDim.x) emit(start + i, s[i], tile_hi, codes, vals);
+        for (int i = threadIdx.x; i < m; i += blockDim.x) emit_any(pr, start + i, s[i], tile_hi, codes, vals);
         return;
     }
     // large segment: padded copy in scratch[2 start, 2 start + P) (P < 2 m, so the regions of
@@ -373,7 +445,7 @@ __global__ void GS3D_SEGSORT_LB k_tile_segsort(
         }
         if (k <= kSegCap) k = kSegCap;  // every k <= kSegCap was just done
     }
-    for (int i = threadIdx.x; i < m; i += blockDim.x) emit(start + i, g[i], tile_hi, codes, vals);
+    for (int i = threadIdx.x; i < m; i += blockDim.x) emit_any(pr, start + i, g[i], tile_hi, codes, vals);
 }
 
 }  // namespace
@@ -454,7 +526,62 @@ int tile_sort_order(void* ws, const int32_t* counts, const int4* ranges, const f
                                                                 capacity_dup, L.cursor, L.bcount, keys);
     GS3D_LAUNCHED("k_tile_scatter");
     k_tile_segsort<<<(unsigned)nb_tiles, kSegThreads, 0, stream>>>(counts, capacity_dup, tiles_end, keys,
-                                                                   L.big, sorted_codes, sorted_vals);
+                                                                   L.big, sorted_codes, sorted_vals,
+                                                                   Pairs{nullptr, nullptr});
+    GS3D_LAUNCHED("k_tile_segsort");
+    return GS3D_OK;
+}
+
+// ---- generic pair sort --------------------------------------------------------------------
+// workspace: counts (4 int32), bucket counts + starts (2 T int32), bucket ends (T int32), block
+// counts (kHistBlocks x T int32), large-segment scratch (2 n uint64), entries (n uint64)
+bool bucket_sort_applies(int64_t n, int highest_key_bit) {
+    return highest_key_bit > 32 && highest_key_bit <= 32 + kMaxBucketBits && n < ((int64_t)1 << 31);
+}
+
+size_t bucket_sort_workspace_bytes(int64_t n, int highest_key_bit) {
+    if (n < 1) n = 1;
+    const int T = 1 << std::max(1, std::min(kMaxBucketBits, highest_key_bit - 32));
+    return align256(4 * sizeof(int32_t)) + align256((size_t)T * sizeof(int32_t)) +
+           tile_sort_workspace_bytes(n, T) + align256((size_t)n * sizeof(uint64_t));
+}
+
+int bucket_sort_pairs(void* ws, size_t ws_bytes, const int64_t* keys_in, int64_t* keys_out,
+                      const int32_t* vals_in, int32_t* vals_out, int64_t n, int highest_key_bit,
+                      cudaStream_t stream) {
+    if (!bucket_sort_applies(n, highest_key_bit))
+        return set_error("bucket sort: %d key bits / %lld items not supported", highest_key_bit,
+                         (long long)n),
+               GS3D_ERR_UNSUPPORTED;
+    if (ws_bytes < bucket_sort_workspace_bytes(n, highest_key_bit))
+        return set_error("sort temp storage too small: %zu < %zu", ws_bytes,
+                         bucket_sort_workspace_bytes(n, highest_key_bit)),
+               GS3D_ERR_WORKSPACE;
+    if (n == 0) return GS3D_OK;
+    const int T = 1 << (highest_key_bit - 32);
+    unsigned char* w = static_cast<unsigned char*>(ws);
+    int32_t* counts = reinterpret_cast<int32_t*>(w);
+    w += align256(4 * sizeof(int32_t));
+    int32_t* ends = reinterpret_cast<int32_t*>(w);
+    w += align256((size_t)T * sizeof(int32_t));
+    const TsLayout L = ts_layout(w, T);
+    w += tile_sort_workspace_bytes(n, T);
+    uint64_t* entries = reinterpret_cast<uint64_t*>(w);
+    const int smem = T * (int)sizeof(int32_t);
+    GS3D_CUDA(cudaFuncSetAttribute(k_key_hist, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+              "key histogram shared memory");
+    GS3D_CUDA(cudaFuncSetAttribute(k_key_scatter, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+              "key scatter shared memory");
+    k_key_hist<<<kHistBlocks, kHistThreads, smem, stream>>>(keys_in, n, T, L.bcount, counts);
+    GS3D_LAUNCHED("k_key_hist");
+    k_tile_colscan<<<(unsigned)ceil_div(T, 32), 256, 0, stream>>>(L.bcount, T, L.tcount);
+    GS3D_LAUNCHED("k_tile_colscan");
+    k_tile_scan<<<1, 1024, 0, stream>>>(L.tcount, T, n, ends, L.cursor, counts);
+    GS3D_LAUNCHED("k_tile_scan");
+    k_key_scatter<<<kHistBlocks, kHistThreads, smem, stream>>>(keys_in, n, T, L.cursor, L.bcount, entries);
+    GS3D_LAUNCHED("k_key_scatter");
+    k_tile_segsort<<<(unsigned)T, kSegThreads, 0, stream>>>(counts, n, ends, entries, L.big, keys_out,
+                                                           vals_out, Pairs{keys_in, vals_in});
     GS3D_LAUNCHED("k_tile_segsort");
     return GS3D_OK;
 }
