@@ -45,9 +45,19 @@ class AdcBuffers:
                    torch.zeros(2 * m, dtype=torch.int32, device=dev),
                    torch.empty(int(nbytes.value), **u8))
 
+    @property
+    def capacity(self) -> int:
+        return self.accumulated_mean2d_grad_norms_ndc.shape[0]
+
     def set_nb_gaussians(self, n: int) -> None:
-        """set_nb_gaussians! (training_structs.jl): resize and reset the statistics."""
-        fresh = AdcBuffers.create(n, self.workspace.device)
+        """set_nb_gaussians! (training_structs.jl): reset the statistics for n Gaussians. The
+        arrays are kept when they hold n (the other arrays are outputs the next plan writes in
+        full), else replaced with 25% headroom for the growth of later densify steps."""
+        if n <= self.capacity:
+            self.accumulated_mean2d_grad_norms_ndc.zero_()
+            self.rendering_contribution_counts.zero_()
+            return
+        fresh = AdcBuffers.create(n + n // 4, self.workspace.device)
         self.__dict__.update(fresh.__dict__)
 
     def to_c(self) -> _abi.AdcBuffersC:
@@ -95,7 +105,7 @@ def densify_apply(adc: AdcBuffers, gaussians: GaussiansVector, moments: AdamMome
     S = gaussians.sh_coeffs.shape[2]
     ng = GaussiansVector(torch.empty((new_n, 4), **f), torch.empty((new_n, 3), **f),
                          torch.empty((new_n, 4), **f), torch.empty((new_n, 3, S), **f))
-    nm = AdamMoments.zeros(new_n, moments.sh_degree, dev)
+    nm = AdamMoments.empty(new_n, moments.sh_degree, dev)  # k_adc_apply writes every moment
     a, og, om, ngc, nmc = adc.to_c(), gaussians.to_c(), moments.to_c(), ng.to_c(), nm.to_c()
     log_split = float(np.log(np.float32(splitting_scale_factor)))
     _abi.check(_abi.lib().gs3d_densify_apply(

@@ -32,6 +32,13 @@ class AdamMoments:
         return cls(torch.zeros((n, 3, 2), **f), torch.zeros((n, 2), **f), torch.zeros((n, 3, 2), **f),
                    torch.zeros((n, 4, 2), **f), torch.zeros((n, 3, (sh_degree + 1) ** 2, 2), **f))
 
+    @classmethod
+    def empty(cls, n: int, sh_degree: int, device) -> "AdamMoments":
+        """Uninitialised moments (for outputs a kernel writes in full)."""
+        f = dict(dtype=torch.float32, device=device)
+        return cls(torch.empty((n, 3, 2), **f), torch.empty((n, 2), **f), torch.empty((n, 3, 2), **f),
+                   torch.empty((n, 4, 2), **f), torch.empty((n, 3, (sh_degree + 1) ** 2, 2), **f))
+
     @property
     def n(self) -> int:
         return self.means_moments.shape[0]

@@ -207,11 +207,17 @@ class Trainer:
         return True
 
     def complete_adc_step(self) -> None:
+        """complete_adc_step! (training.jl:455-459): buffers for the new Gaussian count. The
+        gradient and render buffers are kept while they hold n Gaussians, else replaced with
+        25% headroom (the reference reallocates them at every densify step)."""
         n = self.gaussians.n
-        self.fgradients.resize(n)
+        if n > self.fgradients.capacity:
+            self.fgradients.resize(n + n // 4)
         rb = self.render_buffers
-        self.render_buffers = RenderBuffers.create(n, self.tiling.nb_tiles, self.device,
-                                                   capacity_dup=max(rb.capacity_dup, 4 * n))
+        if n > rb.capacity_n:
+            cap = n + n // 4
+            self.render_buffers = RenderBuffers.create(cap, self.tiling.nb_tiles, self.device,
+                                                       capacity_dup=max(rb.capacity_dup, 4 * cap))
 
     # -- one iteration (training.jl:173-244) -----------------------------------------------
     def target_for(self, idx: int) -> torch.Tensor:
