@@ -166,66 +166,116 @@ struct ApplyArgs {
     const int32_t* counts;  // device F
 };
 
-__device__ __forceinline__ void copy_moments(const ApplyArgs& a, size_t from, size_t to, bool zero) {
+// The small per-Gaussian fields are written by the Gaussian's own thread; the SH rows (3 S
+// coefficients and 6 S moments per Gaussian: 192 and 384 bytes at degree 3) are copied by the
+// whole warp over its 32 Gaussians' contiguous source rows, so reads and writes are coalesced.
+__device__ __forceinline__ void copy_small_moments(const ApplyArgs& a, size_t from, size_t to, bool zero) {
     for (int k = 0; k < 6; ++k) a.nmm[6 * to + k] = zero ? 0.0f : a.mm[6 * from + k];
     for (int k = 0; k < 2; ++k) a.nom[2 * to + k] = zero ? 0.0f : a.om[2 * from + k];
     for (int k = 0; k < 6; ++k) a.nsm[6 * to + k] = zero ? 0.0f : a.sm[6 * from + k];
     for (int k = 0; k < 8; ++k) a.nrm[8 * to + k] = zero ? 0.0f : a.rm[8 * from + k];
-    const int L = 6 * a.Sm;
-    for (int k = 0; k < L; ++k) a.nshm[(size_t)L * to + k] = zero ? 0.0f : a.shm[(size_t)L * from + k];
 }
 
-__device__ __forceinline__ void copy_rest(const ApplyArgs& a, size_t from, size_t to) {
+__device__ __forceinline__ void copy_rotation(const ApplyArgs& a, size_t from, size_t to) {
     for (int k = 0; k < 4; ++k) a.nrf[4 * to + k] = a.rf[4 * from + k];
-    const int L = 3 * a.S;
-    for (int k = 0; k < L; ++k) a.nsh[(size_t)L * to + k] = a.sh[(size_t)L * from + k];
 }
+
+// kinds of an old Gaussian
+constexpr int kPruned = 0, kCarry = 1, kClone = 2, kSplit = 3;
 
 __global__ void __launch_bounds__(128) k_adc_apply(const ApplyArgs a) {
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += gridDim.x * blockDim.x) {
-        if (a.prune[i]) continue;
-        const size_t last = (size_t)a.counts_cs[i] - 1;
-        const float* mo = a.mo + 4 * (size_t)i;
-        const float* sf = a.sf + 3 * (size_t)i;
-        if (a.densify[i]) {
-            const size_t first = last - 1;
-            if (a.clone[i]) {
-                for (int k = 0; k < 4; ++k) { a.nmo[4 * first + k] = mo[k]; a.nmo[4 * last + k] = mo[k]; }
-                for (int k = 0; k < 3; ++k) { a.nsf[3 * first + k] = sf[k]; a.nsf[3 * last + k] = sf[k]; }
-                copy_moments(a, i, first, false);
-                copy_moments(a, i, last, true);
-            } else {
-                const float* q = a.rf + 4 * (size_t)i;
-                const float qss = q[0] * q[0] + q[1] * q[1] + q[2] * q[2] + q[3] * q[3];
-                const float qs = sqrtf(2.0f * (1.0f / qss));
-                const float r = q[0] * qs, x = q[1] * qs, y = q[2] * qs, z = q[3] * qs;
-                const float R[3][3] = {{1.0f - (y * y + z * z), x * y - r * z, x * z + r * y},
-                                       {x * y + r * z, 1.0f - (x * x + z * z), y * z - r * x},
-                                       {x * z - r * y, y * z + r * x, 1.0f - (x * x + y * y)}};
-                const float s[3] = {gs_expf(sf[0]), gs_expf(sf[1]), gs_expf(sf[2])};
-                float nrm[6];
-                split_normals(a.seed, (uint64_t)i + 1, nrm);
-                for (int k = 0; k < 2; ++k) {
-                    const size_t to = k == 0 ? first : last;
-                    for (int rr = 0; rr < 3; ++rr) {
-                        const float sh = R[rr][0] * (nrm[0 + 3 * k] * s[0]) + R[rr][1] * (nrm[1 + 3 * k] * s[1]) +
-                                         R[rr][2] * (nrm[2 + 3 * k] * s[2]);
-                        a.nmo[4 * to + rr] = mo[rr] + sh;
+    __shared__ int wkind[4][32];
+    __shared__ int2 wdst[4][32];  // (first, last) new rows
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t i0 = ((int64_t)blockIdx.x * (blockDim.x >> 5) + wib) * 32; i0 < a.n; i0 += nw * 32) {
+        const int64_t i = i0 + lane;
+        int kind = kPruned;
+        int2 d = make_int2(-1, -1);
+        if (i < a.n && !a.prune[i]) {
+            const size_t last = (size_t)a.counts_cs[i] - 1;
+            const float* mo = a.mo + 4 * (size_t)i;
+            const float* sf = a.sf + 3 * (size_t)i;
+            if (a.densify[i]) {
+                const size_t first = last - 1;
+                d = make_int2((int)first, (int)last);
+                if (a.clone[i]) {
+                    kind = kClone;
+                    for (int k = 0; k < 4; ++k) { a.nmo[4 * first + k] = mo[k]; a.nmo[4 * last + k] = mo[k]; }
+                    for (int k = 0; k < 3; ++k) { a.nsf[3 * first + k] = sf[k]; a.nsf[3 * last + k] = sf[k]; }
+                    copy_small_moments(a, i, first, false);
+                    copy_small_moments(a, i, last, true);
+                } else {
+                    kind = kSplit;
+                    const float* q = a.rf + 4 * (size_t)i;
+                    const float qss = q[0] * q[0] + q[1] * q[1] + q[2] * q[2] + q[3] * q[3];
+                    const float qs = sqrtf(2.0f * (1.0f / qss));
+                    const float r = q[0] * qs, x = q[1] * qs, y = q[2] * qs, z = q[3] * qs;
+                    const float R[3][3] = {{1.0f - (y * y + z * z), x * y - r * z, x * z + r * y},
+                                           {x * y + r * z, 1.0f - (x * x + z * z), y * z - r * x},
+                                           {x * z - r * y, y * z + r * x, 1.0f - (x * x + y * y)}};
+                    const float s[3] = {gs_expf(sf[0]), gs_expf(sf[1]), gs_expf(sf[2])};
+                    float nrm[6];
+                    split_normals(a.seed, (uint64_t)i + 1, nrm);
+                    for (int k = 0; k < 2; ++k) {
+                        const size_t to = k == 0 ? first : last;
+                        for (int rr = 0; rr < 3; ++rr) {
+                            const float sh = R[rr][0] * (nrm[0 + 3 * k] * s[0]) + R[rr][1] * (nrm[1 + 3 * k] * s[1]) +
+                                             R[rr][2] * (nrm[2 + 3 * k] * s[2]);
+                            a.nmo[4 * to + rr] = mo[rr] + sh;
+                        }
+                        a.nmo[4 * to + 3] = mo[3];
+                        for (int rr = 0; rr < 3; ++rr) a.nsf[3 * to + rr] = sf[rr] + a.log_split;
                     }
-                    a.nmo[4 * to + 3] = mo[3];
-                    for (int rr = 0; rr < 3; ++rr) a.nsf[3 * to + rr] = sf[rr] + a.log_split;
+                    copy_small_moments(a, i, first, true);
+                    copy_small_moments(a, i, last, true);
                 }
-                copy_moments(a, i, first, true);
-                copy_moments(a, i, last, true);
+                copy_rotation(a, i, first);
+                copy_rotation(a, i, last);
+            } else {
+                kind = kCarry;
+                d = make_int2(-1, (int)last);
+                for (int k = 0; k < 4; ++k) a.nmo[4 * last + k] = mo[k];
+                for (int k = 0; k < 3; ++k) a.nsf[3 * last + k] = sf[k];
+                copy_small_moments(a, i, last, false);
+                copy_rotation(a, i, last);
             }
-            copy_rest(a, i, first);
-            copy_rest(a, i, last);
-        } else {
-            for (int k = 0; k < 4; ++k) a.nmo[4 * last + k] = mo[k];
-            for (int k = 0; k < 3; ++k) a.nsf[3 * last + k] = sf[k];
-            copy_moments(a, i, last, false);
-            copy_rest(a, i, last);
         }
+        wkind[wib][lane] = kind;
+        wdst[wib][lane] = d;
+        __syncwarp();
+        const int cnt = (int)min((int64_t)32, (int64_t)a.n - i0);
+        // SH coefficients: every new copy gets the old row
+        const int L = 3 * a.S;
+        const float* src = a.sh + (size_t)i0 * L;
+        for (int e = lane; e < cnt * L; e += 32) {
+            const int jg = e / L, col = e - jg * L;
+            const int k = wkind[wib][jg];
+            if (k == kPruned) continue;
+            const float v = src[e];
+            const int2 dd = wdst[wib][jg];
+            a.nsh[(size_t)dd.y * L + col] = v;
+            if (k != kCarry) a.nsh[(size_t)dd.x * L + col] = v;
+        }
+        // SH moments: carried and first clone keep them, second clone and both splits start at 0
+        const int Lm = 6 * a.Sm;
+        const float* srcm = a.shm + (size_t)i0 * Lm;
+        for (int e = lane; e < cnt * Lm; e += 32) {
+            const int jg = e / Lm, col = e - jg * Lm;
+            const int k = wkind[wib][jg];
+            if (k == kPruned) continue;
+            const int2 dd = wdst[wib][jg];
+            if (k == kCarry) {
+                a.nshm[(size_t)dd.y * Lm + col] = srcm[e];
+            } else if (k == kClone) {
+                a.nshm[(size_t)dd.x * Lm + col] = srcm[e];
+                a.nshm[(size_t)dd.y * Lm + col] = 0.0f;
+            } else {
+                a.nshm[(size_t)dd.x * Lm + col] = 0.0f;
+                a.nshm[(size_t)dd.y * Lm + col] = 0.0f;
+            }
+        }
+        __syncwarp();
     }
     // adjust_fgidx_to_gidx_adc_kernel!
     if (a.f2g) {
