@@ -134,8 +134,9 @@ typedef struct gs3d_render_buffers {
     void* workspace;               /* scan / sort scratch                               */
     size_t workspace_bytes;
     /* Optional (NULL: not used). Per-pixel contribution masks the forward blend writes for
-     * the backward blend: one bit per (pixel, duplicated entry) the pixel evaluated with
-     * alpha >= 0.999 min_alpha before it stopped, 32 entries of a tile per 32-bit word. The
+     * the backward blend: one bit per (pixel, duplicated entry) the pixel blended or evaluated
+     * with alpha in [0.999 min_alpha, min_alpha) before it stopped, 32 entries of a tile per
+     * 32-bit word. The
      * backward then visits only those pairs. The forward writes them (and sets
      * device_counts[3]) when contrib_mask_words >= (D / 32 + #tiles + 1) * tile pixels and
      * the tile has a multiple of 32 pixels; otherwise the backward tests every entry itself,

@@ -90,9 +90,10 @@ __global__ void __launch_bounds__(512, GS3D_RASTER_MINB) k_raster(const RasterAr
     const int end = a.tiles_end[tile - 1];
     // contribution masks: row (start / 32 + tile - 1 + c) holds, for chunk c of 32 consecutive
     // entries of this tile, one 32-bit word per thread; bit j of thread t's word is set when
-    // thread t's pixel evaluated entry 32 c + j with alpha >= min_alpha_mark before it stopped
-    // (every entry it blended, plus those within 0.1% below min_alpha). Rows of distinct tiles
-    // never overlap, and D / 32 + #tiles + 1 rows cover every tile.
+    // thread t's pixel blended entry 32 c + j, or evaluated it with alpha within 0.1% below
+    // min_alpha, before it stopped (the entry that stops it comes after its last contributor,
+    // where the backward never looks). Rows of distinct tiles never overlap, and
+    // D / 32 + #tiles + 1 rows cover every tile.
     const bool wmask = MASKS && a.cmask != nullptr && (nthr & 31) == 0 &&
                        (Draw / 32 + (int64_t)a.tiles_x * gridDim.y + 1) * nthr <= a.cmask_words;
     if (wmask && t == 0 && blockIdx.x == 0 && blockIdx.y == 0) *a.mask_flag = 1;
@@ -151,10 +152,13 @@ __global__ void __launch_bounds__(512, GS3D_RASTER_MINB) k_raster(const RasterAr
                     const float q = A.x * uu + A.y * vv + A.z * uv + A.w * cu + B.x * cv + B.y;
                     if (q < a.q_skip) continue;
                     const float alpha = min_hi(a.max_alpha, gs_expf_blend(q));
-                    if (MASKS && alpha >= a.min_alpha_mark) mw |= 1u << (jj - ch);
-                    if (alpha < a.min_alpha) continue;
+                    if (alpha < a.min_alpha) {
+                        if (MASKS && alpha >= a.min_alpha_mark) mw |= 1u << (jj - ch);
+                        continue;
+                    }
                     const float nT = T * (1.0f - alpha);
                     if (nT < a.min_T) { done = true; continue; }
+                    if (MASKS) mw |= 1u << (jj - ch);
                     const float w = T * alpha;
                     const float4 C = sC[jj];
                     c0 += w * B.z;
