@@ -351,7 +351,14 @@ def test_multi_view_step_equals_summed_views(cuda, factored):
     _abi.check(_abi.lib().gs3d_adam_step_dense(C.byref(gc), C.byref(mc), C.c_void_p(total.data_ptr()),
                                                C.byref(pc), None))
     torch.cuda.synchronize()
-    for x, y in zip(t.gaussians.tensors(), g.tensors()):
+    # Adam's first step moves each parameter by its learning rate times the sign of its
+    # gradient: a gradient that is zero up to the rounding noise may flip, which moves that
+    # parameter by up to twice its learning rate
+    lrs = opts.learning_rates()
+    bounds = (max(adam.lrs.means, lrs.opacity_features), lrs.scaling_features, lrs.rotation_features,
+              max(lrs.sh_coeffs_dc, lrs.sh_coeffs_rest))
+    for x, y, lr in zip(t.gaussians.tensors(), g.tensors(), bounds):
         same = (x[:n] == y).float().mean().item()
-        assert same >= 0.999, same
+        assert same >= 0.99, same
+        assert float((x[:n] - y).abs().max()) <= 2.01 * lr
     assert t.optimizer.update_count == 1
