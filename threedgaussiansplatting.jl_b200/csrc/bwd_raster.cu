@@ -72,6 +72,11 @@ __device__ __forceinline__ int reduce9_index(int lane) {
     return idx < 9 && (lane & 1) == 0 ? idx : -1;
 }
 
+#ifndef GS3D_BWD_PX
+#define GS3D_BWD_PX 2
+#endif
+constexpr int kBwdPixelsPerThread = GS3D_BWD_PX;
+
 #ifndef GS3D_BWD_DIRECT_MAX
 #define GS3D_BWD_DIRECT_MAX 8
 #endif
@@ -270,18 +275,65 @@ __device__ __forceinline__ void fwd_pixel(int compact, int tw, int th, int t, in
     }
 }
 
-#ifndef GS3D_BWDM_MINB
-#define GS3D_BWDM_MINB 2
-#endif
+// One pixel's state in the reverse walk.
+struct PixelState {
+    float T, p0, p1, p2, g0, g1, g2, cpu, cpv;
+    int rl;  // entries [0, rl) of the tile may be taken (relative to its start)
+};
 
-__global__ void __launch_bounds__(512, GS3D_BWDM_MINB) k_bwd_raster_masks(const BwdArgs a,
-                                                                          const uint32_t* cmask) {
+// The reference's per-pair update for one pixel (backward_core.jl:226-286), branch-free: a pair
+// not taken (take == false) leaves the state exactly unchanged and adds exact zeros to v.
+__device__ __forceinline__ bool pair_update(PixelState& s, bool mine, const float4 A, const float4 B,
+                                            float cb, float min_alpha, float max_alpha, float (&v)[9]) {
+    const float du = s.cpu - A.x, dv = s.cpv - A.y;
+    const float ic11 = A.z, ic21 = A.w, ic22 = B.x;
+    const float du2 = du * du, dv2 = dv * dv, duv = du * dv;
+    const float q = fmaf(-0.5f, fmaf(ic11, du2, ic22 * dv2), -ic21 * duv);
+    float ge = __expf(q);
+    float alpha = min_hi(max_alpha, B.y * ge);
+    if (mine && fabsf(alpha - min_alpha) <= 4e-6f * min_alpha) {
+        ge = gs_expf_blend(q);
+        alpha = min_hi(max_alpha, B.y * ge);
+    }
+    const bool take = mine && alpha >= min_alpha;
+    const float al = take ? alpha : 0.0f;
+    ge = take ? ge : 0.0f;
+    const float inv1m = take ? __fdividef(1.0f, 1.0f - alpha) : 1.0f;
+    s.T *= inv1m;
+    const float tc0 = s.T * B.z, tc1 = s.T * B.w, tc2 = s.T * cb;
+    s.p0 = fmaf(al, tc0, s.p0);
+    s.p1 = fmaf(al, tc1, s.p1);
+    s.p2 = fmaf(al, tc2, s.p2);
+    const float ag = inv1m * fmaf(s.g0, tc0 - s.p0, fmaf(s.g1, tc1 - s.p1, s.g2 * (tc2 - s.p2)));
+    const float aga = al * ag;
+    const float sc = -0.5f * aga;
+    const float g21 = sc * duv;
+    const float ta = s.T * al;
+    v[0] += aga * fmaf(du, ic11, dv * ic21);
+    v[1] += aga * fmaf(du, ic21, dv * ic22);
+    v[2] += ge * ag;
+    v[3] += sc * du2;
+    v[4] += g21 + g21;
+    v[5] += sc * dv2;
+    v[6] += ta * s.g0;
+    v[7] += ta * s.g1;
+    v[8] += ta * s.g2;
+    return take;
+}
+
+// PX pixels per thread: thread t of warp w takes the forward's threads (PX w + p) 32 + lane,
+// p < PX, i.e. PX of the forward's 4 x 8 warp blocks side by side, so one walk over the entries
+// the PX blocks marked serves PX pixels per lane, and one warp reduction per entry covers them.
+template <int PX>
+__global__ void __launch_bounds__(512 / PX, PX == 1 ? 2 : 3) k_bwd_raster_masks(const BwdArgs a,
+                                                                               const uint32_t* cmask) {
     extern __shared__ __align__(16) float4 sm4[];
-    const int nthr = blockDim.x;                             // tile pixels, a multiple of 32
+    const int nthr = blockDim.x;
+    const int npx = nthr * PX;                               // tile pixels (forward threads)
     float4* E0 = sm4;                                        // x y ic11 ic21
-    float4* E1 = sm4 + nthr;                                 // ic22 opacity r g
-    float* E2 = reinterpret_cast<float*>(sm4 + 2 * nthr);    // b
-    int* EF = reinterpret_cast<int*>(E2 + nthr);             // fgidx (0-based)
+    float4* E1 = sm4 + npx;                                  // ic22 opacity r g
+    float* E2 = reinterpret_cast<float*>(sm4 + 2 * npx);     // b
+    int* EF = reinterpret_cast<int*>(E2 + npx);              // fgidx (0-based)
     __shared__ int red[32];
 
     const int F = a.counts[0];
@@ -290,27 +342,40 @@ __global__ void __launch_bounds__(512, GS3D_BWDM_MINB) k_bwd_raster_masks(const 
 
     const int t = threadIdx.x;
     const int lane = t & 31, warp = t >> 5;
-    int lu, lv;
-    fwd_pixel(a.compact, a.tile_w, a.tile_h, t, lu, lv);
     const int txi = blockIdx.x, tyi = blockIdx.y;
-    const int U = txi * a.tile_w + lu + 1, V = tyi * a.tile_h + lv + 1;
-    const bool inside = U <= a.width && V <= a.height;
-    const size_t px = (size_t)(V - 1) + (size_t)a.height * (size_t)(U - 1);
     const int tile = txi + tyi * a.tiles_x + 1;
     const int start = tile == 1 ? 0 : a.tiles_end[tile - 2];
     const int end = a.tiles_end[tile - 1];
-
-    float T = 0.0f, g0 = 0.0f, g1 = 0.0f, g2 = 0.0f;
-    int lastc = 0;
-    if (inside) {
-        lastc = a.last[px];
-        T = a.trans[px];
-        g0 = a.rgb_grad[3 * px];
-        g1 = a.rgb_grad[3 * px + 1];
-        g2 = a.rgb_grad[3 * px + 2];
+    const uint32_t* mrow[PX];
+    PixelState st[PX];
+    int lrl = 0;
+#pragma unroll
+    for (int p = 0; p < PX; ++p) {
+        const int ft = (warp * PX + p) * 32 + lane;
+        int lu, lv;
+        fwd_pixel(a.compact, a.tile_w, a.tile_h, ft, lu, lv);
+        const int U = txi * a.tile_w + lu + 1, V = tyi * a.tile_h + lv + 1;
+        const bool inside = U <= a.width && V <= a.height;
+        const size_t px = (size_t)(V - 1) + (size_t)a.height * (size_t)(U - 1);
+        PixelState& s = st[p];
+        s.T = s.g0 = s.g1 = s.g2 = 0.0f;
+        int lastc = 0;
+        if (inside) {
+            lastc = a.last[px];
+            s.T = a.trans[px];
+            s.g0 = a.rgb_grad[3 * px];
+            s.g1 = a.rgb_grad[3 * px + 1];
+            s.g2 = a.rgb_grad[3 * px + 2];
+        }
+        s.p0 = s.T * a.bg0;
+        s.p1 = s.T * a.bg1;
+        s.p2 = s.T * a.bg2;
+        s.cpu = (float)U - 0.5f;
+        s.cpv = (float)V - 0.5f;
+        s.rl = lastc > start ? lastc - start : 0;
+        lrl = max(lrl, s.rl);
+        mrow[p] = cmask + ((int64_t)(start >> 5) + (tile - 1)) * npx + ft;
     }
-    float p0 = T * a.bg0, p1 = T * a.bg1, p2 = T * a.bg2;
-    const float cpu = (float)U - 0.5f, cpv = (float)V - 0.5f;
 
     // this lane's share of the warp-reduced atomics: pointer and stride of value reduce9_index
     const int vi = reduce9_index(lane);
@@ -323,80 +388,59 @@ __global__ void __launch_bounds__(512, GS3D_BWDM_MINB) k_bwd_raster_masks(const 
         else { vptr = a.color_g + (vi - 6); vstride = 3; }
     }
 
-    // entries are indexed relative to the tile start; this pixel may take entries [0, rl)
-    const int rl = lastc > start ? lastc - start : 0;
-    const int wrl = (int)__reduce_max_sync(0xffffffffu, (unsigned)rl);
+    const int wrl = (int)__reduce_max_sync(0xffffffffu, (unsigned)lrl);
     if (lane == 0) red[warp] = wrl;
     __syncthreads();
     int brl = 0;
     for (int w = 0; w < (nthr >> 5); ++w) brl = max(brl, red[w]);
-    const uint32_t* mrow = cmask + ((int64_t)(start >> 5) + (tile - 1)) * nthr + t;
     const float min_alpha = a.min_alpha, max_alpha = a.max_alpha;
 
-    for (int b0 = brl > 0 ? ((brl - 1) / nthr) * nthr : -1; b0 >= 0; b0 -= nthr) {
+    for (int b0 = brl > 0 ? ((brl - 1) / npx) * npx : -1; b0 >= 0; b0 -= npx) {
         __syncthreads();  // every warp is done with the previous batch's entries
-        const int e = start + b0 + t;
-        if (e < end) {
-            const int fg = a.sfgidx[e] - 1;
-            const float* r = a.f2d + 9 * (size_t)fg;
-            E0[t] = make_float4(r[0], r[1], r[3], r[4]);
-            E1[t] = make_float4(r[5], r[2], r[6], r[7]);
-            E2[t] = r[8];
-            EF[t] = fg;
+#pragma unroll
+        for (int p = 0; p < PX; ++p) {
+            const int k = t + p * nthr;
+            const int e = start + b0 + k;
+            if (e < end) {
+                const int fg = a.sfgidx[e] - 1;
+                const float* r = a.f2d + 9 * (size_t)fg;
+                E0[k] = make_float4(r[0], r[1], r[3], r[4]);
+                E1[k] = make_float4(r[5], r[2], r[6], r[7]);
+                E2[k] = r[8];
+                EF[k] = fg;
+            }
         }
         __syncthreads();
-        const int whi = min(wrl - b0, nthr);  // the warp's exclusive bound inside the batch
+        const int whi = min(wrl - b0, npx);  // the warp's exclusive bound inside the batch
         if (whi <= 0) continue;
-        const int hi = min(rl - b0, nthr);    // this lane's
         int w = (whi - 1) >> 5;
-        uint32_t mnext = mrow[(int64_t)((b0 >> 5) + w) * nthr];
+        uint32_t mnext[PX];
+#pragma unroll
+        for (int p = 0; p < PX; ++p) mnext[p] = mrow[p][(int64_t)((b0 >> 5) + w) * npx];
         for (; w >= 0; --w) {
-            uint32_t m = mnext;
-            if (w > 0) mnext = mrow[(int64_t)((b0 >> 5) + w - 1) * nthr];
-            const int nb = hi - (w << 5);  // this lane's bits below its bound
-            m = nb >= 32 ? m : (nb <= 0 ? 0u : (m & ((1u << nb) - 1u)));
-            uint32_t wm = __reduce_or_sync(0xffffffffu, m);
+            uint32_t m[PX];
+            uint32_t any = 0;
+#pragma unroll
+            for (int p = 0; p < PX; ++p) {
+                m[p] = mnext[p];
+                if (w > 0) mnext[p] = mrow[p][(int64_t)((b0 >> 5) + w - 1) * npx];
+                const int nb = min(st[p].rl - b0, npx) - (w << 5);  // bits below the pixel's bound
+                m[p] = nb >= 32 ? m[p] : (nb <= 0 ? 0u : (m[p] & ((1u << nb) - 1u)));
+                any |= m[p];
+            }
+            uint32_t wm = __reduce_or_sync(0xffffffffu, any);
             while (wm) {
                 const int j = 31 - __clz(wm);
                 wm &= ~(1u << j);
                 const int en = (w << 5) + j;
                 const float4 A = E0[en];
                 const float4 B = E1[en];
-                const float du = cpu - A.x, dv = cpv - A.y;
-                const float ic11 = A.z, ic21 = A.w, ic22 = B.x;
-                const float du2 = du * du, dv2 = dv * dv, duv = du * dv;
-                const float q = fmaf(-0.5f, fmaf(ic11, du2, ic22 * dv2), -ic21 * duv);
-                float ge = __expf(q);
-                float alpha = min_hi(max_alpha, B.y * ge);
-                const bool mine = (m >> j) & 1u;
-                if (mine && fabsf(alpha - min_alpha) <= 4e-6f * min_alpha) {
-                    ge = gs_expf_blend(q);
-                    alpha = min_hi(max_alpha, B.y * ge);
-                }
-                const bool take = mine && alpha >= min_alpha;
-                const float al = take ? alpha : 0.0f;
-                ge = take ? ge : 0.0f;
-                const float inv1m = take ? __fdividef(1.0f, 1.0f - alpha) : 1.0f;
-                T *= inv1m;
-                const float tc0 = T * B.z, tc1 = T * B.w, tc2 = T * E2[en];
-                p0 = fmaf(al, tc0, p0);
-                p1 = fmaf(al, tc1, p1);
-                p2 = fmaf(al, tc2, p2);
-                const float ag = inv1m * fmaf(g0, tc0 - p0, fmaf(g1, tc1 - p1, g2 * (tc2 - p2)));
-                const float aga = al * ag;
-                const float sc = -0.5f * aga;
-                const float g21 = sc * duv;
-                const float ta = T * al;
-                float v[9];
-                v[0] = aga * fmaf(du, ic11, dv * ic21);
-                v[1] = aga * fmaf(du, ic21, dv * ic22);
-                v[2] = ge * ag;
-                v[3] = sc * du2;
-                v[4] = g21 + g21;
-                v[5] = sc * dv2;
-                v[6] = ta * g0;
-                v[7] = ta * g1;
-                v[8] = ta * g2;
+                const float cb = E2[en];
+                float v[9] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                bool take = false;
+#pragma unroll
+                for (int p = 0; p < PX; ++p)
+                    take |= pair_update(st[p], (m[p] >> j) & 1u, A, B, cb, min_alpha, max_alpha, v);
                 const unsigned cm = __ballot_sync(0xffffffffu, take);
                 if (cm == 0) continue;
                 const int fg = EF[en];
@@ -461,7 +505,11 @@ int launch_bwd_raster(const gs3d_fgradients* fg, const float* rgb_grad,
     ProfScope prof("bwd_raster", stream);
     const dim3 grid(til->nb_tiles_x, til->nb_tiles_y);
     if (a.use_masks) {
-        k_bwd_raster_masks<<<grid, nthr, smem_m, stream>>>(a, buf->contrib_masks);
+        // two pixels per thread when the tile's warps pair up
+        if ((nthr & 63) == 0 && kBwdPixelsPerThread == 2)
+            k_bwd_raster_masks<2><<<grid, nthr / 2, smem_m, stream>>>(a, buf->contrib_masks);
+        else
+            k_bwd_raster_masks<1><<<grid, nthr, smem_m, stream>>>(a, buf->contrib_masks);
         GS3D_LAUNCHED("k_bwd_raster_masks");
     }
     k_bwd_raster<<<grid, nthr, smem, stream>>>(a);
