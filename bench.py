@@ -3,20 +3,25 @@
 BASELINE.json's headline workload: 3M Gaussians at 1920x1080.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl gs3d|reference]
+                    [--views-per-gpu V | --global-batch B] [--no-extra] [--no-e2e]
 
-Workload (synthetic, seeded; BASELINE.json config 4 with one view per GPU per step):
-3,000,000 Gaussians, means ~ N(0, 2^2 I), log-scales ~ N(-5.5, 0.6), opacity logits ~ N(1, 1.5),
-SH degree 3 (48 coefficients, DC ~ N(0, 0.3), rest ~ N(0, 0.05)); 256 pinhole cameras at
-1920x1080 (50 deg horizontal FOV) on a Fibonacci hemisphere of radius 5 looking at the
-origin; uniform [0, 1] target images. A step is one training iteration of the reference's
-training_step! (training.jl:173-244) per GPU: render!, loss, backward!, ADC statistics,
-learning-rate annealing and the Adam update, at iterations 3001.. (SH degree 3, between
-densify steps; densification happens once every 100 iterations and is not timed).
-N = 1 uses the reference's sparse Adam; N > 1 is multi-view data parallelism (one view per
-rank; dense gradient rows reduce-scattered over NCCL, each rank updates its 1/N of the
-Gaussians, parameters all-gathered), so the per-GPU work is fixed ("weak" scaling). Inputs
-are larger than L2 (2.1 GB of parameters and moments), so no L2 flush is needed between steps.
-The line also carries the render-only throughput (frames/s) of the same scene and cameras.
+Workload (synthetic, seeded; the BASELINE config 4 scene): 3,000,000 Gaussians, means
+~ N(0, 2^2 I), log-scales ~ N(-5.5, 0.6), opacity logits ~ N(1, 1.5), SH degree 3 (48
+coefficients, DC ~ N(0, 0.3), rest ~ N(0, 0.05)); 256 pinhole cameras at 1920x1080 (50 deg
+horizontal FOV) on a Fibonacci hemisphere of radius 5 looking at the origin; uniform [0, 1]
+target images. A step is one training iteration of the reference's training_step!
+(training.jl:173-244) per GPU: render!, loss, backward!, ADC statistics, learning-rate annealing
+and the Adam update, at iterations 3001.. (SH degree 3, between densify steps). By default one
+view per GPU per step: at N = 1 the reference's iteration with its sparse Adam; at N > 1
+multi-view data parallelism (gradient rows reduce-scattered over NCCL, each rank updates its 1/N
+of the Gaussians, parameters all-gathered), so the per-GPU work is fixed ("weak" scaling).
+--views-per-gpu / --global-batch train V views per GPU per step (config 4's batches of 8/16/32).
+Inputs are larger than L2 (2.1 GB of parameters and moments), so no L2 flush is needed.
+
+Beside the timed steps the line carries, measured outside the timed region: the rasterisers'
+FP32-issue rooflines from exact work counts, render-only frames/s of the same scene, config 3's
+4K render-only frames/s (6M Gaussians), the cost of one densify step, the drop-in sort against the
+reference's CUB build, and the CPU baselines (--no-extra skips the 4K and densify legs).
 
 `--impl reference` times the CPU restatement of the same training step (the reference has no
 runnable implementation here: it is Julia/CUDA.jl and Julia is not installed) on all host
