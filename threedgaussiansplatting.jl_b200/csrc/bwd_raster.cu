@@ -282,7 +282,9 @@ struct PixelState {
 };
 
 // The reference's per-pair update for one pixel (backward_core.jl:226-286), branch-free: a pair
-// not taken (take == false) leaves the state exactly unchanged and adds exact zeros to v.
+// not taken (take == false) leaves the state exactly unchanged and gives exact zeros. ADD: add
+// the 9 gradients to v, else write them.
+template <bool ADD>
 __device__ __forceinline__ bool pair_update(PixelState& s, bool mine, const float4 A, const float4 B,
                                             float cb, float min_alpha, float max_alpha, float (&v)[9]) {
     const float du = s.cpu - A.x, dv = s.cpv - A.y;
@@ -309,15 +311,10 @@ __device__ __forceinline__ bool pair_update(PixelState& s, bool mine, const floa
     const float sc = -0.5f * aga;
     const float g21 = sc * duv;
     const float ta = s.T * al;
-    v[0] += aga * fmaf(du, ic11, dv * ic21);
-    v[1] += aga * fmaf(du, ic21, dv * ic22);
-    v[2] += ge * ag;
-    v[3] += sc * du2;
-    v[4] += g21 + g21;
-    v[5] += sc * dv2;
-    v[6] += ta * s.g0;
-    v[7] += ta * s.g1;
-    v[8] += ta * s.g2;
+    const float w[9] = {aga * fmaf(du, ic11, dv * ic21), aga * fmaf(du, ic21, dv * ic22), ge * ag,
+                        sc * du2, g21 + g21, sc * dv2, ta * s.g0, ta * s.g1, ta * s.g2};
+#pragma unroll
+    for (int k = 0; k < 9; ++k) v[k] = ADD ? v[k] + w[k] : w[k];
     return take;
 }
 
@@ -436,11 +433,11 @@ __global__ void __launch_bounds__(512 / PX, PX == 1 ? 2 : 3) k_bwd_raster_masks(
                 const float4 A = E0[en];
                 const float4 B = E1[en];
                 const float cb = E2[en];
-                float v[9] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-                bool take = false;
+                float v[9];
+                bool take = pair_update<false>(st[0], (m[0] >> j) & 1u, A, B, cb, min_alpha, max_alpha, v);
 #pragma unroll
-                for (int p = 0; p < PX; ++p)
-                    take |= pair_update(st[p], (m[p] >> j) & 1u, A, B, cb, min_alpha, max_alpha, v);
+                for (int p = 1; p < PX; ++p)
+                    take |= pair_update<true>(st[p], (m[p] >> j) & 1u, A, B, cb, min_alpha, max_alpha, v);
                 const unsigned cm = __ballot_sync(0xffffffffu, take);
                 if (cm == 0) continue;
                 const int fg = EF[en];
