@@ -636,6 +636,8 @@ def main() -> None:
     e0.record(stream)
     for _ in range(args.steps):
         trainer.training_step()
+    if hasattr(trainer, "sync_parameters"):
+        trainer.sync_parameters()  # the last step's parameter all-gathers belong to the timed work
     e1.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
@@ -669,6 +671,8 @@ def main() -> None:
             loss_host.copy_(trainer.training_step(), non_blocking=True)
             stream.synchronize()
             float(loss_host[0])
+        if hasattr(trainer, "sync_parameters"):
+            trainer.sync_parameters()
         e1.record(stream)
         torch.cuda.synchronize()
         ms2 = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
@@ -678,6 +682,8 @@ def main() -> None:
         e2e = {"value": world * V * args.steps / (float(ms2.item()) / 1000.0), "unit": UNIT,
                "h2d_bytes_per_step": 3 * w * h * 4 * world * V, "d2h_bytes_per_step": 16 * world}
 
+    if hasattr(trainer, "sync_parameters"):
+        trainer.sync_parameters()
     # ---- render-only throughput (the metric's "render frames/s"): same scene and cameras,
     # each rank renders its own frames, device-timed, max over ranks --------------------------
     from gs3d import render as gs_render

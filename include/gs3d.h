@@ -49,6 +49,9 @@ typedef struct CUstream_st* gs3d_stream_t; /* ABI-compatible with cudaStream_t *
 #define GS3D_RENDER_REFERENCE_ORDER 2u /* F4-F7 as the reference stages them (see below)   */
 #define GS3D_RENDER_NO_CONTRIB_MASKS 4u /* leave render_buffers.contrib_masks unwritten (a
                                        render that no backward follows)                   */
+#define GS3D_RENDER_DEFER_COLOUR 8u /* stop before the colours and the blend (F1-F7 only, the
+                                       SH coefficients not read); gs3d_render_forward_colour
+                                       completes the render                              */
 
 /* backward flags */
 #define GS3D_BACKWARD_FIX_SH16 1u /* use coefficient 16 in the degree-3 direction Jacobian
@@ -285,6 +288,18 @@ GS3D_API int gs3d_render_forward_render_only(
     const gs3d_camera* camera, const gs3d_tiling* tiling,
     const gs3d_render_options* options, gs3d_render_buffers* buffers,
     int32_t* host_counts, uint32_t flags, gs3d_stream_t stream);
+
+/* Second half of a gs3d_render_forward called with GS3D_RENDER_DEFER_COLOUR (same arguments,
+ * the same Gaussians): the colours of the filtered Gaussians (sh_coeffs_to_color, sh.jl:38-112;
+ * the first half reads no SH coefficient) and the blend (F8 / F9). Together they equal one
+ * gs3d_render_forward bit for bit. No counterpart in the reference: it lets a data-parallel
+ * caller start a render while the SH coefficients of the previous update are still arriving.
+ * Only GS3D_RENDER_NO_CONTRIB_MASKS is read from flags. */
+GS3D_API int gs3d_render_forward_colour(
+    const gs3d_render_outputs* outputs, const gs3d_gaussians* gaussians,
+    const gs3d_camera* camera, const gs3d_tiling* tiling,
+    const gs3d_render_options* options, gs3d_render_buffers* buffers, uint32_t flags,
+    gs3d_stream_t stream);
 
 /* Work counts of the last gs3d_render_forward with these buffers (sorted arrays, tile ends,
  * 2D records and device counts as it left them), as the reference's blend loop performs the

@@ -314,3 +314,30 @@ def test_work_counts_vs_oracle(cuda, case):
     want = O.work_counts(ref, cam, til, opt)
     assert (blends, contrib) == want
     assert 0 < contrib <= blends
+
+
+@pytest.mark.parametrize("case", [c for c in CASES if c[0] in ("cfg0", "ragged_720p", "deg1_of3")],
+                         ids=lambda c: c[0])
+def test_deferred_colour_render_equals_render(cuda, case):
+    """render(defer_colour=True) (filter, projection without colours, duplication, sort) followed
+    by render_colour (colours, blend) gives the render's outputs and buffers bit for bit."""
+    from gs3d.render import render_colour
+    _, spec, seed, (w, h, fov, pos), tile, kw, deg = case
+    gv = synthetic_gaussians(spec, seed)
+    cam = look_at_camera(w, h, fov, pos)
+    opt = RenderOptions.for_camera(cam, deg, **kw)
+    til = Tiling.for_camera(cam, *(tile or (None, None)))
+    one, buf1 = gpu_render(gv, cam, til, opt, cuda)
+    g = gv.to(cuda)
+    out = RenderOutputs.create(cam.width, cam.height, cuda, include_depth=True)
+    buf = RenderBuffers.create(g.n, til.nb_tiles, cuda)
+    gs3d.render(out, g, cam, til, opt, buf, defer_colour=True)
+    render_colour(out, g, cam, til, opt, buf)
+    torch.cuda.synchronize()
+    F, D = one["F"], one["D"]
+    assert gs3d.counts(buf) == (F, D)
+    for a, b in ((out.rgb, one["rgb"]), (out.transmittance, one["trans"]), (out.depth, one["depth"]),
+                 (out.last_contributing_sdfgids, one["last"]), (buf.f2d[:F], one["f2d"]),
+                 (buf.sdfgidx_to_fgidx[:D], one["sfg"])):
+        assert np.array_equal(a.cpu().numpy().view(np.uint32) if a.dtype == torch.float32 else a.cpu().numpy(),
+                              b.view(np.uint32) if b.dtype == np.float32 else b)

@@ -159,8 +159,38 @@ struct ProjectArgs {
 #define GS3D_PROJECT_MINB 4
 #endif
 
-// RO: render-only input (stored opacity and 3D covariance).
-template <int DEG, bool RO>
+// Colour of Gaussian gi (mean m) seen from the camera: sh_coeffs_to_color over the normalised
+// view direction (sh.jl:38-112).
+template <int DEG>
+__device__ __forceinline__ float3 gaussian_colour(const ProjectArgs& a, const gs3d_camera& cam, int gi,
+                                                  float mx0, float my0, float mz0) {
+    const float vx = mx0 - cam.position[0], vy = my0 - cam.position[1], vz = mz0 - cam.position[2];
+    const float inv = 1.0f / sqrtf(vx * vx + vy * vy + vz * vz);
+    const float dx = vx * inv, dy = vy * inv, dz = vz * inv;
+    const float* h = a.sh + (size_t)gi * 3 * a.sh_stride;
+    constexpr int NC = (DEG + 1) * (DEG + 1);
+    float hc[3][NC];
+    if (NC == a.sh_stride && ((3 * NC) % 4) == 0 && (reinterpret_cast<uintptr_t>(a.sh) & 15) == 0) {
+        const float4* h4 = reinterpret_cast<const float4*>(h);
+#pragma unroll
+        for (int k = 0; k < (3 * NC) / 4; ++k) {
+            const float4 v = h4[k];
+            (&hc[0][0])[4 * k] = v.x; (&hc[0][0])[4 * k + 1] = v.y;
+            (&hc[0][0])[4 * k + 2] = v.z; (&hc[0][0])[4 * k + 3] = v.w;
+        }
+    } else {
+#pragma unroll
+        for (int c = 0; c < 3; ++c)
+#pragma unroll
+            for (int i = 0; i < NC; ++i) hc[c][i] = h[c * a.sh_stride + i];
+    }
+    return make_float3(sh_channel<DEG>(hc[0], dx, dy, dz), sh_channel<DEG>(hc[1], dx, dy, dz),
+                       sh_channel<DEG>(hc[2], dx, dy, dz));
+}
+
+// RO: render-only input (stored opacity and 3D covariance). COL: also the colour (else left
+// for k_project_colour).
+template <int DEG, bool RO, bool COL = true>
 __global__ void __launch_bounds__(256, GS3D_PROJECT_MINB) k_project(const ProjectArgs a, const gs3d_camera cam,
                                                  const gs3d_tiling til,
                                                  const gs3d_render_options opt) {
@@ -249,37 +279,14 @@ __global__ void __launch_bounds__(256, GS3D_PROJECT_MINB) k_project(const Projec
             bottom = min(cam.height, sat_i32(rintf(my + yr)));
             empty = left > right || top > bottom;
         }
-        // colour from the normalised view direction (sh.jl:38-112)
-        const float vx = mo.x - cam.position[0], vy = mo.y - cam.position[1],
-                    vz = mo.z - cam.position[2];
-        const float inv = 1.0f / sqrtf(vx * vx + vy * vy + vz * vz);
-        const float dx = vx * inv, dy = vy * inv, dz = vz * inv;
-        const float* h = a.sh + (size_t)gi * 3 * a.sh_stride;
-        constexpr int NC = (DEG + 1) * (DEG + 1);
-        float hc[3][NC];
-        if (NC == a.sh_stride && ((3 * NC) % 4) == 0 && (reinterpret_cast<uintptr_t>(a.sh) & 15) == 0) {
-            const float4* h4 = reinterpret_cast<const float4*>(h);
-#pragma unroll
-            for (int k = 0; k < (3 * NC) / 4; ++k) {
-                const float4 v = h4[k];
-                (&hc[0][0])[4 * k] = v.x; (&hc[0][0])[4 * k + 1] = v.y;
-                (&hc[0][0])[4 * k + 2] = v.z; (&hc[0][0])[4 * k + 3] = v.w;
-            }
-        } else {
-#pragma unroll
-            for (int c = 0; c < 3; ++c)
-#pragma unroll
-                for (int i = 0; i < NC; ++i) hc[c][i] = h[c * a.sh_stride + i];
-        }
-        const float col0 = sh_channel<DEG>(hc[0], dx, dy, dz);
-        const float col1 = sh_channel<DEG>(hc[1], dx, dy, dz);
-        const float col2 = sh_channel<DEG>(hc[2], dx, dy, dz);
+        float3 col = make_float3(0.0f, 0.0f, 0.0f);
+        if (COL) col = gaussian_colour<DEG>(a, cam, gi, mo.x, mo.y, mo.z);
 
         a.depths[f] = depth;
         float* rr = a.f2d + 9 * (size_t)f;
         rr[0] = mx; rr[1] = my; rr[2] = opacity;
         rr[3] = c22 * icov_det; rr[4] = -c21 * icov_det; rr[5] = c11 * icov_det;
-        rr[6] = col0; rr[7] = col1; rr[8] = col2;
+        if (COL) { rr[6] = col.x; rr[7] = col.y; rr[8] = col.z; }
         int4 rect;
         int count;
         if (empty) {
@@ -294,6 +301,21 @@ __global__ void __launch_bounds__(256, GS3D_PROJECT_MINB) k_project(const Projec
         }
         reinterpret_cast<int4*>(a.ranges)[f] = rect;
         a.ntiles[f] = count;
+    }
+}
+
+// The colours of the filtered Gaussians (floats 6..8 of their 2D records), for a render whose
+// projection ran without them (GS3D_RENDER_DEFER_COLOUR).
+template <int DEG>
+__global__ void __launch_bounds__(256, GS3D_PROJECT_MINB) k_project_colour(const ProjectArgs a,
+                                                                           const gs3d_camera cam) {
+    const int F = a.counts[0];
+    for (int f = blockIdx.x * blockDim.x + threadIdx.x; f < F; f += gridDim.x * blockDim.x) {
+        const int gi = a.f2g[f] - 1;
+        const float4 mo = a.mo4[gi];
+        const float3 col = gaussian_colour<DEG>(a, cam, gi, mo.x, mo.y, mo.z);
+        float* rr = a.f2d + 9 * (size_t)f;
+        rr[6] = col.x; rr[7] = col.y; rr[8] = col.z;
     }
 }
 
@@ -431,6 +453,8 @@ static int render_forward_impl(const gs3d_render_outputs* outputs, const gs3d_ga
                                int32_t* host_counts, uint32_t flags, gs3d_stream_t stream_) {
     cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
     GS3D_RETURN_IF(check_common(g, cam, til, opt));
+    if (cov && (flags & GS3D_RENDER_DEFER_COLOUR))
+        return invalid("GS3D_RENDER_DEFER_COLOUR is for trainable Gaussians");
     if (!outputs || !buf) return invalid("NULL outputs or buffers");
     if (g->n > buf->capacity_n) return invalid("n = %d exceeds capacity_n = %lld", g->n, (long long)buf->capacity_n);
     if (!buf->keep_gaussians || !buf->fgidx_to_gidx || !buf->depths ||
@@ -493,6 +517,13 @@ static int render_forward_impl(const gs3d_render_outputs* outputs, const gs3d_ga
                 case 2: k_project<2, true><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
                 default: k_project<3, true><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
             }
+        } else if (flags & GS3D_RENDER_DEFER_COLOUR) {
+            switch (opt->sh_degree) {
+                case 0: k_project<0, false, false><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
+                case 1: k_project<1, false, false><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
+                case 2: k_project<2, false, false><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
+                default: k_project<3, false, false><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
+            }
         } else {
             switch (opt->sh_degree) {
                 case 0: k_project<0, false><<<pgrid, 256, 0, stream>>>(pa, *cam, *til, *opt); break;
@@ -531,7 +562,7 @@ static int render_forward_impl(const gs3d_render_outputs* outputs, const gs3d_ga
                                            buf->tiles_end_sdfgidx, buf->df2dgs_codes,
                                            buf->sdf2dgs_codes, buf->sdfgidx_to_fgidx, stream));
         }
-        {
+        if (!(flags & GS3D_RENDER_DEFER_COLOUR)) {
             ProfScope prof("raster", stream);
             GS3D_RETURN_IF(launch_raster(*outputs, *cam, *til, *opt, *buf,
                                          !(flags & GS3D_RENDER_NO_CONTRIB_MASKS), stream));
@@ -586,7 +617,7 @@ static int render_forward_impl(const gs3d_render_outputs* outputs, const gs3d_ga
         GS3D_LAUNCHED("k_tiles_end");
     }
     // F8 / F9
-    {
+    if (!(flags & GS3D_RENDER_DEFER_COLOUR)) {
         ProfScope prof("raster", stream);
         GS3D_RETURN_IF(launch_raster(*outputs, *cam, *til, *opt, *buf,
                                          !(flags & GS3D_RENDER_NO_CONTRIB_MASKS), stream));
@@ -622,6 +653,40 @@ GS3D_API int gs3d_render_forward_render_only(const gs3d_render_outputs* outputs,
     g.sh_coeffs = ro->sh_coeffs;
     return render_forward_impl(outputs, &g, ro->n > 0 ? ro->covariances : nullptr, cam, til, opt,
                                buf, host_counts, flags, stream);
+}
+
+GS3D_API int gs3d_render_forward_colour(const gs3d_render_outputs* outputs,
+                                       const gs3d_gaussians* g, const gs3d_camera* cam,
+                                       const gs3d_tiling* til, const gs3d_render_options* opt,
+                                       gs3d_render_buffers* buf, uint32_t flags,
+                                       gs3d_stream_t stream_) {
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+    GS3D_RETURN_IF(check_common(g, cam, til, opt));
+    if (!outputs || !buf || !buf->fgidx_to_gidx || !buf->device_counts ||
+        !buf->means2d_opacities_inverse_covariances_colors)
+        return invalid("NULL outputs or buffers");
+    if (g->n > buf->capacity_n) return invalid("n = %d exceeds capacity_n = %lld", g->n, (long long)buf->capacity_n);
+    ProjectArgs pa{};
+    pa.mo4 = reinterpret_cast<const float4*>(g->means_opacity_features);
+    pa.sh = g->sh_coeffs;
+    pa.sh_stride = (g->sh_degree + 1) * (g->sh_degree + 1);
+    pa.f2g = buf->fgidx_to_gidx;
+    pa.counts = buf->device_counts;
+    pa.f2d = buf->means2d_opacities_inverse_covariances_colors;
+    const int pgrid = grid_for(g->n, 256, 8);
+    {
+        ProfScope prof("project", stream);
+        switch (opt->sh_degree) {
+            case 0: k_project_colour<0><<<pgrid, 256, 0, stream>>>(pa, *cam); break;
+            case 1: k_project_colour<1><<<pgrid, 256, 0, stream>>>(pa, *cam); break;
+            case 2: k_project_colour<2><<<pgrid, 256, 0, stream>>>(pa, *cam); break;
+            default: k_project_colour<3><<<pgrid, 256, 0, stream>>>(pa, *cam); break;
+        }
+        GS3D_LAUNCHED("k_project_colour");
+    }
+    ProfScope prof("raster", stream);
+    return launch_raster(*outputs, *cam, *til, *opt, *buf, !(flags & GS3D_RENDER_NO_CONTRIB_MASKS),
+                         stream);
 }
 
 GS3D_API int gs3d_render_work_counts(const gs3d_camera* cam, const gs3d_tiling* til,

@@ -20,6 +20,7 @@ GS3D_STATUS_DUP_OVERFLOW = 1
 GS3D_RENDER_NO_HOST_SYNC = 1
 GS3D_RENDER_REFERENCE_ORDER = 2
 GS3D_RENDER_NO_CONTRIB_MASKS = 4
+GS3D_RENDER_DEFER_COLOUR = 8
 GS3D_BACKWARD_FIX_SH16 = 1
 GS3D_BACKWARD_SKIP_SH_GRADS = 2
 GS3D_BACKWARD_ACCUMULATE_ROWS = 4
@@ -139,6 +140,9 @@ SIGNATURES = {
     "gs3d_render_forward": (C.c_int, [P(RenderOutputsC), P(GaussiansC), P(Camera), P(TilingC),
                                       P(RenderOptionsC), P(RenderBuffersC), C.c_void_p,
                                       C.c_uint32, C.c_void_p]),
+    "gs3d_render_forward_colour": (C.c_int, [P(RenderOutputsC), P(GaussiansC), P(Camera), P(TilingC),
+                                             P(RenderOptionsC), P(RenderBuffersC), C.c_uint32,
+                                             C.c_void_p]),
     "gs3d_render_work_counts": (C.c_int, [P(Camera), P(TilingC), P(RenderOptionsC),
                                           P(RenderBuffersC), C.c_void_p, C.c_void_p]),
     "gs3d_render_forward_render_only": (C.c_int, [P(RenderOutputsC), P(RenderOnlyGaussiansC),

@@ -35,7 +35,7 @@ from torch.distributed.distributed_c10d import _coalescing_manager
 from . import _abi
 from . import adc as adc_mod
 from .backward import backward_project_dense, backward_project_factored, backward_raster
-from .render import _stream_handle, render
+from .render import _stream_handle, render, render_colour
 from .training import Trainer
 
 DENSE_ROW = _abi.GS3D_DENSE_ROW
@@ -120,6 +120,10 @@ class DataParallelTrainer(Trainer):
         self.colour = None
         self.colour_recv = None
         self._side = None
+        # all-gathers of the last update still in flight: geometry arrays, SH coefficients
+        self._pending_geom = []
+        self._pending_sh = []
+        self.defer_colour = True  # False: every render waits for all of the last update's gathers
         self._ensure_padded()
 
     # -- padded storage -------------------------------------------------------------------
@@ -209,14 +213,48 @@ class DataParallelTrainer(Trainer):
                           len(self.cameras), self.views, k % self.views)
 
     # -- one step ---------------------------------------------------------------------------
+    def maybe_increase_sh_degree(self) -> None:
+        if (self.iteration_nb % self.options.sh_degree_increase_interval == 0 and
+                self.gaussians.sh_degree < 3):
+            self.sync_parameters()  # the SH arrays are replaced
+        super().maybe_increase_sh_degree()
+
+    def maybe_opacity_reset(self) -> None:
+        o = self.options
+        if (o.opacity_reset_start_iteration_nb <= self.iteration_nb <= o.opacity_reset_final_iteration_nb
+                and self.iteration_nb % o.opacity_reset_interval == 0):
+            self.sync_parameters()  # the reset writes every opacity, the all-gathers some
+        super().maybe_opacity_reset()
+
+    def sync_parameters(self) -> None:
+        """Make the current stream wait for the parameter all-gathers of the last update (a
+        training step starts its first render before the SH coefficients have arrived); call it
+        before reading the parameters outside training_step."""
+        for w in self._pending_geom + self._pending_sh:
+            w.wait()
+        self._pending_geom, self._pending_sh = [], []
+
     def _render_view(self, compute):
         """Render the current view, its loss and its 2D gradients (backward_raster); returns
-        (camera, loss tensor)."""
+        (camera, loss tensor). While the last update's SH all-gathers are in flight, the render
+        runs without colours (filter, projection, duplication, sort) once the geometry arrays
+        have arrived, then waits for the SH coefficients and completes (render_colour)."""
         idx = self.current_camera_index()
         cam = self.cameras[idx]
         rb = self.render_buffers
-        render(self.render_outputs, self.gaussians, cam, self.tiling, self.render_options, rb,
-               host_sync=self.render_host_sync)
+        if self._pending_sh and self.defer_colour:
+            for w in self._pending_geom:
+                w.wait()
+            render(self.render_outputs, self.gaussians, cam, self.tiling, self.render_options, rb,
+                   host_sync=self.render_host_sync, defer_colour=True)
+            for w in self._pending_sh:
+                w.wait()
+            self._pending_geom, self._pending_sh = [], []
+            render_colour(self.render_outputs, self.gaussians, cam, self.tiling, self.render_options, rb)
+        else:
+            self.sync_parameters()
+            render(self.render_outputs, self.gaussians, cam, self.tiling, self.render_options, rb,
+                   host_sync=self.render_host_sync)
         gt = self.target_for(idx)
         loss = self.loss(self.render_outputs.rgb, gt, self.rgb_image_grad)
         if gt is self._gt_buffers[self._gt_slot]:
@@ -376,9 +414,14 @@ class DataParallelTrainer(Trainer):
                     _abi.check(lib.gs3d_adam_step_dense_range(C.byref(g), C.byref(m),
                                                               C.c_void_p(rows.data_ptr()), lo, hi,
                                                               C.byref(params), stream))
-                ag.extend(self._gather_chunk(("mo", "sf", "rf", "sh"), c, async_op=True))
-            for w in ag:
-                w.wait()
+                ag.extend(self._gather_chunk(("mo", "sf", "rf"), c, async_op=True))
+            # the SH coefficients (192 of the 236 bytes per Gaussian) go last; the next step's
+            # first render waits for the geometry arrays, filters, projects, duplicates and sorts,
+            # and only then for the SH coefficients (_render_view)
+            sh = []
+            for c in range(self.chunks):
+                sh.extend(self._gather_chunk(("sh",), c, async_op=True))
+            self._pending_geom, self._pending_sh = ag, sh
         self.optimizer.update_count += 1
         if in_adc:
             self.complete_adc_step()
@@ -392,6 +435,7 @@ class DataParallelTrainer(Trainer):
         return loss_sum
 
     def _densify(self) -> None:
+        self.sync_parameters()
         o = self.options
         a = self.adc_buffers
         self._allreduce(a.accumulated_mean2d_grad_norms_ndc)

@@ -234,6 +234,8 @@ def save_checkpoint(path, trainer) -> None:
     accumulators, iteration number, render SH degree, camera-order state."""
     if trainer.device.type == "cuda":
         torch.cuda.synchronize(trainer.device)
+    if hasattr(trainer, "sync_parameters"):  # data-parallel: all-gathers still in flight
+        trainer.sync_parameters()
     g, m, a = trainer.gaussians, trainer.optimizer.moments, trainer.adc_buffers
     state = {
         "format": "gs3d-checkpoint-1",

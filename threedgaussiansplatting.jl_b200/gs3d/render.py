@@ -19,7 +19,8 @@ def _stream_handle(stream: torch.cuda.Stream | None) -> int:
 def render(outputs: RenderOutputs, gaussians: GaussiansVector, camera: PinholeCamera,
            tiling: Tiling, options: RenderOptions, buffers: RenderBuffers,
            stream: torch.cuda.Stream | None = None, host_sync: bool = True,
-           reference_order: bool = False, contrib_masks: bool = True) -> RenderOutputs:
+           reference_order: bool = False, contrib_masks: bool = True,
+           defer_colour: bool = False) -> RenderOutputs:
     """Render `gaussians` for `camera` into `outputs` (in place), like the reference's
     GPU `render!`. With `host_sync` the call waits once for the duplicate count and grows the
     duplicate buffers when they are too small (the reference's set_nb_dfgaussians!);
@@ -29,7 +30,8 @@ def render(outputs: RenderOutputs, gaussians: GaussiansVector, camera: PinholeCa
     images are the same either way. `gaussians` may also be a RenderOnlyGaussiansVector
     (stored opacities and 3D covariances; gs3d_render_forward_render_only).
     `contrib_masks=False` leaves the buffers' contribution masks unwritten (for renders that no
-    backward follows; GS3D_RENDER_NO_CONTRIB_MASKS)."""
+    backward follows; GS3D_RENDER_NO_CONTRIB_MASKS). `defer_colour=True` stops before the colours
+    and the blend (the SH coefficients are not read); `render_colour` completes the render."""
     if gaussians.n > buffers.capacity_n:
         raise ValueError(f"{gaussians.n} Gaussians exceed the buffers' capacity {buffers.capacity_n}")
     lib = _abi.lib()
@@ -38,6 +40,8 @@ def render(outputs: RenderOutputs, gaussians: GaussiansVector, camera: PinholeCa
         flags |= _abi.GS3D_RENDER_REFERENCE_ORDER
     if not contrib_masks:
         flags |= _abi.GS3D_RENDER_NO_CONTRIB_MASKS
+    if defer_colour:
+        flags |= _abi.GS3D_RENDER_DEFER_COLOUR
     host = buffers.host_counts
     hptr = C.c_void_p(host.data_ptr()) if host is not None else None
     args = (outputs.to_c(), gaussians.to_c(), camera.to_c(), tiling.to_c(), options.to_c())
@@ -54,6 +58,20 @@ def render(outputs: RenderOutputs, gaussians: GaussiansVector, camera: PinholeCa
         _abi.check(st)
         return outputs
     raise RuntimeError("duplicate-key capacity did not converge")
+
+
+def render_colour(outputs: RenderOutputs, gaussians: GaussiansVector, camera: PinholeCamera,
+                  tiling: Tiling, options: RenderOptions, buffers: RenderBuffers,
+                  stream: torch.cuda.Stream | None = None, contrib_masks: bool = True) -> RenderOutputs:
+    """Second half of render(..., defer_colour=True) with the same arguments: the filtered
+    Gaussians' colours and the blend (gs3d_render_forward_colour). The two halves equal one
+    render bit for bit."""
+    flags = 0 if contrib_masks else _abi.GS3D_RENDER_NO_CONTRIB_MASKS
+    args = (outputs.to_c(), gaussians.to_c(), camera.to_c(), tiling.to_c(), options.to_c(),
+            buffers.to_c())
+    _abi.check(_abi.lib().gs3d_render_forward_colour(*(C.byref(x) for x in args), flags,
+                                                     C.c_void_p(_stream_handle(stream))))
+    return outputs
 
 
 def counts(buffers: RenderBuffers) -> tuple[int, int]:
