@@ -136,14 +136,14 @@ typedef struct gs3d_render_buffers {
                                       [3] 1 when the render wrote contrib_masks          */
     void* workspace;               /* scan / sort scratch                               */
     size_t workspace_bytes;
-    /* Optional (NULL: not used). Per-pixel contribution masks the forward blend writes for
-     * the backward blend: one bit per (pixel, duplicated entry) the pixel blended or evaluated
-     * with alpha in [0.999 min_alpha, min_alpha) before it stopped, 32 entries of a tile per
-     * 32-bit word. The
-     * backward then visits only those pairs. The forward writes them (and sets
-     * device_counts[3]) when contrib_mask_words >= (D / 32 + #tiles + 1) * tile pixels and
-     * the tile has a multiple of 32 pixels; otherwise the backward tests every entry itself,
-     * with the same results. */
+    /* Optional (NULL: not used). Contribution masks the forward blend writes for the backward
+     * blend: per 32 duplicated entries of a tile and per warp of the tile (32 pixels), one
+     * 32-bit word whose bit j says that one of the warp's pixels blended entry j, or evaluated
+     * it with alpha in [0.999 min_alpha, min_alpha), before it stopped. The backward then
+     * visits only those entries. The forward writes them (and sets device_counts[3]) when
+     * contrib_mask_words >= (D / 32 + #tiles + 1) * tile pixels / 32 and the tile has a
+     * multiple of 32 pixels; otherwise the backward tests every entry itself, with the same
+     * results. */
     uint32_t* contrib_masks;
     int64_t contrib_mask_words;
 } gs3d_render_buffers;

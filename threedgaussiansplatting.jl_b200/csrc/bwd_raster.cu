@@ -321,6 +321,9 @@ __device__ __forceinline__ bool pair_update(PixelState& s, bool mine, const floa
 // PX pixels per thread: thread t of warp w takes the forward's threads (PX w + p) 32 + lane,
 // p < PX, i.e. PX of the forward's 4 x 8 warp blocks side by side, so one walk over the entries
 // the PX blocks marked serves PX pixels per lane, and one warp reduction per entry covers them.
+// A marked entry is a candidate for every lane: a lane takes it when it lies before its pixel's
+// last contributor and alpha >= min_alpha, the reference's test (an entry its own pixel did not
+// mark has alpha below 0.999 min_alpha there, so the test fails for it as it does in k_bwd_raster).
 template <int PX>
 __global__ void __launch_bounds__(512 / PX, PX == 1 ? 2 : 3) k_bwd_raster_masks(const BwdArgs a,
                                                                                const uint32_t* cmask) {
@@ -343,7 +346,8 @@ __global__ void __launch_bounds__(512 / PX, PX == 1 ? 2 : 3) k_bwd_raster_masks(
     const int tile = txi + tyi * a.tiles_x + 1;
     const int start = tile == 1 ? 0 : a.tiles_end[tile - 2];
     const int end = a.tiles_end[tile - 1];
-    const uint32_t* mrow[PX];
+    const int fwarps = npx >> 5;  // the forward's warps per tile: mask words per row
+    const uint32_t* mrow = cmask + ((int64_t)(start >> 5) + (tile - 1)) * fwarps + warp * PX;
     PixelState st[PX];
     int lrl = 0;
 #pragma unroll
@@ -371,7 +375,6 @@ __global__ void __launch_bounds__(512 / PX, PX == 1 ? 2 : 3) k_bwd_raster_masks(
         s.cpv = (float)V - 0.5f;
         s.rl = lastc > start ? lastc - start : 0;
         lrl = max(lrl, s.rl);
-        mrow[p] = cmask + ((int64_t)(start >> 5) + (tile - 1)) * npx + ft;
     }
 
     // this lane's share of the warp-reduced atomics: pointer and stride of value reduce9_index
@@ -411,33 +414,32 @@ __global__ void __launch_bounds__(512 / PX, PX == 1 ? 2 : 3) k_bwd_raster_masks(
         const int whi = min(wrl - b0, npx);  // the warp's exclusive bound inside the batch
         if (whi <= 0) continue;
         int w = (whi - 1) >> 5;
-        uint32_t mnext[PX];
+        auto words = [&](int ww) {  // the warp's candidates in row ww of the batch
+            const uint32_t* r = mrow + (int64_t)((b0 >> 5) + ww) * fwarps;
+            uint32_t x = r[0];
 #pragma unroll
-        for (int p = 0; p < PX; ++p) mnext[p] = mrow[p][(int64_t)((b0 >> 5) + w) * npx];
+            for (int p = 1; p < PX; ++p) x |= r[p];
+            return x;
+        };
+        uint32_t mnext = words(w);
         for (; w >= 0; --w) {
-            uint32_t m[PX];
-            uint32_t any = 0;
-#pragma unroll
-            for (int p = 0; p < PX; ++p) {
-                m[p] = mnext[p];
-                if (w > 0) mnext[p] = mrow[p][(int64_t)((b0 >> 5) + w - 1) * npx];
-                const int nb = min(st[p].rl - b0, npx) - (w << 5);  // bits below the pixel's bound
-                m[p] = nb >= 32 ? m[p] : (nb <= 0 ? 0u : (m[p] & ((1u << nb) - 1u)));
-                any |= m[p];
-            }
-            uint32_t wm = __reduce_or_sync(0xffffffffu, any);
+            uint32_t wm = mnext;
+            if (w > 0) mnext = words(w - 1);
+            const int nb = whi - (w << 5);  // drop bits at or beyond the warp's bound
+            if (nb < 32) wm &= (1u << nb) - 1u;
             while (wm) {
                 const int j = 31 - __clz(wm);
                 wm &= ~(1u << j);
                 const int en = (w << 5) + j;
+                const int rel = b0 + en;
                 const float4 A = E0[en];
                 const float4 B = E1[en];
                 const float cb = E2[en];
                 float v[9];
-                bool take = pair_update<false>(st[0], (m[0] >> j) & 1u, A, B, cb, min_alpha, max_alpha, v);
+                bool take = pair_update<false>(st[0], rel < st[0].rl, A, B, cb, min_alpha, max_alpha, v);
 #pragma unroll
                 for (int p = 1; p < PX; ++p)
-                    take |= pair_update<true>(st[p], (m[p] >> j) & 1u, A, B, cb, min_alpha, max_alpha, v);
+                    take |= pair_update<true>(st[p], rel < st[p].rl, A, B, cb, min_alpha, max_alpha, v);
                 const unsigned cm = __ballot_sync(0xffffffffu, take);
                 if (cm == 0) continue;
                 const int fg = EF[en];

@@ -89,15 +89,17 @@ __global__ void __launch_bounds__(512, GS3D_RASTER_MINB) k_raster(const RasterAr
     const int start = tile == 1 ? 0 : a.tiles_end[tile - 2];
     const int end = a.tiles_end[tile - 1];
     // contribution masks: row (start / 32 + tile - 1 + c) holds, for chunk c of 32 consecutive
-    // entries of this tile, one 32-bit word per thread; bit j of thread t's word is set when
-    // thread t's pixel blended entry 32 c + j, or evaluated it with alpha within 0.1% below
-    // min_alpha, before it stopped (the entry that stops it comes after its last contributor,
-    // where the backward never looks). Rows of distinct tiles never overlap, and
-    // D / 32 + #tiles + 1 rows cover every tile.
+    // entries of this tile, one 32-bit word per warp; bit j of warp w's word is set when one of
+    // the warp's pixels blended entry 32 c + j, or evaluated it with alpha within 0.1% below
+    // min_alpha, before it stopped (the entry that stops a pixel comes after its last
+    // contributor, where the backward never looks). Rows of distinct tiles never overlap, and
+    // D / 32 + #tiles + 1 rows of nthr / 32 words cover every tile.
+    const int nwarps = nthr >> 5;
     const bool wmask = MASKS && a.cmask != nullptr && (nthr & 31) == 0 &&
-                       (Draw / 32 + (int64_t)a.tiles_x * gridDim.y + 1) * nthr <= a.cmask_words;
+                       (Draw / 32 + (int64_t)a.tiles_x * gridDim.y + 1) * nwarps <= a.cmask_words;
     if (wmask && t == 0 && blockIdx.x == 0 && blockIdx.y == 0) *a.mask_flag = 1;
-    uint32_t* const mrow = wmask ? a.cmask + ((int64_t)(start >> 5) + (tile - 1)) * nthr + t : nullptr;
+    uint32_t* const mrow =
+        wmask ? a.cmask + ((int64_t)(start >> 5) + (tile - 1)) * nwarps + (t >> 5) : nullptr;
 
     const float cu = (float)(lu + 1) - 0.5f, cv = (float)(lv + 1) - 0.5f;
     const float uu = cu * cu, uv = cu * cv, vv = cv * cv;
@@ -168,7 +170,10 @@ __global__ void __launch_bounds__(512, GS3D_RASTER_MINB) k_raster(const RasterAr
                     dep += w * C.y;
                     lastc = base + jj + 1;
                 }
-                if (MASKS && mrow) mrow[(int64_t)((base - start + ch) >> 5) * nthr] = mw;
+                if (MASKS && mrow) {
+                    const uint32_t ww = __reduce_or_sync(0xffffffffu, mw);
+                    if (lane == 0) mrow[(int64_t)((base - start + ch) >> 5) * nwarps] = ww;
+                }
                 if (__all_sync(0xffffffffu, done)) break;
             }
         }

@@ -432,7 +432,8 @@ class RenderBuffers:
     device_counts: torch.Tensor
     workspace: torch.Tensor
     host_counts: torch.Tensor = field(default=None)
-    # per-pixel contribution masks written by the forward blend for the backward blend
+    # contribution masks (one word per warp and 32 entries) written by the forward blend for the
+    # backward blend
     # (gs3d_render_buffers.contrib_masks); None: not used
     contrib_masks: torch.Tensor = field(default=None)
 
@@ -464,7 +465,7 @@ class RenderBuffers:
         if mask_dup == -1:
             mask_dup = min(capacity_dup, 2 * max(capacity_n, 1) + 65536)
         if mask_dup:
-            words = (mask_dup // 32 + max(nb_tiles, 1) + 1) * MAX_TILE_PIXELS
+            words = (mask_dup // 32 + max(nb_tiles, 1) + 1) * (MAX_TILE_PIXELS // 32)
             b.contrib_masks = torch.empty(words, dtype=torch.int32, device=dev)
         return b
 
