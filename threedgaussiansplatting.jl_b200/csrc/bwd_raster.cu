@@ -321,10 +321,11 @@ __device__ __forceinline__ bool pair_update(PixelState& s, bool mine, const floa
 // PX pixels per thread: thread t of warp w takes the forward's threads (PX w + p) 32 + lane,
 // p < PX, i.e. PX of the forward's 4 x 8 warp blocks side by side, so one walk over the entries
 // the PX blocks marked serves PX pixels per lane, and one warp reduction per entry covers them.
-// A marked entry is a candidate for every lane: a lane takes it when it lies before its pixel's
-// last contributor and alpha >= min_alpha, the reference's test (an entry its own pixel did not
-// mark has alpha below 0.999 min_alpha there, so the test fails for it as it does in k_bwd_raster).
-template <int PX>
+// An entry a block marked is a candidate for every pixel of that block: a lane takes it when it
+// lies before its pixel's last contributor and alpha >= min_alpha, the reference's test (where
+// its own pixel did not mark the entry, alpha is below 0.999 min_alpha there and the test fails,
+// as it does in k_bwd_raster). A pixel whose block did not mark the entry skips it as a whole.
+template <int PX>  // 1 or 2
 __global__ void __launch_bounds__(512 / PX, PX == 1 ? 2 : 3) k_bwd_raster_masks(const BwdArgs a,
                                                                                const uint32_t* cmask) {
     extern __shared__ __align__(16) float4 sm4[];
@@ -414,19 +415,22 @@ __global__ void __launch_bounds__(512 / PX, PX == 1 ? 2 : 3) k_bwd_raster_masks(
         const int whi = min(wrl - b0, npx);  // the warp's exclusive bound inside the batch
         if (whi <= 0) continue;
         int w = (whi - 1) >> 5;
-        auto words = [&](int ww) {  // the warp's candidates in row ww of the batch
-            const uint32_t* r = mrow + (int64_t)((b0 >> 5) + ww) * fwarps;
-            uint32_t x = r[0];
+        // the PX forward warps' words of row w of the batch: pixel p takes part in an entry
+        // only when its own 4 x 8 block marked it (a warp-uniform test)
+        uint32_t nxt[PX];
 #pragma unroll
-            for (int p = 1; p < PX; ++p) x |= r[p];
-            return x;
-        };
-        uint32_t mnext = words(w);
+        for (int p = 0; p < PX; ++p) nxt[p] = mrow[(int64_t)((b0 >> 5) + w) * fwarps + p];
         for (; w >= 0; --w) {
-            uint32_t wm = mnext;
-            if (w > 0) mnext = words(w - 1);
+            uint32_t wp[PX];
+            uint32_t wm = 0;
             const int nb = whi - (w << 5);  // drop bits at or beyond the warp's bound
-            if (nb < 32) wm &= (1u << nb) - 1u;
+            const uint32_t keep = nb < 32 ? (1u << nb) - 1u : 0xffffffffu;
+#pragma unroll
+            for (int p = 0; p < PX; ++p) {
+                wp[p] = nxt[p] & keep;
+                if (w > 0) nxt[p] = mrow[(int64_t)((b0 >> 5) + w - 1) * fwarps + p];
+                wm |= wp[p];
+            }
             while (wm) {
                 const int j = 31 - __clz(wm);
                 wm &= ~(1u << j);
@@ -436,10 +440,18 @@ __global__ void __launch_bounds__(512 / PX, PX == 1 ? 2 : 3) k_bwd_raster_masks(
                 const float4 B = E1[en];
                 const float cb = E2[en];
                 float v[9];
-                bool take = pair_update<false>(st[0], rel < st[0].rl, A, B, cb, min_alpha, max_alpha, v);
-#pragma unroll
-                for (int p = 1; p < PX; ++p)
-                    take |= pair_update<true>(st[p], rel < st[p].rl, A, B, cb, min_alpha, max_alpha, v);
+                bool take;
+                const bool u0 = (wp[0] >> j) & 1u;
+                if (PX == 1 || !((wp[PX - 1] >> j) & 1u)) {
+                    take = pair_update<false>(st[0], rel < st[0].rl, A, B, cb, min_alpha, max_alpha, v);
+                } else if (!u0) {
+                    take = pair_update<false>(st[PX - 1], rel < st[PX - 1].rl, A, B, cb, min_alpha,
+                                              max_alpha, v);
+                } else {
+                    take = pair_update<false>(st[0], rel < st[0].rl, A, B, cb, min_alpha, max_alpha, v);
+                    take |= pair_update<true>(st[PX - 1], rel < st[PX - 1].rl, A, B, cb, min_alpha,
+                                              max_alpha, v);
+                }
                 const unsigned cm = __ballot_sync(0xffffffffu, take);
                 if (cm == 0) continue;
                 const int fg = EF[en];
