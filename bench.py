@@ -543,7 +543,23 @@ def densify_leg(trainer, world: int, steady_ms: float, device) -> dict:
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     ms = float(ms.item())
     n1 = trainer.gaussians.n
-    # steady state after the densify step, with the changed model
+    # a second densify step 100 iterations later: the allocations of the first one are cached
+    for _ in range(3):
+        trainer.training_step()
+    trainer.iteration_nb = nxt + 99 if (nxt + 100) % o.opacity_reset_interval else nxt + 199
+    second_it = trainer.iteration_nb + 1
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    trainer.training_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms2 = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(ms2, op=dist.ReduceOp.MAX)
+    ms2 = float(ms2.item())
+    # steady state after the densify steps, with the changed model
     for _ in range(3):
         trainer.training_step()
     if world > 1:
@@ -559,9 +575,12 @@ def densify_leg(trainer, world: int, steady_ms: float, device) -> dict:
         dist.all_reduce(after, op=dist.ReduceOp.MAX)
     return {"iteration": nxt, "densify_step_ms": round(ms, 3), "steady_step_ms": round(steady_ms, 3),
             "densify_extra_ms": round(ms - steady_ms, 3), "n_before": n0, "n_after": n1,
+            "second_iteration": second_it, "second_densify_step_ms": round(ms2, 3),
+            "second_densify_extra_ms": round(ms2 - steady_ms, 3),
             "step_ms_after": round(float(after.item()), 3),
-            "amortised_extra_ms_per_step": round((ms - steady_ms) / 100, 4),
-            "note": "one densify step every 100 iterations within the densify window"}
+            "amortised_extra_ms_per_step": round((ms2 - steady_ms) / 100, 4),
+            "note": "one densify step every 100 iterations within the densify window; the first one "
+                    "also pays the allocation of the new arrays, later ones reuse cached memory"}
 
 
 def main() -> None:
