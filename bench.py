@@ -618,7 +618,7 @@ def main() -> None:
         V = args.global_batch // world
     gv_cpu, cams, pool_host, ro, til, radius = build_workload(device, n_override=args.n_gaussians)
     opts = TrainingOptions(scene_radius=radius)
-    if START_ITERATION + args.warmup + 2 * args.steps + 8 >= START_ITERATION + 100:
+    if START_ITERATION + args.warmup + 2 * args.steps + 8 + 11 >= START_ITERATION + 100:
         opts.adc_interval = 10 ** 9  # keep densify steps out of every measured window
     gv = gv_cpu.to(device)
     pool_dev = [t.to(device) for t in pool_host]
@@ -675,6 +675,22 @@ def main() -> None:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms_max = float(ms_t.item())
     value = world * V * args.steps / (ms_max / 1000.0)
+
+    # ---- where a data-parallel step's time goes (untimed extra steps, every rank alike) ----
+    dp_phases = None
+    if isinstance(trainer, DataParallelTrainer):
+        trainer.training_step()  # its gathers in flight, as before every timed step
+        trainer.phase_events = []
+        k = min(args.steps, 10)
+        t0 = time.perf_counter()
+        for _ in range(k):
+            trainer.training_step()
+        # the host's time to issue a step: at or above the device's step time, the host paces it
+        host_ms = (time.perf_counter() - t0) * 1000.0 / k
+        dp_phases = trainer.phase_times()
+        dp_phases["host_issue_ms_per_step"] = round(host_ms, 4)
+        trainer.phase_events = None
+        trainer.sync_parameters()
 
     # ---- end to end through the public API: pinned host targets in, loss out ----------
     e2e = None
@@ -830,6 +846,7 @@ def main() -> None:
                                   if world > 1 else {})},
             "e2e": e2e, "render": render_fps, "roofline": roofline, "rasterisers": train_rates,
             "cpu_baseline": cpu, "clocks": clk, "gpu_launches": gpu_launches, "stages": stages,
+            "dp_phases": dp_phases,
             "render_config3_4k": render_4k, "densify": densify, "sort_vs_reference_cub": sort_1080,
         }
         print(json.dumps(line), flush=True)

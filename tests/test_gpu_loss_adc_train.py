@@ -237,6 +237,36 @@ def test_data_parallel_trainer_one_rank_matches_trainer(cuda, factored):
     assert torch.allclose(runs[0], runs[1], rtol=1e-5, atol=0), (runs[0], runs[1])
 
 
+def test_data_parallel_phase_times(cuda):
+    """phase_events / phase_times: every phase of a data-parallel step (two views per rank) is
+    recorded once per step per view where it repeats, with non-negative times whose sum stays
+    within the steps' own device time."""
+    from gs3d.dp import DataParallelTrainer
+    gv = synthetic_gaussians(SceneSpec(16_384, "uniform:1", -4.0, 0.5), 9)
+    cams = [look_at_camera(256, 256, 60.0, p) for p in ((0, 0, 3), (0.5, 0.2, 2.8))]
+    ro = RenderOptions.for_camera(cams[0], 3)
+    t = DataParallelTrainer(gv.to(cuda), cams, [target_image(256, 256, 300 + i, cuda) for i in range(2)],
+                            ro, Tiling.for_camera(cams[0]), TrainingOptions(scene_radius=3.3), seed=7,
+                            views_per_rank=2)
+    t.iteration_nb = 3000
+    t.training_step()
+    t.phase_events = []
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(4):
+        t.training_step()
+    t._mark("step_start")  # closes the last step
+    e1.record()
+    torch.cuda.synchronize()
+    total = e0.elapsed_time(e1) / 4
+    ph = t.phase_times()
+    for k in ("render", "loss", "backward_raster", "backward_project", "wait_exchange_0", "adam_0"):
+        assert k in ph, ph
+    assert all(v >= 0 for v in ph.values()), ph
+    assert sum(ph.values()) <= total * 1.05 + 0.05, (ph, total)
+    assert t.phase_events == []
+
+
 def test_checkpoint_resume_follows_the_uninterrupted_run(cuda, tmp_path):
     """gs3d.io.save_checkpoint after 5 steps, then 10 more steps (through the densify and
     opacity-reset step at iteration 3000); a fresh Trainer restored from the checkpoint takes the

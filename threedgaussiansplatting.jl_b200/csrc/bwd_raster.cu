@@ -325,12 +325,14 @@ __device__ __forceinline__ bool pair_update(PixelState& s, bool mine, const floa
 // lies before its pixel's last contributor and alpha >= min_alpha, the reference's test (where
 // its own pixel did not mark the entry, alpha is below 0.999 min_alpha there and the test fails,
 // as it does in k_bwd_raster). A pixel whose block did not mark the entry skips it as a whole.
+// Two-pixel blocks: 4 resident per SM (64 registers, a 16-byte spill) measured 1.123 ms at 3M
+// Gaussians, 1080p, against 1.169 ms for 3 (75 registers, no spill).
 #ifndef GS3D_BWDMASK_MINB
-#define GS3D_BWDMASK_MINB 3
+#define GS3D_BWDMASK_MINB 4
 #endif
 
-template <int PX>  // 1, 2 or 4
-__global__ void __launch_bounds__(512 / PX, PX == 1 ? 2 : PX == 2 ? GS3D_BWDMASK_MINB : 4) k_bwd_raster_masks(const BwdArgs a,
+template <int PX>  // 1 or 2
+__global__ void __launch_bounds__(512 / PX, PX == 1 ? 2 : GS3D_BWDMASK_MINB) k_bwd_raster_masks(const BwdArgs a,
                                                                                const uint32_t* cmask) {
     extern __shared__ __align__(16) float4 sm4[];
     const int nthr = blockDim.x;
@@ -446,16 +448,7 @@ __global__ void __launch_bounds__(512 / PX, PX == 1 ? 2 : PX == 2 ? GS3D_BWDMASK
                 float v[9];
                 bool take;
                 const bool u0 = (wp[0] >> j) & 1u;
-                if (PX > 2) {
-                    take = false;
-#pragma unroll
-                    for (int k = 0; k < 9; ++k) v[k] = 0.0f;
-#pragma unroll
-                    for (int p = 0; p < PX; ++p)
-                        if ((wp[p] >> j) & 1u)
-                            take |= pair_update<true>(st[p], rel < st[p].rl, A, B, cb, min_alpha,
-                                                      max_alpha, v);
-                } else if (PX == 1 || !((wp[PX - 1] >> j) & 1u)) {
+                if (PX == 1 || !((wp[PX - 1] >> j) & 1u)) {
                     take = pair_update<false>(st[0], rel < st[0].rl, A, B, cb, min_alpha, max_alpha, v);
                 } else if (!u0) {
                     take = pair_update<false>(st[PX - 1], rel < st[PX - 1].rl, A, B, cb, min_alpha,
@@ -530,9 +523,7 @@ int launch_bwd_raster(const gs3d_fgradients* fg, const float* rgb_grad,
     const dim3 grid(til->nb_tiles_x, til->nb_tiles_y);
     if (a.use_masks) {
         // two pixels per thread when the tile's warps pair up
-        if ((nthr & 127) == 0 && kBwdPixelsPerThread == 4)
-            k_bwd_raster_masks<4><<<grid, nthr / 4, smem_m, stream>>>(a, buf->contrib_masks);
-        else if ((nthr & 63) == 0 && kBwdPixelsPerThread >= 2)
+        if ((nthr & 63) == 0 && kBwdPixelsPerThread == 2)
             k_bwd_raster_masks<2><<<grid, nthr / 2, smem_m, stream>>>(a, buf->contrib_masks);
         else
             k_bwd_raster_masks<1><<<grid, nthr, smem_m, stream>>>(a, buf->contrib_masks);

@@ -124,6 +124,9 @@ class DataParallelTrainer(Trainer):
         self._pending_geom = []
         self._pending_sh = []
         self.defer_colour = True  # False: every render waits for all of the last update's gathers
+        # a list: each training step appends (phase name, CUDA event recorded on the compute
+        # stream at the end of that phase); see phase_times
+        self.phase_events = None
         self._ensure_padded()
 
     # -- padded storage -------------------------------------------------------------------
@@ -226,6 +229,30 @@ class DataParallelTrainer(Trainer):
             self.sync_parameters()  # the reset writes every opacity, the all-gathers some
         super().maybe_opacity_reset()
 
+    def _mark(self, name: str) -> None:
+        if self.phase_events is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self.phase_events.append((name, ev))
+
+    def phase_times(self) -> dict:
+        """Average milliseconds per step of each phase recorded in phase_events (the compute
+        stream's time from the previous marker to this one: a wait for a collective falls in
+        the phase that ends with it). Synchronizes the device and clears the record."""
+        torch.cuda.synchronize()
+        ev = self.phase_events or []
+        tot, cnt = {}, {}
+        for (_, a), (name, b) in zip(ev, ev[1:]):
+            if name == "step_start":
+                continue
+            tot[name] = tot.get(name, 0.0) + a.elapsed_time(b)
+            cnt[name] = cnt.get(name, 0) + 1
+        self.phase_events = [] if self.phase_events is not None else None
+        # steps recorded: step_start markers followed by a phase (a trailing one only closes)
+        steps = max(1, sum(1 for (n, _), (m, _) in zip(ev, ev[1:] + [("", None)])
+                           if n == "step_start" and m not in ("", "step_start")))
+        return {k: round(v / steps, 4) for k, v in tot.items()}
+
     def sync_parameters(self) -> None:
         """Make the current stream wait for the parameter all-gathers of the last update (a
         training step starts its first render before the SH coefficients have arrived); call it
@@ -245,23 +272,30 @@ class DataParallelTrainer(Trainer):
         if self._pending_sh and self.defer_colour:
             for w in self._pending_geom:
                 w.wait()
+            self._mark("wait_geometry_gather")
             render(self.render_outputs, self.gaussians, cam, self.tiling, self.render_options, rb,
                    host_sync=self.render_host_sync, defer_colour=True)
+            self._mark("render_geometry")
             for w in self._pending_sh:
                 w.wait()
             self._pending_geom, self._pending_sh = [], []
+            self._mark("wait_sh_gather")
             render_colour(self.render_outputs, self.gaussians, cam, self.tiling, self.render_options, rb)
         else:
             self.sync_parameters()
+            self._mark("wait_gathers")
             render(self.render_outputs, self.gaussians, cam, self.tiling, self.render_options, rb,
                    host_sync=self.render_host_sync)
+        self._mark("render")
         gt = self.target_for(idx)
         loss = self.loss(self.render_outputs.rgb, gt, self.rgb_image_grad)
         if gt is self._gt_buffers[self._gt_slot]:
             self._gt_free[self._gt_slot].record(compute)
         self.prefetch_target()
+        self._mark("loss")
         backward_raster(self.fgradients, self.rgb_image_grad, self.render_outputs, self.gaussians,
                         cam, self.tiling, self.render_options, rb)
+        self._mark("backward_raster")
         return cam, loss
 
     def training_step(self) -> torch.Tensor:
@@ -274,6 +308,7 @@ class DataParallelTrainer(Trainer):
         in_adc = self.densifies_this_iteration()
         factored = self._use_factored(in_adc)
         V = self.views
+        self._mark("step_start")
         # zero the rows on a side stream while the first forward runs
         if self._side is None:
             self._side = torch.cuda.Stream(self.device)
@@ -386,6 +421,7 @@ class DataParallelTrainer(Trainer):
             if track_adc:
                 adc_mod.adc_stats(self.adc_buffers, self.fgradients, rb.fgidx_to_gidx, rb.device_counts,
                                   self.width, self.height)
+            self._mark("backward_project")
             self.update_learning_rates()
             params = self.optimizer.params_c(self.render_options.sh_degree)
             g, m = self.gaussians.to_c(), self.optimizer.moments.to_c()
@@ -397,6 +433,7 @@ class DataParallelTrainer(Trainer):
                 if rs:
                     for w in (rs[c] if factored else (rs[c],)):
                         w.wait()
+                self._mark(f"wait_exchange_{c}")
                 lo = c * C_ + self.rank * S
                 hi = min(lo + S, n)
                 if factored:
@@ -414,6 +451,7 @@ class DataParallelTrainer(Trainer):
                     _abi.check(lib.gs3d_adam_step_dense_range(C.byref(g), C.byref(m),
                                                               C.c_void_p(rows.data_ptr()), lo, hi,
                                                               C.byref(params), stream))
+                self._mark(f"adam_{c}")
                 ag.extend(self._gather_chunk(("mo", "sf", "rf"), c, async_op=True))
             # the SH coefficients (192 of the 236 bytes per Gaussian) go last; the next step's
             # first render waits for the geometry arrays, filters, projects, duplicates and sorts,
