@@ -146,6 +146,12 @@ typedef struct gs3d_render_buffers {
      * results. */
     uint32_t* contrib_masks;
     int64_t contrib_mask_words;
+    /* Optional (NULL: tiles in row-major order). nb_tiles int32 that every forward blend fills,
+     * once the tile ends are known, with the 0-based tile indices by descending number of
+     * duplicated entries (8 buckets per octave, any order within a bucket); the forward and
+     * backward blends then take tiles in this order, so that the longest tiles start first and
+     * short ones fill the end of the launch. The results do not depend on it. */
+    int32_t* tile_order;
 } gs3d_render_buffers;
 
 /* RenderOutputs (forward_structs.jl:1-65). Any pointer may be NULL except that backward

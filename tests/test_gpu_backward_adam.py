@@ -20,12 +20,14 @@ pytestmark = pytest.mark.gpu
 KEYS = ["mean2d", "opacity", "licov", "color", "mean3d", "opacity_feature", "scaling", "rotation", "sh"]
 
 
-def run_gpu(gv, cam, til, opt, rgb_grad, device, fix16=False, masks=True):
+def run_gpu(gv, cam, til, opt, rgb_grad, device, fix16=False, masks=True, tile_order=True):
     """masks: the forward writes contribution masks and the backward blend walks them
-    (k_bwd_raster_masks); without, the backward blend tests every entry (k_bwd_raster)."""
+    (k_bwd_raster_masks); without, the backward blend tests every entry (k_bwd_raster).
+    tile_order: both blends take the tiles longest first; without, in row-major order."""
     g = gv.to(device)
     out = RenderOutputs.create(cam.width, cam.height, device)
-    buf = RenderBuffers.create(g.n, til.nb_tiles, device, mask_dup=-1 if masks else None)
+    buf = RenderBuffers.create(g.n, til.nb_tiles, device, mask_dup=-1 if masks else None,
+                               tile_order=tile_order)
     gs3d.render(out, g, cam, til, opt, buf)
     assert int(buf.device_counts[3]) == (1 if masks else 0)
     fg = FilteredGaussiansGradients.create(g.n, g.sh_degree, device)
@@ -126,9 +128,10 @@ CASES = [
 
 
 @pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
-@pytest.mark.parametrize("fix16, masks", [(False, True), (True, True), (False, False)],
-                         ids=["masks", "masks_fix16", "no_masks"])
-def test_backward_random(cuda, case, fix16, masks):
+@pytest.mark.parametrize("fix16, masks, tile_order",
+                         [(False, True, True), (True, True, True), (False, False, True), (False, True, False)],
+                         ids=["masks", "masks_fix16", "no_masks", "masks_row_major"])
+def test_backward_random(cuda, case, fix16, masks, tile_order):
     _, spec, seed, (w, h, fov, pos), tile, kw, deg = case
     gv = synthetic_gaussians(spec, seed)
     cam = look_at_camera(w, h, fov, pos)
@@ -136,7 +139,7 @@ def test_backward_random(cuda, case, fix16, masks):
     til = Tiling.for_camera(cam, *(tile or (None, None)))
     rng = np.random.default_rng(seed)
     grad = rng.normal(0, 1e-5, size=(w, h, 3)).astype(np.float32)
-    gpu, _ = run_gpu(gv, cam, til, opt, grad, cuda, fix16, masks)
+    gpu, _ = run_gpu(gv, cam, til, opt, grad, cuda, fix16, masks, tile_order)
     g = O.NpGaussians.from_vector(gv)
     ref_f = O.render(g, cam, til, opt)
     ref = O.backward(g, cam, til, opt, ref_f, grad, flags=1 if fix16 else 0)

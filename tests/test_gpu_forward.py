@@ -316,6 +316,44 @@ def test_work_counts_vs_oracle(cuda, case):
     assert 0 < contrib <= blends
 
 
+@pytest.mark.parametrize("case", [c for c in CASES if c[0] in ("cfg0", "ragged_720p", "big_tiles_1080")],
+                         ids=lambda c: c[0])
+def test_tile_order(cuda, case):
+    """RenderBuffers.tile_order: a permutation of the tiles by non-increasing bucket of their
+    duplicate counts (8 per octave); the render with it equals the row-major render bit for bit
+    (outputs and contribution masks)."""
+    _, spec, seed, (w, h, fov, pos), tile, kw, deg = case
+    gv = synthetic_gaussians(spec, seed)
+    cam = look_at_camera(w, h, fov, pos)
+    opt = RenderOptions.for_camera(cam, deg, **kw)
+    til = Tiling.for_camera(cam, *(tile or (None, None)))
+    g = gv.to(cuda)
+    res = []
+    for order in (True, False):
+        out = RenderOutputs.create(cam.width, cam.height, cuda, include_depth=True)
+        buf = RenderBuffers.create(g.n, til.nb_tiles, cuda, tile_order=order, mask_dup=16 * g.n)
+        buf.contrib_masks.zero_()
+        gs3d.render(out, g, cam, til, opt, buf)
+        torch.cuda.synchronize()
+        res.append((out, buf))
+    (o1, b1), (o2, b2) = res
+    T = til.nb_tiles
+    order = b1.tile_order[:T].cpu().numpy()
+    assert np.array_equal(np.sort(order), np.arange(T))
+    ends = b1.tiles_end_sdfgidx[:T].cpu().numpy().astype(np.int64)
+    n = np.diff(np.concatenate([[0], ends]))
+    assert n.sum() > 0
+    e = np.floor(np.log2(np.maximum(n, 1))).astype(np.int64)
+    m = np.where(e >= 3, n >> np.maximum(e - 3, 0), n << np.maximum(3 - e, 0)) & 7
+    bucket = np.where(n > 0, 1 + 8 * e + m, 0)
+    assert np.all(np.diff(bucket[order]) <= 0)
+    for a, b in ((o1.rgb, o2.rgb), (o1.transmittance, o2.transmittance), (o1.depth, o2.depth),
+                 (o1.last_contributing_sdfgids, o2.last_contributing_sdfgids),
+                 (b1.contrib_masks, b2.contrib_masks)):
+        assert torch.equal(a, b)
+    assert int(b1.device_counts[3]) == 1
+
+
 @pytest.mark.parametrize("case", [c for c in CASES if c[0] in ("cfg0", "ragged_720p", "deg1_of3")],
                          ids=lambda c: c[0])
 def test_deferred_colour_render_equals_render(cuda, case):

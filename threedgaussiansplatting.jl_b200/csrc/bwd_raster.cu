@@ -32,6 +32,8 @@ struct BwdArgs {
     int32_t width, height, tile_w, tile_h, tiles_x, compact;
     float bg0, bg1, bg2, min_alpha, max_alpha, log_min_alpha;
     int32_t use_masks;  // the masks kernel is launched too (it takes renders with masks)
+    const int32_t* order;  // tiles longest first (NULL: row-major)
+    int32_t nb_tiles;
 };
 
 // Sum 9 per-lane values over the warp by recursive halving: at each of the five xor levels a
@@ -104,7 +106,8 @@ __global__ void __launch_bounds__(512, GS3D_BWDRASTER_MINB) k_bwd_raster(const B
     const int lane = t & 31, warp = t >> 5;
     int lu, lv;
     tile_pixel(a.compact, a.tile_w, a.tile_h, t, lu, lv);
-    const int txi = blockIdx.x, tyi = blockIdx.y;
+    int txi, tyi;
+    if (!block_tile(a.order, a.tiles_x, a.nb_tiles, txi, tyi)) return;
     const int u0 = txi * a.tile_w, v0 = tyi * a.tile_h;
     const int U = u0 + lu + 1, V = v0 + lv + 1;
     const bool inside = U <= a.width && V <= a.height;
@@ -349,7 +352,8 @@ __global__ void __launch_bounds__(512 / PX, PX == 1 ? 2 : GS3D_BWDMASK_MINB) k_b
 
     const int t = threadIdx.x;
     const int lane = t & 31, warp = t >> 5;
-    const int txi = blockIdx.x, tyi = blockIdx.y;
+    int txi, tyi;
+    if (!block_tile(a.order, a.tiles_x, a.nb_tiles, txi, tyi)) return;
     const int tile = txi + tyi * a.tiles_x + 1;
     const int start = tile == 1 ? 0 : a.tiles_end[tile - 2];
     const int end = a.tiles_end[tile - 1];
@@ -513,6 +517,8 @@ int launch_bwd_raster(const gs3d_fgradients* fg, const float* rgb_grad,
     a.min_alpha = opt->min_alpha;
     a.max_alpha = opt->max_alpha;
     a.log_min_alpha = opt->min_alpha > 0.0f ? gs_logf(opt->min_alpha) : -INFINITY;
+    a.order = buf->tile_order;  // the forward blend's order
+    a.nb_tiles = til->nb_tiles_x * til->nb_tiles_y;
     const int nthr = til->tile_width * til->tile_height;
     const size_t smem = (size_t)nthr * (3 * sizeof(float4) + sizeof(float2) + sizeof(int));
     // with contribution masks: k_bwd_raster_masks takes renders that wrote them

@@ -234,6 +234,21 @@ GS_HD float sh_basis(int i, float x, float y, float z) {
 // images), else pixel columns (v fastest).
 GS_HD int compact_tiles(int tw, int th) { return (tw % 4 == 0 && th % 8 == 0) ? 1 : 0; }
 
+// The tile (0-based column txi, row tyi) a block of a (tiles_x, tiles_y) grid takes: tile
+// blockIdx.y * tiles_x + blockIdx.x, or with an order (a permutation of the 0-based tiles) that
+// entry of it; false (skip the block) for an entry out of range.
+__device__ __forceinline__ bool block_tile(const int32_t* order, int tiles_x, int nb_tiles, int& txi,
+                                           int& tyi) {
+    int b = blockIdx.x + blockIdx.y * gridDim.x;
+    if (order) {
+        b = order[b];
+        if (b < 0 || b >= nb_tiles) return false;
+    }
+    txi = b % tiles_x;
+    tyi = b / tiles_x;
+    return true;
+}
+
 __device__ __forceinline__ void tile_pixel(int compact, int tw, int th, int t, int& lu, int& lv) {
     if (compact) {
         const int w = t >> 5, lane = t & 31;

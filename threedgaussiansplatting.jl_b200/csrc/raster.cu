@@ -45,6 +45,8 @@ struct RasterArgs {
     int64_t cmask_words;
     float min_alpha_mark;
     int32_t* mask_flag;         // device_counts[3]
+    const int32_t* order;       // tiles longest first (NULL: row-major)
+    int32_t nb_tiles;
 };
 
 #ifndef GS3D_RASTER_MINB
@@ -66,7 +68,8 @@ __global__ void __launch_bounds__(512, GS3D_RASTER_MINB) k_raster(const RasterAr
     const int lane = t & 31;
     int lu, lv;  // 0-based pixel in tile
     const PixelGroups<GS> pg(a.compact, a.tile_w, a.tile_h, t, lu, lv);
-    const int txi = blockIdx.x, tyi = blockIdx.y;
+    int txi, tyi;
+    if (!block_tile(a.order, a.tiles_x, a.nb_tiles, txi, tyi)) return;
     const int u0 = txi * a.tile_w, v0 = tyi * a.tile_h;
     const int U = u0 + lu + 1, V = v0 + lv + 1;
     const bool inside = U <= a.width && V <= a.height;
@@ -96,7 +99,7 @@ __global__ void __launch_bounds__(512, GS3D_RASTER_MINB) k_raster(const RasterAr
     // D / 32 + #tiles + 1 rows of nthr / 32 words cover every tile.
     const int nwarps = nthr >> 5;
     const bool wmask = MASKS && a.cmask != nullptr && (nthr & 31) == 0 &&
-                       (Draw / 32 + (int64_t)a.tiles_x * gridDim.y + 1) * nwarps <= a.cmask_words;
+                       (Draw / 32 + (int64_t)a.nb_tiles + 1) * nwarps <= a.cmask_words;
     if (wmask && t == 0 && blockIdx.x == 0 && blockIdx.y == 0) *a.mask_flag = 1;
     uint32_t* const mrow =
         wmask ? a.cmask + ((int64_t)(start >> 5) + (tile - 1)) * nwarps + (t >> 5) : nullptr;
@@ -295,7 +298,59 @@ RasterArgs raster_args(const gs3d_render_outputs& out, const gs3d_camera& cam,
     a.cmask_words = buf.contrib_mask_words;
     a.min_alpha_mark = opt.min_alpha * 0.999f;
     a.mask_flag = buf.device_counts + 3;
+    a.order = nullptr;
+    a.nb_tiles = til.nb_tiles_x * til.nb_tiles_y;
     return a;
+}
+
+// Bucket of a tile with n duplicated entries: 0 for none, else 1 + 8 floor(log2 n) + the next
+// three bits of n (at most 248).
+__device__ __forceinline__ int order_bucket(int n) {
+    if (n <= 0) return 0;
+    const int e = 31 - __clz(n);
+    const int m = e >= 3 ? (n >> (e - 3)) & 7 : (n << (3 - e)) & 7;
+    return 1 + 8 * e + m;
+}
+
+// One block: the tiles by descending bucket of their duplicate counts (a counting sort over 256
+// buckets; the order within a bucket is that of the shared-memory atomics). Any tile ends give
+// a permutation (a void render's are not read).
+__global__ void __launch_bounds__(1024) k_tile_order(const int32_t* __restrict__ tiles_end,
+                                                     const int32_t* __restrict__ counts,
+                                                     int64_t capacity_dup, int nb_tiles,
+                                                     int32_t* __restrict__ order) {
+    __shared__ int hist[256];
+    __shared__ int offs[256];
+    const int t = threadIdx.x;
+    const int64_t D = counts[1];
+    const bool valid = counts[0] > 0 && D > 0 && D <= capacity_dup;
+    for (int k = t; k < 256; k += blockDim.x) hist[k] = 0;
+    __syncthreads();
+    for (int i = t; i < nb_tiles; i += blockDim.x) {
+        const int n = valid ? tiles_end[i] - (i ? tiles_end[i - 1] : 0) : 0;
+        atomicAdd(&hist[order_bucket(n)], 1);
+    }
+    __syncthreads();
+    if (t < 32) {
+        // lane L: buckets 255 - 8 L down to 248 - 8 L; exclusive prefix over lanes, descending
+        int local = 0;
+        for (int k = 0; k < 8; ++k) local += hist[255 - 8 * t - k];
+        int incl = local;
+        for (int d = 1; d < 32; d <<= 1) {
+            const int o = __shfl_up_sync(0xffffffffu, incl, d);
+            if (t >= d) incl += o;
+        }
+        int run = incl - local;
+        for (int k = 0; k < 8; ++k) {
+            offs[255 - 8 * t - k] = run;
+            run += hist[255 - 8 * t - k];
+        }
+    }
+    __syncthreads();
+    for (int i = t; i < nb_tiles; i += blockDim.x) {
+        const int n = valid ? tiles_end[i] - (i ? tiles_end[i - 1] : 0) : 0;
+        order[atomicAdd(&offs[order_bucket(n)], 1)] = i;
+    }
 }
 }  // namespace
 
@@ -319,6 +374,12 @@ int launch_raster(const gs3d_render_outputs& out, const gs3d_camera& cam, const 
                   cudaStream_t stream) {
     RasterArgs a = raster_args(out, cam, til, opt, buf);
     if (!masks) a.cmask = nullptr;
+    if (buf.tile_order && a.nb_tiles > 0) {
+        k_tile_order<<<1, 1024, 0, stream>>>(buf.tiles_end_sdfgidx, buf.device_counts,
+                                            buf.capacity_dup, a.nb_tiles, buf.tile_order);
+        GS3D_LAUNCHED("k_tile_order");
+        a.order = buf.tile_order;
+    }
     const int nthr = til.tile_width * til.tile_height;
     const size_t smem = (size_t)nthr * (3 * sizeof(float4) + sizeof(float2));
     dim3 grid(til.nb_tiles_x, til.nb_tiles_y);

@@ -77,7 +77,7 @@ class RenderBuffersC(C.Structure):
                 ("sdfgidx_to_fgidx", C.c_void_p), ("tiles_end_sdfgidx", C.c_void_p),
                 ("device_counts", C.c_void_p), ("workspace", C.c_void_p),
                 ("workspace_bytes", C.c_size_t), ("contrib_masks", C.c_void_p),
-                ("contrib_mask_words", C.c_int64)]
+                ("contrib_mask_words", C.c_int64), ("tile_order", C.c_void_p)]
 
 
 class RenderOutputsC(C.Structure):

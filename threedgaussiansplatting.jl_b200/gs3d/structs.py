@@ -436,13 +436,18 @@ class RenderBuffers:
     # backward blend
     # (gs3d_render_buffers.contrib_masks); None: not used
     contrib_masks: torch.Tensor = field(default=None)
+    # tiles by descending duplicate count, filled by the forward blend and taken in that order by
+    # both blends (gs3d_render_buffers.tile_order); None: row-major order
+    tile_order: torch.Tensor = field(default=None)
 
     @classmethod
     def create(cls, capacity_n: int, nb_tiles: int, device, capacity_dup: int | None = None,
-               keep_cs: bool = True, mask_dup: int | None = -1) -> "RenderBuffers":
+               keep_cs: bool = True, mask_dup: int | None = -1,
+               tile_order: bool = True) -> "RenderBuffers":
         """`mask_dup`: duplicated entries the contribution masks can describe (-1: the smaller
         of capacity_dup and 2 capacity_n + 65536; None or 0: no masks). Renders with more
-        duplicates than that run the backward blend without masks."""
+        duplicates than that run the backward blend without masks. `tile_order`: the blends
+        take the longest tiles first."""
         if capacity_dup is None:
             capacity_dup = max(4 * capacity_n, 1 << 16)
         dev = torch.device(device)
@@ -467,6 +472,8 @@ class RenderBuffers:
         if mask_dup:
             words = (mask_dup // 32 + max(nb_tiles, 1) + 1) * (MAX_TILE_PIXELS // 32)
             b.contrib_masks = torch.empty(words, dtype=torch.int32, device=dev)
+        if tile_order:
+            b.tile_order = torch.empty(max(nb_tiles, 1), **i32)
         return b
 
     def grow_dup(self, needed: int) -> None:
@@ -503,6 +510,8 @@ class RenderBuffers:
         if self.contrib_masks is not None:
             b.contrib_masks = _ptr(self.contrib_masks)
             b.contrib_mask_words = self.contrib_masks.numel()
+        if self.tile_order is not None:
+            b.tile_order = _ptr(self.tile_order)
         return b
 
 
