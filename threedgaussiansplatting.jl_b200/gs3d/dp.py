@@ -345,6 +345,7 @@ class DataParallelTrainer(Trainer):
             if track_adc or in_adc:
                 adc_mod.adc_stats(self.adc_buffers, self.fgradients, rb.fgidx_to_gidx, rb.device_counts,
                                   self.width, self.height)
+            self._mark("backward_project")
         # the last view: its projection backward pipelined with the exchange, chunk by chunk
         self._vi = V - 1
         acc = V > 1
