@@ -222,12 +222,12 @@ def stage_bytes(stage: str, F: int, D: int, n: int, w: int, h: int, passes: int,
 # launch's algorithmic bytes; the full-size traffic is that fraction of the full-size bytes
 # (traffic grows with the same units).
 NCU_TRAFFIC_FRACTION = {
-    # k_bwd_raster_masks<2>: 187.69 MB read + 12.21 MB write at F = 992,004, D = 943,223,
-    # 1920x1080; above the algorithmic bytes by the contribution masks it reads (one 32-bit word
-    # per pixel and 32-entry chunk of its tile, ~64 B per duplicate)
-    "bwd_raster": 199.91e6 / (40.0 * 943_223 + 24.0 * 2_073_600 + 36.0 * 992_004),
-    # k_raster<16, true>: 44.31 MB read + 57.95 MB write (the masks it writes)
-    "raster": 102.26e6 / (40.0 * 943_223 + 20.0 * 2_073_600),
+    # k_bwd_raster_masks<2>: 115.94 MB read + 5.59 MB write at F = 992,004, D = 943,223,
+    # 1920x1080 (the contribution masks it reads are one 32-bit word per warp of 32 pixels and
+    # 32-entry chunk, ~2 B per duplicate)
+    "bwd_raster": 121.53e6 / (40.0 * 943_223 + 24.0 * 2_073_600 + 36.0 * 992_004),
+    # k_raster<16, true>: 39.51 MB read + 7.75 MB write (images and the masks it writes)
+    "raster": 47.26e6 / (40.0 * 943_223 + 20.0 * 2_073_600),
 }
 
 
