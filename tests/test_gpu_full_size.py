@@ -1,8 +1,7 @@
 """Full-size checks on the bench workload (3M Gaussians, 1920x1080, 256
-hemisphere cameras) and the 4K render-only config 3 (6M Gaussians, 3840x2160), where the CPU
-oracle would take minutes per frame. The exact comparisons with the oracle run at smaller sizes
-(test_gpu_forward.py, test_gpu_backward_adam.py); here the CUDA path is held to the properties
-that hold at any size:
+hemisphere cameras) and the 4K render-only config 3 (6M Gaussians, 3840x2160). The exact
+comparisons with the oracle at these sizes are in test_gpu_parity_configs.py; here the CUDA path
+is also held to the properties that hold at any size:
 
 * compaction: keep_gaussians_cs is the inclusive prefix of keep_gaussians, fgidx_to_gidx lists
   the kept Gaussians in order;
