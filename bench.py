@@ -74,6 +74,9 @@ def parse():
     ap.add_argument("--ref-seconds", type=float, default=120.0)
     ap.add_argument("--n-gaussians", type=int, default=None,
                     help="override the Gaussian count (same distributions); for small profiling cases")
+    ap.add_argument("--dp-sh", choices=["gather", "shard"], default="gather",
+                    help="data-parallel factored steps: all-gather the SH coefficients after each "
+                         "update, or keep them with their owners and send the next views' colours")
     ap.add_argument("--dp-exchange", choices=["factored", "dense"], default="factored",
                     help="N > 1: gradient rows exchanged as factored rows (16 floats per Gaussian) "
                          "or dense rows (60)")
@@ -628,7 +631,8 @@ def main() -> None:
     if world > 1 or V > 1:
         trainer = DataParallelTrainer(gv, cams, targets_dev, ro, til, opts, seed=0,
                                       capacity_dup=8 * gv.n, chunks=args.dp_chunks,
-                                      factored=args.dp_exchange == "factored", views_per_rank=V)
+                                      factored=args.dp_exchange == "factored", views_per_rank=V,
+                                      shard_sh=args.dp_sh == "shard")
     else:
         trainer = Trainer(gv, cams, targets_dev, ro, til, opts, seed=0, capacity_dup=8 * gv.n)
     trainer.iteration_nb = START_ITERATION
@@ -842,7 +846,8 @@ def main() -> None:
             "scaling": "strong" if args.global_batch else "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "config": workload_config(world, w, h, gv.n, V),
             "workload_stats": {"filtered_F": F, "duplicates_D": D, "tiles": [til.tile_width, til.tile_height],
-                               **({"dp_exchange": args.dp_exchange, "dp_chunks": trainer.chunks}
+                               **({"dp_exchange": args.dp_exchange, "dp_chunks": trainer.chunks,
+                                   "dp_sh": args.dp_sh}
                                   if world > 1 else {})},
             "e2e": e2e, "render": render_fps, "roofline": roofline, "rasterisers": train_rates,
             "cpu_baseline": cpu, "clocks": clk, "gpu_launches": gpu_launches, "stages": stages,

@@ -62,6 +62,10 @@ typedef struct CUstream_st* gs3d_stream_t; /* ABI-compatible with cudaStream_t *
                                      dense or geometry rows add to the rows (several views
                                      per step) instead of overwriting them; colour rows are
                                      per view and always written                          */
+#define GS3D_BACKWARD_NO_COLOUR_DIRECTION 8u /* gs3d_backward_project_factored: leave the
+                                     colour -> direction term out of the mean gradient and
+                                     read no SH coefficient; the owner of the rows adds it
+                                     (gs3d_factored_colour_direction_range)              */
 
 /* ---- POD parameter structs ---------------------------------------------------------- */
 
@@ -414,7 +418,8 @@ GS3D_API int gs3d_adam_step_dense(
  * Gaussian rebuilds the sum over views from the cameras' positions. Geometry row: the dense row's
  * floats 48..59 (mean, opacity feature, scaling, rotation, touched), summed over views like dense
  * rows. Colour row (one per view, not summed): colour gradients 0..2 and flags at 3,
- * 1 + 2 live0 + 4 live1 + 8 live2 where the Gaussian is filtered in that view, else 0. */
+ * 1 + 2 live0 + 4 live1 + 8 live2 + 16 pos0 + 32 pos1 + 64 pos2 where the Gaussian is filtered
+ * in that view (live: colour >= 0; pos: colour > 0), else 0. */
 #define GS3D_GEOM_ROW 12
 #define GS3D_COLOUR_ROW 4
 #define GS3D_MAX_FACTORED_VIEWS 64
@@ -439,6 +444,48 @@ GS3D_API int gs3d_adam_step_factored_range(
     const gs3d_gaussians* gaussians, const gs3d_adam_moments* moments, const float* geom_rows,
     const float* colour_rows, int32_t n_views, int64_t view_stride, const float* view_positions,
     int32_t g_begin, int32_t g_end, const gs3d_adam_params* params, gs3d_stream_t stream);
+
+/* Sharded SH coefficients (no counterpart in the reference, which trains on one GPU): the rank
+ * that owns Gaussians [g_begin, g_end) is the only one whose SH coefficients of that range are
+ * current. It adds the colour -> direction term of the mean gradient that the other ranks left
+ * out (GS3D_BACKWARD_NO_COLOUR_DIRECTION) before its update, and after the update computes the
+ * colours the next step's views will blend, which then travel instead of the SH coefficients
+ * (12 B per Gaussian and view instead of 192 B per Gaussian).
+ *
+ * gs3d_factored_colour_direction_range: for each Gaussian of the range whose geometry row is
+ * touched and each view v (order 0, 1, ...) whose colour row (row v * view_stride + g - g_begin,
+ * flags > 0) says it filtered the Gaussian, adds to the row's mean gradient the term
+ * gs3d_backward_project_factored adds without the flag (compute from the Gaussian's current SH
+ * coefficients and mean, so call it before the update of the range); view_positions (HOST
+ * memory, 3 floats per view) the cameras the views were rendered from; sh_degree the render's
+ * SH degree; flags: GS3D_BACKWARD_FIX_SH16. With one view the row equals the one
+ * gs3d_backward_project_factored writes without the flag, bit for bit. */
+GS3D_API int gs3d_factored_colour_direction_range(
+    const gs3d_gaussians* gaussians, float* geom_rows, const float* colour_rows, int32_t n_views,
+    int64_t view_stride, const float* view_positions, int32_t g_begin, int32_t g_end,
+    int32_t sh_degree, uint32_t flags, gs3d_stream_t stream);
+
+/* gs3d_shard_colours: the colours (sh_coeffs_to_color, sh.jl:38-112, clamped) of Gaussians
+ * [g_begin, g_end) seen from n_views cameras (view_positions: HOST memory, 3 floats per view),
+ * at SH degree sh_degree: float4 row v * view_stride + g - g_begin of `colours` (16-byte
+ * aligned), w = 0. Each is the value the render's projection stores for that Gaussian and
+ * camera, bit for bit. */
+GS3D_API int gs3d_shard_colours(const gs3d_gaussians* gaussians, int32_t sh_degree,
+                                const float* view_positions, int32_t n_views, int32_t g_begin,
+                                int32_t g_end, float* colours, int64_t view_stride,
+                                gs3d_stream_t stream);
+
+/* gs3d_render_forward_colour with the colours given instead of computed from SH coefficients:
+ * Gaussian g = c N S + q S + i (0 <= q < N = n_ranks, 0 <= i < S = shard_rows) takes float4 row
+ * ((c N + q) V + view) S + i of `colours` (V = n_views; the layout in which rank q's
+ * gs3d_shard_colours output for the views of every rank arrives by one all-to-all per chunk
+ * c). `colours` must hold that row for every g < n. Given the colours gs3d_shard_colours
+ * computes, the outputs equal gs3d_render_forward's bit for bit. */
+GS3D_API int gs3d_render_forward_given_colour(
+    const gs3d_render_outputs* outputs, const gs3d_gaussians* gaussians,
+    const gs3d_camera* camera, const gs3d_tiling* tiling, const gs3d_render_options* options,
+    gs3d_render_buffers* buffers, const float* colours, int64_t shard_rows, int32_t n_ranks,
+    int32_t n_views, int32_t view, uint32_t flags, gs3d_stream_t stream);
 
 /* ---- loss: training.jl:196-217 (L1 + weight * DSSIM, with gradient) ----------------- */
 

@@ -14,7 +14,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from gs3d.dp import (CHUNKS, COLOUR_ROW, DENSE_ROW, GEOM_ROW, chunk_layout, exchange_factored_chunk,
-                     shard_range, view_index)
+                     exchange_next_colours_chunk, given_colour_row, shard_range, view_index)
 
 
 def test_shard_ranges_partition_the_gaussians():
@@ -162,6 +162,50 @@ def test_factored_exchange_on_padded_storage(world, views):
     q = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=_factored_worker, args=(r, world, port, q, views)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, ok in results:
+        assert ok is True, (rank, ok)
+
+
+def _colours_worker(rank, world, port, q, views):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        n = 17
+        S, C_ = chunk_layout(n, world, CHUNKS)
+        recv = torch.full((CHUNKS, world * views * S, 4), -1.0)
+        for c in range(CHUNKS):
+            # owner `rank`: slot r * V + v holds its sub-range's colours for view v of rank r,
+            # encoded as gi * 1000 + r * 10 + v
+            send = torch.full((world * views * S, 4), -2.0)
+            for r in range(world):
+                for v in range(views):
+                    for i in range(S):
+                        gi = c * C_ + rank * S + i
+                        send[(r * views + v) * S + i] = gi * 1000 + r * 10 + v
+            exchange_next_colours_chunk(send, recv[c]).wait()
+        flat = recv.reshape(-1, 4)
+        ok = all(bool(torch.all(flat[given_colour_row(gi, S, world, views, v)] == gi * 1000 + rank * 10 + v))
+                 for gi in range(n) for v in range(views))
+        q.put((rank, ok))
+        dist.destroy_process_group()
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, repr(e)))
+
+
+@pytest.mark.parametrize("world, views", [(2, 1), (3, 2)])
+def test_next_colours_exchange_layout(world, views):
+    """shard_sh: every owner's colours for view v of rank r reach rank r at the row
+    gs3d_render_forward_given_colour reads for that Gaussian and view (given_colour_row)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_colours_worker, args=(r, world, port, q, views)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=120) for _ in range(world)]

@@ -398,7 +398,9 @@ def test_factored_rows_rebuild_dense_rows_over_views(cuda):
         assert int(touched.sum()) > n // 4
         assert torch.equal(colour[:, 3] > 0, touched)
         fl = colour[touched, 3].to(torch.int32)
-        assert torch.all((fl & 1) == 1) and torch.all(fl <= 15)
+        assert torch.all((fl & 1) == 1) and torch.all(fl <= 127)
+        # positive colour implies live (colour >= 0)
+        assert torch.all(((fl >> 4) & ~(fl >> 1) & 7) == 0)
         # a colour row reproduces its dense row's SH gradients: cg * basis(k = 1) on live channels
         c0 = (float(np.float32(0.28209479177387814)) * colour[touched, :3].double()).float()
         live = torch.stack([(fl >> (1 + c)) & 1 for c in range(3)], 1).bool()
@@ -428,6 +430,68 @@ def test_factored_rows_rebuild_dense_rows_over_views(cuda):
         assert torch.equal(x, y)
     for x, y in zip(a1.moments.tensors(), a2.moments.tensors()):
         assert torch.equal(x, y)
+
+
+@pytest.mark.parametrize("deg, fix16", [(3, False), (3, True), (2, False), (0, False)])
+def test_owner_colour_direction_rows(cuda, deg, fix16):
+    """shard_sh's split of the mean gradient: gs3d_backward_project_factored with
+    GS3D_BACKWARD_NO_COLOUR_DIRECTION leaves the colour -> direction term out (the colour rows
+    and the other geometry columns unchanged), and gs3d_factored_colour_direction_range adds it
+    back: with one view the rows equal the full projection backward's bit for bit (render degree
+    `deg`, storage degree 3, two Gaussian ranges); over three views accumulated, the non-mean
+    columns are equal and the means within float rounding of the per-view sums."""
+    from gs3d.backward import backward_project_factored, backward_raster, colour_direction_rows
+    spec = SceneSpec(16_384, "uniform:1", -4.0, 0.5)
+    g = synthetic_gaussians(spec, 5).to(cuda)
+    n = g.n
+    k = 6007
+    f32 = dict(dtype=torch.float32, device=cuda)
+    acc_full = torch.zeros((n, 12), **f32)
+    acc_own = torch.zeros((n, 12), **f32)
+    colours = torch.zeros((3, n, 4), **f32)
+    positions = []
+    for v, pos in enumerate([(0, 0, 3), (2.0, 0.5, 2.2), (-1.5, 1.0, 2.5)]):
+        cam = look_at_camera(256, 256, 60.0, pos)
+        opt = RenderOptions.for_camera(cam, deg)
+        til = Tiling.for_camera(cam)
+        out = RenderOutputs.create(cam.width, cam.height, cuda)
+        buf = RenderBuffers.create(n, til.nb_tiles, cuda)
+        gs3d.render(out, g, cam, til, opt, buf)
+        fg = FilteredGaussiansGradients.create(n, 3, cuda)
+        grad = np.random.default_rng(20 + v).normal(0, 1e-4, size=(256, 256, 3)).astype(np.float32)
+        backward_raster(fg, torch.from_numpy(grad).to(cuda), out, g, cam, til, opt, buf)
+        full = torch.zeros((n, 12), **f32)
+        own = torch.zeros((n, 12), **f32)
+        col_full = torch.zeros((n, 4), **f32)
+        for lo, hi in ((0, k), (k, n)):
+            backward_project_factored(fg, g, cam, til, opt, buf, full[lo:], col_full[lo:], lo, hi,
+                                      fix_sh16=fix16)
+            backward_project_factored(fg, g, cam, til, opt, buf, own[lo:], colours[v, lo:], lo, hi,
+                                      fix_sh16=fix16, colour_direction=False)
+            backward_project_factored(fg, g, cam, til, opt, buf, acc_full[lo:], col_full[lo:], lo, hi,
+                                      fix_sh16=fix16, accumulate=True)
+            backward_project_factored(fg, g, cam, til, opt, buf, acc_own[lo:], colours[v, lo:], lo, hi,
+                                      fix_sh16=fix16, accumulate=True, colour_direction=False)
+        p = np.array([cam.position], dtype=np.float32)
+        positions.append(cam.position)
+        torch.cuda.synchronize()
+        assert torch.equal(colours[v], col_full)
+        assert torch.equal(own[:, 3:], full[:, 3:])
+        if deg > 0:
+            assert not torch.equal(own[:, :3], full[:, :3])
+        for lo, hi in ((0, k), (k, n)):
+            colour_direction_rows(g, own[lo:], colours[v, lo:], 1, hi - lo, p, lo, hi, deg, fix16)
+        torch.cuda.synchronize()
+        assert torch.equal(own, full), v
+    pos3 = np.array(positions, dtype=np.float32)
+    # colour rows of the three views at rows v * n + g (view stride n)
+    flat = colours.reshape(3 * n, 4)
+    for lo, hi in ((0, k), (k, n)):
+        colour_direction_rows(g, acc_own[lo:], flat[lo:], 3, n, pos3, lo, hi, deg, fix16)
+    torch.cuda.synchronize()
+    assert torch.equal(acc_own[:, 3:], acc_full[:, 3:])
+    scale = acc_full[:, :3].abs().max()
+    assert torch.allclose(acc_own[:, :3], acc_full[:, :3], rtol=1e-5, atol=1e-6 * float(scale))
 
 
 def test_factored_adam_rejects_bad_arguments(cuda):

@@ -379,3 +379,53 @@ def test_deferred_colour_render_equals_render(cuda, case):
                  (buf.sdfgidx_to_fgidx[:D], one["sfg"])):
         assert np.array_equal(a.cpu().numpy().view(np.uint32) if a.dtype == torch.float32 else a.cpu().numpy(),
                               b.view(np.uint32) if b.dtype == np.float32 else b)
+
+
+@pytest.mark.parametrize("case", [c for c in CASES if c[0] in ("cfg0", "ragged_720p", "deg1_of3")],
+                         ids=lambda c: c[0])
+def test_given_colour_render_equals_render(cuda, case):
+    """shard_sh's render: colours computed per owner sub-range (gs3d_shard_colours, here for 3
+    ranks x 2 views x 2 chunks, the camera under test as view 1 of rank 0), laid out as rank 0
+    receives them, then render(defer_colour=True) + gs3d_render_forward_given_colour: the
+    render's outputs and buffers bit for bit."""
+    from gs3d.dp import chunk_layout, given_colour_row
+    from gs3d.render import render_given_colour, shard_colours
+    _, spec, seed, (w, h, fov, pos), tile, kw, deg = case
+    gv = synthetic_gaussians(spec, seed)
+    cam = look_at_camera(w, h, fov, pos)
+    opt = RenderOptions.for_camera(cam, deg, **kw)
+    til = Tiling.for_camera(cam, *(tile or (None, None)))
+    one, _ = gpu_render(gv, cam, til, opt, cuda)
+    g = gv.to(cuda)
+    n = g.n
+    world, views, chunks = 3, 2, 2
+    S, C_ = chunk_layout(n, world, chunks)
+    # slot r * V + v: view v of rank r; rank 0's view 1 is the camera under test
+    slots = [look_at_camera(w, h, fov, (0.3 * s_, 1.0, 4.0)).position for s_ in range(world * views)]
+    slots[0 * views + 1] = cam.position
+    slots = np.array(slots, dtype=np.float32)
+    recv = torch.full((chunks, world * views * S, 4), float("nan"), device=cuda)
+    tmp = torch.empty((world * views * S, 4), device=cuda)
+    for c in range(chunks):
+        for q in range(world):  # owner q's block for rank 0: its slots 0 * V + v
+            lo, hi = c * C_ + q * S, min(c * C_ + (q + 1) * S, n)
+            if lo >= hi:
+                continue
+            shard_colours(g, deg, slots, lo, hi, tmp, S)
+            for v in range(views):
+                recv[c, (q * views + v) * S:(q * views + v) * S + (hi - lo)] = \
+                    tmp[(0 * views + v) * S:(0 * views + v) * S + (hi - lo)]
+    flat = recv.reshape(-1, 4)
+    gi = 12345 % n
+    assert given_colour_row(gi, S, world, views, 1) < flat.shape[0]
+    out = RenderOutputs.create(cam.width, cam.height, cuda, include_depth=True)
+    buf = RenderBuffers.create(g.n, til.nb_tiles, cuda)
+    gs3d.render(out, g, cam, til, opt, buf, defer_colour=True)
+    render_given_colour(out, g, cam, til, opt, buf, recv, S, world, views, 1)
+    torch.cuda.synchronize()
+    F, D = one["F"], one["D"]
+    assert gs3d.counts(buf) == (F, D)
+    for a, b in ((out.rgb, one["rgb"]), (out.transmittance, one["trans"]), (out.depth, one["depth"]),
+                 (out.last_contributing_sdfgids, one["last"]), (buf.f2d[:F], one["f2d"])):
+        assert np.array_equal(a.cpu().numpy().view(np.uint32) if a.dtype == torch.float32 else a.cpu().numpy(),
+                              b.view(np.uint32) if b.dtype == np.float32 else b)

@@ -237,6 +237,40 @@ def test_data_parallel_trainer_one_rank_matches_trainer(cuda, factored):
     assert torch.allclose(runs[0], runs[1], rtol=1e-5, atol=0), (runs[0], runs[1])
 
 
+@pytest.mark.parametrize("views", [1, 2])
+def test_data_parallel_sharded_sh_follows_gathered_sh(cuda, views):
+    """DataParallelTrainer(shard_sh=True) on one rank: the owner adds the mean gradients'
+    colour -> direction terms and computes the next step's colours, which the next render takes.
+    Over 8 steps crossing a densify step (which needs every SH coefficient and takes the
+    gathered path), the run equals shard_sh=False bit for bit with one view per step, and within
+    float rounding with two (the mean gradients are then summed in another order)."""
+    from gs3d.dp import DataParallelTrainer
+    cams = [look_at_camera(256, 256, 60.0, p)
+            for p in ((0, 0, 3), (0.5, 0.2, 2.8), (-0.4, 0.3, 2.9), (0.2, -0.5, 3.1))]
+    runs = []
+    for shard in (False, True):
+        gv = synthetic_gaussians(SceneSpec(16_384, "uniform:1", -4.0, 0.5), 9)
+        ro = RenderOptions.for_camera(cams[0], 3)
+        t = DataParallelTrainer(gv.to(cuda), cams, [target_image(256, 256, 300 + i, cuda) for i in range(4)],
+                                ro, Tiling.for_camera(cams[0]), TrainingOptions(scene_radius=3.3), seed=7,
+                                views_per_rank=views, shard_sh=shard)
+        t.iteration_nb = 3096  # steps 3097 .. 3104: a densify step at 3100
+        losses = torch.stack([t.training_step().clone() for _ in range(8)])[:, :3].cpu()
+        t.sync_parameters()
+        torch.cuda.synchronize()
+        runs.append((losses, [x.clone() for x in t.gaussians.tensors()], t.gaussians.n))
+    (l0, p0, n0), (l1, p1, n1) = runs
+    assert n0 == n1
+    if views == 1:
+        assert torch.equal(l0, l1), (l0, l1)
+        for a, b in zip(p0, p1):
+            assert torch.equal(a, b)
+    else:
+        assert torch.allclose(l0, l1, rtol=1e-5, atol=0), (l0, l1)
+        for a, b in zip(p0, p1):
+            assert torch.allclose(a, b, rtol=1e-4, atol=1e-5)
+
+
 def test_data_parallel_phase_times(cuda):
     """phase_events / phase_times: every phase of a data-parallel step (two views per rank) is
     recorded once per step per view where it repeats, with non-negative times whose sum stays

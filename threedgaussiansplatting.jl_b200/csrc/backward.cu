@@ -39,6 +39,77 @@ __device__ __forceinline__ int low3(int i, int j) {
     return lo == 0 ? hi : (lo == 1 ? 2 + hi : 5);
 }
 
+// The colour -> direction Jacobian of sh.jl:175-267 for the channels whose colour is positive
+// (`pos`): Jt[i][c] = d colour_c / d direction_i at the unit direction (x, y, z), from the SH row
+// read linearly as the reference does (hc = mys + c MAXO: coefficients 0 .. 3 MAXO - 1 of the
+// row, sh.jl:196); coefficient 15 in the last degree-3 term unless fix_sh16.
+template <int DEG>
+__device__ __forceinline__ void colour_dir_jacobian(const float* mys, float x, float y, float z,
+                                                    const bool (&pos)[3], int fix_sh16,
+                                                    float (&Jt)[3][3]) {
+    constexpr int MAXO = (DEG + 1) * (DEG + 1);
+#pragma unroll
+    for (int i = 0; i < 3; ++i)
+#pragma unroll
+        for (int c = 0; c < 3; ++c) Jt[i][c] = 0.0f;
+    if (DEG > 0) {
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            if (!pos[c]) continue;
+            const float* hc = mys + c * MAXO;
+            float dy = -sh_c(2) * hc[1];
+            float dz = sh_c(3) * hc[2];
+            float dx = -sh_c(4) * hc[3];
+            if (DEG >= 2) {
+                { const float q = sh_c(5) * hc[4]; dx += y * q; dy += x * q; }
+                { const float q = sh_c(6) * hc[5]; dy += z * q; dz += y * q; }
+                { const float q = sh_c(7) * hc[6]; dx -= 2.0f * x * q; dy -= 2.0f * y * q; dz += 4.0f * z * q; }
+                { const float q = sh_c(8) * hc[7]; dx += z * q; dz += x * q; }
+                { const float q = sh_c(9) * hc[8]; dx += 2.0f * x * q; dy -= 2.0f * y * q; }
+                if (DEG >= 3) {
+                    { const float q = sh_c(10) * hc[9]; dx += 6.0f * x * y * q; dy += 3.0f * (x * x - y * y) * q; }
+                    { const float q = sh_c(11) * hc[10]; dx += y * z * q; dy += x * z * q; dz += x * y * q; }
+                    { const float q = sh_c(12) * hc[11];
+                      dx -= 2.0f * x * y * q;
+                      dy += (4.0f * (z * z) - x * x - 3.0f * (y * y)) * q;
+                      dz += 8.0f * y * z * q; }
+                    { const float q = sh_c(13) * hc[12];
+                      dx -= 6.0f * x * z * q;
+                      dy -= 6.0f * y * z * q;
+                      dz += 3.0f * (2.0f * (z * z) - x * x - y * y) * q; }
+                    { const float q = sh_c(14) * hc[13];
+                      dx += (4.0f * (z * z) - 3.0f * (x * x) - y * y) * q;
+                      dy -= 2.0f * x * y * q;
+                      dz += 8.0f * x * z * q; }
+                    { const float q = sh_c(15) * hc[14]; dx += 2.0f * x * z * q; dy -= 2.0f * y * z * q; dz += (x * x - y * y) * q; }
+                    { const float q = sh_c(16) * (fix_sh16 ? hc[15] : hc[14]);
+                      dx += 3.0f * (x * x - y * y) * q;
+                      dy -= 6.0f * x * y * q; }
+                }
+            }
+            Jt[0][c] = dx; Jt[1][c] = dy; Jt[2][c] = dz;
+        }
+    }
+}
+
+// m3 += the mean3d gradient through the direction's normalisation: inv_vn (I - nd nd^T) Jt cgr.
+__device__ __forceinline__ void add_colour_dir_term(const float (&Jt)[3][3], const float (&cgr)[3],
+                                                    const float (&nd)[3], float inv_vn, float (&m3)[3]) {
+    float ndg[3];
+#pragma unroll
+    for (int i = 0; i < 3; ++i) ndg[i] = Jt[i][0] * cgr[0] + Jt[i][1] * cgr[1] + Jt[i][2] * cgr[2];
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+        float w = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+            const float Nij = i == j ? 1.0f - nd[i] * nd[i] : -nd[i < j ? i : j] * nd[i < j ? j : i];
+            w = w + Nij * ndg[j];
+        }
+        m3[i] = m3[i] + inv_vn * w;
+    }
+}
+
 struct BProjArgs {
     const float4* mo4;
     const float* scal;
@@ -60,13 +131,15 @@ struct BProjArgs {
     int sh_grad_stride;
     int fix_sh16;
     int skip_sh;  // GS3D_BACKWARD_SKIP_SH_GRADS: no SH gradients (F-compact output only)
+    int no_dir;   // GS3D_BACKWARD_NO_COLOUR_DIRECTION: no colour -> direction term, SH not read
     int accumulate;  // GS3D_BACKWARD_ACCUMULATE_ROWS: add into dense / geometry rows
     // NULL, or dense gradient rows indexed by Gaussian (kDenseRow floats, layout in gs3d.h):
     // the 3D gradients then go to row gidx - g_begin instead of the F-compact arrays above
     float* dense;
     // NULL, or the factored rows (dense == NULL): geometry row gidx - g_begin (kGeomRow floats,
     // the dense row's last 12) and colour row gidx - g_begin (the three colour gradients and
-    // the flags 1 + 2 live0 + 4 live1 + 8 live2) instead of the SH gradients
+    // the flags 1 + 2 live0 + 4 live1 + 8 live2 + 16 pos0 + 32 pos1 + 64 pos2) instead of the
+    // SH gradients
     float* geom;
     float4* colour;
     // only filtered Gaussians whose 0-based Gaussian index is in [g_begin, g_end) are done
@@ -243,72 +316,26 @@ __global__ void __launch_bounds__(128, GS3D_BWDPROJ_MINB) k_bwd_project(const BP
         const float cgr[3] = {a.color_g[3 * (size_t)f], a.color_g[3 * (size_t)f + 1],
                               a.color_g[3 * (size_t)f + 2]};
         const float* h = a.sh + (size_t)gi * 3 * a.sh_stride;
-        // the Jacobian reads coefficients 0 .. 3 MAXO - 1 of the row linearly (sh.jl:196)
-        if (DEG > 0) {
-            if ((NSH % 4) == 0 && (reinterpret_cast<uintptr_t>(h) & 15) == 0) {
+        // colour channels that take part in the direction term (positive colour)
+        const bool pos[3] = {!(col[0] <= 0.0f), !(col[1] <= 0.0f), !(col[2] <= 0.0f)};
+        if (!a.no_dir) {
+            // the Jacobian reads coefficients 0 .. 3 MAXO - 1 of the row linearly (sh.jl:196)
+            if (DEG > 0) {
+                if ((NSH % 4) == 0 && (reinterpret_cast<uintptr_t>(h) & 15) == 0) {
 #pragma unroll
-                for (int k = 0; k < NSH / 4; ++k) {
-                    const float4 v4 = reinterpret_cast<const float4*>(h)[k];
-                    mys[4 * k] = v4.x; mys[4 * k + 1] = v4.y; mys[4 * k + 2] = v4.z; mys[4 * k + 3] = v4.w;
-                }
-            } else {
-#pragma unroll
-                for (int k = 0; k < NSH; ++k) mys[k] = h[k];
-            }
-        }
-        float Jt[3][3] = {{0.f, 0.f, 0.f}, {0.f, 0.f, 0.f}, {0.f, 0.f, 0.f}};
-        if (DEG > 0) {
-            const float x = nd0, y = nd1, z = nd2;
-#pragma unroll
-            for (int c = 0; c < 3; ++c) {
-                if (col[c] <= 0.0f) continue;
-                const float* hc = mys + c * MAXO;  // linear indexing with the options order (sh.jl:196)
-                float dy = -sh_c(2) * hc[1];
-                float dz = sh_c(3) * hc[2];
-                float dx = -sh_c(4) * hc[3];
-                if (DEG >= 2) {
-                    { const float q = sh_c(5) * hc[4]; dx += y * q; dy += x * q; }
-                    { const float q = sh_c(6) * hc[5]; dy += z * q; dz += y * q; }
-                    { const float q = sh_c(7) * hc[6]; dx -= 2.0f * x * q; dy -= 2.0f * y * q; dz += 4.0f * z * q; }
-                    { const float q = sh_c(8) * hc[7]; dx += z * q; dz += x * q; }
-                    { const float q = sh_c(9) * hc[8]; dx += 2.0f * x * q; dy -= 2.0f * y * q; }
-                    if (DEG >= 3) {
-                        { const float q = sh_c(10) * hc[9]; dx += 6.0f * x * y * q; dy += 3.0f * (x * x - y * y) * q; }
-                        { const float q = sh_c(11) * hc[10]; dx += y * z * q; dy += x * z * q; dz += x * y * q; }
-                        { const float q = sh_c(12) * hc[11];
-                          dx -= 2.0f * x * y * q;
-                          dy += (4.0f * (z * z) - x * x - 3.0f * (y * y)) * q;
-                          dz += 8.0f * y * z * q; }
-                        { const float q = sh_c(13) * hc[12];
-                          dx -= 6.0f * x * z * q;
-                          dy -= 6.0f * y * z * q;
-                          dz += 3.0f * (2.0f * (z * z) - x * x - y * y) * q; }
-                        { const float q = sh_c(14) * hc[13];
-                          dx += (4.0f * (z * z) - 3.0f * (x * x) - y * y) * q;
-                          dy -= 2.0f * x * y * q;
-                          dz += 8.0f * x * z * q; }
-                        { const float q = sh_c(15) * hc[14]; dx += 2.0f * x * z * q; dy -= 2.0f * y * z * q; dz += (x * x - y * y) * q; }
-                        { const float q = sh_c(16) * hc[a.fix_sh16 ? 15 : 14];
-                          dx += 3.0f * (x * x - y * y) * q;
-                          dy -= 6.0f * x * y * q; }
+                    for (int k = 0; k < NSH / 4; ++k) {
+                        const float4 v4 = reinterpret_cast<const float4*>(h)[k];
+                        mys[4 * k] = v4.x; mys[4 * k + 1] = v4.y; mys[4 * k + 2] = v4.z; mys[4 * k + 3] = v4.w;
                     }
+                } else {
+#pragma unroll
+                    for (int k = 0; k < NSH; ++k) mys[k] = h[k];
                 }
-                Jt[0][c] = dx; Jt[1][c] = dy; Jt[2][c] = dz;
             }
-        }
-        const float nd[3] = {nd0, nd1, nd2};
-        float ndg[3];
-#pragma unroll
-        for (int i = 0; i < 3; ++i) ndg[i] = Jt[i][0] * cgr[0] + Jt[i][1] * cgr[1] + Jt[i][2] * cgr[2];
-#pragma unroll
-        for (int i = 0; i < 3; ++i) {
-            float w = 0.0f;
-#pragma unroll
-            for (int j = 0; j < 3; ++j) {
-                const float Nij = i == j ? 1.0f - nd[i] * nd[i] : -nd[i < j ? i : j] * nd[i < j ? j : i];
-                w = w + Nij * ndg[j];
-            }
-            m3[i] = m3[i] + inv_vn * w;
+            float Jt[3][3];
+            colour_dir_jacobian<DEG>(mys, nd0, nd1, nd2, pos, a.fix_sh16, Jt);
+            const float nd[3] = {nd0, nd1, nd2};
+            add_colour_dir_term(Jt, cgr, nd, inv_vn, m3);
         }
         float* const m3out = drow ? drow + kDMean : a.mean3d_g + 3 * (size_t)f;
         const bool acc = drow && a.accumulate;
@@ -388,7 +415,8 @@ __global__ void __launch_bounds__(128, GS3D_BWDPROJ_MINB) k_bwd_project(const BP
         // their factors: the colour gradients and which channels are live
         if (a.colour) {
             const float fl = 1.0f + (col[0] >= 0.0f ? 2.0f : 0.0f) + (col[1] >= 0.0f ? 4.0f : 0.0f) +
-                             (col[2] >= 0.0f ? 8.0f : 0.0f);
+                             (col[2] >= 0.0f ? 8.0f : 0.0f) + (pos[0] ? 16.0f : 0.0f) +
+                             (pos[1] ? 32.0f : 0.0f) + (pos[2] ? 64.0f : 0.0f);
             a.colour[gi - a.g_begin] = make_float4(cgr[0], cgr[1], cgr[2], fl);
         } else if (!a.skip_sh) {
 #pragma unroll
@@ -426,6 +454,58 @@ __global__ void __launch_bounds__(128, GS3D_BWDPROJ_MINB) k_bwd_project(const BP
       }
       __syncwarp();
     }
+}
+
+// Camera positions of up to GS3D_MAX_FACTORED_VIEWS views, passed by value.
+struct DirViews {
+    float p[GS3D_MAX_FACTORED_VIEWS][3];
+};
+
+// The colour -> direction part of the mean3d gradient, added to factored geometry rows whose
+// projection backward left it out (GS3D_BACKWARD_NO_COLOUR_DIRECTION): for Gaussian g_begin + i
+// and each view v that filtered it (colour row flag > 0), in order v = 0, 1, ..., the term
+// k_bwd_project adds for that view (the same SH row, mean, camera position, colour gradients
+// and positive-colour flags, the same operations), added to the row's mean gradient. With one
+// view this gives the row k_bwd_project writes without the flag, bit for bit.
+template <int DEG>
+__global__ void __launch_bounds__(128) k_colour_dir_rows(const float4* __restrict__ mo4,
+                                                         const float* __restrict__ sh, int sh_stride,
+                                                         float* __restrict__ geom,
+                                                         const float4* __restrict__ colour, int nv,
+                                                         int64_t view_stride, const DirViews vp,
+                                                         int fix_sh16, int64_t g_begin, int64_t g_end) {
+    constexpr int MAXO = (DEG + 1) * (DEG + 1);
+    constexpr int NSH = 3 * MAXO;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= g_end - g_begin) return;
+    float* row = geom + (size_t)i * kGeomRow;
+    if (!(row[kDTouched] > 0.0f)) return;
+    const size_t gi = (size_t)(g_begin + i);
+    const float4 mo = mo4[gi];
+    float mys[NSH];
+    if (DEG > 0) {
+        const float* h = sh + gi * 3 * (size_t)sh_stride;
+#pragma unroll
+        for (int k = 0; k < NSH; ++k) mys[k] = h[k];
+    }
+    float m3[3] = {row[kDMean], row[kDMean + 1], row[kDMean + 2]};
+    for (int v = 0; v < nv; ++v) {
+        const float4 cr = colour[(size_t)v * view_stride + i];
+        if (!(cr.w > 0.0f)) continue;  // not filtered in view v
+        const int fl = (int)cr.w;
+        const bool pos[3] = {((fl >> 4) & 1) != 0, ((fl >> 5) & 1) != 0, ((fl >> 6) & 1) != 0};
+        const float vx = mo.x - vp.p[v][0], vy = mo.y - vp.p[v][1], vz = mo.z - vp.p[v][2];
+        const float inv_vn = 1.0f / sqrtf(vx * vx + vy * vy + vz * vz);
+        const float nd0 = vx * inv_vn, nd1 = vy * inv_vn, nd2 = vz * inv_vn;
+        const float cgr[3] = {cr.x, cr.y, cr.z};
+        float Jt[3][3];
+        colour_dir_jacobian<DEG>(mys, nd0, nd1, nd2, pos, fix_sh16, Jt);
+        const float nd[3] = {nd0, nd1, nd2};
+        add_colour_dir_term(Jt, cgr, nd, inv_vn, m3);
+    }
+    row[kDMean] = m3[0];
+    row[kDMean + 1] = m3[1];
+    row[kDMean + 2] = m3[2];
 }
 
 int grid_for(int64_t items, int threads, int per_sm) {
@@ -510,6 +590,7 @@ int backward_impl(const gs3d_fgradients* fg, const float* rgb_grad,
     p.sh_grad_stride = (fg->sh_degree + 1) * (fg->sh_degree + 1);
     p.fix_sh16 = (flags & GS3D_BACKWARD_FIX_SH16) ? 1 : 0;
     p.skip_sh = (compact_out && (flags & GS3D_BACKWARD_SKIP_SH_GRADS)) ? 1 : 0;
+    p.no_dir = (geom && (flags & GS3D_BACKWARD_NO_COLOUR_DIRECTION)) ? 1 : 0;
     p.accumulate = (!compact_out && (flags & GS3D_BACKWARD_ACCUMULATE_ROWS)) ? 1 : 0;
     p.dense = dense;
     p.geom = geom;
@@ -577,6 +658,43 @@ extern "C" GS3D_API int gs3d_backward_project_dense(const gs3d_fgradients* fg,
     if (!g || g_end > g->n) return invalid("Gaussian range end %d > n", g_end);
     return backward_impl(fg, nullptr, nullptr, g, cam, til, opt, buf, flags, kPhaseProject,
                          dense_rows, 0, g_begin, g_end, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" GS3D_API int gs3d_factored_colour_direction_range(
+    const gs3d_gaussians* g, float* geom_rows, const float* colour_rows, int32_t n_views,
+    int64_t view_stride, const float* view_positions, int32_t g_begin, int32_t g_end,
+    int32_t sh_degree, uint32_t flags, gs3d_stream_t stream_) {
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+    if (!g || !geom_rows || !colour_rows || !view_positions) return invalid("NULL argument");
+    if (sh_degree < 0 || sh_degree > 3 || sh_degree > g->sh_degree)
+        return invalid("SH degree %d (storage %d)", sh_degree, g->sh_degree);
+    if (g_begin < 0 || g_end < g_begin || g_end > g->n)
+        return invalid("Gaussian range [%d, %d) of n = %d", g_begin, g_end, g->n);
+    if (n_views < 1 || n_views > GS3D_MAX_FACTORED_VIEWS)
+        return invalid("%d views (1 .. %d)", n_views, GS3D_MAX_FACTORED_VIEWS);
+    if (view_stride < (int64_t)g_end - g_begin) return invalid("view stride %lld < range", (long long)view_stride);
+    if ((reinterpret_cast<uintptr_t>(colour_rows) & 15) != 0 ||
+        (reinterpret_cast<uintptr_t>(g->means_opacity_features) & 15) != 0)
+        return invalid("colour rows and means must be 16-byte aligned");
+    if (g_end == g_begin) return GS3D_OK;
+    DirViews vp{};
+    for (int v = 0; v < n_views; ++v)
+        for (int k = 0; k < 3; ++k) vp.p[v][k] = view_positions[3 * v + k];
+    const int64_t cnt = (int64_t)g_end - g_begin;
+    const unsigned grid = (unsigned)ceil_div(cnt, 128);
+    const float4* mo4 = reinterpret_cast<const float4*>(g->means_opacity_features);
+    const float4* col = reinterpret_cast<const float4*>(colour_rows);
+    const int stride = (g->sh_degree + 1) * (g->sh_degree + 1);
+    const int fix = (flags & GS3D_BACKWARD_FIX_SH16) ? 1 : 0;
+    ProfScope prof("bwd_project", stream);
+    switch (sh_degree) {
+        case 0: k_colour_dir_rows<0><<<grid, 128, 0, stream>>>(mo4, g->sh_coeffs, stride, geom_rows, col, n_views, view_stride, vp, fix, g_begin, g_end); break;
+        case 1: k_colour_dir_rows<1><<<grid, 128, 0, stream>>>(mo4, g->sh_coeffs, stride, geom_rows, col, n_views, view_stride, vp, fix, g_begin, g_end); break;
+        case 2: k_colour_dir_rows<2><<<grid, 128, 0, stream>>>(mo4, g->sh_coeffs, stride, geom_rows, col, n_views, view_stride, vp, fix, g_begin, g_end); break;
+        default: k_colour_dir_rows<3><<<grid, 128, 0, stream>>>(mo4, g->sh_coeffs, stride, geom_rows, col, n_views, view_stride, vp, fix, g_begin, g_end); break;
+    }
+    GS3D_LAUNCHED("k_colour_dir_rows");
+    return GS3D_OK;
 }
 
 extern "C" GS3D_API int gs3d_backward_project_factored(const gs3d_fgradients* fg,

@@ -161,15 +161,12 @@ struct ProjectArgs {
 
 // Colour of Gaussian gi (mean m) seen from the camera: sh_coeffs_to_color over the normalised
 // view direction (sh.jl:38-112).
+// The SH rows of Gaussian gi (3 channels x (DEG + 1)^2 coefficients) into registers.
 template <int DEG>
-__device__ __forceinline__ float3 gaussian_colour(const ProjectArgs& a, const gs3d_camera& cam, int gi,
-                                                  float mx0, float my0, float mz0) {
-    const float vx = mx0 - cam.position[0], vy = my0 - cam.position[1], vz = mz0 - cam.position[2];
-    const float inv = 1.0f / sqrtf(vx * vx + vy * vy + vz * vz);
-    const float dx = vx * inv, dy = vy * inv, dz = vz * inv;
+__device__ __forceinline__ void load_sh_rows(const ProjectArgs& a, int gi,
+                                             float (&hc)[3][(DEG + 1) * (DEG + 1)]) {
     const float* h = a.sh + (size_t)gi * 3 * a.sh_stride;
     constexpr int NC = (DEG + 1) * (DEG + 1);
-    float hc[3][NC];
     if (NC == a.sh_stride && ((3 * NC) % 4) == 0 && (reinterpret_cast<uintptr_t>(a.sh) & 15) == 0) {
         const float4* h4 = reinterpret_cast<const float4*>(h);
 #pragma unroll
@@ -184,8 +181,25 @@ __device__ __forceinline__ float3 gaussian_colour(const ProjectArgs& a, const gs
 #pragma unroll
             for (int i = 0; i < NC; ++i) hc[c][i] = h[c * a.sh_stride + i];
     }
+}
+
+// sh_coeffs_to_color (sh.jl:38-112) seen from camera position p: the clamped colour.
+template <int DEG>
+__device__ __forceinline__ float3 colour_from_sh(const float (&hc)[3][(DEG + 1) * (DEG + 1)],
+                                                 const float* p, float mx0, float my0, float mz0) {
+    const float vx = mx0 - p[0], vy = my0 - p[1], vz = mz0 - p[2];
+    const float inv = 1.0f / sqrtf(vx * vx + vy * vy + vz * vz);
+    const float dx = vx * inv, dy = vy * inv, dz = vz * inv;
     return make_float3(sh_channel<DEG>(hc[0], dx, dy, dz), sh_channel<DEG>(hc[1], dx, dy, dz),
                        sh_channel<DEG>(hc[2], dx, dy, dz));
+}
+
+template <int DEG>
+__device__ __forceinline__ float3 gaussian_colour(const ProjectArgs& a, const gs3d_camera& cam, int gi,
+                                                  float mx0, float my0, float mz0) {
+    float hc[3][(DEG + 1) * (DEG + 1)];
+    load_sh_rows<DEG>(a, gi, hc);
+    return colour_from_sh<DEG>(hc, cam.position, mx0, my0, mz0);
 }
 
 // RO: render-only input (stored opacity and 3D covariance). COL: also the colour (else left
@@ -314,6 +328,46 @@ __global__ void __launch_bounds__(256, GS3D_PROJECT_MINB) k_project_colour(const
         const int gi = a.f2g[f] - 1;
         const float4 mo = a.mo4[gi];
         const float3 col = gaussian_colour<DEG>(a, cam, gi, mo.x, mo.y, mo.z);
+        float* rr = a.f2d + 9 * (size_t)f;
+        rr[6] = col.x; rr[7] = col.y; rr[8] = col.z;
+    }
+}
+
+// Camera positions of up to GS3D_MAX_FACTORED_VIEWS views, passed by value.
+struct ColourViews {
+    float p[GS3D_MAX_FACTORED_VIEWS][3];
+};
+
+// The colours of Gaussians [g_begin, g_end) seen from nv cameras: row v * view_stride + (gi -
+// g_begin) of out gets view v's colour (the value k_project would store for that Gaussian and
+// camera: same loads, same operations), w = 0.
+template <int DEG>
+__global__ void __launch_bounds__(128) k_shard_colours(const ProjectArgs a, const ColourViews cv,
+                                                       int nv, int64_t g_begin, int64_t g_end,
+                                                       float4* __restrict__ out, int64_t view_stride) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= g_end - g_begin) return;
+    const int gi = (int)(g_begin + i);
+    const float4 mo = a.mo4[gi];
+    float hc[3][(DEG + 1) * (DEG + 1)];
+    load_sh_rows<DEG>(a, gi, hc);
+    for (int v = 0; v < nv; ++v) {
+        const float3 c = colour_from_sh<DEG>(hc, cv.p[v], mo.x, mo.y, mo.z);
+        out[(size_t)v * view_stride + i] = make_float4(c.x, c.y, c.z, 0.0f);
+    }
+}
+
+// Floats 6..8 of the filtered Gaussians' 2D records from colours computed elsewhere: Gaussian gi
+// = c N S + q S + i (0 <= q < N, 0 <= i < S) takes row ((c N + q) V + view) S + i.
+__global__ void __launch_bounds__(256) k_fill_colours(const ProjectArgs a,
+                                                      const float4* __restrict__ colours,
+                                                      int64_t S, int N, int V, int view) {
+    const int F = a.counts[0];
+    const int64_t C = (int64_t)N * S;
+    for (int f = blockIdx.x * blockDim.x + threadIdx.x; f < F; f += gridDim.x * blockDim.x) {
+        const int64_t gi = a.f2g[f] - 1;
+        const int64_t c = gi / C, rem = gi - c * C, q = rem / S, i = rem - q * S;
+        const float4 col = colours[((c * N + q) * V + view) * S + i];
         float* rr = a.f2d + 9 * (size_t)f;
         rr[6] = col.x; rr[7] = col.y; rr[8] = col.z;
     }
@@ -687,6 +741,75 @@ GS3D_API int gs3d_render_forward_colour(const gs3d_render_outputs* outputs,
     ProfScope prof("raster", stream);
     return launch_raster(*outputs, *cam, *til, *opt, *buf, !(flags & GS3D_RENDER_NO_CONTRIB_MASKS),
                          stream);
+}
+
+GS3D_API int gs3d_render_forward_given_colour(const gs3d_render_outputs* outputs,
+                                             const gs3d_gaussians* g, const gs3d_camera* cam,
+                                             const gs3d_tiling* til,
+                                             const gs3d_render_options* opt,
+                                             gs3d_render_buffers* buf, const float* colours,
+                                             int64_t shard_rows, int32_t n_ranks,
+                                             int32_t n_views, int32_t view, uint32_t flags,
+                                             gs3d_stream_t stream_) {
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+    GS3D_RETURN_IF(check_common(g, cam, til, opt));
+    if (!outputs || !buf || !buf->fgidx_to_gidx || !buf->device_counts ||
+        !buf->means2d_opacities_inverse_covariances_colors || !colours)
+        return invalid("NULL outputs, buffers or colours");
+    if (g->n > buf->capacity_n) return invalid("n = %d exceeds capacity_n = %lld", g->n, (long long)buf->capacity_n);
+    if (shard_rows < 1 || n_ranks < 1 || n_views < 1 || view < 0 || view >= n_views)
+        return invalid("colour layout S = %lld, N = %d, V = %d, view %d", (long long)shard_rows,
+                       n_ranks, n_views, view);
+    if ((reinterpret_cast<uintptr_t>(colours) & 15) != 0) return invalid("colours not 16-byte aligned");
+    ProjectArgs pa{};
+    pa.f2g = buf->fgidx_to_gidx;
+    pa.counts = buf->device_counts;
+    pa.f2d = buf->means2d_opacities_inverse_covariances_colors;
+    {
+        ProfScope prof("project", stream);
+        k_fill_colours<<<grid_for(g->n, 256, 8), 256, 0, stream>>>(
+            pa, reinterpret_cast<const float4*>(colours), shard_rows, n_ranks, n_views, view);
+        GS3D_LAUNCHED("k_fill_colours");
+    }
+    ProfScope prof("raster", stream);
+    return launch_raster(*outputs, *cam, *til, *opt, *buf, !(flags & GS3D_RENDER_NO_CONTRIB_MASKS),
+                         stream);
+}
+
+GS3D_API int gs3d_shard_colours(const gs3d_gaussians* g, int32_t sh_degree,
+                                const float* view_positions, int32_t n_views, int32_t g_begin,
+                                int32_t g_end, float* colours, int64_t view_stride,
+                                gs3d_stream_t stream_) {
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+    if (!g || !view_positions || !colours) return invalid("NULL argument");
+    if (sh_degree < 0 || sh_degree > 3 || sh_degree > g->sh_degree)
+        return invalid("SH degree %d (storage %d)", sh_degree, g->sh_degree);
+    if (g_begin < 0 || g_end < g_begin || g_end > g->n)
+        return invalid("Gaussian range [%d, %d) of n = %d", g_begin, g_end, g->n);
+    if (n_views < 1 || n_views > GS3D_MAX_FACTORED_VIEWS)
+        return invalid("%d views (1 .. %d)", n_views, GS3D_MAX_FACTORED_VIEWS);
+    if (view_stride < (int64_t)g_end - g_begin) return invalid("view stride %lld < range", (long long)view_stride);
+    if ((reinterpret_cast<uintptr_t>(colours) & 15) != 0) return invalid("colours not 16-byte aligned");
+    if (g_end == g_begin) return GS3D_OK;
+    ProjectArgs pa{};
+    pa.mo4 = reinterpret_cast<const float4*>(g->means_opacity_features);
+    pa.sh = g->sh_coeffs;
+    pa.sh_stride = (g->sh_degree + 1) * (g->sh_degree + 1);
+    ColourViews cv{};
+    for (int v = 0; v < n_views; ++v)
+        for (int k = 0; k < 3; ++k) cv.p[v][k] = view_positions[3 * v + k];
+    const int64_t cnt = (int64_t)g_end - g_begin;
+    const unsigned grid = (unsigned)ceil_div(cnt, 128);
+    float4* out = reinterpret_cast<float4*>(colours);
+    ProfScope prof("shard_colours", stream);
+    switch (sh_degree) {
+        case 0: k_shard_colours<0><<<grid, 128, 0, stream>>>(pa, cv, n_views, g_begin, g_end, out, view_stride); break;
+        case 1: k_shard_colours<1><<<grid, 128, 0, stream>>>(pa, cv, n_views, g_begin, g_end, out, view_stride); break;
+        case 2: k_shard_colours<2><<<grid, 128, 0, stream>>>(pa, cv, n_views, g_begin, g_end, out, view_stride); break;
+        default: k_shard_colours<3><<<grid, 128, 0, stream>>>(pa, cv, n_views, g_begin, g_end, out, view_stride); break;
+    }
+    GS3D_LAUNCHED("k_shard_colours");
+    return GS3D_OK;
 }
 
 GS3D_API int gs3d_render_work_counts(const gs3d_camera* cam, const gs3d_tiling* til,

@@ -24,6 +24,7 @@ GS3D_RENDER_DEFER_COLOUR = 8
 GS3D_BACKWARD_FIX_SH16 = 1
 GS3D_BACKWARD_SKIP_SH_GRADS = 2
 GS3D_BACKWARD_ACCUMULATE_ROWS = 4
+GS3D_BACKWARD_NO_COLOUR_DIRECTION = 8
 GS3D_DENSE_ROW = 60
 GS3D_GEOM_ROW = 12
 GS3D_COLOUR_ROW = 4
@@ -143,6 +144,16 @@ SIGNATURES = {
     "gs3d_render_forward_colour": (C.c_int, [P(RenderOutputsC), P(GaussiansC), P(Camera), P(TilingC),
                                              P(RenderOptionsC), P(RenderBuffersC), C.c_uint32,
                                              C.c_void_p]),
+    "gs3d_render_forward_given_colour": (C.c_int, [P(RenderOutputsC), P(GaussiansC), P(Camera),
+                                                   P(TilingC), P(RenderOptionsC), P(RenderBuffersC),
+                                                   C.c_void_p, C.c_int64, C.c_int32, C.c_int32,
+                                                   C.c_int32, C.c_uint32, C.c_void_p]),
+    "gs3d_shard_colours": (C.c_int, [P(GaussiansC), C.c_int32, P(C.c_float), C.c_int32, C.c_int32,
+                                     C.c_int32, C.c_void_p, C.c_int64, C.c_void_p]),
+    "gs3d_factored_colour_direction_range": (C.c_int, [P(GaussiansC), C.c_void_p, C.c_void_p,
+                                                       C.c_int32, C.c_int64, P(C.c_float),
+                                                       C.c_int32, C.c_int32, C.c_int32, C.c_uint32,
+                                                       C.c_void_p]),
     "gs3d_render_work_counts": (C.c_int, [P(Camera), P(TilingC), P(RenderOptionsC),
                                           P(RenderBuffersC), C.c_void_p, C.c_void_p]),
     "gs3d_render_forward_render_only": (C.c_int, [P(RenderOutputsC), P(RenderOnlyGaussiansC),

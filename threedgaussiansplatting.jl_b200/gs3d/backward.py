@@ -166,20 +166,42 @@ def backward_project_factored(fgradients: FilteredGaussiansGradients, gaussians:
                               colour_rows: torch.Tensor, g_begin: int, g_end: int,
                               fix_sh16: bool = False,
                               stream: torch.cuda.Stream | None = None,
-                              accumulate: bool = False) -> None:
+                              accumulate: bool = False, colour_direction: bool = True) -> None:
     """backward_project_dense() into factored rows: geometry row (12 floats) and colour row
-    (3 colour gradients + live flags) gidx - g_begin of views starting at row g_begin.
+    (3 colour gradients + flags) gidx - g_begin of views starting at row g_begin.
     `accumulate`: add to the geometry rows (another view of the same step); the colour rows are
-    this view's own."""
+    this view's own. `colour_direction=False`: leave the colour -> direction term of the mean
+    gradient to the rows' owner (colour_direction_rows); the SH coefficients are not read."""
     for t in (geom_rows, colour_rows):
         assert t.is_contiguous() and t.dtype == torch.float32
     lib = _abi.lib()
     args = [fgradients.to_c(), gaussians.to_c(), camera.to_c(), tiling.to_c(), options.to_c(),
             buffers.to_c()]
     flags = (_abi.GS3D_BACKWARD_FIX_SH16 if fix_sh16 else 0) | \
-        (_abi.GS3D_BACKWARD_ACCUMULATE_ROWS if accumulate else 0)
+        (_abi.GS3D_BACKWARD_ACCUMULATE_ROWS if accumulate else 0) | \
+        (0 if colour_direction else _abi.GS3D_BACKWARD_NO_COLOUR_DIRECTION)
     _abi.check(lib.gs3d_backward_project_factored(
         C.byref(args[0]), C.byref(args[1]), C.byref(args[2]), C.byref(args[3]), C.byref(args[4]),
         C.byref(args[5]), flags, C.c_void_p(geom_rows.data_ptr()),
         C.c_void_p(colour_rows.data_ptr()), int(g_begin), int(g_end),
+        C.c_void_p(_stream_handle(stream))))
+
+
+def colour_direction_rows(gaussians: GaussiansVector, geom_rows: torch.Tensor,
+                          colour_rows: torch.Tensor, n_views: int, view_stride: int, positions,
+                          g_begin: int, g_end: int, sh_degree: int, fix_sh16: bool = False,
+                          stream: torch.cuda.Stream | None = None) -> None:
+    """Add to geometry rows [g_begin, g_end) the colour -> direction term of the mean gradient
+    that backward_project_factored(colour_direction=False) left out, for each view whose colour
+    row (row v * view_stride + g - g_begin) filtered the Gaussian
+    (gs3d_factored_colour_direction_range). `positions`: (n_views, 3) camera positions (host)."""
+    import numpy as np
+    pos = np.ascontiguousarray(positions, dtype=np.float32)
+    for t in (geom_rows, colour_rows):
+        assert t.is_contiguous() and t.dtype == torch.float32
+    flags = _abi.GS3D_BACKWARD_FIX_SH16 if fix_sh16 else 0
+    _abi.check(_abi.lib().gs3d_factored_colour_direction_range(
+        C.byref(gaussians.to_c()), C.c_void_p(geom_rows.data_ptr()),
+        C.c_void_p(colour_rows.data_ptr()), int(n_views), int(view_stride),
+        pos.ctypes.data_as(C.POINTER(C.c_float)), int(g_begin), int(g_end), int(sh_degree), flags,
         C.c_void_p(_stream_handle(stream))))

@@ -34,8 +34,9 @@ from torch.distributed.distributed_c10d import _coalescing_manager
 
 from . import _abi
 from . import adc as adc_mod
-from .backward import backward_project_dense, backward_project_factored, backward_raster
-from .render import _stream_handle, render, render_colour
+from .backward import (backward_project_dense, backward_project_factored, backward_raster,
+                       colour_direction_rows)
+from .render import _stream_handle, render, render_colour, render_given_colour, shard_colours
 from .training import Trainer
 
 DENSE_ROW = _abi.GS3D_DENSE_ROW
@@ -85,6 +86,24 @@ def exchange_factored_chunk(geom: torch.Tensor, colour: torch.Tensor, colour_rec
     return tuple(works)
 
 
+def exchange_next_colours_chunk(send: torch.Tensor, recv: torch.Tensor, group=None):
+    """One all-to-all of chunk c's next-step colours (shard_sh): `send` is this rank's
+    (world * V * S, 4) block, slot r * V + v holding its sub-range's colours for view v of rank r;
+    rank r receives in `recv` ((world * V * S, 4)) slot q * V + v from owner q. Over all chunks
+    the received rows are laid out as gs3d_render_forward_given_colour reads them
+    (given_colour_row). Returns the async work."""
+    return dist.all_to_all_single(recv.reshape(-1), send.reshape(-1), group=group, async_op=True)
+
+
+def given_colour_row(gi: int, S: int, world: int, views: int, v: int) -> int:
+    """Row of Gaussian gi's colour for view v in the chunks' received colours (the index
+    k_fill_colours uses): gi = c N S + q S + i -> ((c N + q) V + v) S + i."""
+    C_ = world * S
+    c, rem = divmod(gi, C_)
+    q, i = divmod(rem, S)
+    return ((c * world + q) * views + v) * S + i
+
+
 class DataParallelTrainer(Trainer):
     """`optimizer_step`: "sharded" (reduce-scatter rows, Adam on the rank's sub-ranges,
     all-gather parameters) or "replicated" (all-reduce rows chunk by chunk, the full Adam update
@@ -92,10 +111,17 @@ class DataParallelTrainer(Trainer):
     densify steps): exchange factored rows instead of dense rows, i.e. reduce-scatter the 12
     geometry floats per Gaussian and send each owner the 3 colour gradients of every view
     (all-to-all), from which it rebuilds the 48 SH gradients (gs3d_adam_step_factored_range):
-    16 floats per Gaussian cross the links instead of 60."""
+    16 floats per Gaussian cross the links instead of 60. `shard_sh` (factored steps): the SH
+    coefficients stay with their owners; the projection backward leaves the colour -> direction
+    term of the mean gradient to the owner (gs3d_factored_colour_direction_range), and after its
+    update the owner computes the colours of its Gaussians for every view of the next step
+    (gs3d_shard_colours) and sends them (one all-to-all per chunk, 16 B per Gaussian and view)
+    instead of all-gathering 192 B of SH coefficients per Gaussian; the next render takes them
+    (gs3d_render_forward_given_colour). Steps that need every SH coefficient everywhere (a
+    densify step, sync_parameters) all-gather them first."""
 
     def __init__(self, *args, group=None, optimizer_step: str = "sharded", chunks: int | None = None,
-                 factored: bool = True, views_per_rank: int = 1, **kw):
+                 factored: bool = True, views_per_rank: int = 1, shard_sh: bool = False, **kw):
         super().__init__(*args, **kw)
         if views_per_rank < 1:
             raise ValueError(f"views_per_rank {views_per_rank} < 1")
@@ -124,6 +150,12 @@ class DataParallelTrainer(Trainer):
         self._pending_geom = []
         self._pending_sh = []
         self.defer_colour = True  # False: every render waits for all of the last update's gathers
+        self.shard_sh = bool(shard_sh)
+        self._sh_stale = False  # other ranks' SH sub-ranges out of date here (shard_sh)
+        self._given = None  # colours of this step's views from their owners (shard_sh)
+        self._pending_colours = []  # their all-to-alls still in flight
+        self.colour_send = None
+        self.colour_next = None
         # a list: each training step appends (phase name, CUDA event recorded on the compute
         # stream at the end of that phase); see phase_times
         self.phase_events = None
@@ -167,6 +199,12 @@ class DataParallelTrainer(Trainer):
                 self.colour = torch.zeros((self.views, rows, COLOUR_ROW), **f)
             if self.world > 1 and (self.colour_recv is None or self.colour_recv.shape[3] != S):
                 self.colour_recv = torch.empty((self.chunks, self.views, self.world, S, COLOUR_ROW), **f)
+            if self.shard_sh:
+                shape = (self.chunks, self.world * self.views * S, 4)
+                if self.colour_send is None or self.colour_send.shape != shape:
+                    self.colour_send = torch.zeros(shape, **f)
+                    self.colour_next = torch.zeros(shape, **f) if self.world > 1 else None
+                    self._given = None
 
     def _use_factored(self, in_adc: bool) -> bool:
         return (self.factored and self.optimizer_step == "sharded" and not in_adc and
@@ -181,6 +219,19 @@ class DataParallelTrainer(Trainer):
                                                 len(self.cameras), self.views, v)].position
                         for v in range(self.views) for p in range(self.world)]).astype(np.float32)
         return np.ascontiguousarray(pos)
+
+    def _next_positions(self):
+        """Camera positions (float32) of the next step's views in the order of the colour slots
+        the owners fill: view v of rank r at slot r * views + v."""
+        import numpy as np
+        pos = np.stack([self.cameras[view_index(self.step_index + 1, r, self.world, self.perm,
+                                                len(self.cameras), self.views, v)].position
+                        for r in range(self.world) for v in range(self.views)]).astype(np.float32)
+        return np.ascontiguousarray(pos)
+
+    def _densifies_at(self, it: int) -> bool:
+        o = self.options
+        return o.adc_start_iteration_nb <= it <= o.adc_final_iteration_nb and it % o.adc_interval == 0
 
     def _exchange_factored(self, c: int, S: int, C_: int):
         return exchange_factored_chunk(self.geom, self.colour, self.colour_recv[c], c, S, C_,
@@ -255,11 +306,17 @@ class DataParallelTrainer(Trainer):
 
     def sync_parameters(self) -> None:
         """Make the current stream wait for the parameter all-gathers of the last update (a
-        training step starts its first render before the SH coefficients have arrived); call it
-        before reading the parameters outside training_step."""
-        for w in self._pending_geom + self._pending_sh:
+        training step starts its first render before the SH coefficients have arrived) and,
+        with sharded SH coefficients, all-gather them; call it before reading the parameters
+        outside training_step. With shard_sh it is a collective: every rank calls it at the same
+        point."""
+        for w in self._pending_geom + self._pending_sh + self._pending_colours:
             w.wait()
-        self._pending_geom, self._pending_sh = [], []
+        self._pending_geom, self._pending_sh, self._pending_colours = [], [], []
+        if self._sh_stale:
+            for c in range(self.chunks):
+                self._gather_chunk(("sh",), c, async_op=False)
+            self._sh_stale = False
 
     def _render_view(self, compute):
         """Render the current view, its loss and its 2D gradients (backward_raster); returns
@@ -269,7 +326,24 @@ class DataParallelTrainer(Trainer):
         idx = self.current_camera_index()
         cam = self.cameras[idx]
         rb = self.render_buffers
-        if self._pending_sh and self.defer_colour:
+        if self._given is not None:
+            # the colours of this view come from their owners (shard_sh)
+            for w in self._pending_geom:
+                w.wait()
+            self._pending_geom = []
+            self._mark("wait_geometry_gather")
+            render(self.render_outputs, self.gaussians, cam, self.tiling, self.render_options, rb,
+                   host_sync=self.render_host_sync, defer_colour=True)
+            self._mark("render_geometry")
+            for w in self._pending_colours:
+                w.wait()
+            self._pending_colours = []
+            self._mark("wait_colours")
+            S, _ = chunk_layout(self.gaussians.n, self.world, self.chunks)
+            render_given_colour(self.render_outputs, self.gaussians, cam, self.tiling,
+                                self.render_options, rb, self._given, S, self.world, self.views,
+                                self._vi)
+        elif self._pending_sh and self.defer_colour:
             for w in self._pending_geom:
                 w.wait()
             self._mark("wait_geometry_gather")
@@ -308,6 +382,8 @@ class DataParallelTrainer(Trainer):
         in_adc = self.densifies_this_iteration()
         factored = self._use_factored(in_adc)
         V = self.views
+        if self._sh_stale and not factored:
+            self.sync_parameters()  # this step reads every SH coefficient on every rank
         self._mark("step_start")
         # zero the rows on a side stream while the first forward runs
         if self._side is None:
@@ -338,7 +414,7 @@ class DataParallelTrainer(Trainer):
             if factored:
                 backward_project_factored(self.fgradients, self.gaussians, cam, self.tiling,
                                           self.render_options, rb, self.geom, self.colour[v], 0, n,
-                                          accumulate=v > 0)
+                                          accumulate=v > 0, colour_direction=not self.shard_sh)
             else:
                 backward_project_dense(self.fgradients, self.gaussians, cam, self.tiling,
                                        self.render_options, rb, self.dense, 0, n, accumulate=v > 0)
@@ -405,7 +481,8 @@ class DataParallelTrainer(Trainer):
                     if lo < hi:
                         backward_project_factored(self.fgradients, self.gaussians, cam, self.tiling,
                                                   self.render_options, rb, self.geom[lo:],
-                                                  self.colour[V - 1, lo:], lo, hi, accumulate=acc)
+                                                  self.colour[V - 1, lo:], lo, hi, accumulate=acc,
+                                                  colour_direction=not self.shard_sh)
                     if self.world > 1:
                         rs.append(self._exchange_factored(c, S, C_))
                     continue
@@ -427,9 +504,16 @@ class DataParallelTrainer(Trainer):
             params = self.optimizer.params_c(self.render_options.sh_degree)
             g, m = self.gaussians.to_c(), self.optimizer.moments.to_c()
             ag = []
+            cw = []
+            # shard_sh: the owners send the next step's colours instead of all-gathering the SH
+            # coefficients, unless the next step densifies (it needs them everywhere)
+            give = factored and self.shard_sh and not self._densifies_at(self.iteration_nb + 1)
+            self._given = None  # every view of this step has been rendered
             if factored:
                 pos = self._view_positions()
                 pos_p = pos.ctypes.data_as(C.POINTER(C.c_float))
+                if give:
+                    next_pos = self._next_positions()
             for c in range(self.chunks):
                 if rs:
                     for w in (rs[c] if factored else (rs[c],)):
@@ -443,10 +527,19 @@ class DataParallelTrainer(Trainer):
                             views, stride = self.colour_recv[c], S
                         else:
                             views, stride = self.colour[0, lo:], self.colour.shape[1]
+                        if self.shard_sh:
+                            # the mean gradients' colour -> direction terms, from the SH
+                            # coefficients and means before their update
+                            colour_direction_rows(self.gaussians, self.geom[lo:], views,
+                                                  self.world * V, stride, pos, lo, hi,
+                                                  self.render_options.sh_degree)
                         _abi.check(lib.gs3d_adam_step_factored_range(
                             C.byref(g), C.byref(m), C.c_void_p(self.geom[lo:].data_ptr()),
                             C.c_void_p(views.data_ptr()), self.world * V, stride, pos_p, lo, hi,
                             C.byref(params), stream))
+                        if give:
+                            shard_colours(self.gaussians, self.render_options.sh_degree, next_pos,
+                                          lo, hi, self.colour_send[c], S)
                 elif lo < hi:
                     rows = self.dense[lo:]
                     _abi.check(lib.gs3d_adam_step_dense_range(C.byref(g), C.byref(m),
@@ -454,13 +547,21 @@ class DataParallelTrainer(Trainer):
                                                               C.byref(params), stream))
                 self._mark(f"adam_{c}")
                 ag.extend(self._gather_chunk(("mo", "sf", "rf"), c, async_op=True))
+                if give and self.world > 1:
+                    cw.append(exchange_next_colours_chunk(self.colour_send[c], self.colour_next[c],
+                                                          self.group))
             # the SH coefficients (192 of the 236 bytes per Gaussian) go last; the next step's
             # first render waits for the geometry arrays, filters, projects, duplicates and sorts,
-            # and only then for the SH coefficients (_render_view)
+            # and only then for the SH coefficients or the colours (_render_view)
             sh = []
-            for c in range(self.chunks):
-                sh.extend(self._gather_chunk(("sh",), c, async_op=True))
-            self._pending_geom, self._pending_sh = ag, sh
+            if give:
+                self._given = self.colour_next if self.world > 1 else self.colour_send
+                self._sh_stale = self.world > 1
+            else:
+                for c in range(self.chunks):
+                    sh.extend(self._gather_chunk(("sh",), c, async_op=True))
+                self._sh_stale = False
+            self._pending_geom, self._pending_sh, self._pending_colours = ag, sh, cw
         self.optimizer.update_count += 1
         if in_adc:
             self.complete_adc_step()

@@ -74,6 +74,37 @@ def render_colour(outputs: RenderOutputs, gaussians: GaussiansVector, camera: Pi
     return outputs
 
 
+def render_given_colour(outputs: RenderOutputs, gaussians: GaussiansVector, camera: PinholeCamera,
+                        tiling: Tiling, options: RenderOptions, buffers: RenderBuffers,
+                        colours: torch.Tensor, shard_rows: int, n_ranks: int = 1,
+                        n_views: int = 1, view: int = 0, stream: torch.cuda.Stream | None = None,
+                        contrib_masks: bool = True) -> RenderOutputs:
+    """Second half of render(..., defer_colour=True) with the colours given (float4 rows of
+    `colours` in the layout of gs3d_render_forward_given_colour: Gaussian g = c N S + q S + i takes
+    row ((c N + q) V + view) S + i) instead of computed from the SH coefficients."""
+    assert colours.is_contiguous() and colours.dtype == torch.float32
+    flags = 0 if contrib_masks else _abi.GS3D_RENDER_NO_CONTRIB_MASKS
+    args = (outputs.to_c(), gaussians.to_c(), camera.to_c(), tiling.to_c(), options.to_c(),
+            buffers.to_c())
+    _abi.check(_abi.lib().gs3d_render_forward_given_colour(
+        *(C.byref(x) for x in args), C.c_void_p(colours.data_ptr()), int(shard_rows), int(n_ranks),
+        int(n_views), int(view), flags, C.c_void_p(_stream_handle(stream))))
+    return outputs
+
+
+def shard_colours(gaussians: GaussiansVector, sh_degree: int, positions, g_begin: int, g_end: int,
+                  out: torch.Tensor, view_stride: int, stream: torch.cuda.Stream | None = None) -> None:
+    """Colours of Gaussians [g_begin, g_end) from the cameras at `positions` ((n, 3) float32,
+    host) into float4 rows v * view_stride + g - g_begin of `out` (gs3d_shard_colours)."""
+    import numpy as np
+    pos = np.ascontiguousarray(positions, dtype=np.float32)
+    assert out.is_contiguous() and out.dtype == torch.float32
+    _abi.check(_abi.lib().gs3d_shard_colours(
+        C.byref(gaussians.to_c()), int(sh_degree), pos.ctypes.data_as(C.POINTER(C.c_float)),
+        int(pos.shape[0]), int(g_begin), int(g_end), C.c_void_p(out.data_ptr()), int(view_stride),
+        C.c_void_p(_stream_handle(stream))))
+
+
 def counts(buffers: RenderBuffers) -> tuple[int, int]:
     """(F, D) of the last render (reads device memory; synchronises)."""
     c = buffers.device_counts.cpu()
