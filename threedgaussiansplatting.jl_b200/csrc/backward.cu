@@ -485,8 +485,16 @@ __global__ void __launch_bounds__(128) k_colour_dir_rows(const float4* __restric
     float mys[NSH];
     if (DEG > 0) {
         const float* h = sh + gi * 3 * (size_t)sh_stride;
+        if ((NSH % 4) == 0 && (reinterpret_cast<uintptr_t>(h) & 15) == 0) {
 #pragma unroll
-        for (int k = 0; k < NSH; ++k) mys[k] = h[k];
+            for (int k = 0; k < NSH / 4; ++k) {
+                const float4 v4 = __ldg(reinterpret_cast<const float4*>(h) + k);
+                mys[4 * k] = v4.x; mys[4 * k + 1] = v4.y; mys[4 * k + 2] = v4.z; mys[4 * k + 3] = v4.w;
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < NSH; ++k) mys[k] = h[k];
+        }
     }
     float m3[3] = {row[kDMean], row[kDMean + 1], row[kDMean + 2]};
     for (int v = 0; v < nv; ++v) {
