@@ -74,9 +74,10 @@ def parse():
     ap.add_argument("--ref-seconds", type=float, default=120.0)
     ap.add_argument("--n-gaussians", type=int, default=None,
                     help="override the Gaussian count (same distributions); for small profiling cases")
-    ap.add_argument("--dp-sh", choices=["gather", "shard"], default="gather",
+    ap.add_argument("--dp-sh", choices=["auto", "gather", "shard"], default="auto",
                     help="data-parallel factored steps: all-gather the SH coefficients after each "
-                         "update, or keep them with their owners and send the next views' colours")
+                         "update, or keep them with their owners and send the next views' colours "
+                         "(auto: shard with N > 1)")
     ap.add_argument("--dp-exchange", choices=["factored", "dense"], default="factored",
                     help="N > 1: gradient rows exchanged as factored rows (16 floats per Gaussian) "
                          "or dense rows (60)")
@@ -632,7 +633,7 @@ def main() -> None:
         trainer = DataParallelTrainer(gv, cams, targets_dev, ro, til, opts, seed=0,
                                       capacity_dup=8 * gv.n, chunks=args.dp_chunks,
                                       factored=args.dp_exchange == "factored", views_per_rank=V,
-                                      shard_sh=args.dp_sh == "shard")
+                                      shard_sh=None if args.dp_sh == "auto" else args.dp_sh == "shard")
     else:
         trainer = Trainer(gv, cams, targets_dev, ro, til, opts, seed=0, capacity_dup=8 * gv.n)
     trainer.iteration_nb = START_ITERATION
@@ -847,7 +848,7 @@ def main() -> None:
             "data": "synthetic", "config": workload_config(world, w, h, gv.n, V),
             "workload_stats": {"filtered_F": F, "duplicates_D": D, "tiles": [til.tile_width, til.tile_height],
                                **({"dp_exchange": args.dp_exchange, "dp_chunks": trainer.chunks,
-                                   "dp_sh": args.dp_sh}
+                                   "dp_sh": "shard" if trainer.shard_sh else "gather"}
                                   if world > 1 else {})},
             "e2e": e2e, "render": render_fps, "roofline": roofline, "rasterisers": train_rates,
             "cpu_baseline": cpu, "clocks": clk, "gpu_launches": gpu_launches, "stages": stages,

@@ -121,7 +121,8 @@ class DataParallelTrainer(Trainer):
     densify step, sync_parameters) all-gather them first."""
 
     def __init__(self, *args, group=None, optimizer_step: str = "sharded", chunks: int | None = None,
-                 factored: bool = True, views_per_rank: int = 1, shard_sh: bool = False, **kw):
+                 factored: bool = True, views_per_rank: int = 1, shard_sh: bool | None = None,
+                 **kw):
         super().__init__(*args, **kw)
         if views_per_rank < 1:
             raise ValueError(f"views_per_rank {views_per_rank} < 1")
@@ -150,7 +151,9 @@ class DataParallelTrainer(Trainer):
         self._pending_geom = []
         self._pending_sh = []
         self.defer_colour = True  # False: every render waits for all of the last update's gathers
-        self.shard_sh = bool(shard_sh)
+        # default: on with several ranks (one rank saves no traffic and would only add the
+        # owner's work)
+        self.shard_sh = self.world > 1 if shard_sh is None else bool(shard_sh)
         self._sh_stale = False  # other ranks' SH sub-ranges out of date here (shard_sh)
         self._given = None  # colours of this step's views from their owners (shard_sh)
         self._pending_colours = []  # their all-to-alls still in flight
