@@ -242,7 +242,8 @@ def test_data_parallel_sharded_sh_follows_gathered_sh(cuda, views):
     """DataParallelTrainer(shard_sh=True) on one rank: the owner adds the mean gradients'
     colour -> direction terms and computes the next step's colours, which the next render takes.
     Over 8 steps crossing a densify step (which needs every SH coefficient and takes the
-    gathered path), the run follows shard_sh=False within float rounding (the backward blend's
+    gathered path), then a jump to a densify step and two more steps, the run follows
+    shard_sh=False within float rounding (the backward blend's
     float atomics make two runs differ in the last bits; with one view the split rows and the
     given colours are themselves bit-exact: test_owner_colour_direction_rows,
     test_given_colour_render_equals_render)."""
@@ -257,7 +258,12 @@ def test_data_parallel_sharded_sh_follows_gathered_sh(cuda, views):
                                 ro, Tiling.for_camera(cams[0]), TrainingOptions(scene_radius=3.3), seed=7,
                                 views_per_rank=views, shard_sh=shard)
         t.iteration_nb = 3096  # steps 3097 .. 3104: a densify step at 3100
-        losses = torch.stack([t.training_step().clone() for _ in range(8)])[:, :3].cpu()
+        ls = [t.training_step().clone() for _ in range(8)]
+        # a jump straight to a densify step (as bench.py's densify leg does), after a step that
+        # prepared colours for its successor, and two more steps
+        t.iteration_nb = 3199
+        ls += [t.training_step().clone() for _ in range(3)]
+        losses = torch.stack(ls)[:, :3].cpu()
         t.sync_parameters()
         torch.cuda.synchronize()
         runs.append((losses, [x.clone() for x in t.gaussians.tensors()], t.gaussians.n))

@@ -429,6 +429,7 @@ class DataParallelTrainer(Trainer):
         self._vi = V - 1
         acc = V > 1
         cam, loss = self._render_view(compute)
+        self._given = None  # every view of this step has been rendered
         loss_sum = loss if loss_sum is None else loss_sum.add_(loss)
         if V == 1:
             compute.wait_event(zeroed)
@@ -511,7 +512,6 @@ class DataParallelTrainer(Trainer):
             # shard_sh: the owners send the next step's colours instead of all-gathering the SH
             # coefficients, unless the next step densifies (it needs them everywhere)
             give = factored and self.shard_sh and not self._densifies_at(self.iteration_nb + 1)
-            self._given = None  # every view of this step has been rendered
             if factored:
                 pos = self._view_positions()
                 pos_p = pos.ctypes.data_as(C.POINTER(C.c_float))
