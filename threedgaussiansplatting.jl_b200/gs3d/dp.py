@@ -8,9 +8,11 @@ every chunk. For each chunk in turn the projection backward writes its rows
 (gs3d_backward_project_dense) and an in-place NCCL reduce-scatter sums them into the owners'
 sub-ranges while the next chunk's rows are computed; then, chunk by chunk, each rank applies
 the Adam update to the touched Gaussians of its sub-range (gs3d_adam_step_dense_range) and
-in-place all-gathers of the four parameter arrays replicate the result while the next chunk
-is updated. Parameters are identical on every rank after each step; each rank keeps its own
-sub-ranges' moments current. Parameters, moments and rows live in storage padded to
+in-place all-gathers of the parameter arrays replicate the result while the next chunk is
+updated. Parameters are identical on every rank after each step (with sharded SH coefficients,
+the default with several ranks, the SH coefficients after sync_parameters(): between steps each
+rank holds current coefficients only for its own sub-ranges and receives the colours of its
+next views instead); each rank keeps its own sub-ranges' moments current. Parameters, moments and rows live in storage padded to
 chunks * C rows so that every collective runs in place. A densify step all-gathers the
 moments, all-reduces the rows and the statistics, and every rank then makes the same
 decisions and the full update, as the reference retargets fgidx_to_gidx. With one rank this
